@@ -1,0 +1,628 @@
+"""Benchmark of the Axon B200 backend on the BASELINE configs.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl axon|reference]
+
+One JSON line on rank 0. The headline workload is the rope config (Llama-3-8B
+GQA rotary embedding); the other BASELINE configs
+(rmsnorm, nucleus cumsum, 1e9-parameter Adam, SwiGLU MLP) are measured in the
+same run and reported under "workloads" unless --no-extra is given.
+
+A step is one pass of the hot path over one batch of synthetic input: one
+launch of the config's kernel (two tcgen05 GEMMs for the SwiGLU MLP). Timing:
+W untimed steps, then exactly K steps replayed from a CUDA graph, bracketed by
+a barrier and torch.cuda.synchronize() on both sides, CUDA events on the
+launching stream, max over ranks. Memory-bound workloads rotate over enough
+input/output sets that the working set exceeds 2 x L2 (126 MB), so every
+launch reads HBM. `e2e` times the same step through the public API with
+pinned host inputs copied in and the result copied back inside the timed loop.
+
+--impl reference times the reference's CPU path for the same workload (the
+specs' torch references, restated in oracle/cpu_torch.py) on all host cores.
+Multi-GPU (torchrun): memory-bound configs run as replicas (weak scaling);
+Adam shards the 1e9 parameters across ranks with no collective; the SwiGLU
+MLP runs column/row tensor-parallel with an NCCL all-reduce of its output.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import sys
+import time
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from enzyme_b200 import ops, roofline, timing  # noqa: E402
+
+THETA = 500000.0
+
+
+# ---------------------------------------------------------------------------------
+# workloads
+
+
+class Workload:
+    name = ""
+    spec = ""
+    kind = "hbm"
+    dtype = "bf16"
+    launches_per_step = 1
+    use_graph = True
+    scaling = "weak"
+
+    def __init__(self, dev, rank, world):
+        self.dev, self.rank, self.world = dev, rank, world
+        self.gen = torch.Generator(device=dev).manual_seed(42 + rank)
+
+    @property
+    def unit(self):
+        return "GB/s" if self.kind == "hbm" else "TFLOP/s"
+
+    def metric(self):
+        return ("HBM GB/s" if self.kind == "hbm" else "bf16 TFLOP/s") + f" ({self.name})"
+
+    def per_step_work(self) -> float:  # bytes or flops per rank per step
+        return roofline.work(self.spec, self.dims, self.itemsize)[1]
+
+    def job_work(self) -> float:  # whole-job work per step (all ranks)
+        return self.per_step_work() * self.world
+
+    itemsize = 2
+
+
+class Rope(Workload):
+    name, spec = "rope", "rope_gqa"
+
+    def __init__(self, dev, rank, world):
+        super().__init__(dev, rank, world)
+        self.dims = dict(s=4096, hq=32, hkv=8, half_d=64)
+        s, h = 4096, 64
+        inv = THETA ** (-torch.arange(h, dtype=torch.float64) * 2 / 128)
+        ang = torch.arange(s, dtype=torch.float64)[:, None] * inv[None, :]
+        self.cos_h, self.sin_h = torch.cos(ang).float(), torch.sin(ang).float()
+        set_bytes = int(self.per_step_work())
+        self.nsets = timing.sets_to_defeat_l2(set_bytes)
+        self.sets = []
+        for _ in range(self.nsets):
+            q = torch.randn(s, 32, 128, device=dev, generator=self.gen).to(torch.bfloat16)
+            k = torch.randn(s, 8, 128, device=dev, generator=self.gen).to(torch.bfloat16)
+            self.sets.append((q, k, self.cos_h.to(dev), self.sin_h.to(dev), torch.empty_like(q), torch.empty_like(k)))
+        self.working_set = set_bytes * self.nsets
+
+    def launch(self, i):
+        q, k, c, s, qo, ko = self.sets[i % self.nsets]
+        ops.rope_rotate_half(q, k, c, s, q_out=qo, k_out=ko)
+
+    def e2e_setup(self):
+        q, k, c, s, qo, ko = self.sets[0]
+        self.h = [t.cpu().pin_memory() for t in (q, k, c, s)]
+        self.ho = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in (qo, ko)]
+        self.h2d = sum(t.numel() * t.element_size() for t in self.h)
+        self.d2h = sum(t.numel() * t.element_size() for t in self.ho)
+
+    def e2e_step(self, i):
+        q, k, c, s, qo, ko = self.sets[i % self.nsets]
+        for d, h in zip((q, k, c, s), self.h):
+            d.copy_(h, non_blocking=True)
+        ops.rope_rotate_half(q, k, c, s, q_out=qo, k_out=ko)
+        self.ho[0].copy_(qo, non_blocking=True)
+        self.ho[1].copy_(ko, non_blocking=True)
+
+    def cpu_step(self):
+        from oracle import cpu_torch
+
+        tok = 256
+        if not hasattr(self, "_cpu"):
+            g = torch.Generator().manual_seed(1)
+            self._cpu = (torch.randn(tok, 32, 2, 64, generator=g), torch.randn(tok, 8, 2, 64, generator=g),
+                         self.cos_h[:tok].clone(), self.sin_h[:tok].clone())
+        q, k, c, s = self._cpu
+        cpu_torch.rope_rotate_half(q, c, s)
+        cpu_torch.rope_rotate_half(k, c, s)
+        return self.per_step_work() * tok / 4096, f"{tok} of 4096 tokens (q 32 heads + k 8 heads, fp32 torch_ref)"
+
+    def config(self):
+        return {"workload": "rope_gqa: q [4096,32,128] + k [4096,8,128] bf16, fp32 cos/sin [4096,64], theta 5e5",
+                "rotating_sets": self.nsets, "l2": f"inputs rotate over {self.working_set / 2**20:.0f} MiB > 2x L2"}
+
+
+class RmsNorm(Workload):
+    name, spec = "rmsnorm", "rmsnorm_llama"
+
+    def __init__(self, dev, rank, world):
+        super().__init__(dev, rank, world)
+        self.dims = dict(m=2048, n=4096)
+        self.nsets = timing.sets_to_defeat_l2(int(self.per_step_work()))
+        self.sets = []
+        for _ in range(self.nsets):
+            x = torch.randn(2048, 4096, device=dev, generator=self.gen).to(torch.bfloat16)
+            w = (1 + 0.1 * torch.randn(4096, device=dev, generator=self.gen)).to(torch.bfloat16)
+            self.sets.append((x, w, torch.empty_like(x)))
+
+    def launch(self, i):
+        x, w, y = self.sets[i % self.nsets]
+        ops.rmsnorm(x, w, scale=1.0 / 4096, eps=1e-6, out=y)
+
+    def e2e_setup(self):
+        x, w, y = self.sets[0]
+        self.h = [x.cpu().pin_memory(), w.cpu().pin_memory()]
+        self.ho = torch.empty(y.shape, dtype=y.dtype).pin_memory()
+        self.h2d = sum(t.numel() * t.element_size() for t in self.h)
+        self.d2h = self.ho.numel() * 2
+
+    def e2e_step(self, i):
+        x, w, y = self.sets[i % self.nsets]
+        x.copy_(self.h[0], non_blocking=True)
+        w.copy_(self.h[1], non_blocking=True)
+        ops.rmsnorm(x, w, scale=1.0 / 4096, eps=1e-6, out=y)
+        self.ho.copy_(y, non_blocking=True)
+
+    def cpu_step(self):
+        from oracle import cpu_torch
+
+        rows = 256
+        if not hasattr(self, "_cpu"):
+            g = torch.Generator().manual_seed(1)
+            self._cpu = (torch.randn(rows, 4096, generator=g), 1 + 0.1 * torch.randn(4096, generator=g))
+        cpu_torch.rmsnorm_mean(*self._cpu)
+        return self.per_step_work() * rows / 2048, f"{rows} of 2048 rows (fp32 torch_ref)"
+
+    def config(self):
+        return {"workload": "rmsnorm_llama: x [2048,4096] bf16, w [4096], eps 1e-6, mean form",
+                "rotating_sets": self.nsets}
+
+
+class Cumsum(Workload):
+    name, spec = "cumsum", "cumsum_nucleus_sorted"
+    dtype = "f32"
+    itemsize = 4
+
+    def __init__(self, dev, rank, world):
+        super().__init__(dev, rank, world)
+        self.dims = dict(m=256, n=128256)
+        self.nsets = timing.sets_to_defeat_l2(int(self.per_step_work()))
+        self.sets = []
+        for _ in range(self.nsets):
+            logits = 2.0 * torch.randn(256, 128256, device=dev, generator=self.gen)
+            x = torch.sort(torch.softmax(logits, dim=1), dim=1, descending=True).values.contiguous()
+            ws = torch.empty(ops.cumsum_workspace_bytes(256, 128256), dtype=torch.uint8, device=dev)
+            self.sets.append((x, torch.empty_like(x), ws))
+
+    def launch(self, i):
+        x, y, ws = self.sets[i % self.nsets]
+        ops.cumsum(x, out=y, workspace=ws)
+
+    def check(self):
+        for _, _, ws in self.sets:
+            ops.cumsum_status(ws)
+
+    def e2e_setup(self):
+        x, y, _ = self.sets[0]
+        self.h = x.cpu().pin_memory()
+        self.ho = torch.empty(y.shape, dtype=y.dtype).pin_memory()
+        self.h2d = self.h.numel() * 4
+        self.d2h = self.ho.numel() * 4
+
+    def e2e_step(self, i):
+        x, y, ws = self.sets[i % self.nsets]
+        x.copy_(self.h, non_blocking=True)
+        ops.cumsum(x, out=y, workspace=ws)
+        self.ho.copy_(y, non_blocking=True)
+
+    def cpu_step(self):
+        from oracle import cpu_torch
+
+        rows = 32
+        if not hasattr(self, "_cpu"):
+            self._cpu = self.sets[0][0][:rows].cpu()
+        cpu_torch.cumsum(self._cpu)
+        return self.per_step_work() * rows / 256, f"{rows} of 256 rows (fp32 torch.cumsum)"
+
+    def config(self):
+        return {"workload": "cumsum_nucleus_sorted: 256 x 128256 fp32 sorted softmax rows", "rotating_sets": self.nsets}
+
+
+class Adam(Workload):
+    name, spec = "fused_adam", "fused_adam_cfg"
+    dtype = "f32"
+    TOTAL = 1_000_000_000
+
+    def __init__(self, dev, rank, world):
+        super().__init__(dev, rank, world)
+        n = self.TOTAL // world
+        self.n = n
+        self.scaling = "strong"
+        self.dims = dict(p=1, f=n)
+        self.p = torch.randn(n, device=dev, generator=self.gen).mul_(0.02)
+        self.g = torch.randn(n, device=dev, generator=self.gen).mul_(1e-3).to(torch.bfloat16)
+        self.m = torch.zeros(n, device=dev)
+        self.v = torch.zeros(n, device=dev)
+        self.ss = 3e-4 / (1 - 0.9 ** 10)
+        self.ib = 1 / math.sqrt(1 - 0.95 ** 10)
+        self.nsets = 1
+
+    def per_step_work(self):
+        return 26.0 * self.n
+
+    def launch(self, i):
+        ops.adam(self.p, self.g, self.m, self.v, step_size=self.ss, inv_bc2_sqrt=self.ib, wd=0.1, beta1=0.9,
+                 beta2=0.95, eps=1e-8, out=(self.p, self.m, self.v))
+
+    def e2e_setup(self):
+        # end to end at this size is a PCIe stream of 26 GB per step; time a
+        # 1e8-parameter slice through the same call and scale per byte.
+        self.e2e_n = min(self.n, 100_000_000)
+        sl = slice(0, self.e2e_n)
+        self.h = [t[sl].cpu().pin_memory() for t in (self.p, self.g, self.m, self.v)]
+        self.ho = [torch.empty(self.e2e_n).pin_memory() for _ in range(3)]
+        self.h2d = sum(t.numel() * t.element_size() for t in self.h)
+        self.d2h = 12 * self.e2e_n
+        self.e2e_scale = self.e2e_n / self.n
+
+    def e2e_step(self, i):
+        sl = slice(0, self.e2e_n)
+        dst = (self.p[sl], self.g[sl], self.m[sl], self.v[sl])
+        for d, h in zip(dst, self.h):
+            d.copy_(h, non_blocking=True)
+        ops.adam(*dst, step_size=self.ss, inv_bc2_sqrt=self.ib, wd=0.1, beta1=0.9, beta2=0.95,
+                 out=(dst[0], dst[2], dst[3]))
+        for h, d in zip(self.ho, (dst[0], dst[2], dst[3])):
+            h.copy_(d, non_blocking=True)
+
+    def cpu_step(self):
+        from oracle import cpu_torch
+
+        n = 10_000_000
+        if not hasattr(self, "_cpu"):
+            g = torch.Generator().manual_seed(1)
+            self._cpu = (0.02 * torch.randn(n, generator=g), 1e-3 * torch.randn(n, generator=g),
+                         torch.zeros(n), torch.zeros(n))
+        cpu_torch.adam(*self._cpu, self.ss, self.ib, 0.1, beta1=0.9, beta2=0.95)
+        return 26.0 * n, f"1e7 of 1e9 parameters (fp32 torch_ref)"
+
+    def config(self):
+        return {"workload": f"fused_adam_cfg: 1e9 fp32 params (+bf16 grads), {self.n} per rank, in place",
+                "l2": "working set 26 GB >> L2"}
+
+
+class SwiGLU(Workload):
+    name, spec = "silu_mlp", "silu_mlp_swiglu"
+    kind = "tensor"
+    launches_per_step = 2
+
+    def __init__(self, dev, rank, world):
+        super().__init__(dev, rank, world)
+        m, h, inter = 4096, 4096, 14336
+        if inter % world:
+            raise SystemExit(f"intermediate {inter} not divisible by {world} ranks")
+        self.shard = inter // world
+        self.dims = dict(m=m, n=inter, k=h, p=h)
+        g = torch.Generator(device=dev).manual_seed(42)  # same x on every rank
+        self.x = torch.randn(m, h, device=dev, generator=g).to(torch.bfloat16)
+        self.w1 = (0.02 * torch.randn(h, self.shard, device=dev, generator=self.gen)).to(torch.bfloat16)
+        self.w2 = (0.02 * torch.randn(h, self.shard, device=dev, generator=self.gen)).to(torch.bfloat16)
+        self.w3 = (0.02 * torch.randn(self.shard, h, device=dev, generator=self.gen)).to(torch.bfloat16)
+        self.act = torch.empty(m * self.shard * 2, dtype=torch.uint8, device=dev)
+        self.y = torch.empty(m, h, dtype=torch.bfloat16 if world == 1 else torch.float32, device=dev)
+        self.nsets = 1
+        self.scaling = "strong" if world > 1 else "weak"
+        self.use_graph = world == 1
+        if world > 1:
+            self.launches_per_step = 2
+
+    def per_step_work(self):
+        m, n, k, p = 4096, self.shard, 4096, 4096
+        return 2.0 * m * k * n * 2 + 2.0 * m * n * p
+
+    def job_work(self):
+        return roofline.work(self.spec, self.dims)[1]
+
+    def launch(self, i):
+        ops.silu_mlp(self.x, self.w1, self.w2, self.w3, out=self.y, workspace=self.act)
+        if self.world > 1:
+            dist.all_reduce(self.y)
+
+    def e2e_setup(self):
+        self.h = self.x.cpu().pin_memory()
+        self.ho = torch.empty(self.y.shape, dtype=self.y.dtype).pin_memory()
+        self.h2d = self.h.numel() * 2
+        self.d2h = self.ho.numel() * self.ho.element_size()
+
+    def e2e_step(self, i):
+        self.x.copy_(self.h, non_blocking=True)
+        self.launch(i)
+        self.ho.copy_(self.y, non_blocking=True)
+
+    def cpu_step(self):
+        from oracle import cpu_torch
+
+        rows = 64
+        if not hasattr(self, "_cpu"):
+            g = torch.Generator().manual_seed(1)
+            self._cpu = (torch.randn(rows, 4096, generator=g), 0.02 * torch.randn(4096, 14336, generator=g),
+                         0.02 * torch.randn(4096, 14336, generator=g), 0.02 * torch.randn(14336, 4096, generator=g))
+        cpu_torch.silu_mlp(*self._cpu)
+        return roofline.work(self.spec, dict(m=rows, n=14336, k=4096, p=4096))[1], \
+            f"{rows} of 4096 tokens (fp32 torch, same weights shape)"
+
+    def config(self):
+        par = "tp1" if self.world == 1 else f"tp{self.world} (column/row, NCCL all-reduce fp32)"
+        return {"workload": "silu_mlp_swiglu: m 4096, hidden 4096, inter 14336, bf16, W ~ N(0, 0.02)",
+                "parallelism": par}
+
+
+WORKLOADS = {"rope": Rope, "rmsnorm": RmsNorm, "cumsum": Cumsum, "fused_adam": Adam, "silu_mlp": SwiGLU}
+
+
+# ---------------------------------------------------------------------------------
+# measurement
+
+
+def barrier():
+    if dist.is_initialized():
+        dist.barrier()
+
+
+def max_over_ranks(v: float, dev) -> float:
+    if not dist.is_initialized():
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def measure(w: Workload, steps: int, warmup: int, sampler_gpu: int | None):
+    """Returns (ms for exactly K steps, max over ranks; clocks summary or None)."""
+    if w.use_graph:
+        chunk = steps if steps <= w.nsets else min(steps, 64 * w.nsets) // w.nsets * w.nsets
+        reps, rem = divmod(steps, chunk)
+        graph = timing.capture_graph(w.launch, chunk)
+        tail = timing.capture_graph(lambda i: w.launch(reps * chunk + i), rem) if rem else None
+        wchunk = max(1, min(warmup, chunk))
+        wgraph = timing.capture_graph(w.launch, wchunk)
+
+        def run_timed():
+            for _ in range(reps):
+                graph.replay()
+            if tail is not None:
+                tail.replay()
+
+        def run_warm():
+            for _ in range(math.ceil(warmup / wchunk)):
+                wgraph.replay()
+
+        soak = graph.replay
+    else:
+        def run_timed():
+            for i in range(steps):
+                w.launch(i)
+
+        def run_warm():
+            for i in range(warmup):
+                w.launch(i)
+
+        def soak():
+            w.launch(0)
+
+    sampler = timing.ClockSampler(sampler_gpu) if sampler_gpu is not None else None
+    if sampler:
+        sampler.__enter__()
+        # keep the GPU busy so clocks settle and the sampler sees the load
+        t_end = time.time() + 0.6
+        while time.time() < t_end:
+            soak()
+            torch.cuda.synchronize()
+    run_warm()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    run_timed()
+    end.record()
+    end.synchronize()
+    torch.cuda.synchronize()
+    barrier()
+    ms = start.elapsed_time(end)
+    clocks = None
+    if sampler:
+        sampler.__exit__(None, None, None)
+        clocks = sampler.summary()
+        clocks["window"] = "soak + warmup + timed region of this workload"
+    return max_over_ranks(ms, w.dev), clocks
+
+
+def measure_e2e(w: Workload, steps: int):
+    w.e2e_setup()
+    iters = max(3, min(steps, 20))
+    w.e2e_step(0)
+    torch.cuda.synchronize()
+    barrier()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(iters):
+        w.e2e_step(i)
+    end.record()
+    end.synchronize()
+    ms = max_over_ranks(start.elapsed_time(end), w.dev) / iters
+    scale = getattr(w, "e2e_scale", 1.0)
+    work = w.job_work() * scale
+    val = work / (ms / 1e3) / (1e9 if w.kind == "hbm" else 1e12)
+    return {"value": val, "unit": w.unit, "h2d_bytes_per_step": int(w.h2d), "d2h_bytes_per_step": int(w.d2h),
+            "ms_per_step": ms, "steps": iters,
+            **({"note": f"measured on a {scale:.0%} slice of the step, same call"} if scale != 1.0 else {})}
+
+
+def cpu_baseline(w: Workload, seconds: float):
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    w.cpu_step()  # warm
+    done, t0 = 0.0, time.perf_counter()
+    sample = ""
+    while time.perf_counter() - t0 < seconds:
+        work, sample = w.cpu_step()
+        done += work
+    dt = time.perf_counter() - t0
+    val = done / dt / (1e9 if w.kind == "hbm" else 1e12)
+    return {"value": val, "unit": w.unit, "cores": threads, "kind": "port", "sample": sample,
+            "seconds": round(dt, 2)}
+
+
+def load_traffic() -> dict:
+    p = ROOT / "profiles" / "ncu_traffic.json"
+    if p.is_file():
+        try:
+            return json.loads(p.read_text())
+        except ValueError:
+            return {}
+    return {}
+
+
+def run_workload(name, dev, rank, world, steps, warmup, sampler_gpu, with_e2e=True):
+    w = WORKLOADS[name](dev, rank, world)
+    ms, clocks = measure(w, steps, warmup, sampler_gpu)
+    if hasattr(w, "check"):
+        w.check()
+    ops.gemm_status()
+    per_step_ms = ms / steps
+    value = w.job_work() / (per_step_ms / 1e3) / (1e9 if w.kind == "hbm" else 1e12)
+    # per rank: the step's algorithmic work over the step's device time
+    roof = roofline.fraction(w.kind, w.per_step_work(), per_step_ms / 1e3)
+    tr = load_traffic().get(w.spec)
+    roof["traffic"] = tr.get("bytes_per_launch") if tr else None
+    roof["traffic_source"] = tr.get("source") if tr else None
+    res = {"metric": w.metric(), "value": value, "unit": w.unit, "ms_per_step": per_step_ms, "dtype": w.dtype,
+           "scaling": w.scaling, "roofline": roof, "config": w.config(), "clocks": clocks,
+           "gpu_launches": steps * w.launches_per_step}
+    if with_e2e:
+        res["e2e"] = measure_e2e(w, steps)
+    return w, res
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="rope")
+    ap.add_argument("--impl", choices=("axon", "reference"), default="axon")
+    ap.add_argument("--no-extra", action="store_true", help="skip the other BASELINE configs")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        # The reference's CPU path; under torchrun only rank 0 runs it.
+        if rank != 0:
+            return 0
+        dev = torch.device("cuda", local) if torch.cuda.is_available() else None
+        w = WORKLOADS[args.workload].__new__(WORKLOADS[args.workload])
+        w.dev, w.rank, w.world = dev, 0, 1
+        _prepare_cpu_only(w)
+        t_steps = []
+        for i in range(args.warmup):
+            w.cpu_step()
+        threads = os.cpu_count() or 1
+        torch.set_num_threads(threads)
+        t0 = time.perf_counter()
+        work = 0.0
+        sample = ""
+        for i in range(args.steps):
+            a, sample = w.cpu_step()
+            work += a
+        dt = time.perf_counter() - t0
+        val = work / dt / (1e9 if w.kind == "hbm" else 1e12)
+        line = {"impl": "reference", "metric": w.metric(), "value": val, "unit": w.unit, "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded)", "config": {"workload": w.name + " (bounded CPU sample per step)"},
+                "cpu_baseline": {"value": val, "unit": w.unit, "cores": threads, "kind": "port", "sample": sample},
+                "e2e": {"value": val, "unit": w.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return 0
+
+    if world > 1:
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    sampler_gpu = local if rank == 0 else None
+
+    head, res = run_workload(args.workload, dev, rank, world, args.steps, args.warmup, sampler_gpu)
+    line = {
+        "metric": res["metric"], "value": res["value"], "unit": res["unit"], "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
+        "higher_is_better": True, "scaling": res["scaling"], "vs_baseline": None, "dtype": res["dtype"],
+        "data": "synthetic (seeded randn on device; no dataset)",
+        "config": {**res["config"], "parallelism": res["config"].get("parallelism", f"replicas x{world}")},
+        "roofline": res["roofline"], "clocks": res["clocks"], "e2e": res["e2e"],
+        "gpu_launches": res["gpu_launches"],
+    }
+    if rank == 0 and world == 1:
+        line["cpu_baseline"] = cpu_baseline(head, args.cpu_seconds)
+    del head
+    torch.cuda.empty_cache()
+    if not args.no_extra:
+        extra = {}
+        for name in WORKLOADS:
+            if name == args.workload:
+                continue
+            w, r = run_workload(name, dev, rank, world, max(3, min(args.steps, 20 if name in ("fused_adam", "silu_mlp") else args.steps)),
+                                args.warmup, None, with_e2e=False)
+            extra[name] = {k: r[k] for k in ("metric", "value", "unit", "ms_per_step", "roofline", "scaling",
+                                             "gpu_launches")}
+            extra[name]["config"] = r["config"]
+            del w
+            torch.cuda.empty_cache()
+        line["workloads"] = extra
+    if rank == 0:
+        print(json.dumps(line))
+    if dist.is_initialized():
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def _prepare_cpu_only(w):
+    """Fields the CPU step needs, without touching a GPU."""
+    name = type(w).__name__
+    if name == "Rope":
+        w.dims = dict(s=4096, hq=32, hkv=8, half_d=64)
+        inv = THETA ** (-torch.arange(64, dtype=torch.float64) * 2 / 128)
+        ang = torch.arange(4096, dtype=torch.float64)[:, None] * inv[None, :]
+        w.cos_h, w.sin_h = torch.cos(ang).float(), torch.sin(ang).float()
+    elif name == "RmsNorm":
+        w.dims = dict(m=2048, n=4096)
+    elif name == "Cumsum":
+        w.dims = dict(m=256, n=128256)
+        logits = 2.0 * torch.randn(32, 128256, generator=torch.Generator().manual_seed(1))
+        x = torch.sort(torch.softmax(logits, dim=1), dim=1, descending=True).values.contiguous()
+        w.sets = [(x, None, None)]
+    elif name == "Adam":
+        w.n = Adam.TOTAL
+        w.dims = dict(p=1, f=w.n)
+        w.ss = 3e-4 / (1 - 0.9 ** 10)
+        w.ib = 1 / math.sqrt(1 - 0.95 ** 10)
+    elif name == "SwiGLU":
+        w.dims = dict(m=4096, n=14336, k=4096, p=4096)
+        w.shard = 14336
+
+
+if __name__ == "__main__":
+    sys.exit(main())

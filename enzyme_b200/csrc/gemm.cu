@@ -1,0 +1,561 @@
+// Dense path: a persistent, warp-specialised tcgen05 GEMM for sm_100a.
+//
+//   C[m, n] = epilogue(A[m, k] @ B[k, n])      A, B bf16 (or both f16)
+//
+// A is row-major (K-major for the MMA); B is the [k, n] row-major weight the
+// Axon specs pass (kernels/matmul/refs.py:24-25), consumed in place as an
+// MN-major operand, so no transpose pass runs.
+//
+// One CTA per SM, 192 threads:
+//   warp 0      TMA producer: streams 128x64 A slabs and BNx64 B slabs into a
+//               ring of `stages` shared-memory buffers (128-byte swizzle),
+//               one mbarrier per stage carrying the transaction bytes;
+//   warp 1      TMEM owner and MMA issuer: one thread issues
+//               tcgen05.mma.cta_group::1.kind::f16 (M=128, N=BN, K=16) into a
+//               double-buffered fp32 accumulator in tensor memory, and frees
+//               each smem stage with tcgen05.commit when its MMAs retire;
+//   warps 2..5  epilogue: tcgen05.ld the accumulator (each warp owns its
+//               32-lane quarter of TMEM), apply the epilogue in registers and
+//               store to global memory, overlapping the next tile's mainloop.
+// Epilogues: NONE; ROWSCALE (C = r[i] * acc, the rmsnorm_matmul norm);
+// SILU_GATE (the B tile holds BN/2 gate columns from w1 and the matching BN/2
+// up columns from w2, so one N=BN MMA yields both and C = silu(g) * u).
+//
+// No TMA multicast is used anywhere, so the kernel is legal when its operands
+// live in any GPU's memory. Every mbarrier wait is bounded (about two seconds
+// of %globaltimer); a wait that gives up raises a CTA-wide abort flag and the
+// device error word read by axon_gemm_status(), and every role drains out.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+
+namespace axon {
+
+__device__ int g_gemm_error;
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;              // bf16 elements per 128-byte swizzle row
+constexpr int A_BYTES = BM * BK * 2;
+constexpr int B_CHUNK = 64 * BK * 2;  // one 64-column MN-major swizzle block
+constexpr int EPI_THREADS = 128;
+constexpr unsigned long long kTimeoutNs = 2000000000ull;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait on an mbarrier phase. Returns false if this CTA has aborted or
+// the wait ran past the time limit (which then aborts the CTA).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 127) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer() - t0 > kTimeoutNs) {
+        *abort_flag = 1;
+        atomicExch(&g_gemm_error, AXON_E_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit TMEM columns -> 32 registers per thread.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor (sm_100 format): start address, leading and
+// stride byte offsets (all >> 4), descriptor version 1 at bit 46, 128-byte
+// swizzle (layout type 2) at bits 61..63, base offset 0 (buffers are
+// 1024-byte aligned).
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= 1ull << 46;
+  d |= 2ull << 61;
+  return d;
+}
+
+template <typename TC>
+__device__ __forceinline__ void store32(TC* dst, const float* v, int64_t col, int64_t n) {
+  if (col + 32 <= n) {
+    if constexpr (sizeof(TC) == 4) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4)
+        *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        Vec<TC> p;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) p.e[e] = from_f<TC>(v[j + e]);
+        st_vec(dst + j, p);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (col + j < n) dst[j] = from_f<TC>(v[j]);
+  }
+}
+
+struct GemmParams {
+  void* c;
+  const float* row_scale;
+  int m, n, k;       // n = output columns
+  int64_t ldc;
+  int stages;
+  uint32_t idesc;
+};
+
+template <int BN, int EPI, typename TC>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tcgen05(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                 const __grid_constant__ CUtensorMap tmB2, GemmParams p) {
+  constexpr int B_BYTES = BN * BK * 2;
+  constexpr int STAGE = A_BYTES + B_BYTES;
+  constexpr int BN_OUT = EPI == AXON_EPI_SILU_GATE ? BN / 2 : BN;
+  constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int S = p.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * STAGE);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* issued = reinterpret_cast<int*>(tmem_slot + 2);  // TMA slabs issued, per stage
+  int* consumed = issued + S;                            // slabs the MMA warp consumed, per stage
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_m = (p.m + BM - 1) / BM;
+  const int num_n = (p.n + BN_OUT - 1) / BN_OUT;
+  const int tiles = num_m * num_n;
+  const int kblocks = (p.k + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      issued[s] = 0;
+      consumed[s] = 0;
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], EPI_THREADS);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer ----------------
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+      const int tm = t % num_m, tn = t / num_m;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) goto producer_done;
+        mbar_expect_tx(&full[stage], STAGE);
+        uint8_t* sa = smem + stage * STAGE;
+        uint8_t* sb = sa + A_BYTES;
+        tma_load_2d(&tmA, &full[stage], sa, kb * BK, tm * BM);
+        if constexpr (EPI == AXON_EPI_SILU_GATE) {
+#pragma unroll
+          for (int j = 0; j < BN / 128; ++j)
+            tma_load_2d(&tmB, &full[stage], sb + j * B_CHUNK, tn * BN_OUT + j * 64, kb * BK);
+#pragma unroll
+          for (int j = 0; j < BN / 128; ++j)
+            tma_load_2d(&tmB2, &full[stage], sb + (BN / 128 + j) * B_CHUNK, tn * BN_OUT + j * 64, kb * BK);
+        } else {
+#pragma unroll
+          for (int j = 0; j < BN / 64; ++j)
+            tma_load_2d(&tmB, &full[stage], sb + j * B_CHUNK, tn * BN + j * 64, kb * BK);
+        }
+        issued[stage] += 1;
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  producer_done:;
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer ----------------
+    int stage = 0;
+    uint32_t phase = 0;
+    int local = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++local) {
+      const int buf = local & 1;
+      if (!mbar_wait(&tempty[buf], ((local >> 1) & 1) ^ 1u, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t d = tmem_base + static_cast<uint32_t>(buf * BN);
+      bool ok = true;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!mbar_wait(&full[stage], phase, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + stage * STAGE);
+        const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k) {
+          const uint64_t ad = sdesc(sa + k * 32, 16, 1024);
+          const uint64_t bd = sdesc(sb + k * 2048, B_CHUNK, 1024);
+          tc_mma(d, ad, bd, p.idesc, (kb | k) != 0);
+        }
+        tc_commit(&empty[stage]);
+        consumed[stage] += 1;
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+      tc_commit(&tfull[buf]);
+    }
+  } else if (warp >= 2) {
+    // ---------------- epilogue ----------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int local = 0;
+    TC* C = static_cast<TC*>(p.c);
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++local) {
+      const int tm = t % num_m, tn = t / num_m;
+      const int buf = local & 1;
+      if (!mbar_wait(&tfull[buf], (local >> 1) & 1, abort_flag)) break;
+      tc_fence_after();
+      const int64_t row = static_cast<int64_t>(tm) * BM + q * 32 + lane;
+      const bool row_ok = row < p.m;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN);
+      TC* crow = C + (row_ok ? row : 0) * p.ldc;
+      float scale = 1.f;
+      if constexpr (EPI == AXON_EPI_ROWSCALE) scale = row_ok ? p.row_scale[row] : 0.f;
+      if constexpr (EPI == AXON_EPI_SILU_GATE) {
+#pragma unroll 1
+        for (int c = 0; c < BN_OUT / 32; ++c) {
+          float g[32], u[32];
+          __syncwarp();
+          tmem_ld32(tbase + c * 32, g);
+          tmem_ld32(tbase + BN_OUT + c * 32, u);
+          tmem_wait_ld();
+          const int64_t col = static_cast<int64_t>(tn) * BN_OUT + c * 32;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) g[j] = g[j] / (1.0f + __expf(-g[j])) * u[j];
+          if (row_ok && col < p.n) store32<TC>(crow + col, g, col, p.n);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          __syncwarp();
+          tmem_ld32(tbase + c * 32, v);
+          tmem_wait_ld();
+          const int64_t col = static_cast<int64_t>(tn) * BN + c * 32;
+          if constexpr (EPI == AXON_EPI_ROWSCALE) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] *= scale;
+          }
+          if (row_ok && col < p.n) store32<TC>(crow + col, v, col, p.n);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[buf]);
+    }
+  }
+
+  __syncthreads();
+  if (threadIdx.x == 0 && *abort_flag) {
+    // Drain TMA copies that were issued but never consumed, so no copy is in
+    // flight into shared memory when the CTA exits.
+    for (int s = 0; s < S; ++s) {
+      if (issued[s] > consumed[s]) {
+        volatile int never = 0;
+        mbar_wait(&full[s], static_cast<uint32_t>((issued[s] - 1) & 1), &never);
+      }
+    }
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// ---- host side -------------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 2-D tensor map over a row-major [outer, inner] matrix with 128-byte swizzle.
+int make_map(CUtensorMap* map, const void* base, int32_t dtype, uint64_t inner, uint64_t outer, uint64_t ld,
+             uint32_t box_inner, uint32_t box_outer, const char* what) {
+  auto fn = encode_fn();
+  if (!fn) return fail(AXON_E_CUDA, "axon_gemm: cuTensorMapEncodeTiled unavailable");
+  const CUtensorMapDataType dt =
+      dtype == AXON_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(AXON_E_ARG, "axon_gemm: tensor map for %s rejected (CUresult %d)", what, (int)r);
+  return AXON_OK;
+}
+
+template <int BN, int EPI, typename TC>
+int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb2, const GemmParams& gp,
+                cudaStream_t s) {
+  constexpr int STAGE = A_BYTES + BN * BK * 2;
+  const size_t smem = static_cast<size_t>(gp.stages) * STAGE + 1024 + 256;
+  auto kern = gemm_tcgen05<BN, EPI, TC>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return fail(AXON_E_LAUNCH, "axon_gemm: smem attribute: %s", cudaGetErrorString(e));
+  constexpr int BN_OUT = EPI == AXON_EPI_SILU_GATE ? BN / 2 : BN;
+  const int64_t tiles = static_cast<int64_t>((gp.m + BM - 1) / BM) * ((gp.n + BN_OUT - 1) / BN_OUT);
+  const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
+  kern<<<grid, 192, smem, s>>>(ma, mb, mb2, gp);
+  return launch_status("axon_gemm");
+}
+
+template <int BN, int EPI>
+int dispatch_c(int32_t c_dtype, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb2,
+               const GemmParams& gp, cudaStream_t s) {
+  switch (c_dtype) {
+    case AXON_BF16: return launch_gemm<BN, EPI, __nv_bfloat16>(ma, mb, mb2, gp, s);
+    case AXON_F16: return launch_gemm<BN, EPI, __half>(ma, mb, mb2, gp, s);
+    case AXON_F32: return launch_gemm<BN, EPI, float>(ma, mb, mb2, gp, s);
+    default: return fail(AXON_E_UNSUPPORTED, "axon_gemm: unsupported output dtype %d", c_dtype);
+  }
+}
+
+int max_stages(int bn) {
+  const int stage = A_BYTES + bn * BK * 2;
+  const int avail = 232448 - 1024 - 256;
+  int s = avail / stage;
+  return s > 8 ? 8 : s;
+}
+
+}  // namespace
+}  // namespace axon
+
+using namespace axon;
+
+extern "C" int axon_gemm(const void* a, const void* b, const void* b2, void* c, const float* row_scale, int64_t m,
+                         int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int32_t ab_dtype,
+                         int32_t c_dtype, int32_t epilogue, const axon_tune_t* tune, void* stream) {
+  axon_tune_t t = tune_or_default(tune);
+  if (!a || !b || !c) return fail(AXON_E_ARG, "axon_gemm: NULL operand");
+  if (ab_dtype != AXON_BF16 && ab_dtype != AXON_F16)
+    return fail(AXON_E_UNSUPPORTED, "axon_gemm: A/B dtype must be bf16 or f16 (got %d)", ab_dtype);
+  if (epilogue < AXON_EPI_NONE || epilogue > AXON_EPI_SILU_GATE)
+    return fail(AXON_E_ARG, "axon_gemm: unknown epilogue %d", epilogue);
+  if (epilogue == AXON_EPI_SILU_GATE && !b2) return fail(AXON_E_ARG, "axon_gemm: SILU_GATE needs b2");
+  if (epilogue == AXON_EPI_ROWSCALE && !row_scale) return fail(AXON_E_ARG, "axon_gemm: ROWSCALE needs row_scale");
+  if (m < 0 || n < 0 || k < 0 || m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff)
+    return fail(AXON_E_SHAPE, "axon_gemm: sizes out of range");
+  if (k % 8 || n % 8) return fail(AXON_E_SHAPE, "axon_gemm: k and n must be multiples of 8 (k=%lld n=%lld)",
+                                  (long long)k, (long long)n);
+  if (lda < k || ldb < n || ldc < n) return fail(AXON_E_SHAPE, "axon_gemm: leading dimension too small");
+  if (lda % 8 || ldb % 8 || ldc % 8) return fail(AXON_E_ALIGN, "axon_gemm: leading dimensions must be multiples of 8");
+  if (!aligned16(a) || !aligned16(b) || !aligned16(c) || (b2 && !aligned16(b2)))
+    return fail(AXON_E_ALIGN, "axon_gemm: operands must be 16-byte aligned");
+  if (t.variant != 0) return fail(AXON_E_ARG, "axon_gemm: unknown variant %d", t.variant);
+  if (t.block_m != 0 && t.block_m != 128) return fail(AXON_E_ARG, "axon_gemm: block_m must be 128");
+  if (t.block_k != 0 && t.block_k != 64) return fail(AXON_E_ARG, "axon_gemm: block_k must be 64");
+  if (m == 0 || n == 0) return AXON_OK;
+  if (k == 0) return fail(AXON_E_SHAPE, "axon_gemm: k == 0 not supported");
+
+  int bn = t.block_n;
+  if (bn == 0) bn = epilogue == AXON_EPI_SILU_GATE ? 256 : (n <= 64 ? 64 : n <= 128 ? 128 : 256);
+  if (bn != 64 && bn != 128 && bn != 256) return fail(AXON_E_ARG, "axon_gemm: block_n must be 64, 128 or 256");
+  if (epilogue == AXON_EPI_SILU_GATE && bn == 64) return fail(AXON_E_ARG, "axon_gemm: SILU_GATE needs block_n >= 128");
+  const int smax = max_stages(bn);
+  int stages = t.stages > 0 ? t.stages : smax;
+  if (stages < 2 || stages > smax) return fail(AXON_E_ARG, "axon_gemm: stages must be in [2, %d] for block_n %d", smax, bn);
+
+  CUtensorMap ma, mb, mb2;
+  int rc = make_map(&ma, a, ab_dtype, k, m, lda, BK, BM, "A");
+  if (rc) return rc;
+  rc = make_map(&mb, b, ab_dtype, n, k, ldb, 64, BK, "B");
+  if (rc) return rc;
+  if (b2) {
+    rc = make_map(&mb2, b2, ab_dtype, n, k, ldb, 64, BK, "B2");
+    if (rc) return rc;
+  } else {
+    mb2 = mb;
+  }
+  GemmParams gp;
+  gp.c = c;
+  gp.row_scale = row_scale;
+  gp.m = static_cast<int>(m);
+  gp.n = static_cast<int>(n);
+  gp.k = static_cast<int>(k);
+  gp.ldc = ldc;
+  gp.stages = stages;
+  const uint32_t fmt = ab_dtype == AXON_BF16 ? 1u : 0u;
+  gp.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | (0u << 15) | (1u << 16) |
+             (static_cast<uint32_t>(bn >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
+  cudaStream_t s = as_stream(stream);
+  switch (epilogue * 4 + (bn == 64 ? 0 : bn == 128 ? 1 : 2)) {
+    case 0: return dispatch_c<64, AXON_EPI_NONE>(c_dtype, ma, mb, mb2, gp, s);
+    case 1: return dispatch_c<128, AXON_EPI_NONE>(c_dtype, ma, mb, mb2, gp, s);
+    case 2: return dispatch_c<256, AXON_EPI_NONE>(c_dtype, ma, mb, mb2, gp, s);
+    case 4: return dispatch_c<64, AXON_EPI_ROWSCALE>(c_dtype, ma, mb, mb2, gp, s);
+    case 5: return dispatch_c<128, AXON_EPI_ROWSCALE>(c_dtype, ma, mb, mb2, gp, s);
+    case 6: return dispatch_c<256, AXON_EPI_ROWSCALE>(c_dtype, ma, mb, mb2, gp, s);
+    case 9: return dispatch_c<128, AXON_EPI_SILU_GATE>(c_dtype, ma, mb, mb2, gp, s);
+    case 10: return dispatch_c<256, AXON_EPI_SILU_GATE>(c_dtype, ma, mb, mb2, gp, s);
+    default: return fail(AXON_E_ARG, "axon_gemm: unsupported tile/epilogue combination");
+  }
+}
+
+extern "C" int axon_gemm_status(void* stream) {
+  int v = 0;
+  cudaStream_t s = as_stream(stream);
+  cudaError_t e = cudaMemcpyFromSymbolAsync(&v, g_gemm_error, sizeof(int), 0, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return fail(AXON_E_CUDA, "axon_gemm_status: %s", cudaGetErrorString(e));
+  if (v != 0) {
+    int zero = 0;
+    cudaMemcpyToSymbolAsync(g_gemm_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s);
+    cudaStreamSynchronize(s);
+    return fail(v, "axon_gemm: a pipeline wait gave up (status %d)", v);
+  }
+  return AXON_OK;
+}
+
+extern "C" int axon_rmsnorm_matmul(const void* x, const void* w, void* y, void* workspace, int64_t m, int64_t n,
+                                   int64_t k, int32_t ab_dtype, int32_t c_dtype, const axon_tune_t* tune,
+                                   void* stream) {
+  if (!workspace) return fail(AXON_E_ARG, "axon_rmsnorm_matmul: workspace (4*m bytes) required");
+  int rc = axon_row_rsqrt(x, static_cast<float*>(workspace), m, k, k, ab_dtype, 1.0f, 0.0f, stream);
+  if (rc) return rc;
+  return axon_gemm(x, w, nullptr, y, static_cast<const float*>(workspace), m, n, k, k, n, n, ab_dtype, c_dtype,
+                   AXON_EPI_ROWSCALE, tune, stream);
+}
+
+extern "C" int64_t axon_silu_mlp_workspace_bytes(int64_t m, int64_t n, int32_t ab_dtype) {
+  (void)ab_dtype;
+  return m * n * 2;
+}
+
+extern "C" int axon_silu_mlp(const void* x, const void* w1, const void* w2, const void* w3, void* y,
+                             void* workspace, int64_t workspace_bytes, int64_t m, int64_t n, int64_t k, int64_t p,
+                             int32_t ab_dtype, int32_t c_dtype, const axon_tune_t* tune, void* stream) {
+  if (!workspace || workspace_bytes < m * n * 2)
+    return fail(AXON_E_ARG, "axon_silu_mlp: workspace of %lld bytes needed", (long long)(m * n * 2));
+  axon_tune_t t = tune_or_default(tune);
+  axon_tune_t up = t, down = t;
+  up.block_n = t.block_n == 64 ? 0 : t.block_n;
+  int rc = axon_gemm(x, w1, w2, workspace, nullptr, m, n, k, k, n, n, ab_dtype, ab_dtype, AXON_EPI_SILU_GATE, &up,
+                     stream);
+  if (rc) return rc;
+  down.stages = 0;
+  return axon_gemm(workspace, w3, nullptr, y, nullptr, m, p, n, n, p, p, ab_dtype, c_dtype, AXON_EPI_NONE, &down,
+                   stream);
+}

@@ -1,0 +1,362 @@
+// Row-wise kernels: rmsnorm (sum and mean forms, optional weight), layernorm,
+// softmax, and the per-row rsqrt(sum x^2) prologue of rmsnorm_matmul.
+//
+// Variant 0 ("row_resident") keeps each row in registers as raw 16-byte
+// packets: one group of threads per row (a warp up to a full 1024-thread CTA)
+// issues every load of the row before it reduces, so each row costs exactly
+// one HBM read and one HBM write. Statistics are fp32, reduced with warp
+// shuffles and (for multi-warp rows) a small shared-memory exchange.
+// Variant 1 ("row_streaming") handles rows too long for registers, and rows
+// whose starts are not 16-byte aligned: a CTA walks its row once per pass;
+// the second pass re-reads the row from L2 (rows in flight are far smaller
+// than the 126 MB L2).
+#include "common.cuh"
+
+namespace axon {
+namespace {
+
+enum RowOp { OP_RMS = 0, OP_LN = 1, OP_SM = 2, OP_RSQRT = 3 };
+
+struct RowArgs {
+  const void* x;
+  void* y;
+  const void* w;   // rmsnorm weight [n] or NULL
+  float* r_out;    // OP_RSQRT output [m]
+  int64_t m, n, ld_x, ld_y;
+  int32_t w_dtype;
+  float scale, eps;
+};
+
+// Sum (or max) across the threads that own one row. `red` holds one slot per
+// warp of the CTA; rows never share a warp.
+template <bool MAX>
+__device__ __forceinline__ float row_allreduce(float v, float* red, int gw, int row_in_cta) {
+  v = MAX ? warp_max(v) : warp_sum(v);
+  if (gw == 1) return v;
+  const int warp = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) red[warp] = v;
+  __syncthreads();
+  float r = red[row_in_cta * gw];
+  for (int i = 1; i < gw; ++i) {
+    float o = red[row_in_cta * gw + i];
+    r = MAX ? fmaxf(r, o) : r + o;
+  }
+  __syncthreads();
+  return r;
+}
+
+__device__ __forceinline__ float weight_at(const RowArgs& a, int64_t col) {
+  return a.w ? load_any(a.w, col, a.w_dtype) : 1.0f;
+}
+
+// 16-bit rows are capped at 512 threads per CTA so a thread may hold up to
+// eight 16-byte packets (64 elements) without spilling.
+template <typename T>
+constexpr int max_row_threads() { return sizeof(T) == 2 ? 512 : 1024; }
+
+template <typename T, int VPT, int OP>
+__global__ void __launch_bounds__(max_row_threads<T>()) row_resident_kernel(RowArgs a, int gw, int rows_per_cta) {
+  constexpr int E = Vec<T>::E;
+  __shared__ float red[32];
+  const int tpr = gw * 32;
+  const int lane = threadIdx.x % tpr;
+  const int row_in_cta = threadIdx.x / tpr;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * rows_per_cta + row_in_cta;
+  const bool active = row < a.m;
+  const int64_t n = a.n;
+  const T* xr = static_cast<const T*>(a.x) + (active ? row : 0) * a.ld_x;
+
+  Vec<T> raw[VPT];
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int64_t col = (static_cast<int64_t>(i) * tpr + lane) * E;
+    if (active && col + E <= n) {
+      raw[i] = ld_vec(xr + col);
+    } else {
+#pragma unroll
+      for (int e = 0; e < E; ++e) raw[i].e[e] = (active && col + e < n) ? xr[col + e] : from_f<T>(0.f);
+    }
+  }
+  auto valid = [&](int i, int e) -> bool {
+    return active && (static_cast<int64_t>(i) * tpr + lane) * E + e < n;
+  };
+
+  float s0 = 0.f, s1 = 0.f;  // op-specific statistics
+  if constexpr (OP == OP_RMS || OP == OP_RSQRT) {
+#pragma unroll
+    for (int i = 0; i < VPT; ++i)
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        float v = to_f(raw[i].e[e]);
+        s0 = fmaf(v, v, s0);
+      }
+    s0 = row_allreduce<false>(s0, red, gw, row_in_cta);
+    s1 = rsqrtf(a.scale * s0 + a.eps);
+    if constexpr (OP == OP_RSQRT) {
+      if (active && lane == 0) a.r_out[row] = s1;
+      return;
+    }
+  } else if constexpr (OP == OP_LN) {
+#pragma unroll
+    for (int i = 0; i < VPT; ++i)
+#pragma unroll
+      for (int e = 0; e < E; ++e) s0 += to_f(raw[i].e[e]);
+    const float mean = row_allreduce<false>(s0, red, gw, row_in_cta) / static_cast<float>(n);
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i)
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        float c = valid(i, e) ? to_f(raw[i].e[e]) - mean : 0.f;
+        ss = fmaf(c, c, ss);
+      }
+    ss = row_allreduce<false>(ss, red, gw, row_in_cta);
+    s0 = mean;
+    s1 = rsqrtf(ss / static_cast<float>(n) + a.eps);
+  } else {  // OP_SM
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i)
+#pragma unroll
+      for (int e = 0; e < E; ++e)
+        if (valid(i, e)) mx = fmaxf(mx, to_f(raw[i].e[e]));
+    mx = row_allreduce<true>(mx, red, gw, row_in_cta);
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i)
+#pragma unroll
+      for (int e = 0; e < E; ++e)
+        if (valid(i, e)) sum += __expf(to_f(raw[i].e[e]) - mx);
+    sum = row_allreduce<false>(sum, red, gw, row_in_cta);
+    s0 = mx;
+    s1 = 1.0f / sum;
+  }
+
+  if (!active) return;
+  T* yr = static_cast<T*>(a.y) + row * a.ld_y;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int64_t col = (static_cast<int64_t>(i) * tpr + lane) * E;
+    if (col >= n) continue;
+    Vec<T> o;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      float v = to_f(raw[i].e[e]);
+      float r;
+      if constexpr (OP == OP_RMS) r = v * s1 * weight_at(a, col + e < n ? col + e : 0);
+      else if constexpr (OP == OP_LN) r = (v - s0) * s1;
+      else r = __expf(v - s0) * s1;
+      o.e[e] = from_f<T>(r);
+    }
+    if (col + E <= n) {
+      st_vec(yr + col, o);
+    } else {
+#pragma unroll
+      for (int e = 0; e < E; ++e)
+        if (col + e < n) yr[col + e] = o.e[e];
+    }
+  }
+}
+
+// One CTA per row, any length / alignment. VEC selects 16-byte packets (the
+// row start and length must then be packet-aligned) or single elements.
+template <typename T, bool VEC, int OP>
+__global__ void __launch_bounds__(1024) row_streaming_kernel(RowArgs a) {
+  constexpr int E = VEC ? Vec<T>::E : 1;
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const int64_t n = a.n;
+  const int gw = blockDim.x / 32;
+  const T* xr = static_cast<const T*>(a.x) + row * a.ld_x;
+  T* yr = static_cast<T*>(a.y) + row * a.ld_y;
+  const int64_t nchunks = (n + E - 1) / E;
+
+  auto load = [&](int64_t c, float* v) {
+    const int64_t col = c * E;
+    if constexpr (VEC) {
+      if (col + E <= n) {
+        Vec<T> p = ld_vec(xr + col);
+#pragma unroll
+        for (int e = 0; e < E; ++e) v[e] = to_f(p.e[e]);
+        return;
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < E; ++e) v[e] = col + e < n ? to_f(xr[col + e]) : 0.f;
+  };
+
+  float s0 = 0.f, s1 = 0.f;
+  float v[E];
+  if constexpr (OP == OP_RMS || OP == OP_RSQRT) {
+    for (int64_t c = threadIdx.x; c < nchunks; c += blockDim.x) {
+      load(c, v);
+#pragma unroll
+      for (int e = 0; e < E; ++e) s0 = fmaf(v[e], v[e], s0);
+    }
+    s0 = row_allreduce<false>(s0, red, gw, 0);
+    s1 = rsqrtf(a.scale * s0 + a.eps);
+    if constexpr (OP == OP_RSQRT) {
+      if (threadIdx.x == 0) a.r_out[row] = s1;
+      return;
+    }
+  } else if constexpr (OP == OP_LN) {
+    for (int64_t c = threadIdx.x; c < nchunks; c += blockDim.x) {
+      load(c, v);
+#pragma unroll
+      for (int e = 0; e < E; ++e) s0 += v[e];
+    }
+    const float mean = row_allreduce<false>(s0, red, gw, 0) / static_cast<float>(n);
+    float ss = 0.f;
+    for (int64_t c = threadIdx.x; c < nchunks; c += blockDim.x) {
+      load(c, v);
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        float d = c * E + e < n ? v[e] - mean : 0.f;
+        ss = fmaf(d, d, ss);
+      }
+    }
+    ss = row_allreduce<false>(ss, red, gw, 0);
+    s0 = mean;
+    s1 = rsqrtf(ss / static_cast<float>(n) + a.eps);
+  } else {  // OP_SM: online max / rescaled sum in one pass
+    float mx = -INFINITY, sum = 0.f;
+    for (int64_t c = threadIdx.x; c < nchunks; c += blockDim.x) {
+      load(c, v);
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        if (c * E + e >= n) continue;
+        if (v[e] > mx) {
+          sum = sum * __expf(mx - v[e]) + 1.f;
+          mx = v[e];
+        } else {
+          sum += __expf(v[e] - mx);
+        }
+      }
+    }
+    const float gmx = row_allreduce<true>(mx, red, gw, 0);
+    sum = mx == -INFINITY ? 0.f : sum * __expf(mx - gmx);
+    sum = row_allreduce<false>(sum, red, gw, 0);
+    s0 = gmx;
+    s1 = 1.0f / sum;
+  }
+
+  if constexpr (OP != OP_RSQRT) {
+  for (int64_t c = threadIdx.x; c < nchunks; c += blockDim.x) {
+    load(c, v);
+    const int64_t col = c * E;
+    float r[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      if constexpr (OP == OP_RMS) r[e] = v[e] * s1 * weight_at(a, col + e < n ? col + e : 0);
+      else if constexpr (OP == OP_LN) r[e] = (v[e] - s0) * s1;
+      else r[e] = __expf(v[e] - s0) * s1;
+    }
+    if constexpr (VEC) {
+      if (col + E <= n) {
+        Vec<T> o;
+#pragma unroll
+        for (int e = 0; e < E; ++e) o.e[e] = from_f<T>(r[e]);
+        st_vec(yr + col, o);
+        continue;
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < E; ++e)
+      if (col + e < n) yr[col + e] = from_f<T>(r[e]);
+  }
+  }
+}
+
+template <typename T, int OP>
+int launch_rows(const RowArgs& a, const axon_tune_t& t, cudaStream_t s, const char* name) {
+  constexpr int E = Vec<T>::E;
+  if (a.m == 0 || a.n == 0) return AXON_OK;
+  const bool vec_ok = aligned16(a.x) && (a.ld_x * sizeof(T)) % 16 == 0 &&
+                      (OP == OP_RSQRT || (aligned16(a.y) && (a.ld_y * sizeof(T)) % 16 == 0));
+  const int64_t nv = (a.n + E - 1) / E;
+  int tpr = 0, vpt = 0;
+  if (t.variant == 0 && vec_ok) {
+    if (t.threads > 0) {
+      tpr = t.threads;
+      if (tpr > max_row_threads<T>())
+        return fail(AXON_E_ARG, "%s: at most %d threads per row for this dtype", name, max_row_threads<T>());
+    } else {
+      tpr = 32;
+      while (tpr < max_row_threads<T>() && (nv + tpr - 1) / tpr > 4) tpr *= 2;
+    }
+    int64_t need = (nv + tpr - 1) / tpr;
+    vpt = need <= 1 ? 1 : need <= 2 ? 2 : need <= 4 ? 4 : need <= 8 ? 8 : 0;
+  }
+  if (vpt > 0) {
+    const int gw = tpr / 32;
+    const int rows_per_cta = tpr >= 128 ? 1 : 128 / tpr;
+    const int64_t grid = (a.m + rows_per_cta - 1) / rows_per_cta;
+    if (grid > 0x7fffffff) return fail(AXON_E_SHAPE, "%s: too many rows (%lld)", name, (long long)a.m);
+    dim3 block(tpr * rows_per_cta);
+    switch (vpt) {
+      case 1: row_resident_kernel<T, 1, OP><<<grid, block, 0, s>>>(a, gw, rows_per_cta); break;
+      case 2: row_resident_kernel<T, 2, OP><<<grid, block, 0, s>>>(a, gw, rows_per_cta); break;
+      case 4: row_resident_kernel<T, 4, OP><<<grid, block, 0, s>>>(a, gw, rows_per_cta); break;
+      default: row_resident_kernel<T, 8, OP><<<grid, block, 0, s>>>(a, gw, rows_per_cta); break;
+    }
+    return launch_status(name);
+  }
+  if (a.m > 0x7fffffff) return fail(AXON_E_SHAPE, "%s: too many rows (%lld)", name, (long long)a.m);
+  int threads = t.threads > 0 ? t.threads : 1024;
+  if (vec_ok)
+    row_streaming_kernel<T, true, OP><<<a.m, threads, 0, s>>>(a);
+  else
+    row_streaming_kernel<T, false, OP><<<a.m, threads, 0, s>>>(a);
+  return launch_status(name);
+}
+
+template <int OP>
+int dispatch_rows(const RowArgs& a, int32_t dtype, const axon_tune_t* tune, void* stream, const char* name) {
+  axon_tune_t t = tune_or_default(tune);
+  if (t.variant < 0 || t.variant > 1) return fail(AXON_E_ARG, "%s: unknown variant %d", name, t.variant);
+  if (t.threads != 0 && (t.threads < 32 || t.threads > 1024 || (t.threads & (t.threads - 1))))
+    return fail(AXON_E_ARG, "%s: threads must be a power of two in [32, 1024], got %d", name, t.threads);
+  if (a.x == nullptr || (OP != OP_RSQRT && a.y == nullptr) || (OP == OP_RSQRT && a.r_out == nullptr))
+    return fail(AXON_E_ARG, "%s: NULL tensor pointer", name);
+  if (a.m < 0 || a.n < 0) return fail(AXON_E_SHAPE, "%s: negative size", name);
+  if (a.ld_x < a.n || (OP != OP_RSQRT && a.ld_y < a.n))
+    return fail(AXON_E_SHAPE, "%s: leading dimension smaller than n", name);
+  cudaStream_t s = as_stream(stream);
+  switch (dtype) {
+    case AXON_F32: return launch_rows<float, OP>(a, t, s, name);
+    case AXON_BF16: return launch_rows<__nv_bfloat16, OP>(a, t, s, name);
+    case AXON_F16: return launch_rows<__half, OP>(a, t, s, name);
+    default: return fail(AXON_E_UNSUPPORTED, "%s: unsupported dtype %d", name, dtype);
+  }
+}
+
+}  // namespace
+}  // namespace axon
+
+using namespace axon;
+
+extern "C" int axon_rmsnorm(const void* x, const void* w, void* y, int64_t m, int64_t n, int64_t ld_x,
+                            int64_t ld_y, int32_t dtype, int32_t w_dtype, float scale, float eps,
+                            const axon_tune_t* tune, void* stream) {
+  if (w != nullptr && !valid_dtype(w_dtype)) return fail(AXON_E_UNSUPPORTED, "axon_rmsnorm: bad weight dtype %d", w_dtype);
+  RowArgs a{x, y, w, nullptr, m, n, ld_x, ld_y, w_dtype, scale, eps};
+  return dispatch_rows<OP_RMS>(a, dtype, tune, stream, "axon_rmsnorm");
+}
+
+extern "C" int axon_layernorm(const void* x, void* y, int64_t m, int64_t n, int64_t ld_x, int64_t ld_y,
+                              int32_t dtype, float eps, const axon_tune_t* tune, void* stream) {
+  RowArgs a{x, y, nullptr, nullptr, m, n, ld_x, ld_y, 0, 1.f, eps};
+  return dispatch_rows<OP_LN>(a, dtype, tune, stream, "axon_layernorm");
+}
+
+extern "C" int axon_softmax(const void* x, void* y, int64_t m, int64_t n, int64_t ld_x, int64_t ld_y,
+                            int32_t dtype, const axon_tune_t* tune, void* stream) {
+  RowArgs a{x, y, nullptr, nullptr, m, n, ld_x, ld_y, 0, 1.f, 0.f};
+  return dispatch_rows<OP_SM>(a, dtype, tune, stream, "axon_softmax");
+}
+
+extern "C" int axon_row_rsqrt(const void* x, float* r, int64_t m, int64_t n, int64_t ld_x, int32_t dtype,
+                              float scale, float eps, void* stream) {
+  RowArgs a{x, nullptr, nullptr, r, m, n, ld_x, 0, 0, scale, eps};
+  return dispatch_rows<OP_RSQRT>(a, dtype, nullptr, stream, "axon_row_rsqrt");
+}

@@ -1,0 +1,278 @@
+// Inclusive prefix sum along the last axis (Axon kernels/cumsum/refs.py:20-22).
+//
+// Variant 0 -- single-pass decoupled look-back (Merrill & Garland, "Single-pass
+// Parallel Prefix Scan with Decoupled Look-back", NVIDIA TR 2016). Each CTA
+// takes the next tile id from an atomic counter, so a tile's predecessors in
+// its row were always claimed by CTAs that are already running; it scans its
+// tile in registers (thread-serial, then warp shuffles, then across warps),
+// publishes the tile aggregate, looks back over predecessor descriptors with
+// one warp until it meets an inclusive prefix, publishes its own inclusive
+// prefix and writes the tile. Every input byte is read once and every output
+// byte written once. Tile sums and carries are float64, so the error of an
+// element is a few fp32 roundings regardless of the row length. Every wait on
+// a predecessor is bounded: a wait that gives up records AXON_E_TIMEOUT in the
+// workspace status word and the CTA finishes (with a wrong prefix) rather than
+// spinning forever.
+#include "common.cuh"
+
+namespace axon {
+namespace {
+
+struct alignas(32) TileDesc {
+  unsigned flag;  // 0 = empty, 1 = aggregate ready, 2 = inclusive prefix ready
+  unsigned pad;
+  double agg;
+  double incl;
+  double pad2;
+};
+
+constexpr int64_t kHeaderBytes = 32;  // int status, unsigned counter, padding
+constexpr long long kSpinLimit = 1ll << 22;
+
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release(unsigned* p, unsigned v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <typename Tin, int ITEMS>
+__device__ __forceinline__ void load_items(const Tin* row, int64_t col, int64_t n, bool vec, float* v) {
+  if (vec && col + ITEMS <= n) {
+    constexpr int E = Vec<Tin>::E;
+#pragma unroll
+    for (int j = 0; j < ITEMS; j += E) {
+      Vec<Tin> p = ld_vec_stream(row + col + j);
+#pragma unroll
+      for (int e = 0; e < E; ++e) v[j + e] = to_f(p.e[e]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < ITEMS; ++j) v[j] = col + j < n ? to_f(row[col + j]) : 0.f;
+  }
+}
+
+template <typename Tout, int ITEMS>
+__device__ __forceinline__ void store_items(Tout* row, int64_t col, int64_t n, bool vec, const float* v) {
+  if (vec && col + ITEMS <= n) {
+    constexpr int E = Vec<Tout>::E;
+#pragma unroll
+    for (int j = 0; j < ITEMS; j += E) {
+      Vec<Tout> p;
+#pragma unroll
+      for (int e = 0; e < E; ++e) p.e[e] = from_f<Tout>(v[j + e]);
+      st_vec_stream(row + col + j, p);
+    }
+  } else {
+    for (int j = 0; j < ITEMS && col + j < n; ++j) row[col + j] = from_f<Tout>(v[j]);
+  }
+}
+
+template <typename Tin, typename Tout, int ITEMS>
+__global__ void __launch_bounds__(1024) cumsum_lookback(const Tin* __restrict__ x, Tout* __restrict__ y,
+                                                        int64_t n, int64_t ld_x, int64_t ld_y,
+                                                        int64_t tiles_per_row, bool vec, unsigned char* ws) {
+  __shared__ unsigned s_tile;
+  __shared__ float s_warp[32];
+  __shared__ double s_prefix;
+  int* status = reinterpret_cast<int*>(ws);
+  unsigned* counter = reinterpret_cast<unsigned*>(ws + 4);
+  TileDesc* desc = reinterpret_cast<TileDesc*>(ws + kHeaderBytes);
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+  if (tid == 0) s_tile = atomicAdd(counter, 1u);
+  __syncthreads();
+  const int64_t t = s_tile;
+  const int64_t row = t / tiles_per_row;
+  const int64_t tr = t - row * tiles_per_row;
+  const int64_t tile_elems = static_cast<int64_t>(blockDim.x) * ITEMS;
+  const int64_t col = tr * tile_elems + static_cast<int64_t>(tid) * ITEMS;
+  const Tin* xr = x + row * ld_x;
+  Tout* yr = y + row * ld_y;
+
+  float v[ITEMS];
+  load_items<Tin, ITEMS>(xr, col, n, vec, v);
+#pragma unroll
+  for (int j = 1; j < ITEMS; ++j) v[j] += v[j - 1];
+  const float tsum = v[ITEMS - 1];
+  float incl = tsum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    float up = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += up;
+  }
+  if (lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    float w = lane < nwarps ? s_warp[lane] : 0.f;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      float up = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += up;
+    }
+    if (lane < nwarps) s_warp[lane] = w;
+  }
+  __syncthreads();
+  const float thread_excl = (warp > 0 ? s_warp[warp - 1] : 0.f) + (incl - tsum);
+  const double tile_agg = static_cast<double>(s_warp[nwarps - 1]);
+
+  if (warp == 0) {
+    double prefix = 0.0;
+    if (tr == 0) {
+      if (lane == 0) {
+        desc[t].incl = tile_agg;
+        st_release(&desc[t].flag, 2u);
+      }
+    } else {
+      if (lane == 0) {
+        desc[t].agg = tile_agg;
+        st_release(&desc[t].flag, 1u);
+      }
+      const int64_t first = t - tr;
+      int64_t base = t - 1;
+      long long spins = 0;
+      bool timed_out = false;
+      while (true) {
+        const int64_t idx = base - lane;
+        const unsigned f = idx >= first ? ld_acquire(&desc[idx].flag) : 2u;
+        const unsigned pmask = __ballot_sync(0xffffffffu, f == 2u);
+        const unsigned zmask = __ballot_sync(0xffffffffu, f == 0u);
+        const int plane = pmask ? __ffs(pmask) - 1 : 32;
+        const unsigned need = plane >= 31 ? 0xffffffffu : ((2u << plane) - 1u);
+        if ((zmask & need) && !timed_out) {
+          if (++spins > kSpinLimit) {
+            timed_out = true;
+            if (lane == 0) atomicExch(status, AXON_E_TIMEOUT);
+          } else {
+            __nanosleep(spins < 64 ? 32 : 256);
+          }
+          continue;
+        }
+        double c = 0.0;
+        if (idx >= first && f != 0u) {
+          if (lane < plane) c = desc[idx].agg;
+          else if (lane == plane) c = desc[idx].incl;
+        }
+        prefix += warp_sum_d(c);
+        if (plane < 32) break;
+        base -= 32;
+        if (base < first) break;
+      }
+      if (lane == 0) {
+        desc[t].incl = prefix + tile_agg;
+        st_release(&desc[t].flag, 2u);
+      }
+    }
+    if (lane == 0) s_prefix = prefix;
+  }
+  __syncthreads();
+  const double p = s_prefix + static_cast<double>(thread_excl);
+  float out[ITEMS];
+#pragma unroll
+  for (int j = 0; j < ITEMS; ++j) out[j] = static_cast<float>(p + static_cast<double>(v[j]));
+  store_items<Tout, ITEMS>(yr, col, n, vec, out);
+}
+
+void tile_shape(const axon_tune_t& t, int& threads, int& items) {
+  switch (t.split) {
+    case 2048: threads = 256; items = 8; break;
+    case 4096: threads = 512; items = 8; break;
+    case 16384: threads = 1024; items = 16; break;
+    default: threads = 512; items = 16; break;  // 8192
+  }
+}
+
+int64_t lookback_ws_bytes(int64_t m, int64_t n, const axon_tune_t& t) {
+  int threads, items;
+  tile_shape(t, threads, items);
+  const int64_t tile = static_cast<int64_t>(threads) * items;
+  const int64_t tpr = n > 0 ? (n + tile - 1) / tile : 0;
+  return kHeaderBytes + static_cast<int64_t>(sizeof(TileDesc)) * m * tpr;
+}
+
+template <typename Tin, typename Tout>
+int launch_lookback(const void* x, void* y, int64_t m, int64_t n, int64_t ld_x, int64_t ld_y, void* ws,
+                    const axon_tune_t& t, cudaStream_t s) {
+  int threads, items;
+  tile_shape(t, threads, items);
+  const int64_t tile = static_cast<int64_t>(threads) * items;
+  const int64_t tpr = (n + tile - 1) / tile;
+  const int64_t tiles = m * tpr;
+  if (tiles > 0x7fffffffLL) return fail(AXON_E_SHAPE, "axon_cumsum: too many tiles (%lld)", (long long)tiles);
+  const bool vec = aligned16(x) && aligned16(y) && (ld_x * sizeof(Tin)) % 16 == 0 &&
+                   (ld_y * sizeof(Tout)) % 16 == 0;
+  cudaError_t e = cudaMemsetAsync(ws, 0, lookback_ws_bytes(m, n, t), s);
+  if (e != cudaSuccess) return fail(AXON_E_CUDA, "axon_cumsum: workspace clear failed: %s", cudaGetErrorString(e));
+  auto* ws8 = static_cast<unsigned char*>(ws);
+  if (items == 8)
+    cumsum_lookback<Tin, Tout, 8><<<static_cast<int>(tiles), threads, 0, s>>>(
+        static_cast<const Tin*>(x), static_cast<Tout*>(y), n, ld_x, ld_y, tpr, vec, ws8);
+  else
+    cumsum_lookback<Tin, Tout, 16><<<static_cast<int>(tiles), threads, 0, s>>>(
+        static_cast<const Tin*>(x), static_cast<Tout*>(y), n, ld_x, ld_y, tpr, vec, ws8);
+  return launch_status("axon_cumsum");
+}
+
+template <typename Tin>
+int dispatch_out(int32_t out_dtype, const void* x, void* y, int64_t m, int64_t n, int64_t ld_x, int64_t ld_y,
+                 void* ws, const axon_tune_t& t, cudaStream_t s) {
+  switch (out_dtype) {
+    case AXON_F32: return launch_lookback<Tin, float>(x, y, m, n, ld_x, ld_y, ws, t, s);
+    case AXON_BF16: return launch_lookback<Tin, __nv_bfloat16>(x, y, m, n, ld_x, ld_y, ws, t, s);
+    default: return fail(AXON_E_UNSUPPORTED, "axon_cumsum: unsupported output dtype %d", out_dtype);
+  }
+}
+
+}  // namespace
+}  // namespace axon
+
+using namespace axon;
+
+extern "C" int64_t axon_cumsum_workspace_bytes(int64_t m, int64_t n, const axon_tune_t* tune) {
+  axon_tune_t t = tune_or_default(tune);
+  if (m < 0 || n < 0) return fail(AXON_E_SHAPE, "axon_cumsum_workspace_bytes: negative size");
+  if (t.variant == 1) return 0;
+  return lookback_ws_bytes(m, n, t);
+}
+
+extern "C" int axon_cumsum(const void* x, void* y, int64_t m, int64_t n, int64_t ld_x, int64_t ld_y,
+                           int32_t in_dtype, int32_t out_dtype, void* workspace, int64_t workspace_bytes,
+                           const axon_tune_t* tune, void* stream) {
+  axon_tune_t t = tune_or_default(tune);
+  if (!x || !y) return fail(AXON_E_ARG, "axon_cumsum: NULL tensor pointer");
+  if (m < 0 || n < 0) return fail(AXON_E_SHAPE, "axon_cumsum: negative size");
+  if (ld_x < n || ld_y < n) return fail(AXON_E_SHAPE, "axon_cumsum: leading dimension smaller than n");
+  if (t.split != 0 && t.split != 2048 && t.split != 4096 && t.split != 8192 && t.split != 16384)
+    return fail(AXON_E_ARG, "axon_cumsum: split must be one of 2048, 4096, 8192, 16384 (got %d)", t.split);
+  if (t.variant != 0) return fail(AXON_E_UNSUPPORTED, "axon_cumsum: variant %d not built", t.variant);
+  if (m == 0 || n == 0) return AXON_OK;
+  const int64_t need = lookback_ws_bytes(m, n, t);
+  if (workspace == nullptr || workspace_bytes < need)
+    return fail(AXON_E_ARG, "axon_cumsum: workspace of %lld bytes needed, got %lld", (long long)need,
+                (long long)workspace_bytes);
+  cudaStream_t s = as_stream(stream);
+  switch (in_dtype) {
+    case AXON_F32: return dispatch_out<float>(out_dtype, x, y, m, n, ld_x, ld_y, workspace, t, s);
+    case AXON_BF16: return dispatch_out<__nv_bfloat16>(out_dtype, x, y, m, n, ld_x, ld_y, workspace, t, s);
+    default: return fail(AXON_E_UNSUPPORTED, "axon_cumsum: unsupported input dtype %d", in_dtype);
+  }
+}
+
+extern "C" int axon_cumsum_status(const void* workspace, void* stream) {
+  if (!workspace) return fail(AXON_E_ARG, "axon_cumsum_status: NULL workspace");
+  int status = 0;
+  cudaError_t e = cudaMemcpyAsync(&status, workspace, sizeof(int), cudaMemcpyDeviceToHost, as_stream(stream));
+  if (e == cudaSuccess) e = cudaStreamSynchronize(as_stream(stream));
+  if (e != cudaSuccess) return fail(AXON_E_CUDA, "axon_cumsum_status: %s", cudaGetErrorString(e));
+  if (status != 0) return fail(status, "axon_cumsum: a look-back wait gave up (status %d)", status);
+  return AXON_OK;
+}

@@ -1,0 +1,71 @@
+"""Algorithmic work per spec (each input read once, each output written once;
+GEMM FLOPs 2*m*n*k) and the roofline denominators.
+
+The peaks are the driver-measured ones in MEASURED_PEAKS.json at the repository
+root (a STREAM-style copy and a cuBLAS bf16 GEMM on this pool's B200s); when
+that file is absent the earlier pool measurement (6650 GB/s, 1590 TFLOP/s) is
+used and reported as "fallback".
+"""
+
+from __future__ import annotations
+
+import json
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parents[1]
+FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.is_file():
+        try:
+            d = json.loads(p.read_text())
+            return {**FALLBACK, **{k: float(d[k]) for k in FALLBACK if k in d}, "source": "measured"}
+        except (ValueError, KeyError):
+            pass
+    return {**FALLBACK, "source": "fallback"}
+
+
+def nbytes(shape, itemsize: int) -> int:
+    return int(np.prod(shape)) * itemsize
+
+
+# spec -> function(dims, itemsize of the activation dtype) -> (kind, amount)
+def work(spec: str, dims: dict, itemsize: int = 2) -> tuple[str, float]:
+    """('hbm', bytes) or ('tensor', flops) for one launch of a spec at dims."""
+    d = dims
+    if spec in ("rmsnorm", "layernorm", "softmax", "cumsum", "cumsum_nucleus_sorted"):
+        return "hbm", 2 * d["m"] * d["n"] * itemsize
+    if spec == "rmsnorm_llama":
+        return "hbm", 2 * d["m"] * d["n"] * itemsize + d["n"] * itemsize
+    if spec == "rope":
+        return "hbm", 6 * d["half_d"] * d["free"] * itemsize
+    if spec == "rope_gqa":
+        qk = d["s"] * (d["hq"] + d["hkv"]) * 2 * d["half_d"] * itemsize
+        return "hbm", 2 * qk + 2 * d["s"] * d["half_d"] * 4
+    if spec == "fused_adam":
+        return "hbm", 7 * d["p"] * d["f"] * itemsize + 3 * d["p"] * itemsize
+    if spec == "fused_adam_cfg":
+        return "hbm", 26 * d["p"] * d["f"] + 3 * 4 * d["p"]
+    if spec in ("matmul", "rmsnorm_matmul"):
+        return "tensor", 2.0 * d["m"] * d["n"] * d["k"]
+    if spec in ("silu_mlp", "silu_mlp_swiglu"):
+        return "tensor", 2.0 * d["m"] * d["k"] * d["n"] * 2 + 2.0 * d["m"] * d["n"] * d["p"]
+    raise KeyError(spec)
+
+
+def fraction(kind: str, amount: float, seconds: float) -> dict:
+    pk = peaks()
+    if kind == "hbm":
+        achieved = amount / seconds / 1e9
+        peak = pk["hbm_gbs"]
+        unit = "GB/s"
+    else:
+        achieved = amount / seconds / 1e12
+        peak = pk["bf16_tflops"]
+        unit = "TFLOP/s"
+    return {"bound": kind, "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
+            "peak_source": pk["source"]}

@@ -1,0 +1,232 @@
+/*
+ * axon_b200.h -- C ABI of the Axon B200 kernel library (libaxon_b200.so).
+ *
+ * This library replaces the compile + bench leg of Axon (src/axon/bench_runner.py:
+ * `_compile_one_nki_kernel` :226-272 and `_bench_one_neff` :144-223, driven by
+ * `run_nki_bench` :576-825): instead of compiling an emitted NKI module to a
+ * NEFF and running it on a NeuronCore, the host calls one of the entry points
+ * below with device pointers.
+ *
+ * Conventions shared by every entry point:
+ *   - Pointers are CUDA device pointers (or managed/peer pointers reachable from
+ *     the current device). The caller owns every allocation; scratch space, where
+ *     a kernel needs any, is passed in (see the *_workspace_bytes queries).
+ *   - Sizes and leading dimensions are in ELEMENTS, int64.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *     No entry point synchronises the host; all work is enqueued on `stream`.
+ *   - The return value is AXON_OK (0) or a negative AXON_E_* code; the message
+ *     for the last failure on the calling thread is axon_last_error().
+ *   - `tune` may be NULL (defaults). Its fields select a kernel variant and its
+ *     tile knobs; axon_variants() lists what each op accepts. A knob the op does
+ *     not use is ignored; a knob outside its legal set is AXON_E_ARG.
+ *   - Row-wise ops require row starts and leading dimensions such that every row
+ *     begins on a 16-byte boundary for the vectorised path; otherwise they take a
+ *     scalar path (same results).
+ */
+#ifndef AXON_B200_H
+#define AXON_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define AXON_API __attribute__((visibility("default")))
+#else
+#define AXON_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------- */
+#define AXON_OK 0
+#define AXON_E_SHAPE (-1)       /* sizes out of range or inconsistent           */
+#define AXON_E_ALIGN (-2)       /* pointer / stride alignment the op requires    */
+#define AXON_E_LAUNCH (-3)      /* kernel launch failed (cudaGetLastError)       */
+#define AXON_E_TIMEOUT (-4)     /* a bounded device-side wait gave up            */
+#define AXON_E_UNSUPPORTED (-5) /* dtype / variant / layout not implemented      */
+#define AXON_E_ARG (-6)         /* bad argument (NULL pointer, bad tune knob)    */
+#define AXON_E_CUDA (-7)        /* other CUDA runtime / driver error             */
+
+/* ---- element types -------------------------------------------------------- */
+typedef enum axon_dtype {
+  AXON_F32 = 0,
+  AXON_BF16 = 1,
+  AXON_F16 = 2
+} axon_dtype_t;
+
+/* ---- variant / tile selection ------------------------------------------- *
+ * The CUDA counterpart of Axon's (hw_variant, TILES_IN_BLOCK_*) key
+ * (src/axon/bench_runner.py:364-388, src/axon/candidate_filter.py:18-45).
+ * Zero in any field means "the op's default".                               */
+typedef struct axon_tune {
+  int32_t variant;      /* kernel variant id within the op (0 = default)      */
+  int32_t threads;      /* CTA size for row / elementwise kernels             */
+  int32_t rows_per_cta; /* rows handled by one CTA (row kernels)              */
+  int32_t block_m;      /* GEMM CTA tile rows (128)                           */
+  int32_t block_n;      /* GEMM CTA tile cols (64..256, multiple of 16)       */
+  int32_t block_k;      /* GEMM k-slab per pipeline stage (64)                */
+  int32_t stages;       /* GEMM smem pipeline depth (2..8)                    */
+  int32_t split;        /* cumsum: elements per tile (variant 0) or CTAs per
+                           row cluster (variant 1)                            */
+} axon_tune_t;
+
+/* ---- library metadata ----------------------------------------------------- */
+
+/* Version string, e.g. "axon_b200 0.1.0 sm_100a". */
+AXON_API const char* axon_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+AXON_API const char* axon_last_error(void);
+
+/* Write a JSON description of `op`'s variants and their tile constraints into
+ * buf (NUL-terminated, truncated to len). Returns the full length needed, or a
+ * negative AXON_E_* code for an unknown op. Replaces the literal
+ * `__axon_tile_constraints__` manifest Axon embeds in each emitted module
+ * (src/axon/candidate_filter.py:13, :56-87). */
+AXON_API int64_t axon_variants(const char* op, char* buf, int64_t len);
+
+/* ---- row-wise normalisation ------------------------------------------------ */
+
+/* y = x * rsqrt(scale * sum_j x[i,j]^2 + eps) * w[j]       (w may be NULL)
+ * scale = 1, eps = 0, w = NULL is Axon's `rmsnorm` spec (x / sqrt(sum x^2),
+ * kernels/rmsnorm/refs.py:26-30); scale = 1/n, eps = 1e-6 with a weight is the
+ * Llama form. Accumulates in fp32. x, y: [m, n] with leading dims ld_x, ld_y;
+ * w: [n] of w_dtype. Replaces the compiled `rmsnorm` NEFF. */
+AXON_API int axon_rmsnorm(const void* x, const void* w, void* y, int64_t m, int64_t n,
+                 int64_t ld_x, int64_t ld_y, int32_t dtype, int32_t w_dtype,
+                 float scale, float eps, const axon_tune_t* tune, void* stream);
+
+/* y = (x - mean) / sqrt(mean((x - mean)^2) + eps) per row, no affine
+ * (Axon kernels/layernorm/refs.py:26-32). */
+AXON_API int axon_layernorm(const void* x, void* y, int64_t m, int64_t n, int64_t ld_x,
+                   int64_t ld_y, int32_t dtype, float eps, const axon_tune_t* tune,
+                   void* stream);
+
+/* y = exp(x) / sum(exp(x)) per row (Axon kernels/softmax/refs.py:11-13),
+ * evaluated max-shifted. */
+AXON_API int axon_softmax(const void* x, void* y, int64_t m, int64_t n, int64_t ld_x,
+                 int64_t ld_y, int32_t dtype, const axon_tune_t* tune, void* stream);
+
+/* ---- rotary embedding ------------------------------------------------------ */
+
+/* Axon's `rope` spec layout (kernels/rope/refs.py:26-30): four [half_d, free]
+ * tensors of `dtype`, two outputs:
+ *   out_even = x_even*cos - x_odd*sin,  out_odd = x_odd*cos + x_even*sin.
+ * Outputs may alias their matching inputs (in-place). */
+AXON_API int axon_rope_split(const void* x_even, const void* x_odd, const void* cos_t,
+                    const void* sin_t, void* out_even, void* out_odd, int64_t half_d,
+                    int64_t free_n, int32_t dtype, const axon_tune_t* tune,
+                    void* stream);
+
+/* Rotate-half rope on q [seq, n_q, head_dim] and k [seq, n_kv, head_dim]
+ * (contiguous, `dtype`), with fp32 tables cos/sin [seq, head_dim/2]:
+ *   out[..., :h] = x1*cos - x2*sin,  out[..., h:] = x2*cos + x1*sin.
+ * k / k_out may be NULL when n_kv == 0. Outputs may alias inputs. */
+AXON_API int axon_rope_rotate_half(const void* q, const void* k, const float* cos_t,
+                          const float* sin_t, void* q_out, void* k_out, int64_t seq,
+                          int64_t n_q, int64_t n_kv, int64_t head_dim, int32_t dtype,
+                          const axon_tune_t* tune, void* stream);
+
+/* ---- prefix sum -------------------------------------------------------------- */
+
+/* Bytes of scratch axon_cumsum needs for this shape and tune (0 if none). */
+AXON_API int64_t axon_cumsum_workspace_bytes(int64_t m, int64_t n, const axon_tune_t* tune);
+
+/* Inclusive scan along the last axis (Axon kernels/cumsum/refs.py:20-22):
+ * y[i, j] = sum_{t<=j} x[i, t], accumulated in fp32 with a float64 running
+ * carry between tiles. in_dtype / out_dtype: AXON_F32 or AXON_BF16.
+ * Variant 0: single-pass decoupled look-back across tiles of a row; needs
+ * `workspace` (zeroed by the call itself, on `stream`); every device-side
+ * wait is bounded and a wait that gives up records AXON_E_TIMEOUT in the
+ * workspace status word (read it with axon_cumsum_status).
+ * Variant 1: one thread-block cluster per row exchanging tile sums through
+ * distributed shared memory; needs no workspace. */
+AXON_API int axon_cumsum(const void* x, void* y, int64_t m, int64_t n, int64_t ld_x,
+                int64_t ld_y, int32_t in_dtype, int32_t out_dtype, void* workspace,
+                int64_t workspace_bytes, const axon_tune_t* tune, void* stream);
+
+/* Synchronise `stream` and read the status word a variant-0 cumsum left in
+ * `workspace`: AXON_OK or AXON_E_TIMEOUT. */
+AXON_API int axon_cumsum_status(const void* workspace, void* stream);
+
+/* ---- optimizer ---------------------------------------------------------------- */
+
+typedef struct axon_adam_hparams {
+  float beta1;        /* 0.9 in Axon's spec (kernels/fused_adam/kernel.py:20) */
+  float beta2;        /* 0.999 in Axon's spec (:21)                           */
+  float eps;          /* 1e-8 (:22)                                           */
+  float step_size;    /* used when step_size_rows == NULL                    */
+  float inv_bc2_sqrt; /* used when inv_bc2_sqrt_rows == NULL                 */
+  float wd;           /* used when wd_rows == NULL                           */
+} axon_adam_hparams_t;
+
+/* L2-regularised Adam over a [rows, cols] block (Axon kernels/fused_adam/
+ * refs.py:38-46):
+ *   g' = g + wd*p;  m' = b1*m + (1-b1)*g';  v' = b2*v + (1-b2)*g'^2;
+ *   p' = p - m' / (sqrt(v')*inv_bc2_sqrt + eps) * step_size.
+ * param / exp_avg / exp_avg_sq and their outputs have `state_dtype`, grad has
+ * `grad_dtype`; per-row scalars (length rows, `row_dtype`) may be NULL to use
+ * the hparams values. Outputs may alias inputs (in-place update). All tensors
+ * are contiguous. */
+AXON_API int axon_adam(const void* param, const void* grad, const void* exp_avg,
+              const void* exp_avg_sq, void* param_out, void* exp_avg_out,
+              void* exp_avg_sq_out, int64_t rows, int64_t cols, int32_t state_dtype,
+              int32_t grad_dtype, const void* step_size_rows,
+              const void* inv_bc2_sqrt_rows, const void* wd_rows, int32_t row_dtype,
+              const axon_adam_hparams_t* hp, const axon_tune_t* tune, void* stream);
+
+/* ---- dense ------------------------------------------------------------------- */
+
+#define AXON_EPI_NONE 0      /* C = A @ B                                        */
+#define AXON_EPI_ROWSCALE 1  /* C = row_scale[i] * (A @ B)                       */
+#define AXON_EPI_SILU_GATE 2 /* C = silu(A @ B) * (A @ B2)  (B2 = up weight)     */
+
+/* tcgen05 / TMEM GEMM: A [m, k] row-major (lda), B [k, n] row-major (ldb) --
+ * the layout Axon's specs pass (kernels/matmul/refs.py:24-25) -- C [m, n]
+ * (ldc). A, B, B2: AXON_BF16 or AXON_F16 (same type); C: AXON_BF16, AXON_F16
+ * or AXON_F32. fp32 accumulation in tensor memory. k and n must be multiples
+ * of 8, lda/ldb/ldc multiples of 8 elements, bases 16-byte aligned (TMA).
+ * row_scale: fp32 [m] for AXON_EPI_ROWSCALE, else NULL. b2: [k, n] for
+ * AXON_EPI_SILU_GATE, else NULL. */
+AXON_API int axon_gemm(const void* a, const void* b, const void* b2, void* c,
+              const float* row_scale, int64_t m, int64_t n, int64_t k, int64_t lda,
+              int64_t ldb, int64_t ldc, int32_t ab_dtype, int32_t c_dtype,
+              int32_t epilogue, const axon_tune_t* tune, void* stream);
+
+/* Synchronise `stream` and report whether a GEMM since the last call gave up
+ * on a bounded pipeline wait (AXON_E_TIMEOUT; the flag is then cleared). */
+AXON_API int axon_gemm_status(void* stream);
+
+/* Per-row scale r[i] = rsqrt(scale * sum_j x[i,j]^2 + eps) in fp32: the norm
+ * prologue of rmsnorm_matmul (Axon kernels/rmsnorm_matmul/refs.py:16-22) and
+ * of the SwiGLU config's optional rmsnorm. */
+AXON_API int axon_row_rsqrt(const void* x, float* r, int64_t m, int64_t n, int64_t ld_x,
+                   int32_t dtype, float scale, float eps, void* stream);
+
+/* (x / sqrt(sum x^2)) @ w (Axon kernels/rmsnorm_matmul/refs.py:16-22): the
+ * row-norm prologue followed by the GEMM with a row-scale epilogue.
+ * workspace: >= 4*m bytes (the per-row scales). */
+AXON_API int axon_rmsnorm_matmul(const void* x, const void* w, void* y, void* workspace,
+                        int64_t m, int64_t n, int64_t k, int32_t ab_dtype,
+                        int32_t c_dtype, const axon_tune_t* tune, void* stream);
+
+/* Bytes of scratch axon_silu_mlp needs: the [m, n] activation in ab_dtype. */
+AXON_API int64_t axon_silu_mlp_workspace_bytes(int64_t m, int64_t n, int32_t ab_dtype);
+
+/* (silu(x @ w1) * (x @ w2)) @ w3 (Axon kernels/silu_mlp/refs.py:16-21):
+ * x [m, k], w1/w2 [k, n], w3 [n, p], y [m, p] of c_dtype. Two tcgen05 GEMMs:
+ * gate and up in one pass with the SiLU-gate epilogue writing the activation
+ * (ab_dtype) into `workspace`, then the down projection. In the column/row
+ * tensor-parallel form each rank passes its shard (n = inter / G) and sums the
+ * fp32 partial outputs across ranks. */
+AXON_API int axon_silu_mlp(const void* x, const void* w1, const void* w2, const void* w3,
+                  void* y, void* workspace, int64_t workspace_bytes, int64_t m,
+                  int64_t n, int64_t k, int64_t p, int32_t ab_dtype, int32_t c_dtype,
+                  const axon_tune_t* tune, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AXON_B200_H */

@@ -1,0 +1,364 @@
+"""GPU parity: every CUDA entry point against the float64 CPU oracle.
+
+Three kinds of evidence per op:
+* the committed golden fixtures (reference `make_inputs` + `baseline_op`),
+  at the reference case tolerances (eval/sizes.json of Axon);
+* the BASELINE configs at full size, seeded, against the oracle (whole
+  tensors where the oracle is cheap, sampled rows otherwise);
+* edge cases the reference exercises: ragged widths, unaligned rows, empty
+  inputs, in-place updates, and argument errors.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_golden, load_spec
+from enzyme_b200 import _native as N
+from enzyme_b200 import ops
+from enzyme_b200.kernel_spec import SEED
+from oracle import f64
+
+pytestmark = pytest.mark.gpu
+
+# Reference case tolerances (Axon eval/sizes.json) and the north-star bars.
+TOL = {
+    "rmsnorm": (1e-2, 1e-2),
+    "layernorm": (2e-2, 2e-2),
+    "rope": (7.8125e-3, 2e-2),
+    "softmax": (2e-2, 2e-2),
+    "cumsum": (1e-3, 1e-3),
+    "cumsum_bf16": (1e-2, 1e-2),
+    "fused_adam": (1e-2, 1e-2),
+    "fused_adam_fp32": (1e-4, 1e-4),
+    "matmul": (2e-2, 2e-2),
+    "silu_mlp": (2e-2, 2e-2),
+    "rmsnorm_matmul": (2e-2, 2e-2),
+}
+
+
+def _t(a, dev):
+    a = np.asarray(a)
+    if a.dtype.name == "bfloat16":
+        return torch.from_numpy(a.view(np.uint16).astype(np.int16)).view(torch.bfloat16).to(dev)
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def _np(t):
+    return t.detach().float().cpu().numpy().astype(np.float64)
+
+
+def _close(got, want, rtol, atol, what=""):
+    got = _np(got) if isinstance(got, torch.Tensor) else got
+    ok = np.allclose(got, want, rtol=rtol, atol=atol)
+    if not ok:
+        err = np.abs(got - want)
+        i = np.unravel_index(np.argmax(err - atol - rtol * np.abs(want)), err.shape)
+        raise AssertionError(f"{what}: max err {err.max():.3e} at {i}: got {got[i]!r} want {want[i]!r}")
+
+
+def _run_spec(spec_name, inputs, dev):
+    """Launch the CUDA kernel for a reference spec on its positional inputs."""
+    t = [_t(a, dev) for a in inputs]
+    if spec_name == "rmsnorm":
+        return (ops.rmsnorm(t[0]),)
+    if spec_name == "layernorm":
+        return (ops.layernorm(t[0], eps=1e-6),)
+    if spec_name == "softmax":
+        return (ops.softmax(t[0]),)
+    if spec_name == "rope":
+        return ops.rope_split(*t)
+    if spec_name == "cumsum":
+        return (ops.cumsum(t[0]),)
+    if spec_name == "fused_adam":
+        return ops.adam(*t[:4], step_size=t[4], inv_bc2_sqrt=t[5], wd=t[6], beta1=0.9, beta2=0.999, eps=1e-8)
+    if spec_name == "matmul":
+        return (ops.gemm(t[0], t[1]),)
+    if spec_name == "silu_mlp":
+        return (ops.silu_mlp(*t),)
+    if spec_name == "rmsnorm_matmul":
+        return (ops.rmsnorm_matmul(t[0], t[1]),)
+    raise KeyError(spec_name)
+
+
+GOLDEN = [
+    "rmsnorm_small", "rmsnorm_ragged", "layernorm_small", "layernorm_ragged", "softmax_small", "softmax_ragged",
+    "rope_small", "rope_ragged", "cumsum_long", "cumsum_ragged", "cumsum_bf16", "fused_adam_bf16",
+    "fused_adam_fp32", "matmul_small", "matmul_tiles", "silu_mlp_small", "rmsnorm_matmul_small",
+]
+
+
+@pytest.mark.parametrize("case", GOLDEN)
+def test_golden_parity(case, cuda_device):
+    spec_name, _, inputs, outs, _ = load_golden(case)
+    tol_key = case if case in TOL else spec_name
+    rtol, atol = TOL[tol_key]
+    got = _run_spec(spec_name, inputs, cuda_device)
+    torch.cuda.synchronize()
+    assert len(got) == len(outs)
+    for g, o in zip(got, outs):
+        _close(g, o.astype(np.float64), rtol, atol, case)
+    # and against the float64 oracle, one output rounding away
+    for g, w in zip(got, f64.evaluate(spec_name, *inputs)):
+        _close(g, w, rtol, atol, case + " vs oracle")
+
+
+# ---- row kernels ---------------------------------------------------------------
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("shape", [(1, 8), (3, 1000), (7, 4096), (5, 8200), (2, 65536), (300, 96)])
+@pytest.mark.parametrize("variant", [0, 1])
+def test_row_ops_shapes(dtype, shape, variant, cuda_device):
+    g = torch.Generator().manual_seed(SEED)
+    x = torch.randn(*shape, generator=g).to(dtype)
+    w = (1 + 0.1 * torch.randn(shape[1], generator=g)).to(dtype)
+    xd, wd = x.to(cuda_device), w.to(cuda_device)
+    xn = x.float().numpy()
+    tune = {"variant": variant}
+    # bf16/f16 outputs round once: 2^-8 relative for bf16, 2^-11 for f16
+    rel = {torch.bfloat16: 8e-3, torch.float16: 1e-3, torch.float32: 1e-5}[dtype]
+    _close(ops.rmsnorm(xd, wd, scale=1 / shape[1], eps=1e-6, tune=tune),
+           f64.rmsnorm_mean(xn, w.float().numpy(), 1e-6), rel, 1e-5, "rmsnorm mean")
+    _close(ops.rmsnorm(xd, tune=tune), f64.rmsnorm_sum(xn), rel, 1e-6, "rmsnorm sum")
+    _close(ops.layernorm(xd, tune=tune), f64.layernorm(xn), rel, 1e-4, "layernorm")
+    _close(ops.softmax(xd, tune=tune), f64.softmax(xn), rel, 1e-7, "softmax")
+
+
+def test_row_ops_strided_and_unaligned(cuda_device):
+    g = torch.Generator().manual_seed(1)
+    base = torch.randn(64, 1040, generator=g).to(torch.bfloat16).to(cuda_device)
+    x = base[:, 3:1003]  # rows start off the 16-byte grid -> scalar path
+    want = f64.layernorm(_np(x))
+    _close(ops.layernorm(x), want, 8e-3, 1e-4, "unaligned layernorm")
+    y = torch.zeros(64, 1040, dtype=torch.bfloat16, device=cuda_device)
+    ops.softmax(base[:, :1024], out=y[:, :1024])  # ld 1040: aligned, strided
+    _close(y[:, :1024], f64.softmax(_np(base[:, :1024])), 8e-3, 1e-7, "strided softmax")
+    assert float(y[:, 1024:].abs().max()) == 0.0
+
+
+def test_row_ops_empty(cuda_device):
+    x = torch.empty(0, 128, dtype=torch.bfloat16, device=cuda_device)
+    assert ops.rmsnorm(x).shape == (0, 128)
+
+
+def test_rmsnorm_config_full_size(cuda_device):
+    spec = load_spec("rmsnorm_llama")
+    x, w = spec.make_inputs(m=2048, n=4096, rng=np.random.default_rng(SEED))
+    y = ops.rmsnorm(_t(x, cuda_device), _t(w, cuda_device), scale=1 / 4096, eps=1e-6)
+    want = f64.rmsnorm_mean(x, w, 1e-6)
+    _close(y, want, 1e-2, 1e-2, "rmsnorm config")
+    _close(y, want, 8e-3, 1e-5, "rmsnorm config (one bf16 rounding)")
+
+
+def test_row_rsqrt(cuda_device):
+    x = torch.randn(33, 777, generator=torch.Generator().manual_seed(3)).to(torch.bfloat16).to(cuda_device)
+    r = ops.row_rsqrt(x)
+    want = 1 / np.sqrt((_np(x) ** 2).sum(1))
+    _close(r, want, 1e-5, 0, "row_rsqrt")
+
+
+# ---- rope ---------------------------------------------------------------------------
+
+def test_rope_config_full_size(cuda_device):
+    spec = load_spec("rope_gqa")
+    q, k, c, s = spec.make_inputs(s=4096, hq=32, hkv=8, half_d=64, rng=np.random.default_rng(SEED))
+    qd, kd = _t(q, cuda_device), _t(k, cuda_device)
+    qo, ko = ops.rope_rotate_half(qd, kd, _t(c, cuda_device), _t(s, cuda_device))
+    rows = np.arange(0, 4096, 37)
+    _close(_np(qo)[rows], f64.rope_rotate_half(q[rows], c[rows], s[rows]), 7.8125e-3, 2e-2, "rope q")
+    _close(_np(ko)[rows], f64.rope_rotate_half(k[rows], c[rows], s[rows]), 7.8125e-3, 2e-2, "rope k")
+    # in place gives the same bits
+    qo2, ko2 = ops.rope_rotate_half(qd, kd, _t(c, cuda_device), _t(s, cuda_device), q_out=qd, k_out=kd)
+    assert torch.equal(qo2, qo) and torch.equal(ko2, ko)
+
+
+def test_rope_odd_head_dim_scalar_path(cuda_device):
+    g = torch.Generator().manual_seed(5)
+    q = torch.randn(9, 3, 2, 6, generator=g).to(torch.bfloat16)
+    ang = torch.rand(9, 6, generator=g) * 6
+    c, s = torch.cos(ang), torch.sin(ang)
+    qo, ko = ops.rope_rotate_half(q.to(cuda_device), None, c.to(cuda_device), s.to(cuda_device))
+    assert ko is None
+    _close(qo, f64.rope_rotate_half(q.float().numpy(), c.numpy(), s.numpy()), 7.8125e-3, 2e-2, "rope odd")
+
+
+# ---- cumsum ------------------------------------------------------------------------------
+
+@pytest.mark.parametrize("split", [0, 2048, 4096, 16384])
+def test_cumsum_config_full_size(split, cuda_device):
+    spec = load_spec("cumsum_nucleus_sorted")
+    (x,) = spec.make_inputs(m=256, n=128256, rng=np.random.default_rng(SEED))
+    tune = {"split": split} if split else None
+    ws = torch.empty(ops.cumsum_workspace_bytes(256, 128256, tune), dtype=torch.uint8, device=cuda_device)
+    y = ops.cumsum(_t(x, cuda_device), workspace=ws, tune=tune)
+    ops.cumsum_status(ws)
+    want = f64.cumsum(x)
+    got = _np(y)
+    rel = np.abs(got - want) / np.abs(want)
+    assert rel.max() <= 1e-5, f"rel err {rel.max():.3e}"
+    # properties: monotone, last column == row sum (== 1 up to rounding)
+    assert np.all(np.diff(got, axis=1) >= 0)
+    np.testing.assert_allclose(got[:, -1], x.astype(np.float64).sum(1), rtol=1e-6)
+
+
+@pytest.mark.parametrize("shape", [(1, 1), (3, 7), (5, 8191), (2, 8193), (64, 100000), (1024, 1024)])
+def test_cumsum_shapes(shape, cuda_device):
+    x = torch.randn(*shape, generator=torch.Generator().manual_seed(11))
+    y = ops.cumsum(x.to(cuda_device))
+    want = f64.cumsum(x.numpy())
+    scale = np.sqrt(np.arange(1, shape[1] + 1))[None, :]
+    err = np.abs(_np(y) - want) / scale
+    assert err.max() < 1e-5
+
+
+def test_cumsum_bf16_in_fp32_out_and_strided(cuda_device):
+    base = torch.randn(16, 3000, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16).to(cuda_device)
+    x = base[:, :2992]
+    y = ops.cumsum(x, out_dtype=torch.float32)
+    np.testing.assert_allclose(_np(y), f64.cumsum(_np(x)), rtol=1e-5, atol=1e-4)
+
+
+def test_cumsum_repeat_calls_reuse_workspace(cuda_device):
+    x = torch.rand(8, 50000, generator=torch.Generator().manual_seed(4)).to(cuda_device)
+    ws = torch.empty(ops.cumsum_workspace_bytes(8, 50000), dtype=torch.uint8, device=cuda_device)
+    a = ops.cumsum(x, workspace=ws)
+    b = ops.cumsum(x, workspace=ws)
+    ops.cumsum_status(ws)
+    assert torch.equal(a, b)
+
+
+# ---- Adam ------------------------------------------------------------------------------------
+
+def test_adam_config_medium_and_inplace(cuda_device):
+    spec = load_spec("fused_adam_cfg")
+    ins = spec.make_inputs(p=1000, f=4096, rng=np.random.default_rng(SEED))
+    p, gr, m, v, ss, ib, wd = (_t(a, cuda_device) for a in ins)
+    want = f64.ORACLES["fused_adam_cfg"](*ins)
+    out = ops.adam(p, gr, m, v, step_size=ss, inv_bc2_sqrt=ib, wd=wd, beta1=0.9, beta2=0.95)
+    for g, w, name in zip(out, want, ("param", "exp_avg", "exp_avg_sq")):
+        got = _np(g)
+        rel = np.abs(got - w) / np.maximum(np.abs(w), 1e-30)
+        assert rel.max() <= 1e-5, f"{name}: rel {rel.max():.3e}"
+    # in place with scalar hyper-parameters == out of place with per-row ones
+    step, inv, wdv = (float(np.asarray(a)[0, 0]) for a in ins[4:])
+    ops.adam(p, gr, m, v, step_size=step, inv_bc2_sqrt=inv, wd=wdv, beta1=0.9, beta2=0.95, out=(p, m, v))
+    for g, o in zip((p, m, v), out):
+        assert torch.equal(g, o)
+
+
+def test_adam_full_size_sampled(cuda_device):
+    """1e9 parameters (the BASELINE config): seeded on the device, one step in
+    place, checked on sampled 1e6-element windows against the oracle."""
+    n = 1_000_000_000
+    gen = torch.Generator(device=cuda_device).manual_seed(SEED)
+    p = torch.randn(n, device=cuda_device, generator=gen).mul_(0.02)
+    g = torch.randn(n, device=cuda_device, generator=gen).mul_(1e-3).to(torch.bfloat16)
+    m = torch.zeros(n, device=cuda_device)
+    v = torch.zeros(n, device=cuda_device)
+    starts = [0, 123_456_789, 500_000_000, n - 1_000_000]
+    saved = [(p[s:s + 1_000_000].cpu().numpy(), g[s:s + 1_000_000].float().cpu().numpy()) for s in starts]
+    ss, ib = 3e-4 / (1 - 0.9 ** 10), 1 / np.sqrt(1 - 0.95 ** 10)
+    ops.adam(p, g, m, v, step_size=ss, inv_bc2_sqrt=ib, wd=0.1, beta1=0.9, beta2=0.95, out=(p, m, v))
+    for s, (p0, g0) in zip(starts, saved):
+        z = np.zeros_like(p0)
+        wp, wm, wv = f64.adam(p0, g0, z, z, ss, ib, 0.1, beta1=0.9, beta2=0.95)
+        for got, want in ((p[s:s + 1_000_000], wp), (m[s:s + 1_000_000], wm), (v[s:s + 1_000_000], wv)):
+            got = _np(got)
+            assert (np.abs(got - want) / np.maximum(np.abs(want), 1e-30)).max() <= 1e-5
+    del p, g, m, v
+    torch.cuda.empty_cache()
+
+
+def test_adam_ragged_scalar_path(cuda_device):
+    g = torch.Generator().manual_seed(8)
+    p, gr, m, v = (torch.randn(7, 13, generator=g) for _ in range(4))
+    v = v.abs()
+    ss = torch.full((7, 1), 1e-3)
+    out = ops.adam(*(t.to(cuda_device) for t in (p, gr, m, v)), step_size=ss.to(cuda_device), inv_bc2_sqrt=1.0,
+                   wd=0.01)
+    want = f64.adam(p.numpy(), gr.numpy(), m.numpy(), v.numpy(), ss.numpy(), 1.0, 0.01)
+    for a, w in zip(out, want):
+        _close(a, w, 1e-5, 1e-7, "adam ragged")
+
+
+# ---- GEMM ---------------------------------------------------------------------------------------
+
+@pytest.mark.parametrize("bn", [64, 128, 256])
+@pytest.mark.parametrize("shape", [(128, 256, 64), (300, 264, 200), (1024, 1024, 1024), (64, 8, 8)])
+def test_gemm_tiles_and_ragged(bn, shape, cuda_device):
+    m, n, k = shape
+    g = torch.Generator().manual_seed(21)
+    a = (torch.randn(m, k, generator=g) / np.sqrt(k)).to(torch.bfloat16)
+    b = torch.randn(k, n, generator=g).to(torch.bfloat16)
+    c = ops.gemm(a.to(cuda_device), b.to(cuda_device), out_dtype=torch.float32, tune={"block_n": bn})
+    ops.gemm_status()
+    want = f64.matmul(a.float().numpy(), b.float().numpy())
+    _close(c, want, 1e-4, 1e-4, f"gemm {shape} bn {bn}")
+
+
+@pytest.mark.parametrize("stages", [2, 3, 4])
+def test_gemm_pipeline_depths(stages, cuda_device):
+    g = torch.Generator().manual_seed(22)
+    a = (torch.randn(512, 768, generator=g) / 28).to(torch.bfloat16).to(cuda_device)
+    b = torch.randn(768, 512, generator=g).to(torch.bfloat16).to(cuda_device)
+    c = ops.gemm(a, b, out_dtype=torch.float32, tune={"stages": stages})
+    _close(c, f64.matmul(_np(a), _np(b)), 1e-4, 1e-4, f"stages {stages}")
+
+
+def test_gemm_bf16_out_f16_inputs_and_strides(cuda_device):
+    g = torch.Generator().manual_seed(23)
+    a = (torch.randn(256, 512, generator=g) / 22).to(cuda_device)
+    b = torch.randn(512, 384, generator=g).to(cuda_device)
+    c = ops.gemm(a.half(), b.half())
+    _close(c, f64.matmul(_np(a.half()), _np(b.half())), 2e-3, 2e-3, "f16 gemm")
+    big = torch.zeros(256, 512, dtype=torch.bfloat16, device=cuda_device)
+    out = big[:, 64:448]
+    ops.gemm(a.bfloat16(), b.bfloat16(), out=out)
+    _close(out, f64.matmul(_np(a.bfloat16()), _np(b.bfloat16())), 8e-3, 8e-3, "strided C")
+    assert float(big[:, :64].abs().max()) == 0 and float(big[:, 448:].abs().max()) == 0
+
+
+def test_gemm_rowscale_and_silu_epilogues(cuda_device):
+    g = torch.Generator().manual_seed(24)
+    x = torch.randn(384, 256, generator=g).to(torch.bfloat16).to(cuda_device)
+    w1 = (0.05 * torch.randn(256, 640, generator=g)).to(torch.bfloat16).to(cuda_device)
+    w2 = (0.05 * torch.randn(256, 640, generator=g)).to(torch.bfloat16).to(cuda_device)
+    r = torch.rand(384, generator=g).add_(0.5).to(cuda_device)
+    c = ops.gemm(x, w1, row_scale=r, epilogue=N.AXON_EPI_ROWSCALE, out_dtype=torch.float32)
+    _close(c, f64.matmul(_np(x), _np(w1)) * _np(r)[:, None], 1e-4, 1e-4, "rowscale")
+    for bn in (128, 256):
+        a = ops.gemm(x, w1, b2=w2, epilogue=N.AXON_EPI_SILU_GATE, out_dtype=torch.float32, tune={"block_n": bn})
+        h1, h2 = f64.matmul(_np(x), _np(w1)), f64.matmul(_np(x), _np(w2))
+        _close(a, h1 / (1 + np.exp(-h1)) * h2, 1e-4, 1e-4, f"silu gate bn {bn}")
+
+
+def test_silu_mlp_config_sampled_rows(cuda_device):
+    """The BASELINE SwiGLU config at full size, checked on sampled rows."""
+    spec = load_spec("silu_mlp_swiglu")
+    x, w1, w2, w3 = spec.make_inputs(m=4096, n=14336, k=4096, p=4096, rng=np.random.default_rng(SEED))
+    y = ops.silu_mlp(*(_t(a, cuda_device) for a in (x, w1, w2, w3)))
+    ops.gemm_status()
+    rows = np.arange(0, 4096, 97)
+    want = f64.silu_mlp(x[rows], w1, w2, w3)
+    got = _np(y)[rows]
+    _close(got, want, 1e-2, 1e-2, "silu_mlp config")
+
+
+def test_rmsnorm_matmul_h8192_sampled(cuda_device):
+    spec = load_spec("rmsnorm_matmul")
+    x, w = spec.make_inputs(m=1024, n=8192, k=8192, rng=np.random.default_rng(SEED))
+    y = ops.rmsnorm_matmul(_t(x, cuda_device), _t(w, cuda_device))
+    rows = np.arange(0, 1024, 61)
+    _close(_np(y)[rows], f64.rmsnorm_matmul(x[rows], w), 2e-2, 2e-2, "rmsnorm_matmul h8192")
+
+
+def test_gemm_argument_errors(cuda_device):
+    a = torch.zeros(16, 12, dtype=torch.bfloat16, device=cuda_device)
+    b = torch.zeros(12, 16, dtype=torch.bfloat16, device=cuda_device)
+    with pytest.raises(N.AxonError) as e:
+        ops.gemm(a, b)
+    assert e.value.code == N.AXON_E_SHAPE
+    with pytest.raises(N.AxonError):
+        ops.gemm(torch.zeros(16, 16, device=cuda_device), torch.zeros(16, 16, device=cuda_device))
