@@ -64,6 +64,7 @@ class Tune(ctypes.Structure):
         ("block_k", ctypes.c_int32),
         ("stages", ctypes.c_int32),
         ("split", ctypes.c_int32),
+        ("precision", ctypes.c_int32),
     ]
 
     @classmethod
@@ -117,7 +118,7 @@ SIGNATURES: dict[str, tuple] = {
     "axon_gemm_status": (_I32, [_P]),
     "axon_row_rsqrt": (_I32, [_P, _P, _I64, _I64, _I64, _I32, _F, _F, _P]),
     "axon_rmsnorm_matmul": (_I32, [_P, _P, _P, _P, _I64, _I64, _I64, _I32, _I32, _TUNE, _P]),
-    "axon_silu_mlp_workspace_bytes": (_I64, [_I64, _I64, _I32]),
+    "axon_silu_mlp_workspace_bytes": (_I64, [_I64, _I64, _I32, _TUNE]),
     "axon_silu_mlp": (
         _I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I32, _I32, _TUNE, _P]
     ),

@@ -1,0 +1,226 @@
+"""The static variant catalogue: which CUDA kernel variants implement each spec,
+how a spec's TILES_IN_BLOCK_* values map onto `axon_tune_t`, and the variant
+modules the bench runner loads.
+
+This replaces Axon's synthesis + emission stage (src/axon/cli.py:697-755
+writes `out/<stem>/<fn>__v<i>_t<j>.py` from e-graph extraction): here the
+hardware variants are hand-written kernels, so "emission" writes one small
+Python module per (hw_variant, tile_variant) whose entry point -- named by
+Axon's identifier rule, with the spec's input names as data parameters and
+the tile args as keyword-only parameters -- launches the kernel through the
+C ABI. Each module embeds the `__axon_tile_constraints__` manifest of its
+variant.
+
+Tile knob meaning (the CUDA counterpart of TILES_IN_BLOCK_*):
+  row ops, rope, Adam   TILES_IN_BLOCK_N = v -> 32*v threads per row / CTA;
+                        TILES_IN_BLOCK_M must be 1 (rows per CTA are derived).
+  cumsum                TILES_IN_BLOCK_N = v -> 1024*v elements per scan tile.
+  GEMM specs            TILES_IN_BLOCK_M must be 1 (128-row tcgen05 tiles),
+                        TILES_IN_BLOCK_N = v -> BLOCK_N = 64*v,
+                        TILES_IN_BLOCK_K = v -> v shared-memory pipeline stages.
+  silu_mlp              N -> gate/up BLOCK_N = 128*v (64*v output columns),
+                        K -> stages, P -> down-projection BLOCK_N = 64*v
+                        (recorded; the down GEMM picks its own tile today).
+                        hw_variant 0/1/2 stores the activation as 1/2/3 bf16
+                        terms (see axon_silu_mlp).
+"""
+
+from __future__ import annotations
+
+from collections.abc import Sequence
+from dataclasses import dataclass
+from pathlib import Path
+
+import numpy as np
+
+from .candidate_filter import TileConstraint, manifest_literal
+from .specs import safe_name
+
+ROW_SPECS = ("rmsnorm", "rmsnorm_llama", "layernorm", "softmax")
+ROPE_SPECS = ("rope", "rope_gqa")
+SCAN_SPECS = ("cumsum", "cumsum_nucleus_sorted")
+ADAM_SPECS = ("fused_adam", "fused_adam_cfg")
+GEMM_SPECS = ("matmul", "rmsnorm_matmul")
+MLP_SPECS = ("silu_mlp", "silu_mlp_swiglu")
+ALL_SPECS = ROW_SPECS + ROPE_SPECS + SCAN_SPECS + ADAM_SPECS + GEMM_SPECS + MLP_SPECS
+
+ADAM_BETAS = {"fused_adam": (0.9, 0.999), "fused_adam_cfg": (0.9, 0.95)}
+
+
+@dataclass(frozen=True)
+class Variant:
+    hw_variant: int
+    name: str
+
+
+def variants(spec_name: str) -> list[Variant]:
+    if spec_name in ROW_SPECS:
+        return [Variant(0, "row_resident"), Variant(1, "row_streaming")]
+    if spec_name == "rope":
+        return [Variant(0, "flat_vec16")]
+    if spec_name == "rope_gqa":
+        return [Variant(0, "token_blocked"), Variant(1, "flat_vec16")]
+    if spec_name in SCAN_SPECS:
+        return [Variant(0, "decoupled_lookback")]
+    if spec_name in ADAM_SPECS:
+        return [Variant(0, "grid_stride_vec")]
+    if spec_name in GEMM_SPECS:
+        return [Variant(0, "tcgen05_ws_persistent")]
+    if spec_name in MLP_SPECS:
+        return [Variant(0, "tcgen05_act_1term"), Variant(1, "tcgen05_act_2term"), Variant(2, "tcgen05_act_3term")]
+    raise KeyError(f"no CUDA variants for spec '{spec_name}'")
+
+
+def _one(arg: str) -> TileConstraint:
+    return TileConstraint(arg, extent=1, tile_size=1, require_divisible=True)
+
+
+def constraints(spec_name: str, hw_variant: int, dims: dict, itemsize: int,
+                tile_args: Sequence[str]) -> list[TileConstraint]:
+    """The feasibility manifest of one variant at concrete dims."""
+    out: list[TileConstraint] = []
+    args = list(tile_args)
+    if spec_name in ROW_SPECS:
+        n = dims["n"]
+        e = 16 // itemsize
+        max_v = (512 if itemsize == 2 else 1024) // 32
+        if hw_variant == 0:
+            allowed = tuple(v for v in (1, 2, 4, 8, 16, 32) if v <= max_v and 32 * v * e * 8 >= n)
+        else:
+            allowed = tuple(v for v in (4, 8, 16, 32) if v <= 32)
+        out.append(TileConstraint(args[1], extent=max(n, 32 * e * max_v), tile_size=32 * e,
+                                  require_divisible=False, allowed=allowed))
+        out.append(_one(args[0]))
+    elif spec_name == "rope_gqa" and hw_variant == 0:
+        out.append(_one(args[1]))  # the token-blocked kernel sizes its CTA from the head count
+        out.append(_one(args[0]))
+    elif spec_name in ROPE_SPECS or spec_name in ADAM_SPECS:
+        out.append(TileConstraint(args[1], extent=256, tile_size=32, require_divisible=True, allowed=(1, 2, 4, 8)))
+        out.append(_one(args[0]))
+    elif spec_name in SCAN_SPECS:
+        out.append(TileConstraint(args[1], extent=16384, tile_size=1024, require_divisible=True,
+                                  allowed=(2, 4, 8, 16)))
+        out.append(_one(args[0]))
+    elif spec_name in GEMM_SPECS:
+        out.append(_one(args[0]))
+        out.append(TileConstraint(args[1], extent=256, tile_size=64, require_divisible=True, allowed=(1, 2, 4)))
+        out.append(TileConstraint(args[2], extent=8, tile_size=1, require_divisible=True, allowed=(2, 4)))
+    elif spec_name in MLP_SPECS:
+        out.append(_one(args[0]))
+        out.append(TileConstraint(args[1], extent=256, tile_size=128, require_divisible=True, allowed=(1, 2)))
+        out.append(TileConstraint(args[2], extent=8, tile_size=1, require_divisible=True, allowed=(2, 4)))
+        out.append(TileConstraint(args[3], extent=256, tile_size=64, require_divisible=True, allowed=(1, 2, 4)))
+    return out
+
+
+def tune_for(spec_name: str, hw_variant: int, tiles: dict[str, int]) -> dict | list[dict]:
+    """axon_tune_t fields for one tile key (two dicts for the two MLP GEMMs)."""
+    t = {k.replace("TILES_IN_BLOCK_", ""): int(x) for k, x in tiles.items()}
+    if spec_name in ROW_SPECS:
+        return {"variant": hw_variant, "threads": 32 * t["N"]}
+    if spec_name == "rope_gqa" and hw_variant == 0:
+        return {"variant": 0}
+    if spec_name in ROPE_SPECS or spec_name in ADAM_SPECS:
+        return {"variant": hw_variant, "threads": 32 * t["N"]}
+    if spec_name in SCAN_SPECS:
+        return {"variant": hw_variant, "split": 1024 * t["N"]}
+    if spec_name in GEMM_SPECS:
+        return {"variant": hw_variant, "block_n": 64 * t["N"], "stages": t["K"]}
+    if spec_name in MLP_SPECS:
+        return {"block_n": 128 * t["N"], "stages": t["K"], "precision": hw_variant + 1, "down_block_n": 64 * t["P"]}
+    raise KeyError(spec_name)
+
+
+# ---- launching -----------------------------------------------------------------
+
+
+def to_device(a, device):
+    """numpy (incl. ml_dtypes bfloat16) -> torch tensor on `device`."""
+    import torch
+
+    a = np.asarray(a)
+    if a.dtype.name == "bfloat16":
+        return torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).view(torch.bfloat16).to(device)
+    return torch.from_numpy(np.ascontiguousarray(a)).to(device)
+
+
+def launch(spec_name: str, hw_variant: int, tiles: dict[str, int], inputs: Sequence, *, out=None):
+    """Run one spec on device tensors (positional, in input_specs order) with
+    the kernel variant and tile key given; returns the output tensors."""
+    from . import _native as N
+    from . import ops
+
+    tune = tune_for(spec_name, hw_variant, tiles)
+    t = list(inputs)
+    if spec_name == "rmsnorm":
+        return (ops.rmsnorm(t[0], tune=tune, out=out and out[0]),)
+    if spec_name == "rmsnorm_llama":
+        n = t[0].shape[1]
+        return (ops.rmsnorm(t[0], t[1], scale=1.0 / n, eps=1e-6, tune=tune, out=out and out[0]),)
+    if spec_name == "layernorm":
+        return (ops.layernorm(t[0], eps=1e-6, tune=tune, out=out and out[0]),)
+    if spec_name == "softmax":
+        return (ops.softmax(t[0], tune=tune, out=out and out[0]),)
+    if spec_name == "rope":
+        oe, oo = (out if out else (None, None))
+        return ops.rope_split(*t, out_even=oe, out_odd=oo, tune=tune)
+    if spec_name == "rope_gqa":
+        qo, ko = (out if out else (None, None))
+        return ops.rope_rotate_half(*t, q_out=qo, k_out=ko, tune=tune)
+    if spec_name in SCAN_SPECS:
+        return (ops.cumsum(t[0], tune=tune, out=out and out[0]),)
+    if spec_name in ADAM_SPECS:
+        b1, b2 = ADAM_BETAS[spec_name]
+        return ops.adam(*t[:4], step_size=t[4], inv_bc2_sqrt=t[5], wd=t[6], beta1=b1, beta2=b2, eps=1e-8,
+                        out=out, tune=tune)
+    if spec_name == "matmul":
+        return (ops.gemm(t[0], t[1], tune=tune, out=out and out[0]),)
+    if spec_name == "rmsnorm_matmul":
+        return (ops.rmsnorm_matmul(t[0], t[1], tune=tune, out=out and out[0]),)
+    if spec_name in MLP_SPECS:
+        tune = dict(tune)
+        tune.pop("down_block_n")
+        return (ops.silu_mlp(*t, out=out and out[0], tune=tune),)
+    raise KeyError(spec_name)
+
+
+# ---- variant modules -------------------------------------------------------------
+
+_MODULE = '''"""Axon B200 variant module: spec {spec!r}, hw_variant {hw} ({vname}), tile_variant {tv}.
+
+Generated by enzyme_b200.catalogue; the bench runner loads it by path and calls
+`{fn}` with device tensors bound by name and the tile key as keywords.
+"""
+
+from enzyme_b200.catalogue import launch as _launch
+
+{manifest_name} = {manifest}
+
+SPEC_NAME = {spec!r}
+HW_VARIANT = {hw}
+
+
+def {fn}({params}, *, {tile_params}):
+    return _launch(SPEC_NAME, HW_VARIANT, {tile_dict}, ({params},))
+'''
+
+
+def emit_variant_modules(spec, dims: dict, itemsize: int, paths) -> list[Path]:
+    """Write one module per hw variant (tile_variant 0) into the run dir."""
+    from .candidate_filter import MANIFEST_NAME
+
+    fn = safe_name(spec.name)
+    params = ", ".join(spec.input_names())
+    tile_params = ", ".join(spec.tile_args)
+    tile_dict = "{" + ", ".join(f"{a!r}: {a}" for a in spec.tile_args) + "}"
+    written = []
+    paths.run_dir.mkdir(parents=True, exist_ok=True)
+    for var in variants(spec.name):
+        cons = constraints(spec.name, var.hw_variant, dims, itemsize, spec.tile_args)
+        text = _MODULE.format(spec=spec.name, hw=var.hw_variant, vname=var.name, tv=0, fn=fn, params=params,
+                              tile_params=tile_params, tile_dict=tile_dict, manifest_name=MANIFEST_NAME,
+                              manifest=manifest_literal(cons))
+        p = paths.variant_module(fn, var.hw_variant, 0)
+        p.write_text(text)
+        written.append(p)
+    return written

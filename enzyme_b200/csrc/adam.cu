@@ -79,6 +79,8 @@ template <typename TS, typename TG>
 __global__ void __launch_bounds__(256) adam_vec(AdamArgs a) {
   const int64_t groups = a.n / G;
   const bool per_row = a.ss_rows || a.ib_rows || a.wd_rows;
+  pdl_wait();
+  pdl_trigger();
   for (int64_t gi = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; gi < groups;
        gi += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t off = gi * G;
@@ -124,7 +126,7 @@ int launch_adam(const AdamArgs& a, int threads, cudaStream_t s) {
   if (grid > cap) grid = cap;
   if (grid < 1) grid = 1;
   if (vec)
-    adam_vec<TS, TG><<<static_cast<int>(grid), threads, 0, s>>>(a);
+    launch_k(adam_vec<TS, TG>, dim3(static_cast<unsigned>(grid)), dim3(threads), 0, s, a);
   else
     adam_scalar<TS, TG><<<static_cast<int>(grid), threads, 0, s>>>(a);
   return launch_status("axon_adam");
@@ -151,9 +153,10 @@ extern "C" int axon_adam(const void* param, const void* grad, const void* exp_av
                          const void* inv_bc2_sqrt_rows, const void* wd_rows, int32_t row_dtype,
                          const axon_adam_hparams_t* hp, const axon_tune_t* tune, void* stream) {
   axon_tune_t t = tune_or_default(tune);
-  if (!param || !grad || !exp_avg || !exp_avg_sq || !param_out || !exp_avg_out || !exp_avg_sq_out || !hp)
-    return fail(AXON_E_ARG, "axon_adam: NULL pointer");
   if (rows < 0 || cols < 0) return fail(AXON_E_SHAPE, "axon_adam: negative size");
+  if (!hp) return fail(AXON_E_ARG, "axon_adam: NULL hyper-parameters");
+  if (rows * cols > 0 && (!param || !grad || !exp_avg || !exp_avg_sq || !param_out || !exp_avg_out || !exp_avg_sq_out))
+    return fail(AXON_E_ARG, "axon_adam: NULL pointer");
   if ((step_size_rows || inv_bc2_sqrt_rows || wd_rows) && !valid_dtype(row_dtype))
     return fail(AXON_E_UNSUPPORTED, "axon_adam: unsupported per-row scalar dtype %d", row_dtype);
   if (t.variant != 0) return fail(AXON_E_ARG, "axon_adam: unknown variant %d", t.variant);

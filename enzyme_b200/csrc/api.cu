@@ -1,4 +1,5 @@
 // Library metadata and error plumbing shared by every entry point.
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -32,6 +33,14 @@ int launch_status(const char* what) {
   return AXON_OK;
 }
 
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("AXON_B200_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 int sm_count() {
   static int cache[64] = {0};
   int dev = 0;
@@ -60,7 +69,8 @@ static const char* kVariants[][2] = {
      "{\"op\":\"softmax\",\"variants\":[{\"id\":0,\"name\":\"row_resident\",\"knobs\":{\"threads\":[0,64,128,256,512,1024]}},"
      "{\"id\":1,\"name\":\"row_streaming\",\"knobs\":{\"threads\":[0,128,256,512,1024]}}]}"},
     {"rope",
-     "{\"op\":\"rope\",\"variants\":[{\"id\":0,\"name\":\"vec16\",\"knobs\":{\"threads\":[0,128,256,512]}}]}"},
+     "{\"op\":\"rope\",\"variants\":[{\"id\":0,\"name\":\"token_blocked\",\"knobs\":{}},"
+     "{\"id\":1,\"name\":\"flat_vec16\",\"knobs\":{\"threads\":[0,128,256]}}]}"},
     {"cumsum",
      "{\"op\":\"cumsum\",\"variants\":[{\"id\":0,\"name\":\"decoupled_lookback\",\"knobs\":{\"split\":[0,2048,4096,8192,16384]}},"
      "{\"id\":1,\"name\":\"cluster_dsmem\",\"knobs\":{\"split\":[0,1,2,4,8,16]}}]}"},

@@ -10,6 +10,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <string>
+#include <utility>
 
 #include "../../include/axon_b200.h"
 
@@ -49,6 +50,36 @@ int sm_count();
 inline axon_tune_t tune_or_default(const axon_tune_t* t) {
   axon_tune_t d{};
   return t ? *t : d;
+}
+
+// ---- programmatic dependent launch --------------------------------------------
+//
+// Memory-bound kernels are launched with programmatic stream serialization:
+// the next kernel in the stream may be scheduled while this one drains, and
+// every such kernel starts with pdl_wait() (griddepcontrol.wait), which
+// blocks until the previous grid has completed and its writes are visible.
+// Data dependencies are therefore exactly those of a plain launch; only the
+// launch latency between back-to-back kernels is hidden. AXON_B200_PDL=0 in
+// the environment turns the attribute off.
+
+bool pdl_enabled();
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 // ---- element conversion -------------------------------------------------------

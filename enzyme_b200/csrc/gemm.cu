@@ -179,10 +179,13 @@ __device__ __forceinline__ void store32(TC* dst, const float* v, int64_t col, in
 struct GemmParams {
   void* c;
   const float* row_scale;
-  int m, n, k;       // n = output columns
+  int m, n, k;         // n = output columns
   int64_t ldc;
   int stages;
   uint32_t idesc;
+  int terms;           // SILU_GATE: write the activation as this many bf16/f16 terms
+  int64_t term_stride; // columns between the terms in C
+  int b_kwrap;         // > 0: B's k coordinate wraps modulo this (B re-read per term)
 };
 
 template <int BN, int EPI, typename TC>
@@ -260,9 +263,10 @@ __global__ void __launch_bounds__(192, 1)
           for (int j = 0; j < BN / 128; ++j)
             tma_load_2d(&tmB2, &full[stage], sb + (BN / 128 + j) * B_CHUNK, tn * BN_OUT + j * 64, kb * BK);
         } else {
+          const int kb_b = p.b_kwrap > 0 ? (kb * BK) % p.b_kwrap : kb * BK;
 #pragma unroll
           for (int j = 0; j < BN / 64; ++j)
-            tma_load_2d(&tmB, &full[stage], sb + j * B_CHUNK, tn * BN + j * 64, kb * BK);
+            tma_load_2d(&tmB, &full[stage], sb + j * B_CHUNK, tn * BN + j * 64, kb_b);
         }
         issued[stage] += 1;
         if (++stage == S) {
@@ -334,7 +338,25 @@ __global__ void __launch_bounds__(192, 1)
           const int64_t col = static_cast<int64_t>(tn) * BN_OUT + c * 32;
 #pragma unroll
           for (int j = 0; j < 32; ++j) g[j] = g[j] / (1.0f + __expf(-g[j])) * u[j];
-          if (row_ok && col < p.n) store32<TC>(crow + col, g, col, p.n);
+          if (row_ok && col < p.n) {
+            if (p.terms <= 1) {
+              store32<TC>(crow + col, g, col, p.n);
+            } else {
+              // Split the fp32 activation into `terms` values of TC whose sum
+              // carries 8 more mantissa bits per term: t_0 = round(a),
+              // t_i = round(a - t_0 - ... - t_{i-1}).
+#pragma unroll 1
+              for (int tt = 0; tt < p.terms; ++tt) {
+                float part[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                  part[j] = to_f(from_f<TC>(g[j]));
+                  g[j] -= part[j];
+                }
+                store32<TC>(crow + tt * p.term_stride + col, part, col, p.n);
+              }
+            }
+          }
         }
       } else {
 #pragma unroll 1
@@ -445,10 +467,19 @@ int max_stages(int bn) {
 
 using namespace axon;
 
-extern "C" int axon_gemm(const void* a, const void* b, const void* b2, void* c, const float* row_scale, int64_t m,
-                         int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int32_t ab_dtype,
-                         int32_t c_dtype, int32_t epilogue, const axon_tune_t* tune, void* stream) {
+namespace axon {
+namespace {
+
+// axon_gemm plus the two silu_mlp-internal knobs: `terms` (SILU_GATE writes
+// the activation as that many split terms, `term_stride` columns apart) and
+// `b_kwrap` (the k coordinate of B wraps modulo b_kwrap, so a K = terms * n
+// contraction re-reads the same [n, p] weight once per term).
+int gemm_impl(const void* a, const void* b, const void* b2, void* c, const float* row_scale, int64_t m, int64_t n,
+              int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int32_t ab_dtype, int32_t c_dtype, int32_t epilogue,
+              const axon_tune_t* tune, void* stream, int terms, int64_t term_stride, int64_t b_kwrap) {
   axon_tune_t t = tune_or_default(tune);
+  if (m < 0 || n < 0 || k < 0) return fail(AXON_E_SHAPE, "axon_gemm: negative size");
+  if (m == 0 || n == 0) return AXON_OK;  // empty output: nothing to launch, pointers may be NULL
   if (!a || !b || !c) return fail(AXON_E_ARG, "axon_gemm: NULL operand");
   if (ab_dtype != AXON_BF16 && ab_dtype != AXON_F16)
     return fail(AXON_E_UNSUPPORTED, "axon_gemm: A/B dtype must be bf16 or f16 (got %d)", ab_dtype);
@@ -460,6 +491,7 @@ extern "C" int axon_gemm(const void* a, const void* b, const void* b2, void* c, 
     return fail(AXON_E_SHAPE, "axon_gemm: sizes out of range");
   if (k % 8 || n % 8) return fail(AXON_E_SHAPE, "axon_gemm: k and n must be multiples of 8 (k=%lld n=%lld)",
                                   (long long)k, (long long)n);
+  const int64_t b_rows = b_kwrap > 0 ? b_kwrap : k;
   if (lda < k || ldb < n || ldc < n) return fail(AXON_E_SHAPE, "axon_gemm: leading dimension too small");
   if (lda % 8 || ldb % 8 || ldc % 8) return fail(AXON_E_ALIGN, "axon_gemm: leading dimensions must be multiples of 8");
   if (!aligned16(a) || !aligned16(b) || !aligned16(c) || (b2 && !aligned16(b2)))
@@ -467,7 +499,6 @@ extern "C" int axon_gemm(const void* a, const void* b, const void* b2, void* c, 
   if (t.variant != 0) return fail(AXON_E_ARG, "axon_gemm: unknown variant %d", t.variant);
   if (t.block_m != 0 && t.block_m != 128) return fail(AXON_E_ARG, "axon_gemm: block_m must be 128");
   if (t.block_k != 0 && t.block_k != 64) return fail(AXON_E_ARG, "axon_gemm: block_k must be 64");
-  if (m == 0 || n == 0) return AXON_OK;
   if (k == 0) return fail(AXON_E_SHAPE, "axon_gemm: k == 0 not supported");
 
   int bn = t.block_n;
@@ -481,10 +512,10 @@ extern "C" int axon_gemm(const void* a, const void* b, const void* b2, void* c, 
   CUtensorMap ma, mb, mb2;
   int rc = make_map(&ma, a, ab_dtype, k, m, lda, BK, BM, "A");
   if (rc) return rc;
-  rc = make_map(&mb, b, ab_dtype, n, k, ldb, 64, BK, "B");
+  rc = make_map(&mb, b, ab_dtype, n, b_rows, ldb, 64, BK, "B");
   if (rc) return rc;
   if (b2) {
-    rc = make_map(&mb2, b2, ab_dtype, n, k, ldb, 64, BK, "B2");
+    rc = make_map(&mb2, b2, ab_dtype, n, b_rows, ldb, 64, BK, "B2");
     if (rc) return rc;
   } else {
     mb2 = mb;
@@ -497,6 +528,9 @@ extern "C" int axon_gemm(const void* a, const void* b, const void* b2, void* c, 
   gp.k = static_cast<int>(k);
   gp.ldc = ldc;
   gp.stages = stages;
+  gp.terms = terms;
+  gp.term_stride = term_stride;
+  gp.b_kwrap = static_cast<int>(b_kwrap);
   const uint32_t fmt = ab_dtype == AXON_BF16 ? 1u : 0u;
   gp.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | (0u << 15) | (1u << 16) |
              (static_cast<uint32_t>(bn >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
@@ -512,6 +546,16 @@ extern "C" int axon_gemm(const void* a, const void* b, const void* b2, void* c, 
     case 10: return dispatch_c<256, AXON_EPI_SILU_GATE>(c_dtype, ma, mb, mb2, gp, s);
     default: return fail(AXON_E_ARG, "axon_gemm: unsupported tile/epilogue combination");
   }
+}
+
+}  // namespace
+}  // namespace axon
+
+extern "C" int axon_gemm(const void* a, const void* b, const void* b2, void* c, const float* row_scale, int64_t m,
+                         int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int32_t ab_dtype,
+                         int32_t c_dtype, int32_t epilogue, const axon_tune_t* tune, void* stream) {
+  return gemm_impl(a, b, b2, c, row_scale, m, n, k, lda, ldb, ldc, ab_dtype, c_dtype, epilogue, tune, stream, 1, 0,
+                   0);
 }
 
 extern "C" int axon_gemm_status(void* stream) {
@@ -539,23 +583,37 @@ extern "C" int axon_rmsnorm_matmul(const void* x, const void* w, void* y, void* 
                    AXON_EPI_ROWSCALE, tune, stream);
 }
 
-extern "C" int64_t axon_silu_mlp_workspace_bytes(int64_t m, int64_t n, int32_t ab_dtype) {
+static int silu_terms(const axon_tune_t* tune) {
+  const int p = tune ? tune->precision : 0;
+  return p <= 0 ? 1 : p;
+}
+
+extern "C" int64_t axon_silu_mlp_workspace_bytes(int64_t m, int64_t n, int32_t ab_dtype, const axon_tune_t* tune) {
   (void)ab_dtype;
-  return m * n * 2;
+  if (m < 0 || n < 0) return fail(AXON_E_SHAPE, "axon_silu_mlp_workspace_bytes: negative size");
+  const int terms = silu_terms(tune);
+  if (terms > 3) return fail(AXON_E_ARG, "axon_silu_mlp: precision must be 1, 2 or 3 terms");
+  return m * n * 2 * terms;
 }
 
 extern "C" int axon_silu_mlp(const void* x, const void* w1, const void* w2, const void* w3, void* y,
                              void* workspace, int64_t workspace_bytes, int64_t m, int64_t n, int64_t k, int64_t p,
                              int32_t ab_dtype, int32_t c_dtype, const axon_tune_t* tune, void* stream) {
-  if (!workspace || workspace_bytes < m * n * 2)
-    return fail(AXON_E_ARG, "axon_silu_mlp: workspace of %lld bytes needed", (long long)(m * n * 2));
+  const int terms = silu_terms(tune);
+  if (terms > 3) return fail(AXON_E_ARG, "axon_silu_mlp: precision must be 1, 2 or 3 terms");
+  if (m < 0 || n < 0 || k < 0 || p < 0) return fail(AXON_E_SHAPE, "axon_silu_mlp: negative size");
+  if (m == 0 || p == 0) return AXON_OK;
+  if (terms > 1 && n % 64) return fail(AXON_E_SHAPE, "axon_silu_mlp: split precision needs n %% 64 == 0 (n=%lld)",
+                                       (long long)n);
+  if (!workspace || workspace_bytes < m * n * 2 * terms)
+    return fail(AXON_E_ARG, "axon_silu_mlp: workspace of %lld bytes needed", (long long)(m * n * 2 * terms));
   axon_tune_t t = tune_or_default(tune);
   axon_tune_t up = t, down = t;
   up.block_n = t.block_n == 64 ? 0 : t.block_n;
-  int rc = axon_gemm(x, w1, w2, workspace, nullptr, m, n, k, k, n, n, ab_dtype, ab_dtype, AXON_EPI_SILU_GATE, &up,
-                     stream);
+  int rc = gemm_impl(x, w1, w2, workspace, nullptr, m, n, k, k, n, n * terms, ab_dtype, ab_dtype, AXON_EPI_SILU_GATE,
+                     &up, stream, terms, n, 0);
   if (rc) return rc;
   down.stages = 0;
-  return axon_gemm(workspace, w3, nullptr, y, nullptr, m, p, n, n, p, p, ab_dtype, c_dtype, AXON_EPI_NONE, &down,
-                   stream);
+  return gemm_impl(workspace, w3, nullptr, y, nullptr, m, p, n * terms, n * terms, p, p, ab_dtype, c_dtype,
+                   AXON_EPI_NONE, &down, stream, 1, 0, terms > 1 ? n : 0);
 }

@@ -64,6 +64,8 @@ __global__ void __launch_bounds__(max_row_threads<T>()) row_resident_kernel(RowA
   const int64_t row = static_cast<int64_t>(blockIdx.x) * rows_per_cta + row_in_cta;
   const bool active = row < a.m;
   const int64_t n = a.n;
+  pdl_wait();
+  pdl_trigger();
   const T* xr = static_cast<const T*>(a.x) + (active ? row : 0) * a.ld_x;
 
   Vec<T> raw[VPT];
@@ -170,6 +172,8 @@ __global__ void __launch_bounds__(1024) row_streaming_kernel(RowArgs a) {
   const T* xr = static_cast<const T*>(a.x) + row * a.ld_x;
   T* yr = static_cast<T*>(a.y) + row * a.ld_y;
   const int64_t nchunks = (n + E - 1) / E;
+  pdl_wait();
+  pdl_trigger();
 
   auto load = [&](int64_t c, float* v) {
     const int64_t col = c * E;
@@ -281,8 +285,13 @@ int launch_rows(const RowArgs& a, const axon_tune_t& t, cudaStream_t s, const ch
       if (tpr > max_row_threads<T>())
         return fail(AXON_E_ARG, "%s: at most %d threads per row for this dtype", name, max_row_threads<T>());
     } else {
+      // Up to eight 16-byte packets per thread keeps the most bytes in flight
+      // per register; widen the row group only while the whole problem still
+      // fits in one wave of resident threads (~1024 per SM at this register use).
       tpr = 32;
-      while (tpr < max_row_threads<T>() && (nv + tpr - 1) / tpr > 4) tpr *= 2;
+      while (tpr < max_row_threads<T>() && (nv + tpr - 1) / tpr > 8) tpr *= 2;
+      const int64_t resident = static_cast<int64_t>(sm_count()) * 1024;
+      while (tpr < max_row_threads<T>() && a.m * tpr * 2 <= resident && tpr * 2 <= nv) tpr *= 2;
     }
     int64_t need = (nv + tpr - 1) / tpr;
     vpt = need <= 1 ? 1 : need <= 2 ? 2 : need <= 4 ? 4 : need <= 8 ? 8 : 0;
@@ -294,19 +303,19 @@ int launch_rows(const RowArgs& a, const axon_tune_t& t, cudaStream_t s, const ch
     if (grid > 0x7fffffff) return fail(AXON_E_SHAPE, "%s: too many rows (%lld)", name, (long long)a.m);
     dim3 block(tpr * rows_per_cta);
     switch (vpt) {
-      case 1: row_resident_kernel<T, 1, OP><<<grid, block, 0, s>>>(a, gw, rows_per_cta); break;
-      case 2: row_resident_kernel<T, 2, OP><<<grid, block, 0, s>>>(a, gw, rows_per_cta); break;
-      case 4: row_resident_kernel<T, 4, OP><<<grid, block, 0, s>>>(a, gw, rows_per_cta); break;
-      default: row_resident_kernel<T, 8, OP><<<grid, block, 0, s>>>(a, gw, rows_per_cta); break;
+      case 1: launch_k(row_resident_kernel<T, 1, OP>, dim3(grid), block, 0, s, a, gw, rows_per_cta); break;
+      case 2: launch_k(row_resident_kernel<T, 2, OP>, dim3(grid), block, 0, s, a, gw, rows_per_cta); break;
+      case 4: launch_k(row_resident_kernel<T, 4, OP>, dim3(grid), block, 0, s, a, gw, rows_per_cta); break;
+      default: launch_k(row_resident_kernel<T, 8, OP>, dim3(grid), block, 0, s, a, gw, rows_per_cta); break;
     }
     return launch_status(name);
   }
   if (a.m > 0x7fffffff) return fail(AXON_E_SHAPE, "%s: too many rows (%lld)", name, (long long)a.m);
   int threads = t.threads > 0 ? t.threads : 1024;
   if (vec_ok)
-    row_streaming_kernel<T, true, OP><<<a.m, threads, 0, s>>>(a);
+    launch_k(row_streaming_kernel<T, true, OP>, dim3(a.m), dim3(threads), 0, s, a);
   else
-    row_streaming_kernel<T, false, OP><<<a.m, threads, 0, s>>>(a);
+    launch_k(row_streaming_kernel<T, false, OP>, dim3(a.m), dim3(threads), 0, s, a);
   return launch_status(name);
 }
 
@@ -316,11 +325,12 @@ int dispatch_rows(const RowArgs& a, int32_t dtype, const axon_tune_t* tune, void
   if (t.variant < 0 || t.variant > 1) return fail(AXON_E_ARG, "%s: unknown variant %d", name, t.variant);
   if (t.threads != 0 && (t.threads < 32 || t.threads > 1024 || (t.threads & (t.threads - 1))))
     return fail(AXON_E_ARG, "%s: threads must be a power of two in [32, 1024], got %d", name, t.threads);
-  if (a.x == nullptr || (OP != OP_RSQRT && a.y == nullptr) || (OP == OP_RSQRT && a.r_out == nullptr))
-    return fail(AXON_E_ARG, "%s: NULL tensor pointer", name);
   if (a.m < 0 || a.n < 0) return fail(AXON_E_SHAPE, "%s: negative size", name);
   if (a.ld_x < a.n || (OP != OP_RSQRT && a.ld_y < a.n))
     return fail(AXON_E_SHAPE, "%s: leading dimension smaller than n", name);
+  if (a.m == 0 || a.n == 0) return AXON_OK;  // empty tensors may carry NULL pointers
+  if (a.x == nullptr || (OP != OP_RSQRT && a.y == nullptr) || (OP == OP_RSQRT && a.r_out == nullptr))
+    return fail(AXON_E_ARG, "%s: NULL tensor pointer", name);
   cudaStream_t s = as_stream(stream);
   switch (dtype) {
     case AXON_F32: return launch_rows<float, OP>(a, t, s, name);

@@ -18,6 +18,8 @@ __global__ void __launch_bounds__(256) rope_split_vec(const T* __restrict__ xe, 
                                                       const T* __restrict__ c, const T* __restrict__ s, T* oe,
                                                       T* oo, int64_t npk) {
   constexpr int E = Vec<T>::E;
+  pdl_wait();
+  pdl_trigger();
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < npk;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t off = i * E;
@@ -62,6 +64,8 @@ __global__ void __launch_bounds__(256) rope_rotate_half_vec(RotArgs a, int64_t i
   const int64_t ppr = a.half / E;               // packets per half-row
   const int64_t heads = a.nq + a.nkv;
   const int64_t per_tok = heads * ppr;
+  pdl_wait();
+  pdl_trigger();
   for (int64_t it = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; it < items;
        it += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t tok = it / per_tok;
@@ -100,6 +104,63 @@ __global__ void __launch_bounds__(256) rope_rotate_half_vec(RotArgs a, int64_t i
     }
     st_vec_stream(dst + col, o1);
     st_vec_stream(dst + a.half + col, o2);
+  }
+}
+
+// Token-blocked vector path (variant 0), used when one token's packets (heads
+// x packets per half-row, at most 512) fit in one CTA: thread t owns head t / ppr and packet t % ppr
+// for TOK consecutive tokens, so all index math is done once per thread, the
+// TOK tokens' loads are issued together, and the heads of a token share the
+// cos/sin row through L1.
+template <typename T, int TOK>
+__global__ void __launch_bounds__(512) rope_rotate_half_tok(RotArgs a, int ppr) {
+  constexpr int E = Vec<T>::E;
+  pdl_wait();
+  pdl_trigger();
+  const int t = threadIdx.x;
+  const int h = t / ppr;
+  const int p = t - h * ppr;
+  if (h >= a.nq + a.nkv) return;
+  const int64_t half = a.half;
+  const bool is_q = h < a.nq;
+  const int64_t hh = is_q ? h : h - a.nq;
+  const int64_t nh = is_q ? a.nq : a.nkv;
+  const T* src = static_cast<const T*>(is_q ? a.q : a.k);
+  T* dst = static_cast<T*>(is_q ? a.q_out : a.k_out);
+  const int64_t tok0 = static_cast<int64_t>(blockIdx.x) * TOK;
+  const int col = p * E;
+  Vec<T> x1[TOK], x2[TOK];
+  float4 cv[TOK][E / 4], sv[TOK][E / 4];
+#pragma unroll
+  for (int i = 0; i < TOK; ++i) {
+    const int64_t tok = tok0 + i;
+    if (tok < a.seq) {
+      const T* s = src + (tok * nh + hh) * 2 * half + col;
+      x1[i] = ld_vec_stream(s);
+      x2[i] = ld_vec_stream(s + half);
+#pragma unroll
+      for (int j = 0; j < E / 4; ++j) {
+        cv[i][j] = __ldg(reinterpret_cast<const float4*>(a.cos_t + tok * half + col) + j);
+        sv[i][j] = __ldg(reinterpret_cast<const float4*>(a.sin_t + tok * half + col) + j);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < TOK; ++i) {
+    const int64_t tok = tok0 + i;
+    if (tok >= a.seq) continue;
+    const float* c = reinterpret_cast<const float*>(cv[i]);
+    const float* s = reinterpret_cast<const float*>(sv[i]);
+    Vec<T> o1, o2;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      const float a1 = to_f(x1[i].e[e]), a2 = to_f(x2[i].e[e]);
+      o1.e[e] = from_f<T>(a1 * c[e] - a2 * s[e]);
+      o2.e[e] = from_f<T>(a2 * c[e] + a1 * s[e]);
+    }
+    T* d = dst + (tok * nh + hh) * 2 * half + col;
+    st_vec_stream(d, o1);
+    st_vec_stream(d + half, o2);
   }
 }
 
@@ -145,9 +206,9 @@ int launch_split(const void* xe, const void* xo, const void* c, const void* s, v
                    aligned16(oo) && n % E == 0;
   if (vec) {
     const int64_t npk = n / E;
-    rope_split_vec<T><<<grid_for(npk, threads), threads, 0, st>>>(
-        static_cast<const T*>(xe), static_cast<const T*>(xo), static_cast<const T*>(c),
-        static_cast<const T*>(s), static_cast<T*>(oe), static_cast<T*>(oo), npk);
+    launch_k(rope_split_vec<T>, dim3(grid_for(npk, threads)), dim3(threads), 0, st, static_cast<const T*>(xe),
+             static_cast<const T*>(xo), static_cast<const T*>(c), static_cast<const T*>(s), static_cast<T*>(oe),
+             static_cast<T*>(oo), npk);
   } else {
     rope_split_scalar<T><<<grid_for(n, threads), threads, 0, st>>>(
         static_cast<const T*>(xe), static_cast<const T*>(xo), static_cast<const T*>(c),
@@ -157,15 +218,23 @@ int launch_split(const void* xe, const void* xo, const void* c, const void* s, v
 }
 
 template <typename T>
-int launch_rot(const RotArgs& a, int threads, cudaStream_t st) {
+int launch_rot(const RotArgs& a, int variant, int threads, cudaStream_t st) {
   constexpr int E = Vec<T>::E;
   bool vec = a.half % E == 0 && aligned16(a.q) && aligned16(a.q_out) && aligned16(a.cos_t) &&
              aligned16(a.sin_t);
   if (a.nkv > 0) vec = vec && aligned16(a.k) && aligned16(a.k_out);
   const int64_t heads = a.nq + a.nkv;
-  if (vec) {
+  const int64_t per_tok = vec ? heads * (a.half / E) : 0;
+  if (vec && variant == 0 && per_tok <= 512) {
+    constexpr int TOK = 2;
+    const int block = static_cast<int>((per_tok + 31) / 32 * 32);
+    const int64_t grid = (a.seq + TOK - 1) / TOK;
+    if (grid > 0x7fffffff) return fail(AXON_E_SHAPE, "axon_rope_rotate_half: sequence too long");
+    launch_k(rope_rotate_half_tok<T, TOK>, dim3(static_cast<unsigned>(grid)), dim3(block), 0, st, a,
+             static_cast<int>(a.half / E));
+  } else if (vec) {
     const int64_t items = a.seq * heads * (a.half / E);
-    rope_rotate_half_vec<T><<<grid_for(items, threads), threads, 0, st>>>(a, items);
+    launch_k(rope_rotate_half_vec<T>, dim3(grid_for(items, threads)), dim3(threads), 0, st, a, items);
   } else {
     const int64_t items = a.seq * heads * a.half;
     rope_rotate_half_scalar<T><<<grid_for(items, threads), threads, 0, st>>>(a, items);
@@ -182,9 +251,10 @@ extern "C" int axon_rope_split(const void* x_even, const void* x_odd, const void
                                void* out_even, void* out_odd, int64_t half_d, int64_t free_n, int32_t dtype,
                                const axon_tune_t* tune, void* stream) {
   axon_tune_t t = tune_or_default(tune);
+  if (half_d < 0 || free_n < 0) return fail(AXON_E_SHAPE, "axon_rope_split: negative size");
+  if (half_d == 0 || free_n == 0) return AXON_OK;
   if (!x_even || !x_odd || !cos_t || !sin_t || !out_even || !out_odd)
     return fail(AXON_E_ARG, "axon_rope_split: NULL tensor pointer");
-  if (half_d < 0 || free_n < 0) return fail(AXON_E_SHAPE, "axon_rope_split: negative size");
   if (t.variant != 0) return fail(AXON_E_ARG, "axon_rope_split: unknown variant %d", t.variant);
   const int threads = t.threads > 0 ? t.threads : 256;
   if (threads > 256 || threads % 32) return fail(AXON_E_ARG, "axon_rope_split: threads must be 32..256, multiple of 32");
@@ -203,20 +273,21 @@ extern "C" int axon_rope_rotate_half(const void* q, const void* k, const float* 
                                      void* q_out, void* k_out, int64_t seq, int64_t n_q, int64_t n_kv,
                                      int64_t head_dim, int32_t dtype, const axon_tune_t* tune, void* stream) {
   axon_tune_t t = tune_or_default(tune);
-  if (!q || !q_out || !cos_t || !sin_t) return fail(AXON_E_ARG, "axon_rope_rotate_half: NULL tensor pointer");
-  if (n_kv > 0 && (!k || !k_out)) return fail(AXON_E_ARG, "axon_rope_rotate_half: NULL k pointer with n_kv > 0");
   if (seq < 0 || n_q < 0 || n_kv < 0 || head_dim < 0 || head_dim % 2)
     return fail(AXON_E_SHAPE, "axon_rope_rotate_half: bad shape (head_dim must be even)");
-  if (t.variant != 0) return fail(AXON_E_ARG, "axon_rope_rotate_half: unknown variant %d", t.variant);
+  if (seq == 0 || head_dim == 0 || n_q + n_kv == 0) return AXON_OK;
+  if (!q || !q_out || !cos_t || !sin_t) return fail(AXON_E_ARG, "axon_rope_rotate_half: NULL tensor pointer");
+  if (n_kv > 0 && (!k || !k_out)) return fail(AXON_E_ARG, "axon_rope_rotate_half: NULL k pointer with n_kv > 0");
+  if (t.variant < 0 || t.variant > 1) return fail(AXON_E_ARG, "axon_rope_rotate_half: unknown variant %d", t.variant);
   const int threads = t.threads > 0 ? t.threads : 256;
   if (threads > 256 || threads % 32) return fail(AXON_E_ARG, "axon_rope_rotate_half: threads must be 32..256, multiple of 32");
   if (seq == 0 || head_dim == 0 || n_q + n_kv == 0) return AXON_OK;
   RotArgs a{q, k, cos_t, sin_t, q_out, k_out, seq, n_q, n_kv, head_dim / 2};
   cudaStream_t s = as_stream(stream);
   switch (dtype) {
-    case AXON_F32: return launch_rot<float>(a, threads, s);
-    case AXON_BF16: return launch_rot<__nv_bfloat16>(a, threads, s);
-    case AXON_F16: return launch_rot<__half>(a, threads, s);
+    case AXON_F32: return launch_rot<float>(a, t.variant, threads, s);
+    case AXON_BF16: return launch_rot<__nv_bfloat16>(a, t.variant, threads, s);
+    case AXON_F16: return launch_rot<__half>(a, t.variant, threads, s);
     default: return fail(AXON_E_UNSUPPORTED, "axon_rope_rotate_half: unsupported dtype %d", dtype);
   }
 }

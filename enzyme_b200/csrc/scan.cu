@@ -4,7 +4,8 @@
 // Parallel Prefix Scan with Decoupled Look-back", NVIDIA TR 2016). Each CTA
 // takes the next tile id from an atomic counter, so a tile's predecessors in
 // its row were always claimed by CTAs that are already running; it scans its
-// tile in registers (thread-serial, then warp shuffles, then across warps),
+// tile in registers (warp-striped 16-byte packets: packet-serial, then warp
+// shuffles per segment, then across warps),
 // publishes the tile aggregate, looks back over predecessor descriptors with
 // one warp until it meets an inclusive prefix, publishes its own inclusive
 // prefix and writes the tile. Every input byte is read once and every output
@@ -45,35 +46,48 @@ __device__ __forceinline__ double warp_sum_d(double v) {
   return v;
 }
 
+// Warp-striped tile layout: warp w of the CTA owns the ITEMS*32 contiguous
+// elements starting at w*ITEMS*32 of the tile, split into S = ITEMS/E
+// segments of 32 packets; lane l holds packet l of every segment. Every warp
+// load or store instruction therefore touches 32 consecutive 16-byte packets.
 template <typename Tin, int ITEMS>
-__device__ __forceinline__ void load_items(const Tin* row, int64_t col, int64_t n, bool vec, float* v) {
-  if (vec && col + ITEMS <= n) {
-    constexpr int E = Vec<Tin>::E;
+__device__ __forceinline__ void load_striped(const Tin* row, int64_t wbase, int lane, int64_t n, bool vec,
+                                             float* v) {
+  constexpr int E = Vec<Tin>::E;
 #pragma unroll
-    for (int j = 0; j < ITEMS; j += E) {
-      Vec<Tin> p = ld_vec_stream(row + col + j);
+  for (int sgi = 0; sgi < ITEMS / E; ++sgi) {
+    const int64_t col = wbase + (static_cast<int64_t>(sgi) * 32 + lane) * E;
+    if (vec && col + E <= n) {
+      Vec<Tin> p = ld_vec_stream(row + col);
 #pragma unroll
-      for (int e = 0; e < E; ++e) v[j + e] = to_f(p.e[e]);
+      for (int e = 0; e < E; ++e) v[sgi * E + e] = to_f(p.e[e]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < E; ++e) v[sgi * E + e] = col + e < n ? to_f(row[col + e]) : 0.f;
     }
-  } else {
-#pragma unroll
-    for (int j = 0; j < ITEMS; ++j) v[j] = col + j < n ? to_f(row[col + j]) : 0.f;
   }
 }
 
-template <typename Tout, int ITEMS>
-__device__ __forceinline__ void store_items(Tout* row, int64_t col, int64_t n, bool vec, const float* v) {
-  if (vec && col + ITEMS <= n) {
-    constexpr int E = Vec<Tout>::E;
+template <typename Tin, typename Tout, int ITEMS>
+__device__ __forceinline__ void store_striped(Tout* row, int64_t wbase, int lane, int64_t n, bool vec,
+                                              const float* v) {
+  constexpr int E = Vec<Tin>::E;  // same packet geometry as the loads
 #pragma unroll
-    for (int j = 0; j < ITEMS; j += E) {
-      Vec<Tout> p;
+  for (int sgi = 0; sgi < ITEMS / E; ++sgi) {
+    const int64_t col = wbase + (static_cast<int64_t>(sgi) * 32 + lane) * E;
+    if (vec && col + E <= n && (sizeof(Tout) * E) % 16 == 0) {
 #pragma unroll
-      for (int e = 0; e < E; ++e) p.e[e] = from_f<Tout>(v[j + e]);
-      st_vec_stream(row + col + j, p);
+      for (int h = 0; h < E; h += Vec<Tout>::E) {
+        Vec<Tout> p;
+#pragma unroll
+        for (int e = 0; e < Vec<Tout>::E; ++e) p.e[e] = from_f<Tout>(v[sgi * E + h + e]);
+        st_vec_stream(row + col + h, p);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < E; ++e)
+        if (col + e < n) row[col + e] = from_f<Tout>(v[sgi * E + e]);
     }
-  } else {
-    for (int j = 0; j < ITEMS && col + j < n; ++j) row[col + j] = from_f<Tout>(v[j]);
   }
 }
 
@@ -81,6 +95,8 @@ template <typename Tin, typename Tout, int ITEMS>
 __global__ void __launch_bounds__(1024) cumsum_lookback(const Tin* __restrict__ x, Tout* __restrict__ y,
                                                         int64_t n, int64_t ld_x, int64_t ld_y,
                                                         int64_t tiles_per_row, bool vec, unsigned char* ws) {
+  constexpr int E = Vec<Tin>::E;
+  constexpr int SEG = ITEMS / E;
   __shared__ unsigned s_tile;
   __shared__ float s_warp[32];
   __shared__ double s_prefix;
@@ -88,6 +104,8 @@ __global__ void __launch_bounds__(1024) cumsum_lookback(const Tin* __restrict__ 
   unsigned* counter = reinterpret_cast<unsigned*>(ws + 4);
   TileDesc* desc = reinterpret_cast<TileDesc*>(ws + kHeaderBytes);
 
+  pdl_wait();
+  pdl_trigger();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
   if (tid == 0) s_tile = atomicAdd(counter, 1u);
   __syncthreads();
@@ -95,34 +113,44 @@ __global__ void __launch_bounds__(1024) cumsum_lookback(const Tin* __restrict__ 
   const int64_t row = t / tiles_per_row;
   const int64_t tr = t - row * tiles_per_row;
   const int64_t tile_elems = static_cast<int64_t>(blockDim.x) * ITEMS;
-  const int64_t col = tr * tile_elems + static_cast<int64_t>(tid) * ITEMS;
+  const int64_t wbase = tr * tile_elems + static_cast<int64_t>(warp) * ITEMS * 32;
   const Tin* xr = x + row * ld_x;
   Tout* yr = y + row * ld_y;
 
   float v[ITEMS];
-  load_items<Tin, ITEMS>(xr, col, n, vec, v);
+  load_striped<Tin, ITEMS>(xr, wbase, lane, n, vec, v);
+  // Per segment: scan the lane's packet, then across lanes; `carry` runs over
+  // the warp's segments in order.
+  float carry = 0.f;
 #pragma unroll
-  for (int j = 1; j < ITEMS; ++j) v[j] += v[j - 1];
-  const float tsum = v[ITEMS - 1];
-  float incl = tsum;
+  for (int sg = 0; sg < SEG; ++sg) {
 #pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    float up = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += up;
+    for (int e = 1; e < E; ++e) v[sg * E + e] += v[sg * E + e - 1];
+    const float own = v[sg * E + E - 1];
+    float incl = own;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float up = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += up;
+    }
+    const float base = carry + (incl - own);
+#pragma unroll
+    for (int e = 0; e < E; ++e) v[sg * E + e] += base;
+    carry += __shfl_sync(0xffffffffu, incl, 31);
   }
-  if (lane == 31) s_warp[warp] = incl;
+  if (lane == 0) s_warp[warp] = carry;
   __syncthreads();
   if (warp == 0) {
     float w = lane < nwarps ? s_warp[lane] : 0.f;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      float up = __shfl_up_sync(0xffffffffu, w, o);
+      const float up = __shfl_up_sync(0xffffffffu, w, o);
       if (lane >= o) w += up;
     }
     if (lane < nwarps) s_warp[lane] = w;
   }
   __syncthreads();
-  const float thread_excl = (warp > 0 ? s_warp[warp - 1] : 0.f) + (incl - tsum);
+  const float warp_excl = warp > 0 ? s_warp[warp - 1] : 0.f;
   const double tile_agg = static_cast<double>(s_warp[nwarps - 1]);
 
   if (warp == 0) {
@@ -175,11 +203,10 @@ __global__ void __launch_bounds__(1024) cumsum_lookback(const Tin* __restrict__ 
     if (lane == 0) s_prefix = prefix;
   }
   __syncthreads();
-  const double p = s_prefix + static_cast<double>(thread_excl);
-  float out[ITEMS];
+  const double p = s_prefix;
 #pragma unroll
-  for (int j = 0; j < ITEMS; ++j) out[j] = static_cast<float>(p + static_cast<double>(v[j]));
-  store_items<Tout, ITEMS>(yr, col, n, vec, out);
+  for (int j = 0; j < ITEMS; ++j) v[j] = static_cast<float>(p + static_cast<double>(warp_excl + v[j]));
+  store_striped<Tin, Tout, ITEMS>(yr, wbase, lane, n, vec, v);
 }
 
 void tile_shape(const axon_tune_t& t, int& threads, int& items) {
@@ -214,11 +241,11 @@ int launch_lookback(const void* x, void* y, int64_t m, int64_t n, int64_t ld_x, 
   if (e != cudaSuccess) return fail(AXON_E_CUDA, "axon_cumsum: workspace clear failed: %s", cudaGetErrorString(e));
   auto* ws8 = static_cast<unsigned char*>(ws);
   if (items == 8)
-    cumsum_lookback<Tin, Tout, 8><<<static_cast<int>(tiles), threads, 0, s>>>(
-        static_cast<const Tin*>(x), static_cast<Tout*>(y), n, ld_x, ld_y, tpr, vec, ws8);
+    launch_k(cumsum_lookback<Tin, Tout, 8>, dim3(static_cast<unsigned>(tiles)), dim3(threads), 0, s,
+             static_cast<const Tin*>(x), static_cast<Tout*>(y), n, ld_x, ld_y, tpr, vec, ws8);
   else
-    cumsum_lookback<Tin, Tout, 16><<<static_cast<int>(tiles), threads, 0, s>>>(
-        static_cast<const Tin*>(x), static_cast<Tout*>(y), n, ld_x, ld_y, tpr, vec, ws8);
+    launch_k(cumsum_lookback<Tin, Tout, 16>, dim3(static_cast<unsigned>(tiles)), dim3(threads), 0, s,
+             static_cast<const Tin*>(x), static_cast<Tout*>(y), n, ld_x, ld_y, tpr, vec, ws8);
   return launch_status("axon_cumsum");
 }
 
@@ -248,8 +275,8 @@ extern "C" int axon_cumsum(const void* x, void* y, int64_t m, int64_t n, int64_t
                            int32_t in_dtype, int32_t out_dtype, void* workspace, int64_t workspace_bytes,
                            const axon_tune_t* tune, void* stream) {
   axon_tune_t t = tune_or_default(tune);
-  if (!x || !y) return fail(AXON_E_ARG, "axon_cumsum: NULL tensor pointer");
   if (m < 0 || n < 0) return fail(AXON_E_SHAPE, "axon_cumsum: negative size");
+  if (m > 0 && n > 0 && (!x || !y)) return fail(AXON_E_ARG, "axon_cumsum: NULL tensor pointer");
   if (ld_x < n || ld_y < n) return fail(AXON_E_SHAPE, "axon_cumsum: leading dimension smaller than n");
   if (t.split != 0 && t.split != 2048 && t.split != 4096 && t.split != 8192 && t.split != 16384)
     return fail(AXON_E_ARG, "axon_cumsum: split must be one of 2048, 4096, 8192, 16384 (got %d)", t.split);

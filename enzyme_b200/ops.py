@@ -215,8 +215,16 @@ def rmsnorm_matmul(x, w, *, out=None, out_dtype=None, workspace=None, tune=None)
     return y
 
 
+def silu_mlp_workspace_bytes(m: int, n: int, dtype_code_: int, tune=None) -> int:
+    nbytes = int(N.lib().axon_silu_mlp_workspace_bytes(m, n, dtype_code_, _tune(tune)))
+    if nbytes < 0:
+        check(nbytes)
+    return nbytes
+
+
 def silu_mlp(x, w1, w2, w3, *, out=None, out_dtype=None, workspace=None, tune=None):
-    """(silu(x @ w1) * (x @ w2)) @ w3 with the activation kept in x's dtype."""
+    """(silu(x @ w1) * (x @ w2)) @ w3. The activation is stored in x's dtype as
+    tune['precision'] terms (default 1)."""
     _require_cuda(x, w1, w2, w3)
     for t in (x, w1, w2, w3):
         if not t.is_contiguous():
@@ -225,7 +233,7 @@ def silu_mlp(x, w1, w2, w3, *, out=None, out_dtype=None, workspace=None, tune=No
     n = w1.shape[1]
     p = w3.shape[1]
     y = out if out is not None else torch.empty((m, p), dtype=out_dtype or x.dtype, device=x.device)
-    need = int(N.lib().axon_silu_mlp_workspace_bytes(m, n, dtype_code(x)))
+    need = silu_mlp_workspace_bytes(m, n, dtype_code(x), tune)
     ws = workspace if workspace is not None else torch.empty(need, dtype=torch.uint8, device=x.device)
     check(N.lib().axon_silu_mlp(_ptr(x), _ptr(w1), _ptr(w2), _ptr(w3), _ptr(y), _ptr(ws), ws.numel() * ws.element_size(),
                                 m, n, k, p, dtype_code(x), dtype_code(y), _tune(tune), _stream(x)))

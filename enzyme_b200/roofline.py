@@ -33,7 +33,11 @@ def nbytes(shape, itemsize: int) -> int:
     return int(np.prod(shape)) * itemsize
 
 
-# spec -> function(dims, itemsize of the activation dtype) -> (kind, amount)
+KNOWN = frozenset({"rmsnorm", "layernorm", "softmax", "cumsum", "cumsum_nucleus_sorted", "rmsnorm_llama", "rope",
+                   "rope_gqa", "fused_adam", "fused_adam_cfg", "matmul", "rmsnorm_matmul", "silu_mlp",
+                   "silu_mlp_swiglu"})
+
+
 def work(spec: str, dims: dict, itemsize: int = 2) -> tuple[str, float]:
     """('hbm', bytes) or ('tensor', flops) for one launch of a spec at dims."""
     d = dims

@@ -69,6 +69,8 @@ typedef struct axon_tune {
   int32_t stages;       /* GEMM smem pipeline depth (2..8)                    */
   int32_t split;        /* cumsum: elements per tile (variant 0) or CTAs per
                            row cluster (variant 1)                            */
+  int32_t precision;    /* silu_mlp: terms of the stored activation (1 = one
+                           bf16 value, 2 = hi + lo, 3 = three terms)          */
 } axon_tune_t;
 
 /* ---- library metadata ----------------------------------------------------- */
@@ -211,13 +213,20 @@ AXON_API int axon_rmsnorm_matmul(const void* x, const void* w, void* y, void* wo
                         int64_t m, int64_t n, int64_t k, int32_t ab_dtype,
                         int32_t c_dtype, const axon_tune_t* tune, void* stream);
 
-/* Bytes of scratch axon_silu_mlp needs: the [m, n] activation in ab_dtype. */
-AXON_API int64_t axon_silu_mlp_workspace_bytes(int64_t m, int64_t n, int32_t ab_dtype);
+/* Bytes of scratch axon_silu_mlp needs: the [m, n] activation in ab_dtype,
+ * times tune->precision terms. */
+AXON_API int64_t axon_silu_mlp_workspace_bytes(int64_t m, int64_t n, int32_t ab_dtype,
+                                               const axon_tune_t* tune);
 
 /* (silu(x @ w1) * (x @ w2)) @ w3 (Axon kernels/silu_mlp/refs.py:16-21):
  * x [m, k], w1/w2 [k, n], w3 [n, p], y [m, p] of c_dtype. Two tcgen05 GEMMs:
  * gate and up in one pass with the SiLU-gate epilogue writing the activation
- * (ab_dtype) into `workspace`, then the down projection. In the column/row
+ * (ab_dtype) into `workspace`, then the down projection. With
+ * tune->precision = T > 1 the activation a is stored as T terms (a ~ t0 + t1
+ * + ..., each rounded to ab_dtype; 8 more mantissa bits per term) and the
+ * down projection contracts over K = T*n, reading w3 once per term; this is
+ * what matches an fp32 reference when the activation is large (n % 64 == 0
+ * required). In the column/row
  * tensor-parallel form each rank passes its shard (n = inter / G) and sums the
  * fp32 partial outputs across ranks. */
 AXON_API int axon_silu_mlp(const void* x, const void* w1, const void* w2, const void* w3,
