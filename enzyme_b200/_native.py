@@ -109,6 +109,7 @@ SIGNATURES: dict[str, tuple] = {
     "axon_cumsum_workspace_bytes": (_I64, [_I64, _I64, _TUNE]),
     "axon_cumsum": (_I32, [_P, _P, _I64, _I64, _I64, _I64, _I32, _I32, _P, _I64, _TUNE, _P]),
     "axon_cumsum_status": (_I32, [_P, _P]),
+    "axon_cumsum_noalloc": (_I32, [_P, _P, _I64, _I64, _I64, _I64, _I32, _I32, _TUNE, _P]),
     "axon_adam": (
         _I32,
         [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _I32, _P, _P, _P, _I32,

@@ -303,3 +303,75 @@ extern "C" int axon_cumsum_status(const void* workspace, void* stream) {
   if (status != 0) return fail(status, "axon_cumsum: a look-back wait gave up (status %d)", status);
   return AXON_OK;
 }
+
+// ---- allocation-free variant ----------------------------------------------------
+//
+// axon_cumsum_noalloc serves callers that must not allocate device memory
+// themselves: a plugin whose host framework owns every device allocation
+// through its own memory planner, or a latency-critical caller for whom
+// cudaMalloc (which can synchronise the whole device) is off limits. It runs
+// the same look-back kernel as axon_cumsum, with its scratch in a fixed
+// file-scope device array instead of a caller workspace. The array exists
+// once per device that loads this library and lives until the process exits.
+
+#include <mutex>
+
+namespace axon {
+namespace {
+
+constexpr int64_t kNoAllocScratchBytes = 1 << 20;  // 1 MiB: up to 32767 look-back tiles
+static __device__ __align__(256) unsigned char g_cumsum_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_addr[kMaxDevices] = {};
+
+// The device address of g_cumsum_scratch on the current device. In host code
+// the symbol is only a stand-in, so the address is looked up with
+// cudaGetSymbolAddress, once per device, with that device current.
+int scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(AXON_E_CUDA, "axon_cumsum_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(AXON_E_UNSUPPORTED, "axon_cumsum_noalloc: device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_cumsum_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(AXON_E_CUDA, "axon_cumsum_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+    g_scratch_addr[dev] = p;
+  }
+  *out = g_scratch_addr[dev];
+  return AXON_OK;
+}
+
+}  // namespace
+}  // namespace axon
+
+extern "C" int axon_cumsum_noalloc(const void* x, void* y, int64_t m, int64_t n, int64_t ld_x, int64_t ld_y,
+                                   int32_t in_dtype, int32_t out_dtype, const axon_tune_t* tune, void* stream) {
+  axon_tune_t t = tune_or_default(tune);
+  if (m < 0 || n < 0) return fail(AXON_E_SHAPE, "axon_cumsum_noalloc: negative size");
+  if (m > 0 && n > 0 && (!x || !y)) return fail(AXON_E_ARG, "axon_cumsum_noalloc: NULL tensor pointer");
+  if (ld_x < n || ld_y < n) return fail(AXON_E_SHAPE, "axon_cumsum_noalloc: leading dimension smaller than n");
+  if (t.split != 0 && t.split != 2048 && t.split != 4096 && t.split != 8192 && t.split != 16384)
+    return fail(AXON_E_ARG, "axon_cumsum_noalloc: split must be one of 2048, 4096, 8192, 16384 (got %d)", t.split);
+  if (t.variant != 0) return fail(AXON_E_UNSUPPORTED, "axon_cumsum_noalloc: only variant 0 uses scratch");
+  if (m == 0 || n == 0) return AXON_OK;
+  const int64_t need = lookback_ws_bytes(m, n, t);
+  if (need > kNoAllocScratchBytes)
+    return fail(AXON_E_SHAPE,
+                "axon_cumsum_noalloc: a %lld x %lld scan needs %lld bytes of look-back scratch but the static "
+                "scratch holds %lld; use a larger split or axon_cumsum with a workspace",
+                (long long)m, (long long)n, (long long)need, (long long)kNoAllocScratchBytes);
+  void* ws = nullptr;
+  const int rc = scratch_address(&ws);
+  if (rc != AXON_OK) return rc;
+  cudaStream_t s = as_stream(stream);
+  switch (in_dtype) {
+    case AXON_F32: return dispatch_out<float>(out_dtype, x, y, m, n, ld_x, ld_y, ws, t, s);
+    case AXON_BF16: return dispatch_out<__nv_bfloat16>(out_dtype, x, y, m, n, ld_x, ld_y, ws, t, s);
+    default: return fail(AXON_E_UNSUPPORTED, "axon_cumsum_noalloc: unsupported input dtype %d", in_dtype);
+  }
+}

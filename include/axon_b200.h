@@ -152,6 +152,25 @@ AXON_API int axon_cumsum(const void* x, void* y, int64_t m, int64_t n, int64_t l
  * `workspace`: AXON_OK or AXON_E_TIMEOUT. */
 AXON_API int axon_cumsum_status(const void* workspace, void* stream);
 
+/* Allocation-free form of axon_cumsum (variant 0 only). No counterpart in the
+ * reference: it exists for callers that must not allocate device memory --
+ * a plugin whose host framework owns every device allocation, or a
+ * latency-critical path where cudaMalloc, which can synchronise the device,
+ * is not allowed. Instead of a caller workspace it uses one 1 MiB static
+ * device array per device that loads the library (held until the process
+ * exits), so a scan may use at most (1 MiB - 32) / 32 = 32767 look-back tiles
+ * (m * ceil(n / tile), tile = tune->split elements, default 8192); larger
+ * shapes return AXON_E_SHAPE. It calls no cudaMalloc or cudaFree. The first
+ * call on a device looks up the array's device address (cudaGetSymbolAddress),
+ * so make that first call before any stream capture. Every call clears the
+ * array on `stream` and then uses it: calls that overlap on the GPU (other
+ * streams, other threads) race on the one array and must be serialised by
+ * the caller. The look-back status word is not exposed; use axon_cumsum with
+ * a workspace where AXON_E_TIMEOUT must be observable. */
+AXON_API int axon_cumsum_noalloc(const void* x, void* y, int64_t m, int64_t n, int64_t ld_x,
+                                 int64_t ld_y, int32_t in_dtype, int32_t out_dtype,
+                                 const axon_tune_t* tune, void* stream);
+
 /* ---- optimizer ---------------------------------------------------------------- */
 
 typedef struct axon_adam_hparams {
