@@ -309,13 +309,19 @@ class SwiGLU(Workload):
         self.w1 = (0.02 * torch.randn(h, self.shard, device=dev, generator=self.gen)).to(torch.bfloat16)
         self.w2 = (0.02 * torch.randn(h, self.shard, device=dev, generator=self.gen)).to(torch.bfloat16)
         self.w3 = (0.02 * torch.randn(self.shard, h, device=dev, generator=self.gen)).to(torch.bfloat16)
-        self.act = torch.empty(m * self.shard * 2, dtype=torch.uint8, device=dev)
+        # The activation is stored as f16 (precision 4): one bf16 term misses
+        # the config's 1e-2 tolerance on ~1e4 outputs; f16 (or two bf16
+        # terms) meets it. The step converts W_down to f16 each call.
+        self.tune = {"precision": self.PRECISION}
+        ws = ops.silu_mlp_workspace_bytes(m, self.shard, h, 1, self.tune)
+        self.act = torch.empty(ws, dtype=torch.uint8, device=dev)
         self.y = torch.empty(m, h, dtype=torch.bfloat16 if world == 1 else torch.float32, device=dev)
         self.nsets = 1
         self.scaling = "strong" if world > 1 else "weak"
         self.use_graph = world == 1
-        if world > 1:
-            self.launches_per_step = 2
+        self.launches_per_step = 3 if self.PRECISION == 4 else 2
+
+    PRECISION = 4
 
     def per_step_work(self):
         m, n, k, p = 4096, self.shard, 4096, 4096
@@ -325,7 +331,7 @@ class SwiGLU(Workload):
         return roofline.work(self.spec, self.dims)[1]
 
     def launch(self, i):
-        ops.silu_mlp(self.x, self.w1, self.w2, self.w3, out=self.y, workspace=self.act)
+        ops.silu_mlp(self.x, self.w1, self.w2, self.w3, out=self.y, workspace=self.act, tune=self.tune)
         if self.world > 1:
             dist.all_reduce(self.y)
 

@@ -67,7 +67,8 @@ def variants(spec_name: str) -> list[Variant]:
     if spec_name in GEMM_SPECS:
         return [Variant(0, "tcgen05_ws_persistent")]
     if spec_name in MLP_SPECS:
-        return [Variant(0, "tcgen05_act_1term"), Variant(1, "tcgen05_act_2term"), Variant(2, "tcgen05_act_3term")]
+        return [Variant(0, "tcgen05_act_1term"), Variant(1, "tcgen05_act_2term"), Variant(2, "tcgen05_act_3term"),
+                Variant(3, "tcgen05_act_f16")]
     raise KeyError(f"no CUDA variants for spec '{spec_name}'")
 
 
@@ -127,7 +128,8 @@ def tune_for(spec_name: str, hw_variant: int, tiles: dict[str, int]) -> dict | l
     if spec_name in GEMM_SPECS:
         return {"variant": hw_variant, "block_n": 64 * t["N"], "stages": t["K"]}
     if spec_name in MLP_SPECS:
-        return {"block_n": 128 * t["N"], "stages": t["K"], "precision": hw_variant + 1, "down_block_n": 64 * t["P"]}
+        precision = 4 if hw_variant == 3 else hw_variant + 1
+        return {"block_n": 128 * t["N"], "stages": t["K"], "precision": precision, "down_block_n": 64 * t["P"]}
     raise KeyError(spec_name)
 
 

@@ -46,6 +46,9 @@ inline bool valid_dtype(int32_t dt) { return dt == AXON_F32 || dt == AXON_BF16 |
 // Number of SMs of the current device (cached per device).
 int sm_count();
 
+// Elementwise dtype conversion of n elements (the body of axon_cast).
+int cast_impl(const void* src, void* dst, int64_t n, int32_t src_dtype, int32_t dst_dtype, cudaStream_t s);
+
 // Resolves a tune pointer (NULL = all defaults).
 inline axon_tune_t tune_or_default(const axon_tune_t* t) {
   axon_tune_t d{};

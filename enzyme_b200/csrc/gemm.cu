@@ -502,7 +502,26 @@ int gemm_impl(const void* a, const void* b, const void* b2, void* c, const float
   if (k == 0) return fail(AXON_E_SHAPE, "axon_gemm: k == 0 not supported");
 
   int bn = t.block_n;
-  if (bn == 0) bn = epilogue == AXON_EPI_SILU_GATE ? 256 : (n <= 64 ? 64 : n <= 128 ? 128 : 256);
+  if (bn == 0) {
+    if (epilogue == AXON_EPI_SILU_GATE) {
+      bn = 256;
+    } else if (n <= 64) {
+      bn = 64;
+    } else if (n <= 128) {
+      bn = 128;
+    } else {
+      // Persistent CTAs take tiles round-robin, so the last wave decides: use
+      // 128-column tiles when 256-column tiles leave the last wave much
+      // emptier (e.g. 4096 x 4096: 512 tiles = 3.46 waves on 148 SMs).
+      const int64_t sms = sm_count();
+      auto eff = [&](int64_t b) {
+        const int64_t tiles = ((m + BM - 1) / BM) * ((n + b - 1) / b);
+        const int64_t waves = (tiles + sms - 1) / sms;
+        return static_cast<double>(tiles) / static_cast<double>(waves * sms);
+      };
+      bn = eff(128) > eff(256) + 0.06 ? 128 : 256;
+    }
+  }
   if (bn != 64 && bn != 128 && bn != 256) return fail(AXON_E_ARG, "axon_gemm: block_n must be 64, 128 or 256");
   if (epilogue == AXON_EPI_SILU_GATE && bn == 64) return fail(AXON_E_ARG, "axon_gemm: SILU_GATE needs block_n >= 128");
   const int smax = max_stages(bn);
@@ -583,37 +602,64 @@ extern "C" int axon_rmsnorm_matmul(const void* x, const void* w, void* y, void* 
                    AXON_EPI_ROWSCALE, tune, stream);
 }
 
+constexpr int kF16Act = 4;  // tune.precision value of the f16-activation mode
+
 static int silu_terms(const axon_tune_t* tune) {
   const int p = tune ? tune->precision : 0;
   return p <= 0 ? 1 : p;
 }
 
-extern "C" int64_t axon_silu_mlp_workspace_bytes(int64_t m, int64_t n, int32_t ab_dtype, const axon_tune_t* tune) {
+static bool silu_mode_ok(int terms) { return (terms >= 1 && terms <= 3) || terms == kF16Act; }
+
+static int64_t silu_ws_bytes(int64_t m, int64_t n, int64_t p, int terms) {
+  return terms == kF16Act ? m * n * 2 + n * p * 2 : m * n * 2 * terms;
+}
+
+extern "C" int64_t axon_silu_mlp_workspace_bytes(int64_t m, int64_t n, int64_t p, int32_t ab_dtype,
+                                                 const axon_tune_t* tune) {
   (void)ab_dtype;
-  if (m < 0 || n < 0) return fail(AXON_E_SHAPE, "axon_silu_mlp_workspace_bytes: negative size");
+  if (m < 0 || n < 0 || p < 0) return fail(AXON_E_SHAPE, "axon_silu_mlp_workspace_bytes: negative size");
   const int terms = silu_terms(tune);
-  if (terms > 3) return fail(AXON_E_ARG, "axon_silu_mlp: precision must be 1, 2 or 3 terms");
-  return m * n * 2 * terms;
+  if (!silu_mode_ok(terms)) return fail(AXON_E_ARG, "axon_silu_mlp: precision must be 1, 2, 3 or 4");
+  return silu_ws_bytes(m, n, p, terms);
 }
 
 extern "C" int axon_silu_mlp(const void* x, const void* w1, const void* w2, const void* w3, void* y,
                              void* workspace, int64_t workspace_bytes, int64_t m, int64_t n, int64_t k, int64_t p,
                              int32_t ab_dtype, int32_t c_dtype, const axon_tune_t* tune, void* stream) {
   const int terms = silu_terms(tune);
-  if (terms > 3) return fail(AXON_E_ARG, "axon_silu_mlp: precision must be 1, 2 or 3 terms");
+  if (!silu_mode_ok(terms)) return fail(AXON_E_ARG, "axon_silu_mlp: precision must be 1, 2, 3 or 4");
   if (m < 0 || n < 0 || k < 0 || p < 0) return fail(AXON_E_SHAPE, "axon_silu_mlp: negative size");
   if (m == 0 || p == 0) return AXON_OK;
-  if (terms > 1 && n % 64) return fail(AXON_E_SHAPE, "axon_silu_mlp: split precision needs n %% 64 == 0 (n=%lld)",
-                                       (long long)n);
-  if (!workspace || workspace_bytes < m * n * 2 * terms)
-    return fail(AXON_E_ARG, "axon_silu_mlp: workspace of %lld bytes needed", (long long)(m * n * 2 * terms));
+  if (terms > 1 && terms <= 3 && n % 64)
+    return fail(AXON_E_SHAPE, "axon_silu_mlp: split precision needs n %% 64 == 0 (n=%lld)", (long long)n);
+  if (terms == kF16Act && (ab_dtype != AXON_BF16 || p % 8))
+    return fail(AXON_E_UNSUPPORTED, "axon_silu_mlp: the f16-activation mode takes bf16 operands and p %% 8 == 0");
+  const int64_t need = silu_ws_bytes(m, n, p, terms);
+  if (!workspace || workspace_bytes < need)
+    return fail(AXON_E_ARG, "axon_silu_mlp: workspace of %lld bytes needed", (long long)need);
   axon_tune_t t = tune_or_default(tune);
   axon_tune_t up = t, down = t;
   up.block_n = t.block_n == 64 ? 0 : t.block_n;
+  down.stages = 0;
+  down.block_n = 0;
+  if (terms == kF16Act) {
+    // The activation is written as f16 (8 more mantissa bits than bf16) and
+    // the down projection runs f16 x f16, on a per-call f16 copy of W_down:
+    // a tcgen05 f16-kind MMA takes both operands in one type.
+    __half* act = static_cast<__half*>(workspace);
+    __half* w3h = reinterpret_cast<__half*>(static_cast<unsigned char*>(workspace) + m * n * 2);
+    int rc = cast_impl(w3, w3h, n * p, AXON_BF16, AXON_F16, as_stream(stream));
+    if (rc) return rc;
+    rc = gemm_impl(x, w1, w2, act, nullptr, m, n, k, k, n, n, ab_dtype, AXON_F16, AXON_EPI_SILU_GATE, &up, stream, 1,
+                   0, 0);
+    if (rc) return rc;
+    return gemm_impl(act, w3h, nullptr, y, nullptr, m, p, n, n, p, p, AXON_F16, c_dtype, AXON_EPI_NONE, &down,
+                     stream, 1, 0, 0);
+  }
   int rc = gemm_impl(x, w1, w2, workspace, nullptr, m, n, k, k, n, n * terms, ab_dtype, ab_dtype, AXON_EPI_SILU_GATE,
                      &up, stream, terms, n, 0);
   if (rc) return rc;
-  down.stages = 0;
   return gemm_impl(workspace, w3, nullptr, y, nullptr, m, p, n * terms, n * terms, p, p, ab_dtype, c_dtype,
                    AXON_EPI_NONE, &down, stream, 1, 0, terms > 1 ? n : 0);
 }

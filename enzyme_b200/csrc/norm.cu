@@ -10,6 +10,8 @@
 // whose starts are not 16-byte aligned: a CTA walks its row once per pass;
 // the second pass re-reads the row from L2 (rows in flight are far smaller
 // than the 126 MB L2).
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace axon {
@@ -82,6 +84,14 @@ __global__ void __launch_bounds__(max_row_threads<T>()) row_resident_kernel(RowA
   auto valid = [&](int i, int e) -> bool {
     return active && (static_cast<int64_t>(i) * tpr + lane) * E + e < n;
   };
+  // Keep only the raw packets live between passes: without this the compiler
+  // holds every converted fp32 value of the previous pass, doubling the
+  // registers (and halving the resident rows).
+  auto pin_raw = [&]() {
+#pragma unroll
+    for (int i = 0; i < VPT; ++i)
+      asm volatile("" : "+r"(raw[i].u.x), "+r"(raw[i].u.y), "+r"(raw[i].u.z), "+r"(raw[i].u.w));
+  };
 
   float s0 = 0.f, s1 = 0.f;  // op-specific statistics
   if constexpr (OP == OP_RMS || OP == OP_RSQRT) {
@@ -104,6 +114,7 @@ __global__ void __launch_bounds__(max_row_threads<T>()) row_resident_kernel(RowA
 #pragma unroll
       for (int e = 0; e < E; ++e) s0 += to_f(raw[i].e[e]);
     const float mean = row_allreduce<false>(s0, red, gw, row_in_cta) / static_cast<float>(n);
+    pin_raw();
     float ss = 0.f;
 #pragma unroll
     for (int i = 0; i < VPT; ++i)
@@ -123,6 +134,7 @@ __global__ void __launch_bounds__(max_row_threads<T>()) row_resident_kernel(RowA
       for (int e = 0; e < E; ++e)
         if (valid(i, e)) mx = fmaxf(mx, to_f(raw[i].e[e]));
     mx = row_allreduce<true>(mx, red, gw, row_in_cta);
+    pin_raw();
     float sum = 0.f;
 #pragma unroll
     for (int i = 0; i < VPT; ++i)
@@ -135,17 +147,30 @@ __global__ void __launch_bounds__(max_row_threads<T>()) row_resident_kernel(RowA
   }
 
   if (!active) return;
+  pin_raw();
   T* yr = static_cast<T*>(a.y) + row * a.ld_y;
+  // The resident path only takes a weight of the row's own dtype, read as
+  // 16-byte packets (all rows share it, so it stays in L1/L2).
+  const T* w = static_cast<const T*>(a.w);
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int64_t col = (static_cast<int64_t>(i) * tpr + lane) * E;
     if (col >= n) continue;
+    Vec<T> wv;
+    if constexpr (OP == OP_RMS) {
+      if (w != nullptr && col + E <= n) {
+        wv = ld_vec(w + col);
+      } else {
+#pragma unroll
+        for (int e = 0; e < E; ++e) wv.e[e] = (w != nullptr && col + e < n) ? w[col + e] : from_f<T>(1.f);
+      }
+    }
     Vec<T> o;
 #pragma unroll
     for (int e = 0; e < E; ++e) {
       float v = to_f(raw[i].e[e]);
       float r;
-      if constexpr (OP == OP_RMS) r = v * s1 * weight_at(a, col + e < n ? col + e : 0);
+      if constexpr (OP == OP_RMS) r = v * s1 * to_f(wv.e[e]);
       else if constexpr (OP == OP_LN) r = (v - s0) * s1;
       else r = __expf(v - s0) * s1;
       o.e[e] = from_f<T>(r);
@@ -275,7 +300,9 @@ template <typename T, int OP>
 int launch_rows(const RowArgs& a, const axon_tune_t& t, cudaStream_t s, const char* name) {
   constexpr int E = Vec<T>::E;
   if (a.m == 0 || a.n == 0) return AXON_OK;
-  const bool vec_ok = aligned16(a.x) && (a.ld_x * sizeof(T)) % 16 == 0 &&
+  constexpr int32_t kCode = sizeof(T) == 4 ? AXON_F32 : std::is_same<T, __half>::value ? AXON_F16 : AXON_BF16;
+  const bool w_ok = a.w == nullptr || (a.w_dtype == kCode && aligned16(a.w));
+  const bool vec_ok = aligned16(a.x) && (a.ld_x * sizeof(T)) % 16 == 0 && w_ok &&
                       (OP == OP_RSQRT || (aligned16(a.y) && (a.ld_y * sizeof(T)) % 16 == 0));
   const int64_t nv = (a.n + E - 1) / E;
   int tpr = 0, vpt = 0;

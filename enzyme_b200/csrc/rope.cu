@@ -108,10 +108,12 @@ __global__ void __launch_bounds__(256) rope_rotate_half_vec(RotArgs a, int64_t i
 }
 
 // Token-blocked vector path (variant 0), used when one token's packets (heads
-// x packets per half-row, at most 512) fit in one CTA: thread t owns head t / ppr and packet t % ppr
-// for TOK consecutive tokens, so all index math is done once per thread, the
-// TOK tokens' loads are issued together, and the heads of a token share the
-// cos/sin row through L1.
+// x packets per half-row, at most 512) fit in one CTA: thread t owns head
+// t / ppr and packet t % ppr for TOK consecutive tokens, so all index math is
+// done once per thread and the TOK tokens' q/k loads are issued together
+// (only the raw packets are held in registers). The cos/sin rows are read in
+// the compute loop: every head of a token reads the same row, so after the
+// first head they are L1 hits.
 template <typename T, int TOK>
 __global__ void __launch_bounds__(512) rope_rotate_half_tok(RotArgs a, int ppr) {
   constexpr int E = Vec<T>::E;
@@ -130,7 +132,6 @@ __global__ void __launch_bounds__(512) rope_rotate_half_tok(RotArgs a, int ppr) 
   const int64_t tok0 = static_cast<int64_t>(blockIdx.x) * TOK;
   const int col = p * E;
   Vec<T> x1[TOK], x2[TOK];
-  float4 cv[TOK][E / 4], sv[TOK][E / 4];
 #pragma unroll
   for (int i = 0; i < TOK; ++i) {
     const int64_t tok = tok0 + i;
@@ -138,19 +139,20 @@ __global__ void __launch_bounds__(512) rope_rotate_half_tok(RotArgs a, int ppr) 
       const T* s = src + (tok * nh + hh) * 2 * half + col;
       x1[i] = ld_vec_stream(s);
       x2[i] = ld_vec_stream(s + half);
-#pragma unroll
-      for (int j = 0; j < E / 4; ++j) {
-        cv[i][j] = __ldg(reinterpret_cast<const float4*>(a.cos_t + tok * half + col) + j);
-        sv[i][j] = __ldg(reinterpret_cast<const float4*>(a.sin_t + tok * half + col) + j);
-      }
     }
   }
 #pragma unroll
   for (int i = 0; i < TOK; ++i) {
     const int64_t tok = tok0 + i;
     if (tok >= a.seq) continue;
-    const float* c = reinterpret_cast<const float*>(cv[i]);
-    const float* s = reinterpret_cast<const float*>(sv[i]);
+    float c[E], s[E];
+#pragma unroll
+    for (int j = 0; j < E; j += 4) {
+      const float4 c4 = __ldg(reinterpret_cast<const float4*>(a.cos_t + tok * half + col + j));
+      const float4 s4 = __ldg(reinterpret_cast<const float4*>(a.sin_t + tok * half + col + j));
+      c[j] = c4.x; c[j + 1] = c4.y; c[j + 2] = c4.z; c[j + 3] = c4.w;
+      s[j] = s4.x; s[j + 1] = s4.y; s[j + 2] = s4.z; s[j + 3] = s4.w;
+    }
     Vec<T> o1, o2;
 #pragma unroll
     for (int e = 0; e < E; ++e) {
@@ -218,7 +220,7 @@ int launch_split(const void* xe, const void* xo, const void* c, const void* s, v
 }
 
 template <typename T>
-int launch_rot(const RotArgs& a, int variant, int threads, cudaStream_t st) {
+int launch_rot(const RotArgs& a, int variant, int threads, int rows_per_cta, cudaStream_t st) {
   constexpr int E = Vec<T>::E;
   bool vec = a.half % E == 0 && aligned16(a.q) && aligned16(a.q_out) && aligned16(a.cos_t) &&
              aligned16(a.sin_t);
@@ -226,12 +228,20 @@ int launch_rot(const RotArgs& a, int variant, int threads, cudaStream_t st) {
   const int64_t heads = a.nq + a.nkv;
   const int64_t per_tok = vec ? heads * (a.half / E) : 0;
   if (vec && variant == 0 && per_tok <= 512) {
-    constexpr int TOK = 2;
+    // tokens per CTA: tune.rows_per_cta in {1, 2, 4, 8}; default 4
+    const int tok = rows_per_cta > 0 ? rows_per_cta : 4;
     const int block = static_cast<int>((per_tok + 31) / 32 * 32);
-    const int64_t grid = (a.seq + TOK - 1) / TOK;
+    const int64_t grid = (a.seq + tok - 1) / tok;
     if (grid > 0x7fffffff) return fail(AXON_E_SHAPE, "axon_rope_rotate_half: sequence too long");
-    launch_k(rope_rotate_half_tok<T, TOK>, dim3(static_cast<unsigned>(grid)), dim3(block), 0, st, a,
-             static_cast<int>(a.half / E));
+    const dim3 g(static_cast<unsigned>(grid)), b(block);
+    const int ppr = static_cast<int>(a.half / E);
+    switch (tok) {
+      case 1: launch_k(rope_rotate_half_tok<T, 1>, g, b, 0, st, a, ppr); break;
+      case 2: launch_k(rope_rotate_half_tok<T, 2>, g, b, 0, st, a, ppr); break;
+      case 4: launch_k(rope_rotate_half_tok<T, 4>, g, b, 0, st, a, ppr); break;
+      case 8: launch_k(rope_rotate_half_tok<T, 8>, g, b, 0, st, a, ppr); break;
+      default: return fail(AXON_E_ARG, "axon_rope_rotate_half: rows_per_cta (tokens per CTA) must be 1, 2, 4 or 8");
+    }
   } else if (vec) {
     const int64_t items = a.seq * heads * (a.half / E);
     launch_k(rope_rotate_half_vec<T>, dim3(grid_for(items, threads)), dim3(threads), 0, st, a, items);
@@ -285,9 +295,9 @@ extern "C" int axon_rope_rotate_half(const void* q, const void* k, const float* 
   RotArgs a{q, k, cos_t, sin_t, q_out, k_out, seq, n_q, n_kv, head_dim / 2};
   cudaStream_t s = as_stream(stream);
   switch (dtype) {
-    case AXON_F32: return launch_rot<float>(a, t.variant, threads, s);
-    case AXON_BF16: return launch_rot<__nv_bfloat16>(a, t.variant, threads, s);
-    case AXON_F16: return launch_rot<__half>(a, t.variant, threads, s);
+    case AXON_F32: return launch_rot<float>(a, t.variant, threads, t.rows_per_cta, s);
+    case AXON_BF16: return launch_rot<__nv_bfloat16>(a, t.variant, threads, t.rows_per_cta, s);
+    case AXON_F16: return launch_rot<__half>(a, t.variant, threads, t.rows_per_cta, s);
     default: return fail(AXON_E_UNSUPPORTED, "axon_rope_rotate_half: unsupported dtype %d", dtype);
   }
 }

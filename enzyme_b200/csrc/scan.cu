@@ -211,8 +211,8 @@ __global__ void __launch_bounds__(1024) cumsum_lookback(const Tin* __restrict__ 
 
 void tile_shape(const axon_tune_t& t, int& threads, int& items) {
   switch (t.split) {
-    case 2048: threads = 256; items = 8; break;
-    case 4096: threads = 512; items = 8; break;
+    case 2048: threads = 128; items = 16; break;
+    case 4096: threads = 256; items = 16; break;
     case 16384: threads = 1024; items = 16; break;
     default: threads = 512; items = 16; break;  // 8192
   }

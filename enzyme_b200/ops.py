@@ -190,6 +190,18 @@ def gemm(a, b, *, b2=None, row_scale=None, epilogue=N.AXON_EPI_NONE, out=None, o
     return c
 
 
+def cast(src, dtype, *, out=None):
+    """Elementwise dtype conversion on the device (contiguous tensors)."""
+    _require_cuda(src, out)
+    if not src.is_contiguous():
+        raise N.AxonError(N.AXON_E_SHAPE, "cast: source must be contiguous")
+    dst = out if out is not None else torch.empty(src.shape, dtype=dtype, device=src.device)
+    if dst.numel() != src.numel() or not dst.is_contiguous():
+        raise N.AxonError(N.AXON_E_SHAPE, "cast: destination must be contiguous with as many elements")
+    check(N.lib().axon_cast(_ptr(src), _ptr(dst), src.numel(), dtype_code(src), dtype_code(dst), _stream(src)))
+    return dst
+
+
 def gemm_status(device=None) -> None:
     check(N.lib().axon_gemm_status(torch.cuda.current_stream(device).cuda_stream))
 
@@ -215,16 +227,16 @@ def rmsnorm_matmul(x, w, *, out=None, out_dtype=None, workspace=None, tune=None)
     return y
 
 
-def silu_mlp_workspace_bytes(m: int, n: int, dtype_code_: int, tune=None) -> int:
-    nbytes = int(N.lib().axon_silu_mlp_workspace_bytes(m, n, dtype_code_, _tune(tune)))
+def silu_mlp_workspace_bytes(m: int, n: int, p: int, dtype_code_: int, tune=None) -> int:
+    nbytes = int(N.lib().axon_silu_mlp_workspace_bytes(m, n, p, dtype_code_, _tune(tune)))
     if nbytes < 0:
         check(nbytes)
     return nbytes
 
 
 def silu_mlp(x, w1, w2, w3, *, out=None, out_dtype=None, workspace=None, tune=None):
-    """(silu(x @ w1) * (x @ w2)) @ w3. The activation is stored in x's dtype as
-    tune['precision'] terms (default 1)."""
+    """(silu(x @ w1) * (x @ w2)) @ w3. tune['precision'] picks how the
+    activation is stored: 1 (default) x's dtype, 2/3 split terms, 4 f16."""
     _require_cuda(x, w1, w2, w3)
     for t in (x, w1, w2, w3):
         if not t.is_contiguous():
@@ -233,7 +245,7 @@ def silu_mlp(x, w1, w2, w3, *, out=None, out_dtype=None, workspace=None, tune=No
     n = w1.shape[1]
     p = w3.shape[1]
     y = out if out is not None else torch.empty((m, p), dtype=out_dtype or x.dtype, device=x.device)
-    need = silu_mlp_workspace_bytes(m, n, dtype_code(x), tune)
+    need = silu_mlp_workspace_bytes(m, n, p, dtype_code(x), tune)
     ws = workspace if workspace is not None else torch.empty(need, dtype=torch.uint8, device=x.device)
     check(N.lib().axon_silu_mlp(_ptr(x), _ptr(w1), _ptr(w2), _ptr(w3), _ptr(y), _ptr(ws), ws.numel() * ws.element_size(),
                                 m, n, k, p, dtype_code(x), dtype_code(y), _tune(tune), _stream(x)))

@@ -69,8 +69,8 @@ typedef struct axon_tune {
   int32_t stages;       /* GEMM smem pipeline depth (2..8)                    */
   int32_t split;        /* cumsum: elements per tile (variant 0) or CTAs per
                            row cluster (variant 1)                            */
-  int32_t precision;    /* silu_mlp: terms of the stored activation (1 = one
-                           bf16 value, 2 = hi + lo, 3 = three terms)          */
+  int32_t precision;    /* silu_mlp activation storage: 1 = one bf16 value,
+                           2 / 3 = split terms, 4 = f16 (see axon_silu_mlp)   */
 } axon_tune_t;
 
 /* ---- library metadata ----------------------------------------------------- */
@@ -219,6 +219,13 @@ AXON_API int axon_gemm(const void* a, const void* b, const void* b2, void* c,
  * on a bounded pipeline wait (AXON_E_TIMEOUT; the flag is then cleared). */
 AXON_API int axon_gemm_status(void* stream);
 
+/* dst[i] = src[i] converted from src_dtype to dst_dtype (AXON_F32 / AXON_BF16 /
+ * AXON_F16; round to nearest even), n elements, contiguous. No counterpart in
+ * Axon's specs: the tensor-parallel SwiGLU step uses it to make the f16 copy
+ * of its W_down shard once per step before its per-slab GEMMs. */
+AXON_API int axon_cast(const void* src, void* dst, int64_t n, int32_t src_dtype, int32_t dst_dtype,
+                       void* stream);
+
 /* Per-row scale r[i] = rsqrt(scale * sum_j x[i,j]^2 + eps) in fp32: the norm
  * prologue of rmsnorm_matmul (Axon kernels/rmsnorm_matmul/refs.py:16-22) and
  * of the SwiGLU config's optional rmsnorm. */
@@ -232,22 +239,28 @@ AXON_API int axon_rmsnorm_matmul(const void* x, const void* w, void* y, void* wo
                         int64_t m, int64_t n, int64_t k, int32_t ab_dtype,
                         int32_t c_dtype, const axon_tune_t* tune, void* stream);
 
-/* Bytes of scratch axon_silu_mlp needs: the [m, n] activation in ab_dtype,
- * times tune->precision terms. */
-AXON_API int64_t axon_silu_mlp_workspace_bytes(int64_t m, int64_t n, int32_t ab_dtype,
+/* Bytes of scratch axon_silu_mlp needs: the [m, n] activation in ab_dtype
+ * times tune->precision terms, or for precision 4 an f16 activation plus an
+ * f16 copy of w3 ([n, p]). */
+AXON_API int64_t axon_silu_mlp_workspace_bytes(int64_t m, int64_t n, int64_t p, int32_t ab_dtype,
                                                const axon_tune_t* tune);
 
 /* (silu(x @ w1) * (x @ w2)) @ w3 (Axon kernels/silu_mlp/refs.py:16-21):
  * x [m, k], w1/w2 [k, n], w3 [n, p], y [m, p] of c_dtype. Two tcgen05 GEMMs:
  * gate and up in one pass with the SiLU-gate epilogue writing the activation
- * (ab_dtype) into `workspace`, then the down projection. With
- * tune->precision = T > 1 the activation a is stored as T terms (a ~ t0 + t1
- * + ..., each rounded to ab_dtype; 8 more mantissa bits per term) and the
- * down projection contracts over K = T*n, reading w3 once per term; this is
- * what matches an fp32 reference when the activation is large (n % 64 == 0
- * required). In the column/row
- * tensor-parallel form each rank passes its shard (n = inter / G) and sums the
- * fp32 partial outputs across ranks. */
+ * into `workspace`, then the down projection. tune->precision selects how the
+ * activation a is stored:
+ *   1 (default)  one ab_dtype value;
+ *   2, 3         T split terms (a ~ t0 + t1 + ..., each rounded to ab_dtype,
+ *                8 more mantissa bits per term); the down projection
+ *                contracts over K = T*n reading w3 once per term (n % 64 == 0);
+ *   4            f16 (ab_dtype bf16 only): the call converts w3 to an f16 copy
+ *                in the workspace and runs the down projection f16 x f16
+ *                (both MMA operands must share a type); 3 more mantissa bits
+ *                than bf16 for ~3% extra traffic, finite only while |a| < 65504.
+ * An fp32 reference at 1e-2 needs precision >= 2 (or 4) at the SwiGLU config
+ * and 3 for N(0, 1) weights. In the column/row tensor-parallel form each rank
+ * passes its shard (n = inter / G) and sums the fp32 partial outputs. */
 AXON_API int axon_silu_mlp(const void* x, const void* w1, const void* w2, const void* w3,
                   void* y, void* workspace, int64_t workspace_bytes, int64_t m,
                   int64_t n, int64_t k, int64_t p, int32_t ab_dtype, int32_t c_dtype,

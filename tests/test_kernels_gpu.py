@@ -234,16 +234,33 @@ def test_cumsum_repeat_calls_reuse_workspace(cuda_device):
 # ---- Adam ------------------------------------------------------------------------------------
 
 def _adam_rel_err(got, want, inputs, beta1, beta2):
-    """Error of each Adam output relative to the magnitude of the terms that
-    form it (|p| + |update| for the parameter, the weighted moment terms for
-    exp_avg / exp_avg_sq): the rel 1e-5 bar of an fp32 update against float64.
-    Plain |got - want| / |want| is ill-posed where p' = p - update cancels."""
+    """Worst ratio, per Adam output, of its error to the allowed error (pass
+    when <= 1). The error is taken relative to the magnitude of the
+    terms that form it (|p| + |update|; b1|m| + (1-b1)(|g| + |wd p|);
+    b2|v| + (1-b2)(|g| + |wd p|)^2), after allowing each element the error
+    the reference's own fp32 path (the spec torch_ref on the CPU) makes there.
+
+    The bar is rel 1e-5 against float64. Plain |got - want| / |want| is
+    ill-posed where p' = p - update or g + wd*p cancels: there no fp32
+    evaluation, the reference's included, is within 1e-5, so an element passes
+    if it is within 1e-5 of its scale or within twice the reference's error."""
+    from oracle import cpu_torch
+
     p, g, m, v, ss, ib, wd = (np.asarray(a, dtype=np.float64) for a in inputs)
-    gp = g + wd * p
+    terms = np.abs(g) + np.abs(wd * p)
     scales = (np.abs(p) + np.abs(p - want[0]),
-              beta1 * np.abs(m) + (1 - beta1) * np.abs(gp),
-              beta2 * np.abs(v) + (1 - beta2) * gp * gp)
-    return [float((np.abs(_np(o) - w) / np.maximum(s, 1e-30)).max()) for o, w, s in zip(got, want, scales)]
+              beta1 * np.abs(m) + (1 - beta1) * terms,
+              beta2 * np.abs(v) + (1 - beta2) * terms * terms)
+    f32 = [torch.from_numpy(np.ascontiguousarray(np.broadcast_to(a, p.shape) if a.ndim else a, dtype=np.float32))
+           for a in (p, g, m, v, ss, ib, wd)]
+    ref32 = cpu_torch.adam(*f32, beta1=beta1, beta2=beta2)
+    out = []
+    for o, r, w, s in zip(got, ref32, want, scales):
+        s = np.maximum(s, 1e-30)
+        ours = np.abs(_np(o) - w) / s
+        theirs = np.abs(r.numpy().astype(np.float64) - w) / s
+        out.append(float((ours / np.maximum(1e-5, 2 * theirs)).max()))
+    return out
 
 
 def test_adam_config_medium_and_inplace(cuda_device):
@@ -253,7 +270,7 @@ def test_adam_config_medium_and_inplace(cuda_device):
     want = f64.ORACLES["fused_adam_cfg"](*ins)
     out = ops.adam(p, gr, m, v, step_size=ss, inv_bc2_sqrt=ib, wd=wd, beta1=0.9, beta2=0.95)
     errs = _adam_rel_err(out, want, ins, 0.9, 0.95)
-    assert max(errs) <= 1e-5, errs
+    assert max(errs) <= 1.0, errs
     # in place with scalar hyper-parameters == out of place with per-row ones
     step, inv, wdv = (float(np.asarray(a)[0, 0]) for a in ins[4:])
     ops.adam(p, gr, m, v, step_size=step, inv_bc2_sqrt=inv, wd=wdv, beta1=0.9, beta2=0.95, out=(p, m, v))
@@ -278,8 +295,8 @@ def test_adam_full_size_sampled(cuda_device):
         z = np.zeros_like(p0)
         want = f64.adam(p0, g0, z, z, ss, ib, 0.1, beta1=0.9, beta2=0.95)
         got = (p[s:s + 1_000_000], m[s:s + 1_000_000], v[s:s + 1_000_000])
-        errs = _adam_rel_err(got, want, (p0, g0, z, z, ss, ib, 0.1), 0.9, 0.95)
-        assert max(errs) <= 1e-5, (s, errs)
+        errs = _adam_rel_err(got, want, (p0, g0, z, z, np.float64(ss), np.float64(ib), np.float64(0.1)), 0.9, 0.95)
+        assert max(errs) <= 1.0, (s, errs)
     del p, g, m, v
     torch.cuda.empty_cache()
 
@@ -360,7 +377,7 @@ def test_silu_precision_ladder(cuda_device):
     assert errs[0] > 100 * errs[1] > 0 and errs[2] <= errs[1] * 1.5, errs
 
 
-@pytest.mark.parametrize("terms", [2])
+@pytest.mark.parametrize("terms", [2, 4])
 def test_silu_mlp_config_sampled_rows(terms, cuda_device):
     """The BASELINE SwiGLU config at full size, checked on sampled rows. A
     one-term bf16 activation is not enough here: over the whole output about
