@@ -320,8 +320,17 @@ class SwiGLU(Workload):
         self.scaling = "strong" if world > 1 else "weak"
         self.use_graph = world == 1
         self.launches_per_step = 3 if self.PRECISION == 4 else 2
+        if world > 1:
+            # column/row tensor parallel: W_gate/W_up column shard, W_down row
+            # shard, fp32 partials all-reduced per m-slab while the next slab
+            # computes (enzyme_b200.tp)
+            from enzyme_b200.tp import TPSwiGLU
+
+            self.tp = TPSwiGLU(self.w1, self.w2, self.w3, slabs=self.SLABS)
+            self.launches_per_step = 1 + 2 * len(self.tp.slab_bounds(m))
 
     PRECISION = 4
+    SLABS = 4
 
     def per_step_work(self):
         m, n, k, p = 4096, self.shard, 4096, 4096
@@ -331,9 +340,10 @@ class SwiGLU(Workload):
         return roofline.work(self.spec, self.dims)[1]
 
     def launch(self, i):
-        ops.silu_mlp(self.x, self.w1, self.w2, self.w3, out=self.y, workspace=self.act, tune=self.tune)
         if self.world > 1:
-            dist.all_reduce(self.y)
+            self.tp.forward(self.x, out=self.y)
+        else:
+            ops.silu_mlp(self.x, self.w1, self.w2, self.w3, out=self.y, workspace=self.act, tune=self.tune)
 
     def e2e_setup(self):
         self.h = self.x.cpu().pin_memory()
