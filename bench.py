@@ -192,16 +192,26 @@ class Cumsum(Workload):
         for _ in range(self.nsets):
             logits = 2.0 * torch.randn(256, 128256, device=dev, generator=self.gen)
             x = torch.sort(torch.softmax(logits, dim=1), dim=1, descending=True).values.contiguous()
-            ws = torch.empty(ops.cumsum_workspace_bytes(256, 128256), dtype=torch.uint8, device=dev)
+            nbytes = ops.cumsum_workspace_bytes(256, 128256, self.TUNE)
+            ws = torch.empty(nbytes, dtype=torch.uint8, device=dev) if nbytes else None
             self.sets.append((x, torch.empty_like(x), ws))
+
+    # the cluster scan (variant 1) is the faster of the two scan variants here
+    # (76 vs 95 us on B200); variant 0, the decoupled look-back, stays the
+    # default of the C ABI and is timed by `--workload cumsum` sweeps
+    TUNE = {"variant": 1}
 
     def launch(self, i):
         x, y, ws = self.sets[i % self.nsets]
-        ops.cumsum(x, out=y, workspace=ws)
+        ops.cumsum(x, out=y, workspace=ws, tune=self.TUNE)
 
     def check(self):
+        from enzyme_b200 import _native as N
+
         for _, _, ws in self.sets:
-            ops.cumsum_status(ws)
+            if ws is not None:
+                ops.cumsum_status(ws)
+        N.check(N.lib().axon_cumsum_status(None, torch.cuda.current_stream().cuda_stream))
 
     def e2e_setup(self):
         x, y, _ = self.sets[0]
@@ -213,7 +223,7 @@ class Cumsum(Workload):
     def e2e_step(self, i):
         x, y, ws = self.sets[i % self.nsets]
         x.copy_(self.h, non_blocking=True)
-        ops.cumsum(x, out=y, workspace=ws)
+        ops.cumsum(x, out=y, workspace=ws, tune=self.TUNE)
         self.ho.copy_(y, non_blocking=True)
 
     def cpu_step(self):

@@ -61,7 +61,7 @@ def variants(spec_name: str) -> list[Variant]:
     if spec_name == "rope_gqa":
         return [Variant(0, "token_blocked"), Variant(1, "flat_vec16")]
     if spec_name in SCAN_SPECS:
-        return [Variant(0, "decoupled_lookback")]
+        return [Variant(0, "decoupled_lookback"), Variant(1, "cluster_dsmem")]
     if spec_name in ADAM_SPECS:
         return [Variant(0, "grid_stride_vec")]
     if spec_name in GEMM_SPECS:
@@ -93,10 +93,15 @@ def constraints(spec_name: str, hw_variant: int, dims: dict, itemsize: int,
                                   require_divisible=False, allowed=allowed))
         out.append(_one(args[0]))
     elif spec_name == "rope_gqa" and hw_variant == 0:
-        out.append(_one(args[1]))  # the token-blocked kernel sizes its CTA from the head count
+        # the token-blocked kernel sizes its CTA from the head count; N = tokens per CTA
+        out.append(TileConstraint(args[1], extent=8, tile_size=1, require_divisible=True, allowed=(1, 2, 4, 8)))
         out.append(_one(args[0]))
     elif spec_name in ROPE_SPECS or spec_name in ADAM_SPECS:
         out.append(TileConstraint(args[1], extent=256, tile_size=32, require_divisible=True, allowed=(1, 2, 4, 8)))
+        out.append(_one(args[0]))
+    elif spec_name in SCAN_SPECS and hw_variant == 1:
+        # N = CTAs per row cluster
+        out.append(TileConstraint(args[1], extent=8, tile_size=1, require_divisible=True, allowed=(1, 2, 4, 8)))
         out.append(_one(args[0]))
     elif spec_name in SCAN_SPECS:
         out.append(TileConstraint(args[1], extent=16384, tile_size=1024, require_divisible=True,
@@ -120,11 +125,11 @@ def tune_for(spec_name: str, hw_variant: int, tiles: dict[str, int]) -> dict | l
     if spec_name in ROW_SPECS:
         return {"variant": hw_variant, "threads": 32 * t["N"]}
     if spec_name == "rope_gqa" and hw_variant == 0:
-        return {"variant": 0}
+        return {"variant": 0, "rows_per_cta": t["N"]}
     if spec_name in ROPE_SPECS or spec_name in ADAM_SPECS:
         return {"variant": hw_variant, "threads": 32 * t["N"]}
     if spec_name in SCAN_SPECS:
-        return {"variant": hw_variant, "split": 1024 * t["N"]}
+        return {"variant": hw_variant, "split": t["N"] if hw_variant == 1 else 1024 * t["N"]}
     if spec_name in GEMM_SPECS:
         return {"variant": hw_variant, "block_n": 64 * t["N"], "stages": t["K"]}
     if spec_name in MLP_SPECS:

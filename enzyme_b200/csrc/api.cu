@@ -73,7 +73,7 @@ static const char* kVariants[][2] = {
      "{\"id\":1,\"name\":\"flat_vec16\",\"knobs\":{\"threads\":[0,128,256]}}]}"},
     {"cumsum",
      "{\"op\":\"cumsum\",\"variants\":[{\"id\":0,\"name\":\"decoupled_lookback\",\"knobs\":{\"split\":[0,2048,4096,8192,16384]}},"
-     "{\"id\":1,\"name\":\"cluster_dsmem\",\"knobs\":{\"split\":[0,1,2,4,8,16]}}]}"},
+     "{\"id\":1,\"name\":\"cluster_dsmem\",\"knobs\":{\"split\":[0,1,2,4,8]}}]}"},
     {"adam",
      "{\"op\":\"adam\",\"variants\":[{\"id\":0,\"name\":\"grid_stride_vec\",\"knobs\":{\"threads\":[0,128,256,512]}}]}"},
     {"gemm",

@@ -14,9 +14,27 @@
 // a predecessor is bounded: a wait that gives up records AXON_E_TIMEOUT in the
 // workspace status word and the CTA finishes (with a wrong prefix) rather than
 // spinning forever.
+//
+// Variant 1 -- one thread-block cluster per row (2..8 CTAs, or one CTA for
+// short rows). Each CTA pulls its contiguous chunk of the row (at most 64 KB
+// at the automatic cluster size) into shared memory with 1-D bulk copies
+// (cp.async.bulk, no multicast), sums it warp by warp, and the chunk sums are
+// exchanged through distributed shared memory between two hardware cluster
+// barriers; each CTA then scans its chunk from shared memory and writes it
+// out. No global flags, no atomics and no scratch memory; the barrier cannot
+// hang because every CTA of a cluster is co-scheduled and runs the same path.
+// The only wait on memory, the bulk copy's mbarrier, is bounded and records
+// AXON_E_TIMEOUT in a device status word (axon_cumsum_status with a NULL
+// workspace reads it).
+#include <cooperative_groups.h>
+
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace axon {
+
+__device__ int g_scan_error;
+
 namespace {
 
 struct alignas(32) TileDesc {
@@ -209,6 +227,213 @@ __global__ void __launch_bounds__(1024) cumsum_lookback(const Tin* __restrict__ 
   store_striped<Tin, Tout, ITEMS>(yr, wbase, lane, n, vec, v);
 }
 
+// ---- variant 1: cluster scan ------------------------------------------------------
+
+constexpr int kClusterThreads = 512;
+constexpr int64_t kChunkTargetBytes = 64 * 1024;
+constexpr int64_t kChunkMaxBytes = 200 * 1024;
+constexpr uint64_t kBulkWaitNs = 2000000000ull;
+
+// Store E consecutive outputs (the first `valid` of them) at dst.
+template <typename Tout, int E>
+__device__ __forceinline__ void store_packet(Tout* dst, const float* v, int64_t valid, bool vec) {
+  if (vec && valid >= E) {
+    if constexpr (sizeof(Tout) * E >= 16) {
+#pragma unroll
+      for (int h = 0; h < E; h += Vec<Tout>::E) {
+        Vec<Tout> p;
+#pragma unroll
+        for (int e = 0; e < Vec<Tout>::E; ++e) p.e[e] = from_f<Tout>(v[h + e]);
+        st_vec_stream(dst + h, p);
+      }
+      return;
+    } else if constexpr (sizeof(Tout) * E == 8) {
+      union {
+        uint2 u;
+        Tout e[E];
+      } p;
+#pragma unroll
+      for (int e = 0; e < E; ++e) p.e[e] = from_f<Tout>(v[e]);
+      *reinterpret_cast<uint2*>(dst) = p.u;
+      return;
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < E; ++e)
+    if (e < valid) dst[e] = from_f<Tout>(v[e]);
+}
+
+template <typename Tin, typename Tout>
+__global__ void __launch_bounds__(kClusterThreads) cumsum_cluster(const Tin* __restrict__ x, Tout* __restrict__ y,
+                                                                  int64_t n, int64_t ld_x, int64_t ld_y,
+                                                                  int64_t chunk, int csize, bool vec) {
+  namespace cg = cooperative_groups;
+  constexpr int E = Vec<Tin>::E;
+  extern __shared__ __align__(128) unsigned char dyn_smem[];
+  Tin* buf = reinterpret_cast<Tin*>(dyn_smem);
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ float s_warp[32];
+  __shared__ double s_total;
+  __shared__ double s_prefix;
+
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = static_cast<int>(cluster.block_rank());
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+  const int64_t row = blockIdx.x / csize;
+  const int64_t c0 = static_cast<int64_t>(rank) * chunk;
+  const int64_t len = c0 < n ? (chunk < n - c0 ? chunk : n - c0) : 0;
+  const Tin* src = x + row * ld_x + c0;
+  Tout* dst = y + row * ld_y + c0;
+
+  pdl_wait();
+  pdl_trigger();
+  // 1. chunk -> shared memory: bulk copies for the 16-byte-aligned body,
+  // plain loads for a ragged tail
+  const int64_t bulk = vec ? (len * static_cast<int64_t>(sizeof(Tin))) / 16 * 16 : 0;
+  if (tid == 0) {
+    sm100::mbar_init(&bar, 1);
+    sm100::mbar_init_fence();
+  }
+  __syncthreads();
+  if (tid == 0 && bulk > 0) {
+    sm100::mbar_expect_tx(&bar, static_cast<uint32_t>(bulk));
+    constexpr int64_t kPiece = 32768;
+    for (int64_t off = 0; off < bulk; off += kPiece) {
+      const int64_t b = bulk - off < kPiece ? bulk - off : kPiece;
+      sm100::bulk_g2s(dyn_smem + off, reinterpret_cast<const unsigned char*>(src) + off, static_cast<uint32_t>(b),
+                      &bar);
+    }
+  }
+  for (int64_t i = bulk / static_cast<int64_t>(sizeof(Tin)) + tid; i < len; i += blockDim.x) buf[i] = src[i];
+  if (bulk > 0 && !sm100::mbar_wait_bounded(&bar, 0, kBulkWaitNs)) {
+    if (tid == 0) atomicExch(&g_scan_error, AXON_E_TIMEOUT);
+    sm100::mbar_wait_bounded(&bar, 0, kBulkWaitNs);  // second bound for copies still in flight
+  }
+  __syncthreads();
+
+  // 2. warp sums over warp-striped packets of E elements
+  const int64_t packets = (len + E - 1) / E;
+  const int64_t ppw = ((packets + nwarps - 1) / nwarps + 31) / 32 * 32;  // packets per warp, whole segments
+  const int64_t wp0 = static_cast<int64_t>(warp) * ppw;
+  auto load = [&](int64_t pk, float* v) {
+    const int64_t e0 = pk * E;
+#pragma unroll
+    for (int e = 0; e < E; ++e) v[e] = (pk < packets && e0 + e < len) ? to_f(buf[e0 + e]) : 0.f;
+  };
+  float wsum = 0.f;
+  for (int64_t j = 0; j < ppw; j += 32) {
+    float v[E];
+    load(wp0 + j + lane, v);
+#pragma unroll
+    for (int e = 0; e < E; ++e) wsum += v[e];
+  }
+  wsum = warp_sum(wsum);
+  if (lane == 0) s_warp[warp] = wsum;
+  __syncthreads();
+  if (warp == 0) {
+    float w = lane < nwarps ? s_warp[lane] : 0.f;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float up = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += up;
+    }
+    if (lane < nwarps) s_warp[lane] = w;
+  }
+  __syncthreads();
+  const float warp_excl = warp > 0 ? s_warp[warp - 1] : 0.f;
+
+  // 3. chunk sums across the cluster through distributed shared memory
+  if (tid == 0) s_total = static_cast<double>(s_warp[nwarps - 1]);
+  cluster.sync();
+  if (tid == 0) {
+    double p = 0.0;
+    for (int r = 0; r < rank; ++r) p += *cluster.map_shared_rank(&s_total, r);
+    s_prefix = p;
+  }
+  cluster.sync();  // also keeps every CTA's s_total alive until all reads are done
+  const double prefix = s_prefix;
+
+  // 4. scan the chunk from shared memory and write it out
+  float carry = warp_excl;
+  for (int64_t j = 0; j < ppw; j += 32) {
+    const int64_t pk = wp0 + j + lane;
+    float v[E];
+    load(pk, v);
+#pragma unroll
+    for (int e = 1; e < E; ++e) v[e] += v[e - 1];
+    const float own = v[E - 1];
+    float incl = own;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float up = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += up;
+    }
+    const float base = carry + (incl - own);
+    float out[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) out[e] = static_cast<float>(prefix + static_cast<double>(base + v[e]));
+    if (pk < packets) store_packet<Tout, E>(dst + pk * E, out, len - pk * E, vec);
+    carry += __shfl_sync(0xffffffffu, incl, 31);
+  }
+}
+
+// Cluster size and chunk for a row of n elements of `size` bytes: the
+// smallest power of two (at most 8) whose chunks fit the 64 KB target, chunks
+// a multiple of 8 elements so every CTA's slice starts 16-byte aligned.
+bool cluster_shape(int64_t n, int size, int want, int& csize, int64_t& chunk) {
+  csize = want;
+  if (csize == 0) {
+    csize = 1;
+    while (csize < 8 && (n + csize - 1) / csize * size > kChunkTargetBytes) csize *= 2;
+  }
+  chunk = ((n + csize - 1) / csize + 7) / 8 * 8;
+  return chunk * size <= kChunkMaxBytes;
+}
+
+template <typename Tin, typename Tout>
+int launch_cluster(const void* x, void* y, int64_t m, int64_t n, int64_t ld_x, int64_t ld_y, const axon_tune_t& t,
+                   cudaStream_t s) {
+  int csize;
+  int64_t chunk;
+  if (!cluster_shape(n, sizeof(Tin), t.split, csize, chunk))
+    return fail(AXON_E_SHAPE, "axon_cumsum: rows of %lld elements are too long for the cluster variant (use 0)",
+                (long long)n);
+  if (m * csize > 0x7fffffffLL) return fail(AXON_E_SHAPE, "axon_cumsum: too many rows (%lld)", (long long)m);
+  const bool vec = aligned16(x) && aligned16(y) && (ld_x * sizeof(Tin)) % 16 == 0 && (ld_y * sizeof(Tout)) % 16 == 0;
+  const size_t smem = static_cast<size_t>(chunk) * sizeof(Tin);
+  auto kern = cumsum_cluster<Tin, Tout>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return fail(AXON_E_LAUNCH, "axon_cumsum: smem attribute: %s", cudaGetErrorString(e));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(m * csize));
+  cfg.blockDim = dim3(kClusterThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = csize;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  e = cudaLaunchKernelEx(&cfg, kern, static_cast<const Tin*>(x), static_cast<Tout*>(y), n, ld_x, ld_y, chunk, csize,
+                         vec);
+  if (e != cudaSuccess) return fail(AXON_E_LAUNCH, "axon_cumsum: cluster launch failed: %s", cudaGetErrorString(e));
+  return launch_status("axon_cumsum");
+}
+
+template <typename Tin>
+int dispatch_cluster(int32_t out_dtype, const void* x, void* y, int64_t m, int64_t n, int64_t ld_x, int64_t ld_y,
+                     const axon_tune_t& t, cudaStream_t s) {
+  switch (out_dtype) {
+    case AXON_F32: return launch_cluster<Tin, float>(x, y, m, n, ld_x, ld_y, t, s);
+    case AXON_BF16: return launch_cluster<Tin, __nv_bfloat16>(x, y, m, n, ld_x, ld_y, t, s);
+    default: return fail(AXON_E_UNSUPPORTED, "axon_cumsum: unsupported output dtype %d", out_dtype);
+  }
+}
+
 void tile_shape(const axon_tune_t& t, int& threads, int& items) {
   switch (t.split) {
     case 2048: threads = 128; items = 16; break;
@@ -278,9 +503,20 @@ extern "C" int axon_cumsum(const void* x, void* y, int64_t m, int64_t n, int64_t
   if (m < 0 || n < 0) return fail(AXON_E_SHAPE, "axon_cumsum: negative size");
   if (m > 0 && n > 0 && (!x || !y)) return fail(AXON_E_ARG, "axon_cumsum: NULL tensor pointer");
   if (ld_x < n || ld_y < n) return fail(AXON_E_SHAPE, "axon_cumsum: leading dimension smaller than n");
+  if (t.variant == 1) {
+    if (t.split != 0 && t.split != 1 && t.split != 2 && t.split != 4 && t.split != 8)
+      return fail(AXON_E_ARG, "axon_cumsum: variant 1 split (CTAs per row cluster) must be 1, 2, 4 or 8");
+    if (m == 0 || n == 0) return AXON_OK;
+    cudaStream_t s = as_stream(stream);
+    switch (in_dtype) {
+      case AXON_F32: return dispatch_cluster<float>(out_dtype, x, y, m, n, ld_x, ld_y, t, s);
+      case AXON_BF16: return dispatch_cluster<__nv_bfloat16>(out_dtype, x, y, m, n, ld_x, ld_y, t, s);
+      default: return fail(AXON_E_UNSUPPORTED, "axon_cumsum: unsupported input dtype %d", in_dtype);
+    }
+  }
   if (t.split != 0 && t.split != 2048 && t.split != 4096 && t.split != 8192 && t.split != 16384)
     return fail(AXON_E_ARG, "axon_cumsum: split must be one of 2048, 4096, 8192, 16384 (got %d)", t.split);
-  if (t.variant != 0) return fail(AXON_E_UNSUPPORTED, "axon_cumsum: variant %d not built", t.variant);
+  if (t.variant != 0) return fail(AXON_E_UNSUPPORTED, "axon_cumsum: unknown variant %d", t.variant);
   if (m == 0 || n == 0) return AXON_OK;
   const int64_t need = lookback_ws_bytes(m, n, t);
   if (workspace == nullptr || workspace_bytes < need)
@@ -295,12 +531,21 @@ extern "C" int axon_cumsum(const void* x, void* y, int64_t m, int64_t n, int64_t
 }
 
 extern "C" int axon_cumsum_status(const void* workspace, void* stream) {
-  if (!workspace) return fail(AXON_E_ARG, "axon_cumsum_status: NULL workspace");
   int status = 0;
-  cudaError_t e = cudaMemcpyAsync(&status, workspace, sizeof(int), cudaMemcpyDeviceToHost, as_stream(stream));
+  cudaError_t e;
+  if (workspace) {
+    e = cudaMemcpyAsync(&status, workspace, sizeof(int), cudaMemcpyDeviceToHost, as_stream(stream));
+  } else {  // the cluster variant's device status word; reading clears it
+    e = cudaMemcpyFromSymbolAsync(&status, g_scan_error, sizeof(int), 0, cudaMemcpyDeviceToHost, as_stream(stream));
+    if (e == cudaSuccess) e = cudaStreamSynchronize(as_stream(stream));
+    if (e == cudaSuccess && status != 0) {
+      const int zero = 0;
+      e = cudaMemcpyToSymbolAsync(g_scan_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, as_stream(stream));
+    }
+  }
   if (e == cudaSuccess) e = cudaStreamSynchronize(as_stream(stream));
   if (e != cudaSuccess) return fail(AXON_E_CUDA, "axon_cumsum_status: %s", cudaGetErrorString(e));
-  if (status != 0) return fail(status, "axon_cumsum: a look-back wait gave up (status %d)", status);
+  if (status != 0) return fail(status, "axon_cumsum: a bounded wait gave up (status %d)", status);
   return AXON_OK;
 }
 

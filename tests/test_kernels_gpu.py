@@ -188,14 +188,18 @@ def test_rope_odd_head_dim_scalar_path(cuda_device):
 
 # ---- cumsum ------------------------------------------------------------------------------
 
-@pytest.mark.parametrize("split", [0, 2048, 4096, 16384])
-def test_cumsum_config_full_size(split, cuda_device):
+@pytest.mark.parametrize("variant,split", [(0, 0), (0, 2048), (0, 4096), (0, 16384), (1, 0), (1, 4), (1, 8)])
+def test_cumsum_config_full_size(variant, split, cuda_device):
     spec = load_spec("cumsum_nucleus_sorted")
     (x,) = spec.make_inputs(m=256, n=128256, rng=np.random.default_rng(SEED))
-    tune = {"split": split} if split else None
-    ws = torch.empty(ops.cumsum_workspace_bytes(256, 128256, tune), dtype=torch.uint8, device=cuda_device)
+    tune = {"variant": variant, "split": split}
+    nbytes = ops.cumsum_workspace_bytes(256, 128256, tune)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=cuda_device) if nbytes else None
     y = ops.cumsum(_t(x, cuda_device), workspace=ws, tune=tune)
-    ops.cumsum_status(ws)
+    if ws is not None:
+        ops.cumsum_status(ws)
+    else:
+        N.check(N.lib().axon_cumsum_status(None, torch.cuda.current_stream().cuda_stream))
     want = f64.cumsum(x)
     got = _np(y)
     rel = np.abs(got - want) / np.abs(want)
@@ -205,21 +209,26 @@ def test_cumsum_config_full_size(split, cuda_device):
     np.testing.assert_allclose(got[:, -1], x.astype(np.float64).sum(1), rtol=1e-6)
 
 
-@pytest.mark.parametrize("shape", [(1, 1), (3, 7), (5, 8191), (2, 8193), (64, 100000), (1024, 1024)])
-def test_cumsum_shapes(shape, cuda_device):
+@pytest.mark.parametrize("variant", [0, 1])
+@pytest.mark.parametrize("shape", [(1, 1), (3, 7), (5, 8191), (2, 8193), (64, 100000), (1024, 1024), (3, 150001)])
+def test_cumsum_shapes(shape, variant, cuda_device):
     x = torch.randn(*shape, generator=torch.Generator().manual_seed(11))
-    y = ops.cumsum(x.to(cuda_device))
+    y = ops.cumsum(x.to(cuda_device), tune={"variant": variant})
     want = f64.cumsum(x.numpy())
     scale = np.sqrt(np.arange(1, shape[1] + 1))[None, :]
     err = np.abs(_np(y) - want) / scale
     assert err.max() < 1e-5
 
 
-def test_cumsum_bf16_in_fp32_out_and_strided(cuda_device):
+@pytest.mark.parametrize("variant", [0, 1])
+def test_cumsum_bf16_in_fp32_out_and_strided(variant, cuda_device):
     base = torch.randn(16, 3000, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16).to(cuda_device)
     x = base[:, :2992]
-    y = ops.cumsum(x, out_dtype=torch.float32)
+    y = ops.cumsum(x, out_dtype=torch.float32, tune={"variant": variant})
     np.testing.assert_allclose(_np(y), f64.cumsum(_np(x)), rtol=1e-5, atol=1e-4)
+    xb = base[:, 1:2990]  # rows off the 16-byte grid: plain loads, no bulk copy
+    yb = ops.cumsum(xb, out_dtype=torch.float32, tune={"variant": variant})
+    np.testing.assert_allclose(_np(yb), f64.cumsum(_np(xb)), rtol=1e-5, atol=1e-4)
 
 
 def test_cumsum_repeat_calls_reuse_workspace(cuda_device):
