@@ -1,0 +1,123 @@
+"""Named benchmark cases and the command each runs.
+
+Axon keeps its cases in eval/sizes.json and generates one make target per
+case (eval/gen_size_targets.py:25-86), each running
+`axon kernels/<kernel> --sizes ... [--dtype D] [--rtol R --atol A] [--lnc 2]
+--out out/<kernel>_<case>.csv`; a case with rtol/atol is a head-to-head case
+(winner + harness exported). This module holds the cases of the specs this
+backend implements -- the reference's own cases for them and one case per
+BASELINE config -- and builds the same command for the CUDA backend:
+
+    python -m enzyme_b200.cases list
+    python -m enzyme_b200.cases run rmsnorm_h4096 [extra CLI flags]
+
+`--lnc 2` cases map to `--gpus 2`.
+"""
+
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[1]
+
+# kernel -> case id -> {sizes (dim_vars order), dtype?, lnc?, rtol?, atol?}
+CASES: dict[str, dict[str, dict]] = {
+    "cumsum": {
+        "fast_small": {"sizes": [1024, 1024], "rtol": 1e-3, "atol": 1e-3},
+        "fast_small_bf16": {"sizes": [1024, 1024], "dtype": "bfloat16", "rtol": 1e-2, "atol": 1e-2},
+        "nucleus": {"sizes": [128, 32768], "rtol": 1e-3, "atol": 1e-3},
+        "fast_large": {"sizes": [4096, 4096], "rtol": 1e-3, "atol": 1e-3},
+        "llama3_vocab": {"sizes": [128, 128256], "rtol": 1e-3, "atol": 1e-3},
+        "qwen_vocab": {"sizes": [128, 151936], "rtol": 1e-3, "atol": 1e-3},
+    },
+    "rmsnorm": {
+        "h1024": {"sizes": [1024, 1024], "rtol": 1e-2, "atol": 1e-2},
+        "h4096": {"sizes": [1024, 4096], "rtol": 1e-2, "atol": 1e-2},
+        "h8192": {"sizes": [128, 8192], "rtol": 1e-2, "atol": 1e-2},
+        "h8192_l2": {"sizes": [128, 8192], "lnc": 2, "rtol": 1e-2, "atol": 1e-2},
+    },
+    "layernorm": {
+        "llama70b": {"sizes": [128, 8192], "rtol": 2e-2, "atol": 2e-2},
+        "qwen32b": {"sizes": [128, 5120], "rtol": 2e-2, "atol": 2e-2},
+        "roofline": {"sizes": [2048, 8192]},
+    },
+    "rope": {
+        "llama3_8b": {"sizes": [128, 4096], "rtol": 7.8125e-3, "atol": 2e-2},
+        "gqa_long": {"sizes": [128, 32768], "rtol": 7.8125e-3, "atol": 2e-2},
+    },
+    "fused_adam": {
+        "opt_1m": {"sizes": [128, 8192], "rtol": 1e-2, "atol": 1e-2},
+        "opt_1m_fp32": {"sizes": [128, 8192], "dtype": "float32", "rtol": 1e-4, "atol": 1e-4},
+    },
+    "matmul": {
+        "sq1k": {"sizes": [1024, 1024, 1024]},
+        "ck_16k_l2": {"sizes": [1024, 1024, 16384], "dtype": "float32", "lnc": 2, "rtol": 1e-3, "atol": 1e-3},
+        "pm_16k_l2": {"sizes": [16384, 1024, 1024], "lnc": 2, "rtol": 2e-2, "atol": 2e-2},
+        "roofline": {"sizes": [4096, 4096, 4096]},
+    },
+    "rmsnorm_matmul": {
+        "sq1k": {"sizes": [1024, 1024, 1024]},
+        "h8192": {"sizes": [1024, 8192, 8192]},
+    },
+    "silu_mlp": {"sq1k": {"sizes": [1024, 1024, 1024, 1024]}},
+    "softmax": {"sq1k": {"sizes": [1024, 1024]}, "roofline": {"sizes": [4096, 32768]}},
+    # the BASELINE configs (sibling specs)
+    "rmsnorm_llama": {"config": {"sizes": [2048, 4096], "rtol": 1e-2, "atol": 1e-2}},
+    "rope_gqa": {"config": {"sizes": [4096, 32, 8, 64], "rtol": 1e-2, "atol": 1e-2}},
+    "cumsum_nucleus_sorted": {"config": {"sizes": [256, 128256], "rtol": 1e-5, "atol": 1e-7}},
+    "silu_mlp_swiglu": {"config": {"sizes": [4096, 14336, 4096, 4096], "rtol": 1e-2, "atol": 1e-2}},
+    "fused_adam_cfg": {"config": {"sizes": [15625, 64000], "rtol": 1e-5, "atol": 1e-9}},
+}
+
+
+def all_cases() -> list[str]:
+    return [f"{k}_{c}" for k, cs in CASES.items() for c in cs]
+
+
+def resolve(case: str) -> tuple[str, str, dict]:
+    """Split `<kernel>_<case>` (kernel names contain underscores: longest
+    kernel prefix wins)."""
+    for k in sorted(CASES, key=len, reverse=True):
+        if case.startswith(k + "_") and case[len(k) + 1:] in CASES[k]:
+            return k, case[len(k) + 1:], CASES[k][case[len(k) + 1:]]
+    raise KeyError(f"unknown case {case!r}; see `python -m enzyme_b200.cases list`")
+
+
+def argv(case: str, out_dir: str = "out") -> list[str]:
+    """The CLI arguments of one case (what the reference's make target runs)."""
+    kernel, cid, c = resolve(case)
+    args = [str(ROOT / "kernels" / kernel), "--sizes", *map(str, c["sizes"])]
+    if "dtype" in c:
+        args += ["--dtype", c["dtype"]]
+    if "rtol" in c and "atol" in c:
+        args += ["--rtol", repr(c["rtol"]), "--atol", repr(c["atol"])]
+    if c.get("lnc", 1) > 1:
+        args += ["--gpus", str(c["lnc"])]
+    args += ["--out", f"{out_dir}/{kernel}_{cid}.csv"]
+    return args
+
+
+def main(argv_in: list[str] | None = None) -> int:
+    a = list(sys.argv[1:] if argv_in is None else argv_in)
+    if not a or a[0] not in ("list", "run", "argv"):
+        print(__doc__)
+        return 2
+    if a[0] == "list":
+        for c in all_cases():
+            print(c)
+        return 0
+    if len(a) < 2:
+        print("usage: python -m enzyme_b200.cases run <kernel>_<case> [extra CLI flags]", file=sys.stderr)
+        return 2
+    cmd = argv(a[1]) + a[2:]
+    if a[0] == "argv":
+        print(" ".join(cmd))
+        return 0
+    from .cli import build_parser, run
+
+    return run(build_parser().parse_args(cmd))
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -82,6 +82,33 @@ def pick_winner(csv_path: Path, spec: KernelSpec, pick_by: PickBy, *, rtol: floa
         sharding=str(row["sharding"]) if "sharding" in row else "cuda")
 
 
+def provenance(spec: KernelSpec, winner: WinnerRow, case_id: str) -> str:
+    """A literal WINNER_PROVENANCE record appended to the exported winner: the
+    device it was measured on, the source commit, the timings and the key
+    (what Axon's specialised winners record in their docstrings)."""
+    import subprocess
+
+    device = "unknown"
+    try:
+        import torch
+
+        if torch.cuda.is_available():
+            device = torch.cuda.get_device_name(0)
+    except Exception:
+        pass
+    try:
+        commit = subprocess.run(["git", "rev-parse", "--short", "HEAD"], capture_output=True, text=True,
+                                cwd=Path(__file__).resolve().parent, timeout=10).stdout.strip() or "unknown"
+    except Exception:
+        commit = "unknown"
+    rec = {"spec": spec.name, "case": case_id, "device": device, "commit": commit,
+           "sizes": dict(zip(spec.dim_vars, winner.sizes)),
+           "tiles": dict(zip(spec.tile_args, winner.tile_values)), "hw_variant": winner.hw_variant,
+           "tile_variant": winner.tile_variant, "median_ms": winner.median_ms, "mean_ms": winner.mean_ms,
+           "min_ms": winner.min_ms}
+    return f"\n\nWINNER_PROVENANCE = {rec!r}\n"
+
+
 def export_winner(spec: KernelSpec, winner: WinnerRow, *, case_id: str, kernel_path: Path | str, paths: RunPaths,
                   dtype: str, rtol: float, atol: float) -> None:
     entry = f"{spec.name}_{case_id}"
@@ -94,6 +121,8 @@ def export_winner(spec: KernelSpec, winner: WinnerRow, *, case_id: str, kernel_p
     dst = paths.winner_kernel(entry)
     dst.parent.mkdir(parents=True, exist_ok=True)
     shutil.copyfile(src, dst)
+    with dst.open("a") as f:
+        f.write(provenance(spec, winner, case_id))
     print(f"  wrote {dst}")
     shape = dict(zip(spec.dim_vars, winner.sizes))
     tiles = {a: int(v) for a, v in zip(spec.tile_args, winner.tile_values)}

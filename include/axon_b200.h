@@ -226,6 +226,14 @@ AXON_API int axon_gemm_status(void* stream);
 AXON_API int axon_cast(const void* src, void* dst, int64_t n, int32_t src_dtype, int32_t dst_dtype,
                        void* stream);
 
+/* Diagnostic with no counterpart in the reference: one thread waits for at
+ * most limit_ns (<= 5 s) on an mbarrier nothing arrives on and on the device
+ * word *flag (which the caller leaves 0), using the bounded waits of the GEMM,
+ * the cluster scan and the look-back scan; status2 (two int32 on the device)
+ * receives AXON_E_TIMEOUT for each wait that gave up (AXON_OK if the flag was
+ * set). Lets tests check the timeout path on a GPU without a fault or hang. */
+AXON_API int axon_selftest_bounded_wait(int64_t limit_ns, void* status2, const void* flag, void* stream);
+
 /* Per-row scale r[i] = rsqrt(scale * sum_j x[i,j]^2 + eps) in fp32: the norm
  * prologue of rmsnorm_matmul (Axon kernels/rmsnorm_matmul/refs.py:16-22) and
  * of the SwiGLU config's optional rmsnorm. */

@@ -180,6 +180,12 @@ def test_export_winner_writes_kernel_and_case(tmp_path):
     mod = importlib.util.module_from_spec(s)
     s.loader.exec_module(mod)
     assert mod.CASE["entry_point"] == "rmsnorm" and mod.CASE["shape_args"]["TILES_IN_BLOCK_N"] == 2
+    import ast
+
+    tree = ast.parse(paths.winner_kernel("rmsnorm_h512").read_text())
+    prov = next(ast.literal_eval(n.value) for n in tree.body if isinstance(n, ast.Assign)
+                and getattr(n.targets[0], "id", "") == "WINNER_PROVENANCE")
+    assert prov["case"] == "h512" and prov["median_ms"] == 1.0 and prov["tiles"]["TILES_IN_BLOCK_N"] == 2
     ins = mod.make_inputs(m=64, n=512, TILES_IN_BLOCK_M=1, TILES_IN_BLOCK_N=2)
     assert ins["x"].shape == (64, 512) and ins["TILES_IN_BLOCK_N"] == 2
     out = mod.torch_ref(ins["x"], 1, 2)
@@ -195,3 +201,33 @@ def test_case_module_needs_torch_ref():
     with pytest.raises(ValueError, match="torch_ref"):
         generate_case_module(spec, KERNELS / "softmax", "float32", Path("/tmp/x_case.py"), name="softmax_x",
                              entry_point="softmax", shape_args={}, rtol=1e-2, atol=1e-2)
+
+
+# ---- case catalogue ---------------------------------------------------------------
+
+
+def test_case_catalogue_builds_the_make_target_command():
+    from enzyme_b200 import cases
+
+    a = cases.argv("rmsnorm_h4096")
+    assert a[0].endswith("kernels/rmsnorm") and a[1:4] == ["--sizes", "1024", "4096"]
+    assert a[a.index("--rtol") + 1] == "0.01" and a[-2:] == ["--out", "out/rmsnorm_h4096.csv"]
+    a = cases.argv("matmul_ck_16k_l2")
+    assert a[a.index("--dtype") + 1] == "float32" and a[a.index("--gpus") + 1] == "2"
+    assert "--rtol" not in cases.argv("matmul_sq1k")
+    # kernel names with underscores resolve to the longest matching spec
+    assert cases.resolve("rmsnorm_matmul_sq1k")[0] == "rmsnorm_matmul"
+    assert cases.resolve("silu_mlp_swiglu_config")[0] == "silu_mlp_swiglu"
+    with pytest.raises(KeyError):
+        cases.resolve("rmsnorm_nope")
+
+
+def test_every_case_parses_and_matches_its_spec():
+    from enzyme_b200 import cases
+
+    for case in cases.all_cases():
+        kernel, _, c = cases.resolve(case)
+        spec = load_spec(kernel)
+        assert len(c["sizes"]) == len(spec.dim_vars), case
+        args = cli.build_parser().parse_args(cases.argv(case))
+        assert args.sizes == c["sizes"]
