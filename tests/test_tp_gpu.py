@@ -1,0 +1,100 @@
+"""Multi-GPU paths on real GPUs (two ranks over NCCL; skipped on a 1-GPU box).
+
+* Tensor-parallel SwiGLU: two ranks, each with its column/row shard, slabbed
+  all-reduce of fp32 partials; the full output is checked on sampled rows
+  against the float64 oracle of the unsharded MLP.
+* Parameter-sharded Adam: each rank updates its contiguous slice; the
+  gathered result equals a one-GPU update of the whole vector.
+NVLS is off (NCCL_NVLS_ENABLE=0) and the process group has a short timeout.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _tp_rank(rank, world, port, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from enzyme_b200 import ops, tp
+
+        dev = torch.device("cuda", rank)
+        g = torch.Generator().manual_seed(0)
+        m, h, inter = 512, 1024, 2048
+        x = torch.randn(m, h, generator=g).bfloat16()
+        wg = (0.02 * torch.randn(h, inter, generator=g)).bfloat16()
+        wu = (0.02 * torch.randn(h, inter, generator=g)).bfloat16()
+        wd = (0.02 * torch.randn(inter, h, generator=g)).bfloat16()
+        shards = [s.to(dev) for s in tp.shard_swiglu(wg, wu, wd, rank, world)]
+        y = tp.TPSwiGLU(*shards, slabs=3).forward(x.to(dev))
+        torch.cuda.synchronize()
+        ops.gemm_status()
+        # adam: 10_000_003 params, each rank its slice
+        n = 10_000_003
+        gen = torch.Generator().manual_seed(1)
+        p = 0.02 * torch.randn(n, generator=gen)
+        gr = (1e-3 * torch.randn(n, generator=gen)).bfloat16()
+        sl = tp.adam_shard(n, rank, world)
+        pd, gd = p[sl].to(dev), gr[sl].to(dev)
+        md, vd = torch.zeros_like(pd), torch.zeros_like(pd)
+        ops.adam(pd, gd, md, vd, step_size=1e-3, inv_bc2_sqrt=1.2, wd=0.1, beta1=0.9, beta2=0.95, out=(pd, md, vd))
+        full = torch.zeros(n, device=dev)
+        full[sl] = pd
+        dist.all_reduce(full)  # gather for the check only
+        whole = p.to(dev)
+        zm, zv = torch.zeros_like(whole), torch.zeros_like(whole)
+        ops.adam(whole, gr.to(dev), zm, zv, step_size=1e-3, inv_bc2_sqrt=1.2, wd=0.1, beta1=0.9, beta2=0.95,
+                 out=(whole, zm, zv))
+        q.put((rank, y.cpu().numpy(), bool(torch.equal(full, whole))))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_tp_swiglu_and_sharded_adam_two_gpus():
+    import torch.multiprocessing as mp
+
+    from oracle import f64
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_tp_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs)
+    g = torch.Generator().manual_seed(0)
+    m, h, inter = 512, 1024, 2048
+    x = torch.randn(m, h, generator=g).bfloat16().float().numpy()
+    wg = (0.02 * torch.randn(h, inter, generator=g)).bfloat16().float().numpy()
+    wu = (0.02 * torch.randn(h, inter, generator=g)).bfloat16().float().numpy()
+    wd = (0.02 * torch.randn(inter, h, generator=g)).bfloat16().float().numpy()
+    rows = np.arange(0, m, 7)
+    want = f64.silu_mlp(x[rows], wg, wu, wd)
+    for rank, y, adam_equal in res:
+        assert adam_equal, f"rank {rank}: sharded Adam differs from the one-GPU update"
+        np.testing.assert_allclose(y[rows], want, rtol=1e-2, atol=1e-2)
+    np.testing.assert_array_equal(res[0][1], res[1][1])  # every rank holds the same reduced output
