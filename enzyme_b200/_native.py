@@ -65,6 +65,7 @@ class Tune(ctypes.Structure):
         ("stages", ctypes.c_int32),
         ("split", ctypes.c_int32),
         ("precision", ctypes.c_int32),
+        ("max_ctas", ctypes.c_int32),
     ]
 
     @classmethod

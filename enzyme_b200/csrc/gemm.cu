@@ -186,6 +186,7 @@ struct GemmParams {
   int terms;           // SILU_GATE: write the activation as this many bf16/f16 terms
   int64_t term_stride; // columns between the terms in C
   int b_kwrap;         // > 0: B's k coordinate wraps modulo this (B re-read per term)
+  int max_ctas;        // > 0: cap on the persistent grid
 };
 
 template <int BN, int EPI, typename TC>
@@ -439,7 +440,9 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
   if (e != cudaSuccess) return fail(AXON_E_LAUNCH, "axon_gemm: smem attribute: %s", cudaGetErrorString(e));
   constexpr int BN_OUT = EPI == AXON_EPI_SILU_GATE ? BN / 2 : BN;
   const int64_t tiles = static_cast<int64_t>((gp.m + BM - 1) / BM) * ((gp.n + BN_OUT - 1) / BN_OUT);
-  const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
+  int64_t cap = sm_count();
+  if (gp.max_ctas > 0 && gp.max_ctas < cap) cap = gp.max_ctas;
+  const int grid = static_cast<int>(tiles < cap ? tiles : cap);
   kern<<<grid, 192, smem, s>>>(ma, mb, mb2, gp);
   return launch_status("axon_gemm");
 }
@@ -536,6 +539,8 @@ int gemm_impl(const void* a, const void* b, const void* b2, void* c, const float
   gp.terms = terms;
   gp.term_stride = term_stride;
   gp.b_kwrap = static_cast<int>(b_kwrap);
+  gp.max_ctas = t.max_ctas;
+  if (t.max_ctas < 0) return fail(AXON_E_ARG, "axon_gemm: max_ctas must be >= 0");
   const uint32_t fmt = ab_dtype == AXON_BF16 ? 1u : 0u;
   gp.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | (0u << 15) | (1u << 16) |
              (static_cast<uint32_t>(bn >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);

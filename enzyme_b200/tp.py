@@ -62,7 +62,12 @@ def shard_swiglu(w_gate: torch.Tensor, w_up: torch.Tensor, w_down: torch.Tensor,
 
 @dataclass
 class _CudaOps:
-    """The CUDA kernels a TP step runs (enzyme_b200.ops)."""
+    """The CUDA kernels a TP step runs (enzyme_b200.ops). `tune` goes to both
+    GEMMs: capping `max_ctas` below the SM count (and/or using fewer stages)
+    leaves room on some SMs for NCCL's kernels, so a slab's all-reduce really
+    runs while the next slab's GEMMs do."""
+
+    tune: dict | None = None
 
     def cast(self, src, dtype, out):
         from . import ops
@@ -73,12 +78,12 @@ class _CudaOps:
         from . import _native as N
         from . import ops
 
-        return ops.gemm(x, w_gate, b2=w_up, epilogue=N.AXON_EPI_SILU_GATE, out=out)
+        return ops.gemm(x, w_gate, b2=w_up, epilogue=N.AXON_EPI_SILU_GATE, out=out, tune=self.tune)
 
     def down(self, act, w_down, out):
         from . import ops
 
-        return ops.gemm(act, w_down, out=out)
+        return ops.gemm(act, w_down, out=out, tune=self.tune)
 
 
 class TPSwiGLU:

@@ -71,6 +71,8 @@ typedef struct axon_tune {
                            row cluster (variant 1)                            */
   int32_t precision;    /* silu_mlp activation storage: 1 = one bf16 value,
                            2 / 3 = split terms, 4 = f16 (see axon_silu_mlp)   */
+  int32_t max_ctas;     /* GEMM: cap on the persistent grid (0 = one CTA per
+                           SM); leaves SMs free for a concurrent collective   */
 } axon_tune_t;
 
 /* ---- library metadata ----------------------------------------------------- */
