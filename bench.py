@@ -334,13 +334,17 @@ class SwiGLU(Workload):
             # column/row tensor parallel: W_gate/W_up column shard, W_down row
             # shard, fp32 partials all-reduced per m-slab while the next slab
             # computes (enzyme_b200.tp)
-            from enzyme_b200.tp import TPSwiGLU
+            from enzyme_b200.tp import TPSwiGLU, _CudaOps
 
-            self.tp = TPSwiGLU(self.w1, self.w2, self.w3, slabs=self.SLABS)
+            self.tp = TPSwiGLU(self.w1, self.w2, self.w3, slabs=self.SLABS, ops=_CudaOps(tune=self.TP_TUNE))
             self.launches_per_step = 1 + 2 * len(self.tp.slab_bounds(m))
 
     PRECISION = 4
-    SLABS = 4
+    # measured on 2 B200s: 1 slab 733 us (no overlap: 568 compute + 161
+    # all-reduce), 2 slabs with the GEMM grid capped at 132 CTAs 692 us, 4
+    # slabs slower (ragged last waves)
+    SLABS = 2
+    TP_TUNE = {"max_ctas": 132}
 
     def per_step_work(self):
         m, n, k, p = 4096, self.shard, 4096, 4096
