@@ -121,6 +121,7 @@ SIGNATURES: dict[str, tuple] = {
     "axon_cast": (_I32, [_P, _P, _I64, _I32, _I32, _P]),
     "axon_selftest_bounded_wait": (_I32, [_I64, _P, _P, _P]),
     "axon_row_rsqrt": (_I32, [_P, _P, _I64, _I64, _I64, _I32, _F, _F, _P]),
+    "axon_row_status": (_I32, [_P]),
     "axon_rmsnorm_matmul": (_I32, [_P, _P, _P, _P, _I64, _I64, _I64, _I32, _I32, _TUNE, _P]),
     "axon_silu_mlp_workspace_bytes": (_I64, [_I64, _I64, _I64, _I32, _TUNE]),
     "axon_silu_mlp": (

@@ -12,12 +12,15 @@ C ABI. Each module embeds the `__axon_tile_constraints__` manifest of its
 variant.
 
 Tile knob meaning (the CUDA counterpart of TILES_IN_BLOCK_*):
-  row ops, rope, Adam   TILES_IN_BLOCK_N = v -> 32*v threads per row / CTA;
+  row ops, rope, Adam   TILES_IN_BLOCK_N = v -> 32*v threads per row / CTA
+                        (row_bulk_warp: v warps per CTA, one row each);
                         TILES_IN_BLOCK_M must be 1 (rows per CTA are derived).
   cumsum                TILES_IN_BLOCK_N = v -> 1024*v elements per scan tile.
-  GEMM specs            TILES_IN_BLOCK_M must be 1 (128-row tcgen05 tiles),
+  GEMM specs            TILES_IN_BLOCK_M must be 1 (128-row tcgen05 tiles per CTA),
                         TILES_IN_BLOCK_N = v -> BLOCK_N = 64*v,
-                        TILES_IN_BLOCK_K = v -> v shared-memory pipeline stages.
+                        TILES_IN_BLOCK_K = v -> min(v, deepest that fits)
+                        shared-memory pipeline stages. hw_variant 0 = one CTA
+                        per tile, 1 = CTA pairs (cta_group::2, 256-row tiles).
   silu_mlp              N -> gate/up BLOCK_N = 128*v (64*v output columns),
                         K -> stages, P -> down-projection BLOCK_N = 64*v
                         (recorded; the down GEMM picks its own tile today).
@@ -55,7 +58,7 @@ class Variant:
 
 def variants(spec_name: str) -> list[Variant]:
     if spec_name in ROW_SPECS:
-        return [Variant(0, "row_resident"), Variant(1, "row_streaming")]
+        return [Variant(0, "row_resident"), Variant(1, "row_streaming"), Variant(2, "row_bulk_warp")]
     if spec_name == "rope":
         return [Variant(0, "flat_vec16")]
     if spec_name == "rope_gqa":
@@ -65,11 +68,19 @@ def variants(spec_name: str) -> list[Variant]:
     if spec_name in ADAM_SPECS:
         return [Variant(0, "grid_stride_vec")]
     if spec_name in GEMM_SPECS:
-        return [Variant(0, "tcgen05_ws_persistent")]
+        # hw_variant i runs axon_gemm variant i + 1 (0 is the library's auto pick)
+        return [Variant(0, "tcgen05_ws_persistent"), Variant(1, "tcgen05_cta_pair")]
     if spec_name in MLP_SPECS:
         return [Variant(0, "tcgen05_act_1term"), Variant(1, "tcgen05_act_2term"), Variant(2, "tcgen05_act_3term"),
                 Variant(3, "tcgen05_act_f16")]
     raise KeyError(f"no CUDA variants for spec '{spec_name}'")
+
+
+def gemm_max_stages(pair: bool, block_n: int) -> int:
+    """Deepest shared-memory ring axon_gemm accepts: 227 KB less barriers over
+    one stage (a 128 x 64 A slab plus the B columns the CTA stages), at most 8."""
+    b_cols = block_n // 2 if pair else block_n
+    return min(8, (232448 - 1280) // (128 * 64 * 2 + b_cols * 64 * 2))
 
 
 def _one(arg: str) -> TileConstraint:
@@ -81,7 +92,16 @@ def constraints(spec_name: str, hw_variant: int, dims: dict, itemsize: int,
     """The feasibility manifest of one variant at concrete dims."""
     out: list[TileConstraint] = []
     args = list(tile_args)
-    if spec_name in ROW_SPECS:
+    if spec_name in ROW_SPECS and hw_variant == 2:
+        # N = warps per CTA, one row per warp staged in shared memory; rows of
+        # a multiple of 16 bytes up to 32 KB (plus the weight, for rmsnorm)
+        row_bytes = dims["n"] * itemsize
+        fixed = row_bytes if spec_name.startswith("rmsnorm") else 0
+        ok = row_bytes % 16 == 0 and row_bytes <= 32768
+        allowed = tuple(v for v in (1, 2, 4, 8, 16, 32) if ok and 512 + fixed + v * row_bytes <= 232448)
+        out.append(TileConstraint(args[1], extent=32, tile_size=1, require_divisible=False, allowed=allowed or (0,)))
+        out.append(_one(args[0]))
+    elif spec_name in ROW_SPECS:
         n = dims["n"]
         e = 16 // itemsize
         max_v = (512 if itemsize == 2 else 1024) // 32
@@ -109,8 +129,9 @@ def constraints(spec_name: str, hw_variant: int, dims: dict, itemsize: int,
         out.append(_one(args[0]))
     elif spec_name in GEMM_SPECS:
         out.append(_one(args[0]))
-        out.append(TileConstraint(args[1], extent=256, tile_size=64, require_divisible=True, allowed=(1, 2, 4)))
-        out.append(TileConstraint(args[2], extent=8, tile_size=1, require_divisible=True, allowed=(2, 4)))
+        out.append(TileConstraint(args[1], extent=256, tile_size=64, require_divisible=True,
+                                  allowed=(1, 2, 4) if hw_variant == 0 else (2, 4)))
+        out.append(TileConstraint(args[2], extent=8, tile_size=1, require_divisible=True, allowed=(2, 4, 8)))
     elif spec_name in MLP_SPECS:
         out.append(_one(args[0]))
         out.append(TileConstraint(args[1], extent=256, tile_size=128, require_divisible=True, allowed=(1, 2)))
@@ -131,7 +152,8 @@ def tune_for(spec_name: str, hw_variant: int, tiles: dict[str, int]) -> dict | l
     if spec_name in SCAN_SPECS:
         return {"variant": hw_variant, "split": t["N"] if hw_variant == 1 else 1024 * t["N"]}
     if spec_name in GEMM_SPECS:
-        return {"variant": hw_variant, "block_n": 64 * t["N"], "stages": t["K"]}
+        bn = 64 * t["N"]
+        return {"variant": hw_variant + 1, "block_n": bn, "stages": min(t["K"], gemm_max_stages(hw_variant == 1, bn))}
     if spec_name in MLP_SPECS:
         precision = 4 if hw_variant == 3 else hw_variant + 1
         return {"block_n": 128 * t["N"], "stages": t["K"], "precision": precision, "down_block_n": 64 * t["P"]}

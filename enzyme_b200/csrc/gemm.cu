@@ -21,6 +21,10 @@
 // SILU_GATE (the B tile holds BN/2 gate columns from w1 and the matching BN/2
 // up columns from w2, so one N=BN MMA yields both and C = silu(g) * u).
 //
+// Variant 2 (below) runs the same roles on a cluster of two CTAs that share one
+// tcgen05.mma.cta_group::2 (M = 256) per k-step, halving the B bytes each SM
+// stages per FLOP.
+//
 // No TMA multicast is used anywhere, so the kernel is legal when its operands
 // live in any GPU's memory. Every mbarrier wait is bounded (about two seconds
 // of %globaltimer); a wait that gives up raises a CTA-wide abort flag and the
@@ -397,6 +401,276 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// ---- variant 2: CTA pairs (tcgen05 cta_group::2) ------------------------------------
+//
+// A cluster of two CTAs on two SMs computes a 256 x BN tile with one
+// tcgen05.mma.cta_group::2 (M = 256) per K = 16 step, issued by the even
+// ("leader") CTA: CTA r holds A rows [128 r, 128 r + 128) and B columns
+// [BN/2 r, BN/2 r + BN/2) of the tile in its own shared memory, and its TMEM
+// receives its 128 rows of the fp32 accumulator. Each CTA therefore stages
+// half of B per k-block, halving B's shared-memory and L2 traffic per CTA.
+// For SILU_GATE the leader holds the gate columns and the peer the matching up
+// columns, so each CTA's TMEM again holds gate | up for its rows.
+//
+// Synchronisation: both CTAs' TMA loads (cp.async.bulk.tensor ... cta_group::2,
+// no multicast) complete transaction bytes on the leader's `full` barrier,
+// which the leader's producer arms with both CTAs' bytes; the leader's MMA
+// thread frees a stage by committing to the `empty` barrier of each CTA, and
+// announces a finished accumulator by committing to each CTA's `tmem_full`;
+// each CTA's epilogue warps release a TMEM buffer by arriving on the leader's
+// `tmem_empty`. Every wait is bounded as in the one-CTA kernel. A cluster barrier
+// precedes exit, so no CTA leaves while its peer may still address it.
+
+__device__ __forceinline__ uint32_t mapa_u32(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_barrier() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr, uint32_t count) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(cluster_addr), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d_pair(const CUtensorMap* map, uint32_t leader_bar, void* dst, int c0,
+                                                 int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+      "%4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(leader_bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_commit_to(uint32_t cluster_bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_bar)
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_mma_pair(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+template <int BN, int EPI, typename TC>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tcgen05_pair(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const __grid_constant__ CUtensorMap tmB2, GemmParams p) {
+  constexpr int BH = BN / 2;                 // B columns staged per CTA
+  constexpr int B_BYTES = BH * BK * 2;
+  constexpr int STAGE = A_BYTES + B_BYTES;
+  constexpr int BN_OUT = EPI == AXON_EPI_SILU_GATE ? BN / 2 : BN;
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int S = p.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * STAGE);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;  // leader: all issued MMAs have retired
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* issued = reinterpret_cast<int*>(tmem_slot + 2);
+
+  uint32_t rank;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+  const bool leader = rank == 0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_m = (p.m + 2 * BM - 1) / (2 * BM);
+  const int num_n = (p.n + BN_OUT - 1) / BN_OUT;
+  const int tiles = num_m * num_n;
+  const int kblocks = (p.k + BK - 1) / BK;
+  const int pair_id = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 8);  // one arrival per epilogue warp of each CTA
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    *issued = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    tc_fence_before();
+  }
+  __syncthreads();
+  cluster_barrier();  // both CTAs' barriers are initialised before either is addressed remotely
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int t = pair_id; t < tiles; t += num_pairs) {
+      const int tm = t % num_m, tn = t / num_m;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) goto producer_done;
+        const uint32_t leader_full = mapa_u32(smem_u32(&full[stage]), 0);
+        if (leader) mbar_expect_tx(&full[stage], 2 * STAGE);
+        uint8_t* sa = smem + stage * STAGE;
+        uint8_t* sb = sa + A_BYTES;
+        tma_load_2d_pair(&tmA, leader_full, sa, kb * BK, tm * 2 * BM + static_cast<int>(rank) * BM);
+        if constexpr (EPI == AXON_EPI_SILU_GATE) {
+          const CUtensorMap* mp = leader ? &tmB : &tmB2;  // gate columns on the leader, up on the peer
+#pragma unroll
+          for (int j = 0; j < BH / 64; ++j)
+            tma_load_2d_pair(mp, leader_full, sb + j * B_CHUNK, tn * BN_OUT + j * 64, kb * BK);
+        } else {
+          const int kb_b = p.b_kwrap > 0 ? (kb * BK) % p.b_kwrap : kb * BK;
+#pragma unroll
+          for (int j = 0; j < BH / 64; ++j)
+            tma_load_2d_pair(&tmB, leader_full, sb + j * B_CHUNK, tn * BN + static_cast<int>(rank) * BH + j * 64,
+                             kb_b);
+        }
+        *issued += 1;
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  producer_done:;
+  } else if (warp == 1 && lane == 0 && leader) {
+    // ---------------- MMA issuer (leader only) ----------------
+    int stage = 0;
+    uint32_t phase = 0;
+    int local = 0;
+    for (int t = pair_id; t < tiles; t += num_pairs, ++local) {
+      const int buf = local & 1;
+      if (!mbar_wait(&tempty[buf], ((local >> 1) & 1) ^ 1u, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t d = tmem_base + static_cast<uint32_t>(buf * BN);
+      bool ok = true;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!mbar_wait(&full[stage], phase, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + stage * STAGE);
+        const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k) {
+          const uint64_t ad = sdesc(sa + k * 32, 16, 1024);
+          const uint64_t bd = sdesc(sb + k * 2048, B_CHUNK, 1024);
+          tc_mma_pair(d, ad, bd, p.idesc, (kb | k) != 0);
+        }
+        tc_commit_to(smem_u32(&empty[stage]));
+        tc_commit_to(mapa_u32(smem_u32(&empty[stage]), 1));
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+      tc_commit_to(smem_u32(&tfull[buf]));
+      tc_commit_to(mapa_u32(smem_u32(&tfull[buf]), 1));
+    }
+    // TMEM is released only after every MMA this thread issued has retired
+    tc_commit_to(smem_u32(drain));
+    volatile int never = 0;
+    mbar_wait(drain, 0, &never);
+  } else if (warp >= 2) {
+    // ---------------- epilogue (both CTAs, their own 128 rows) ----------------
+    const int q = warp & 3;
+    int local = 0;
+    TC* C = static_cast<TC*>(p.c);
+    for (int t = pair_id; t < tiles; t += num_pairs, ++local) {
+      const int tm = t % num_m, tn = t / num_m;
+      const int buf = local & 1;
+      if (!mbar_wait(&tfull[buf], (local >> 1) & 1, abort_flag)) break;
+      tc_fence_after();
+      const int64_t row = static_cast<int64_t>(tm) * 2 * BM + static_cast<int64_t>(rank) * BM + q * 32 + lane;
+      const bool row_ok = row < p.m;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN);
+      TC* crow = C + (row_ok ? row : 0) * p.ldc;
+      float scale = 1.f;
+      if constexpr (EPI == AXON_EPI_ROWSCALE) scale = row_ok ? p.row_scale[row] : 0.f;
+      if constexpr (EPI == AXON_EPI_SILU_GATE) {
+#pragma unroll 1
+        for (int c = 0; c < BN_OUT / 32; ++c) {
+          float g[32], u[32];
+          __syncwarp();
+          tmem_ld32(tbase + c * 32, g);
+          tmem_ld32(tbase + BN_OUT + c * 32, u);
+          tmem_wait_ld();
+          const int64_t col = static_cast<int64_t>(tn) * BN_OUT + c * 32;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) g[j] = g[j] / (1.0f + __expf(-g[j])) * u[j];
+          if (row_ok && col < p.n) {
+            if (p.terms <= 1) {
+              store32<TC>(crow + col, g, col, p.n);
+            } else {
+#pragma unroll 1
+              for (int tt = 0; tt < p.terms; ++tt) {
+                float part[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                  part[j] = to_f(from_f<TC>(g[j]));
+                  g[j] -= part[j];
+                }
+                store32<TC>(crow + tt * p.term_stride + col, part, col, p.n);
+              }
+            }
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          __syncwarp();
+          tmem_ld32(tbase + c * 32, v);
+          tmem_wait_ld();
+          const int64_t col = static_cast<int64_t>(tn) * BN + c * 32;
+          if constexpr (EPI == AXON_EPI_ROWSCALE) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] *= scale;
+          }
+          if (row_ok && col < p.n) store32<TC>(crow + col, v, col, p.n);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_u32(smem_u32(&tempty[buf]), 0), 1);
+    }
+  }
+
+  __syncthreads();
+  if (threadIdx.x == 0 && *abort_flag && *issued > 0) {
+    // copies issued by this CTA may still be landing: give them time before
+    // the pair leaves (this path only runs after a wait gave up)
+    for (int i = 0; i < 1000; ++i) __nanosleep(1000);
+  }
+  cluster_barrier();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                 : "memory");
+  }
+}
+
 // ---- host side -------------------------------------------------------------------
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -447,9 +721,64 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
   return launch_status("axon_gemm");
 }
 
+// Variant 2: clusters of two CTAs, one pair per 256-row tile. The grid is
+// capped at the number of pairs the GPU holds at once (each CTA needs a whole
+// SM), so the kernel stays persistent.
+template <int BN, int EPI, typename TC>
+int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb2, const GemmParams& gp,
+                     cudaStream_t s) {
+  constexpr int STAGE = A_BYTES + (BN / 2) * BK * 2;
+  const size_t smem = static_cast<size_t>(gp.stages) * STAGE + 1024 + 256;
+  auto kern = gemm_tcgen05_pair<BN, EPI, TC>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return fail(AXON_E_LAUNCH, "axon_gemm: smem attribute: %s", cudaGetErrorString(e));
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(192, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // pairs resident at once, for this smem footprint (cached per footprint)
+  static int cached_pairs[9] = {0};
+  int& pairs_cap = cached_pairs[gp.stages > 8 ? 8 : gp.stages];
+  if (pairs_cap == 0) {
+    cfg.gridDim = dim3(2, 1, 1);
+    int clusters = 0;
+    e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+    if (e != cudaSuccess || clusters <= 0)
+      return fail(AXON_E_LAUNCH, "axon_gemm: no room for a CTA pair (%s)", cudaGetErrorString(e));
+    pairs_cap = clusters;
+  }
+  constexpr int BN_OUT = EPI == AXON_EPI_SILU_GATE ? BN / 2 : BN;
+  const int64_t tiles = static_cast<int64_t>((gp.m + 2 * BM - 1) / (2 * BM)) * ((gp.n + BN_OUT - 1) / BN_OUT);
+  int64_t cap = pairs_cap;
+  if (gp.max_ctas > 0 && gp.max_ctas / 2 < cap) cap = gp.max_ctas / 2 > 0 ? gp.max_ctas / 2 : 1;
+  const int pairs = static_cast<int>(tiles < cap ? tiles : cap);
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  e = cudaLaunchKernelEx(&cfg, kern, ma, mb, mb2, gp);
+  if (e != cudaSuccess) return fail(AXON_E_LAUNCH, "axon_gemm: %s", cudaGetErrorString(e));
+  return launch_status("axon_gemm");
+}
+
 template <int BN, int EPI>
-int dispatch_c(int32_t c_dtype, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb2,
+int dispatch_c(int32_t c_dtype, bool pair, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb2,
                const GemmParams& gp, cudaStream_t s) {
+  if (pair) {
+    if constexpr (BN >= 128) {
+      switch (c_dtype) {
+        case AXON_BF16: return launch_gemm_pair<BN, EPI, __nv_bfloat16>(ma, mb, mb2, gp, s);
+        case AXON_F16: return launch_gemm_pair<BN, EPI, __half>(ma, mb, mb2, gp, s);
+        case AXON_F32: return launch_gemm_pair<BN, EPI, float>(ma, mb, mb2, gp, s);
+        default: return fail(AXON_E_UNSUPPORTED, "axon_gemm: unsupported output dtype %d", c_dtype);
+      }
+    }
+    return fail(AXON_E_ARG, "axon_gemm: the CTA-pair variant needs block_n >= 128");
+  }
   switch (c_dtype) {
     case AXON_BF16: return launch_gemm<BN, EPI, __nv_bfloat16>(ma, mb, mb2, gp, s);
     case AXON_F16: return launch_gemm<BN, EPI, __half>(ma, mb, mb2, gp, s);
@@ -458,8 +787,10 @@ int dispatch_c(int32_t c_dtype, const CUtensorMap& ma, const CUtensorMap& mb, co
   }
 }
 
-int max_stages(int bn) {
-  const int stage = A_BYTES + bn * BK * 2;
+// Deepest ring that fits the 227 KB of shared memory; `b_cols` = B columns
+// staged per CTA (block_n, or block_n / 2 for a CTA pair).
+int max_stages(int b_cols) {
+  const int stage = A_BYTES + b_cols * BK * 2;
   const int avail = 232448 - 1024 - 256;
   int s = avail / stage;
   return s > 8 ? 8 : s;
@@ -499,7 +830,7 @@ int gemm_impl(const void* a, const void* b, const void* b2, void* c, const float
   if (lda % 8 || ldb % 8 || ldc % 8) return fail(AXON_E_ALIGN, "axon_gemm: leading dimensions must be multiples of 8");
   if (!aligned16(a) || !aligned16(b) || !aligned16(c) || (b2 && !aligned16(b2)))
     return fail(AXON_E_ALIGN, "axon_gemm: operands must be 16-byte aligned");
-  if (t.variant != 0) return fail(AXON_E_ARG, "axon_gemm: unknown variant %d", t.variant);
+  if (t.variant < 0 || t.variant > 2) return fail(AXON_E_ARG, "axon_gemm: unknown variant %d", t.variant);
   if (t.block_m != 0 && t.block_m != 128) return fail(AXON_E_ARG, "axon_gemm: block_m must be 128");
   if (t.block_k != 0 && t.block_k != 64) return fail(AXON_E_ARG, "axon_gemm: block_k must be 64");
   if (k == 0) return fail(AXON_E_SHAPE, "axon_gemm: k == 0 not supported");
@@ -513,7 +844,12 @@ int gemm_impl(const void* a, const void* b, const void* b2, void* c, const float
   }
   if (bn != 64 && bn != 128 && bn != 256) return fail(AXON_E_ARG, "axon_gemm: block_n must be 64, 128 or 256");
   if (epilogue == AXON_EPI_SILU_GATE && bn == 64) return fail(AXON_E_ARG, "axon_gemm: SILU_GATE needs block_n >= 128");
-  const int smax = max_stages(bn);
+  // variant 1: one CTA per 128-row tile; 2: CTA pairs on 256-row tiles; 0
+  // (default): pairs unless the 256-row tiling would add a mostly empty tile
+  // (m % 256 in 1..128) or block_n is 64.
+  const bool pair = t.variant == 2 || (t.variant == 0 && bn >= 128 && m >= 256 && (m % 256 == 0 || m % 256 > 128));
+  if (pair && bn == 64) return fail(AXON_E_ARG, "axon_gemm: the CTA-pair variant needs block_n >= 128");
+  const int smax = max_stages(pair ? bn / 2 : bn);
   int stages = t.stages > 0 ? t.stages : smax;
   if (stages < 2 || stages > smax) return fail(AXON_E_ARG, "axon_gemm: stages must be in [2, %d] for block_n %d", smax, bn);
 
@@ -542,18 +878,19 @@ int gemm_impl(const void* a, const void* b, const void* b2, void* c, const float
   gp.max_ctas = t.max_ctas;
   if (t.max_ctas < 0) return fail(AXON_E_ARG, "axon_gemm: max_ctas must be >= 0");
   const uint32_t fmt = ab_dtype == AXON_BF16 ? 1u : 0u;
+  const uint32_t mma_m = pair ? 2 * BM : BM;  // a CTA pair issues M = 256
   gp.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | (0u << 15) | (1u << 16) |
-             (static_cast<uint32_t>(bn >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
+             (static_cast<uint32_t>(bn >> 3) << 17) | ((mma_m >> 4) << 24);
   cudaStream_t s = as_stream(stream);
   switch (epilogue * 4 + (bn == 64 ? 0 : bn == 128 ? 1 : 2)) {
-    case 0: return dispatch_c<64, AXON_EPI_NONE>(c_dtype, ma, mb, mb2, gp, s);
-    case 1: return dispatch_c<128, AXON_EPI_NONE>(c_dtype, ma, mb, mb2, gp, s);
-    case 2: return dispatch_c<256, AXON_EPI_NONE>(c_dtype, ma, mb, mb2, gp, s);
-    case 4: return dispatch_c<64, AXON_EPI_ROWSCALE>(c_dtype, ma, mb, mb2, gp, s);
-    case 5: return dispatch_c<128, AXON_EPI_ROWSCALE>(c_dtype, ma, mb, mb2, gp, s);
-    case 6: return dispatch_c<256, AXON_EPI_ROWSCALE>(c_dtype, ma, mb, mb2, gp, s);
-    case 9: return dispatch_c<128, AXON_EPI_SILU_GATE>(c_dtype, ma, mb, mb2, gp, s);
-    case 10: return dispatch_c<256, AXON_EPI_SILU_GATE>(c_dtype, ma, mb, mb2, gp, s);
+    case 0: return dispatch_c<64, AXON_EPI_NONE>(c_dtype, pair, ma, mb, mb2, gp, s);
+    case 1: return dispatch_c<128, AXON_EPI_NONE>(c_dtype, pair, ma, mb, mb2, gp, s);
+    case 2: return dispatch_c<256, AXON_EPI_NONE>(c_dtype, pair, ma, mb, mb2, gp, s);
+    case 4: return dispatch_c<64, AXON_EPI_ROWSCALE>(c_dtype, pair, ma, mb, mb2, gp, s);
+    case 5: return dispatch_c<128, AXON_EPI_ROWSCALE>(c_dtype, pair, ma, mb, mb2, gp, s);
+    case 6: return dispatch_c<256, AXON_EPI_ROWSCALE>(c_dtype, pair, ma, mb, mb2, gp, s);
+    case 9: return dispatch_c<128, AXON_EPI_SILU_GATE>(c_dtype, pair, ma, mb, mb2, gp, s);
+    case 10: return dispatch_c<256, AXON_EPI_SILU_GATE>(c_dtype, pair, ma, mb, mb2, gp, s);
     default: return fail(AXON_E_ARG, "axon_gemm: unsupported tile/epilogue combination");
   }
 }

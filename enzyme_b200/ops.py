@@ -202,6 +202,10 @@ def cast(src, dtype, *, out=None):
     return dst
 
 
+def row_status(device=None) -> None:
+    check(N.lib().axon_row_status(torch.cuda.current_stream(device).cuda_stream))
+
+
 def gemm_status(device=None) -> None:
     check(N.lib().axon_gemm_status(torch.cuda.current_stream(device).cuda_stream))
 

@@ -112,6 +112,15 @@ AXON_API int axon_layernorm(const void* x, void* y, int64_t m, int64_t n, int64_
 AXON_API int axon_softmax(const void* x, void* y, int64_t m, int64_t n, int64_t ld_x,
                  int64_t ld_y, int32_t dtype, const axon_tune_t* tune, void* stream);
 
+/* Row-op variants (tune->variant) for the three calls above: 0 = rows held in
+ * registers (the default), 1 = streaming passes (any length or alignment),
+ * 2 = one warp per row staged in shared memory by bulk copies (16-byte
+ * aligned rows of at most 32 KB; tune->threads = warps per CTA x 32).
+ * Synchronise `stream` and report whether a variant-2 launch since the last
+ * call gave up on a bounded copy wait (AXON_E_TIMEOUT; the flag is cleared).
+ * No counterpart in the reference (NKI kernels have no device status). */
+AXON_API int axon_row_status(void* stream);
+
 /* ---- rotary embedding ------------------------------------------------------ */
 
 /* Axon's `rope` spec layout (kernels/rope/refs.py:26-30): four [half_d, free]
@@ -211,7 +220,13 @@ AXON_API int axon_adam(const void* param, const void* grad, const void* exp_avg,
  * or AXON_F32. fp32 accumulation in tensor memory. k and n must be multiples
  * of 8, lda/ldb/ldc multiples of 8 elements, bases 16-byte aligned (TMA).
  * row_scale: fp32 [m] for AXON_EPI_ROWSCALE, else NULL. b2: [k, n] for
- * AXON_EPI_SILU_GATE, else NULL. */
+ * AXON_EPI_SILU_GATE, else NULL.
+ * tune->variant: 1 = one CTA per 128 x block_n tile (cta_group::1);
+ * 2 = CTA pairs, a cluster of two SMs per 256 x block_n tile
+ * (cta_group::2, block_n 128 or 256); 0 (default) = 2 unless m < 256, the
+ * 256-row tiling would add a mostly empty tile, or block_n is 64.
+ * tune->stages: shared-memory ring depth (0 = deepest that fits);
+ * tune->max_ctas caps the persistent grid (CTAs, pairs count as two). */
 AXON_API int axon_gemm(const void* a, const void* b, const void* b2, void* c,
               const float* row_scale, int64_t m, int64_t n, int64_t k, int64_t lda,
               int64_t ldb, int64_t ldc, int32_t ab_dtype, int32_t c_dtype,
