@@ -196,10 +196,10 @@ class Cumsum(Workload):
             ws = torch.empty(nbytes, dtype=torch.uint8, device=dev) if nbytes else None
             self.sets.append((x, torch.empty_like(x), ws))
 
-    # the cluster scan (variant 1) is the faster of the two scan variants here
-    # (76 vs 95 us on B200); variant 0, the decoupled look-back, stays the
-    # default of the C ABI and is timed by `--workload cumsum` sweeps
-    TUNE = {"variant": 1}
+    # the library default: at 256 aligned rows it runs the row-streaming scan
+    # (variant 2: ~51 us on B200, vs 76 for the cluster scan and 85-95 for
+    # the decoupled look-back)
+    TUNE = None
 
     def launch(self, i):
         x, y, ws = self.sets[i % self.nsets]

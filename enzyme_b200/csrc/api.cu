@@ -60,20 +60,24 @@ int sm_count() {
 // TILES_IN_BLOCK_*) sweep.
 static const char* kVariants[][2] = {
     {"rmsnorm",
-     "{\"op\":\"rmsnorm\",\"variants\":[{\"id\":0,\"name\":\"row_resident\",\"knobs\":{\"threads\":[0,64,128,256,512,1024]}},"
-     "{\"id\":1,\"name\":\"row_streaming\",\"knobs\":{\"threads\":[0,128,256,512,1024]}}]}"},
+     "{\"op\":\"rmsnorm\",\"variants\":[{\"id\":0,\"name\":\"auto_bulk_or_resident\",\"knobs\":{\"threads\":[0,64,128,256,512,1024]}},"
+     "{\"id\":1,\"name\":\"row_streaming\",\"knobs\":{\"threads\":[0,128,256,512,1024]}},"
+     "{\"id\":2,\"name\":\"row_bulk_warp\",\"knobs\":{\"threads\":[0,128,256,512,1024]}}]}"},
     {"layernorm",
-     "{\"op\":\"layernorm\",\"variants\":[{\"id\":0,\"name\":\"row_resident\",\"knobs\":{\"threads\":[0,64,128,256,512,1024]}},"
-     "{\"id\":1,\"name\":\"row_streaming\",\"knobs\":{\"threads\":[0,128,256,512,1024]}}]}"},
+     "{\"op\":\"layernorm\",\"variants\":[{\"id\":0,\"name\":\"auto_bulk_or_resident\",\"knobs\":{\"threads\":[0,64,128,256,512,1024]}},"
+     "{\"id\":1,\"name\":\"row_streaming\",\"knobs\":{\"threads\":[0,128,256,512,1024]}},"
+     "{\"id\":2,\"name\":\"row_bulk_warp\",\"knobs\":{\"threads\":[0,128,256,512,1024]}}]}"},
     {"softmax",
-     "{\"op\":\"softmax\",\"variants\":[{\"id\":0,\"name\":\"row_resident\",\"knobs\":{\"threads\":[0,64,128,256,512,1024]}},"
-     "{\"id\":1,\"name\":\"row_streaming\",\"knobs\":{\"threads\":[0,128,256,512,1024]}}]}"},
+     "{\"op\":\"softmax\",\"variants\":[{\"id\":0,\"name\":\"auto_bulk_or_resident\",\"knobs\":{\"threads\":[0,64,128,256,512,1024]}},"
+     "{\"id\":1,\"name\":\"row_streaming\",\"knobs\":{\"threads\":[0,128,256,512,1024]}},"
+     "{\"id\":2,\"name\":\"row_bulk_warp\",\"knobs\":{\"threads\":[0,128,256,512,1024]}}]}"},
     {"rope",
      "{\"op\":\"rope\",\"variants\":[{\"id\":0,\"name\":\"token_blocked\",\"knobs\":{}},"
      "{\"id\":1,\"name\":\"flat_vec16\",\"knobs\":{\"threads\":[0,128,256]}}]}"},
     {"cumsum",
      "{\"op\":\"cumsum\",\"variants\":[{\"id\":0,\"name\":\"decoupled_lookback\",\"knobs\":{\"split\":[0,2048,4096,8192,16384]}},"
-     "{\"id\":1,\"name\":\"cluster_dsmem\",\"knobs\":{\"split\":[0,1,2,4,8]}}]}"},
+     "{\"id\":1,\"name\":\"cluster_dsmem\",\"knobs\":{\"split\":[0,1,2,4,8]}},"
+     "{\"id\":2,\"name\":\"row_stream\",\"knobs\":{}}]}"},
     {"adam",
      "{\"op\":\"adam\",\"variants\":[{\"id\":0,\"name\":\"grid_stride_vec\",\"knobs\":{\"threads\":[0,128,256,512]}}]}"},
     {"gemm",

@@ -424,6 +424,209 @@ int launch_cluster(const void* x, void* y, int64_t m, int64_t n, int64_t ld_x, i
   return launch_status("axon_cumsum");
 }
 
+// ---- variant 2: one CTA streams a whole row --------------------------------------
+//
+// Rows are independent, so a CTA can own a row and walk it chunk by chunk
+// with the running sum in a register: no flags, no cluster barriers, no
+// scratch. Chunks (24 KB by default) arrive in a ring of shared-memory
+// stages by 1-D bulk copies; a stage is refilled as soon as
+// its chunk has moved into registers, so up to `stages` chunks are in flight
+// per CTA, and two CTAs share an SM (the nucleus config's 256 rows all run at
+// once on 148 SMs). Per chunk: packets into registers and warp sums
+// (warp-striped packets), one CTA exchange of the warp sums, then a shuffle
+// scan per 32-packet segment written out with streaming stores. The running
+// row sum is float64.
+constexpr int kRowThreads = 512;
+constexpr int kRowMaxStages = 8;
+constexpr int kRowStageBytes = 32768;  // default chunk: 8192 fp32 or 16384 bf16 elements
+constexpr int kRowStages = 2;          // default ring depth
+constexpr int64_t kRowStreamMinRows = 128;
+
+// NW warps; `stages` chunks of SKB KB (a multiple of NW / 2 KB, so every
+// warp owns whole 32-packet segments of a chunk).
+// A segment is 32 * K consecutive packets of a warp's range, lane l holding
+// packets l*K .. l*K + K - 1 of it: one shuffle scan covers K packets.
+template <typename Tin, typename Tout, int NW, int SKB, int KREQ>
+__global__ void __launch_bounds__(NW * 32, 2) cumsum_rowstream(const Tin* __restrict__ x, Tout* __restrict__ y,
+                                                               int64_t n, int64_t ld_x, int64_t ld_y, bool vec_out,
+                                                               int stages, int* ws_status) {
+  constexpr int E = Vec<Tin>::E;
+  constexpr int64_t kRowChunk = SKB * 1024 / static_cast<int64_t>(sizeof(Tin));
+  constexpr int64_t PPW = kRowChunk / E / NW;  // packets per warp per chunk
+  constexpr int K = PPW % (32 * KREQ) == 0 ? KREQ : 1;  // whole segments per warp
+  static_assert(PPW % 32 == 0, "whole segments per warp");
+  const int kRowStages = stages;
+  extern __shared__ __align__(128) unsigned char dyn_smem[];
+  __shared__ __align__(8) uint64_t full[kRowMaxStages];
+  __shared__ float s_warp[2][NW];
+  __shared__ int s_abort;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t row = blockIdx.x;
+  const Tin* src = x + row * ld_x;
+  Tout* dst = y + row * ld_y;
+  const int64_t nchunks = (n + kRowChunk - 1) / kRowChunk;
+  constexpr int64_t kStageBytes = SKB * 1024;
+
+  // chunk c: elements [c * kRowChunk, +len); the 16-byte multiple of its bytes
+  // comes by bulk copy, a ragged tail (< 16 bytes) is read from global memory
+  auto chunk_len = [&](int64_t c) { return n - c * kRowChunk < kRowChunk ? n - c * kRowChunk : kRowChunk; };
+  auto issue = [&](int64_t c) {
+    const int st = static_cast<int>(c % kRowStages);
+    const uint32_t bytes = static_cast<uint32_t>(chunk_len(c) * static_cast<int64_t>(sizeof(Tin)) / 16 * 16);
+    if (bytes == 0) {
+      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sm100::smem_addr(&full[st])) : "memory");
+      return;
+    }
+    sm100::mbar_expect_tx(&full[st], bytes);
+    sm100::bulk_g2s(dyn_smem + st * kStageBytes, src + c * kRowChunk, bytes, &full[st]);
+  };
+
+  if (tid == 0) {
+    for (int st = 0; st < kRowStages; ++st) sm100::mbar_init(&full[st], 1);
+    s_abort = 0;
+    sm100::mbar_init_fence();
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_trigger();
+  // a caller workspace, if any, reports OK (waits that give up go to g_scan_error)
+  if (ws_status != nullptr && row == 0 && tid == 0) *ws_status = AXON_OK;
+  if (tid == 0)
+    for (int64_t c = 0; c < nchunks && c < kRowStages; ++c) issue(c);
+
+  double carry = 0.0;
+  const int64_t wp0 = static_cast<int64_t>(warp) * PPW;
+  for (int64_t c = 0; c < nchunks; ++c) {
+    const int st = static_cast<int>(c % kRowStages);
+    const int b = static_cast<int>(c & 1);
+    const int64_t len = chunk_len(c);
+    const int64_t bulk_elems = len * static_cast<int64_t>(sizeof(Tin)) / 16 * 16 / static_cast<int64_t>(sizeof(Tin));
+    const Tin* buf = reinterpret_cast<const Tin*>(dyn_smem + st * kStageBytes);
+    const Tin* gsrc = src + c * kRowChunk;
+    if (!s_abort && !sm100::mbar_wait_bounded(&full[st], static_cast<uint32_t>((c / kRowStages) & 1), kBulkWaitNs)) {
+      s_abort = 1;
+      atomicExch(&g_scan_error, AXON_E_TIMEOUT);
+    }
+    // pass 1: this thread's packets -> registers, and the warp sums. Full
+    // chunks (all but a row's last) take a path with no bounds checks.
+    constexpr int NSEG = static_cast<int>(PPW / (32 * K));
+    const bool full_chunk = len == kRowChunk;
+    const int wbase = warp * static_cast<int>(PPW) + lane * K;  // this lane's first packet
+    Vec<Tin> raw[NSEG * K];
+    float wsum = 0.f;
+#pragma unroll
+    for (int q = 0; q < NSEG * K; ++q) {
+      const int e0 = (wbase + (q / K) * 32 * K + q % K) * E;
+      if (full_chunk || e0 + E <= bulk_elems) {
+        raw[q] = *reinterpret_cast<const Vec<Tin>*>(buf + e0);
+      } else {
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const int64_t i = e0 + e;
+          raw[q].e[e] = i < bulk_elems ? buf[i] : i < len ? gsrc[i] : from_f<Tin>(0.f);
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < E; ++e) wsum += to_f(raw[q].e[e]);
+    }
+    wsum = warp_sum(wsum);
+    if (lane == 0) s_warp[b][warp] = wsum;
+    __syncthreads();
+    // the chunk is in registers: its stage takes chunk c + stages right away
+    if (tid == 0 && c + kRowStages < nchunks) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(c + kRowStages);
+    }
+    // every warp scans the NW warp sums itself (no second CTA barrier)
+    float wi = lane < NW ? s_warp[b][lane] : 0.f;
+#pragma unroll
+    for (int o = 1; o < NW; o <<= 1) {
+      const float up = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += up;
+    }
+    const float chunk_total = __shfl_sync(0xffffffffu, wi, NW - 1);
+    const float warp_excl = __shfl_sync(0xffffffffu, wi, warp > 0 ? warp - 1 : 0);
+    // The row's running sum is float64 across chunks; an output is
+    // (float)carry + its chunk-local fp32 prefix: two roundings at the
+    // output's magnitude, the rest at the (smaller) chunk-local one.
+    const float carry_f = static_cast<float>(carry);
+    float seg_carry = warp > 0 ? warp_excl : 0.f;
+    // pass 2: scan 32-packet segments and write them out
+    Tout* cdst = dst + c * kRowChunk;
+#pragma unroll
+    for (int j = 0; j < NSEG; ++j) {
+      const int e0 = (wbase + j * 32 * K) * E;
+      float v[K * E];
+#pragma unroll
+      for (int q = 0; q < K * E; ++q) v[q] = to_f(raw[j * K + q / E].e[q % E]);
+#pragma unroll
+      for (int q = 1; q < K * E; ++q) v[q] += v[q - 1];
+      const float own = v[K * E - 1];
+      float incl = own;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float up = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += up;
+      }
+      const float base = seg_carry + (incl - own);
+#pragma unroll
+      for (int q = 0; q < K * E; ++q) v[q] = carry_f + (base + v[q]);
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        if (full_chunk) store_packet<Tout, E>(cdst + e0 + k * E, v + k * E, E, vec_out);
+        else if (e0 + k * E < len) store_packet<Tout, E>(cdst + e0 + k * E, v + k * E, len - e0 - k * E, vec_out);
+      }
+      seg_carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    carry += static_cast<double>(chunk_total);
+  }
+  // copies may still be landing only if a wait gave up: let them finish
+  // before the CTA's shared memory is released (failure path only)
+  if (tid == 0 && s_abort)
+    for (int k = 0; k < 2000; ++k) __nanosleep(1000);
+}
+
+// tune: stages 2..8 (default 2), block_k = stage size in KB: 16, 24, 32
+// (default) or 48; stages x block_k at most 200 KB. Measured on B200 at
+// 256 x 128256 fp32: 51.2 us at 2 x 32 KB, 52.1 at 3 x 24, 53.7 at 4 x 16.
+template <typename Tin, typename Tout>
+int launch_rowstream(const void* x, void* y, int64_t m, int64_t n, int64_t ld_x, int64_t ld_y,
+                     const axon_tune_t& t, void* ws, cudaStream_t s) {
+  if (!aligned16(x) || (m > 1 && (ld_x * sizeof(Tin)) % 16))
+    return fail(AXON_E_UNSUPPORTED, "axon_cumsum: variant 2 needs 16-byte aligned input rows");
+  if (m > 0x7fffffffLL) return fail(AXON_E_SHAPE, "axon_cumsum: too many rows (%lld)", (long long)m);
+  const int stages = t.stages ? t.stages : kRowStages;
+  const int kb = t.block_k ? t.block_k : kRowStageBytes / 1024;
+  if (t.threads != 0 && t.threads != kRowThreads)
+    return fail(AXON_E_ARG, "axon_cumsum: variant 2 runs %d threads", kRowThreads);
+  if (stages < 2 || stages > kRowMaxStages) return fail(AXON_E_ARG, "axon_cumsum: variant 2 stages must be 2..8");
+  if ((kb != 16 && kb != 24 && kb != 32 && kb != 48) || stages * kb > 200)
+    return fail(AXON_E_ARG, "axon_cumsum: variant 2 stage size must be 16, 24, 32 or 48 KB, ring <= 200 KB");
+  const bool vec_out = aligned16(y) && (ld_y * sizeof(Tout)) % 16 == 0;
+  const size_t smem = static_cast<size_t>(stages) * kb * 1024;
+  constexpr int NW = kRowThreads / 32;
+  const bool k2 = t.split == 2;  // tune.split: packets per lane per segment (1 or 2)
+  auto kern = kb == 16   ? (k2 ? cumsum_rowstream<Tin, Tout, NW, 16, 2> : cumsum_rowstream<Tin, Tout, NW, 16, 1>)
+              : kb == 24 ? (k2 ? cumsum_rowstream<Tin, Tout, NW, 24, 2> : cumsum_rowstream<Tin, Tout, NW, 24, 1>)
+              : kb == 32 ? (k2 ? cumsum_rowstream<Tin, Tout, NW, 32, 2> : cumsum_rowstream<Tin, Tout, NW, 32, 1>)
+                         : (k2 ? cumsum_rowstream<Tin, Tout, NW, 48, 2> : cumsum_rowstream<Tin, Tout, NW, 48, 1>);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return fail(AXON_E_LAUNCH, "axon_cumsum: smem attribute: %s", cudaGetErrorString(e));
+  launch_k(kern, dim3(static_cast<unsigned>(m)), dim3(kRowThreads), smem, s, static_cast<const Tin*>(x),
+           static_cast<Tout*>(y), n, ld_x, ld_y, vec_out, stages, static_cast<int*>(ws));
+  return launch_status("axon_cumsum");
+}
+
+template <typename Tin>
+int dispatch_rowstream(int32_t out_dtype, const void* x, void* y, int64_t m, int64_t n, int64_t ld_x, int64_t ld_y,
+                       const axon_tune_t& t, void* ws, cudaStream_t s) {
+  switch (out_dtype) {
+    case AXON_F32: return launch_rowstream<Tin, float>(x, y, m, n, ld_x, ld_y, t, ws, s);
+    case AXON_BF16: return launch_rowstream<Tin, __nv_bfloat16>(x, y, m, n, ld_x, ld_y, t, ws, s);
+    default: return fail(AXON_E_UNSUPPORTED, "axon_cumsum: unsupported output dtype %d", out_dtype);
+  }
+}
+
 template <typename Tin>
 int dispatch_cluster(int32_t out_dtype, const void* x, void* y, int64_t m, int64_t n, int64_t ld_x, int64_t ld_y,
                      const axon_tune_t& t, cudaStream_t s) {
@@ -492,7 +695,7 @@ using namespace axon;
 extern "C" int64_t axon_cumsum_workspace_bytes(int64_t m, int64_t n, const axon_tune_t* tune) {
   axon_tune_t t = tune_or_default(tune);
   if (m < 0 || n < 0) return fail(AXON_E_SHAPE, "axon_cumsum_workspace_bytes: negative size");
-  if (t.variant == 1) return 0;
+  if (t.variant == 1 || t.variant == 2) return 0;
   return lookback_ws_bytes(m, n, t);
 }
 
@@ -514,10 +717,34 @@ extern "C" int axon_cumsum(const void* x, void* y, int64_t m, int64_t n, int64_t
       default: return fail(AXON_E_UNSUPPORTED, "axon_cumsum: unsupported input dtype %d", in_dtype);
     }
   }
+  if (t.variant == 2) {
+    if (t.split != 0 && t.split != 1 && t.split != 2)
+      return fail(AXON_E_ARG, "axon_cumsum: variant 2 split (packets per lane) must be 1 or 2");
+    if (m == 0 || n == 0) return AXON_OK;
+    cudaStream_t s = as_stream(stream);
+    switch (in_dtype) {
+      case AXON_F32: return dispatch_rowstream<float>(out_dtype, x, y, m, n, ld_x, ld_y, t, workspace, s);
+      case AXON_BF16:
+        return dispatch_rowstream<__nv_bfloat16>(out_dtype, x, y, m, n, ld_x, ld_y, t, workspace, s);
+      default: return fail(AXON_E_UNSUPPORTED, "axon_cumsum: unsupported input dtype %d", in_dtype);
+    }
+  }
   if (t.split != 0 && t.split != 2048 && t.split != 4096 && t.split != 8192 && t.split != 16384)
     return fail(AXON_E_ARG, "axon_cumsum: split must be one of 2048, 4096, 8192, 16384 (got %d)", t.split);
   if (t.variant != 0) return fail(AXON_E_UNSUPPORTED, "axon_cumsum: unknown variant %d", t.variant);
   if (m == 0 || n == 0) return AXON_OK;
+  // Default (variant 0 without a split): the row-streaming scan when there
+  // are enough rows to fill the GPU and the rows are 16-byte aligned; it beat
+  // the look-back scan on B200 at 256 x 128256 (51 vs 85 us), 1024 x 32768
+  // and 4096 x 4096, and lost at 64 x 1e6 (228 vs 211 us).
+  const int64_t in_size = in_dtype == AXON_F32 ? 4 : 2;
+  if (t.split == 0 && t.threads == 0 && m >= kRowStreamMinRows && aligned16(x) && (ld_x * in_size) % 16 == 0 &&
+      (in_dtype == AXON_F32 || in_dtype == AXON_BF16)) {
+    cudaStream_t s = as_stream(stream);
+    return in_dtype == AXON_F32
+               ? dispatch_rowstream<float>(out_dtype, x, y, m, n, ld_x, ld_y, t, workspace, s)
+               : dispatch_rowstream<__nv_bfloat16>(out_dtype, x, y, m, n, ld_x, ld_y, t, workspace, s);
+  }
   const int64_t need = lookback_ws_bytes(m, n, t);
   if (workspace == nullptr || workspace_bytes < need)
     return fail(AXON_E_ARG, "axon_cumsum: workspace of %lld bytes needed, got %lld", (long long)need,
@@ -531,18 +758,19 @@ extern "C" int axon_cumsum(const void* x, void* y, int64_t m, int64_t n, int64_t
 }
 
 extern "C" int axon_cumsum_status(const void* workspace, void* stream) {
-  int status = 0;
-  cudaError_t e;
-  if (workspace) {
-    e = cudaMemcpyAsync(&status, workspace, sizeof(int), cudaMemcpyDeviceToHost, as_stream(stream));
-  } else {  // the cluster variant's device status word; reading clears it
-    e = cudaMemcpyFromSymbolAsync(&status, g_scan_error, sizeof(int), 0, cudaMemcpyDeviceToHost, as_stream(stream));
-    if (e == cudaSuccess) e = cudaStreamSynchronize(as_stream(stream));
-    if (e == cudaSuccess && status != 0) {
-      const int zero = 0;
-      e = cudaMemcpyToSymbolAsync(g_scan_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, as_stream(stream));
-    }
+  int status = 0, device_word = 0;
+  cudaError_t e = cudaSuccess;
+  if (workspace) e = cudaMemcpyAsync(&status, workspace, sizeof(int), cudaMemcpyDeviceToHost, as_stream(stream));
+  // the device status word of the bulk-copy variants; reading clears it
+  if (e == cudaSuccess)
+    e = cudaMemcpyFromSymbolAsync(&device_word, g_scan_error, sizeof(int), 0, cudaMemcpyDeviceToHost,
+                                  as_stream(stream));
+  if (e == cudaSuccess) e = cudaStreamSynchronize(as_stream(stream));
+  if (e == cudaSuccess && device_word != 0) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbolAsync(g_scan_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, as_stream(stream));
   }
+  if (status == 0) status = device_word;
   if (e == cudaSuccess) e = cudaStreamSynchronize(as_stream(stream));
   if (e != cudaSuccess) return fail(AXON_E_CUDA, "axon_cumsum_status: %s", cudaGetErrorString(e));
   if (status != 0) return fail(status, "axon_cumsum: a bounded wait gave up (status %d)", status);

@@ -152,15 +152,22 @@ AXON_API int64_t axon_cumsum_workspace_bytes(int64_t m, int64_t n, const axon_tu
  * Variant 0: single-pass decoupled look-back across tiles of a row; needs
  * `workspace` (zeroed by the call itself, on `stream`); every device-side
  * wait is bounded and a wait that gives up records AXON_E_TIMEOUT in the
- * workspace status word (read it with axon_cumsum_status).
+ * workspace status word (read it with axon_cumsum_status). With no
+ * tune->split, variant 0 runs variant 2 instead when m >= 128 and the input
+ * rows are 16-byte aligned (the workspace is then unused).
  * Variant 1: one thread-block cluster per row exchanging tile sums through
- * distributed shared memory; needs no workspace. */
+ * distributed shared memory; needs no workspace.
+ * Variant 2: one CTA streams each row through a ring of shared-memory chunks
+ * filled by bulk copies (tune->stages, tune->block_k = chunk KB); needs no
+ * workspace and 16-byte aligned input rows. Variants 1 and 2 record a bulk
+ * copy wait that gave up in a device word: axon_cumsum_status(NULL, ...). */
 AXON_API int axon_cumsum(const void* x, void* y, int64_t m, int64_t n, int64_t ld_x,
                 int64_t ld_y, int32_t in_dtype, int32_t out_dtype, void* workspace,
                 int64_t workspace_bytes, const axon_tune_t* tune, void* stream);
 
-/* Synchronise `stream` and read the status word a variant-0 cumsum left in
- * `workspace`: AXON_OK or AXON_E_TIMEOUT. */
+/* Synchronise `stream` and report AXON_E_TIMEOUT if a bounded wait gave up:
+ * the status word a cumsum left in `workspace` (may be NULL) or the device
+ * word of the bulk-copy variants (read and cleared here). */
 AXON_API int axon_cumsum_status(const void* workspace, void* stream);
 
 /* Allocation-free form of axon_cumsum (variant 0 only). No counterpart in the

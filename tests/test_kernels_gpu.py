@@ -218,7 +218,7 @@ def test_rope_odd_head_dim_scalar_path(cuda_device):
 
 # ---- cumsum ------------------------------------------------------------------------------
 
-@pytest.mark.parametrize("variant,split", [(0, 0), (0, 2048), (0, 4096), (0, 16384), (1, 0), (1, 4), (1, 8)])
+@pytest.mark.parametrize("variant,split", [(0, 0), (0, 2048), (0, 4096), (0, 16384), (1, 0), (1, 4), (1, 8), (2, 0)])
 def test_cumsum_config_full_size(variant, split, cuda_device):
     spec = load_spec("cumsum_nucleus_sorted")
     (x,) = spec.make_inputs(m=256, n=128256, rng=np.random.default_rng(SEED))
@@ -239,10 +239,17 @@ def test_cumsum_config_full_size(variant, split, cuda_device):
     np.testing.assert_allclose(got[:, -1], x.astype(np.float64).sum(1), rtol=1e-6)
 
 
-@pytest.mark.parametrize("variant", [0, 1])
-@pytest.mark.parametrize("shape", [(1, 1), (3, 7), (5, 8191), (2, 8193), (64, 100000), (1024, 1024), (3, 150001)])
+@pytest.mark.parametrize("variant", [0, 1, 2])
+@pytest.mark.parametrize("shape", [(1, 1), (3, 7), (5, 8191), (2, 8193), (64, 100000), (1024, 1024), (3, 150001),
+                                   (2, 6144), (2, 6145), (7, 12290), (200, 1001), (300, 40000)])
 def test_cumsum_shapes(shape, variant, cuda_device):
     x = torch.randn(*shape, generator=torch.Generator().manual_seed(11))
+    if variant == 2 and shape[0] > 1 and shape[1] % 4:
+        # contiguous fp32 rows of n % 4 != 0 start off the 16-byte grid
+        with pytest.raises(N.AxonError) as e:
+            ops.cumsum(x.to(cuda_device), tune={"variant": variant})
+        assert e.value.code == N.AXON_E_UNSUPPORTED
+        return
     y = ops.cumsum(x.to(cuda_device), tune={"variant": variant})
     want = f64.cumsum(x.numpy())
     scale = np.sqrt(np.arange(1, shape[1] + 1))[None, :]
@@ -250,13 +257,20 @@ def test_cumsum_shapes(shape, variant, cuda_device):
     assert err.max() < 1e-5
 
 
-@pytest.mark.parametrize("variant", [0, 1])
+@pytest.mark.parametrize("variant", [0, 1, 2])
 def test_cumsum_bf16_in_fp32_out_and_strided(variant, cuda_device):
-    base = torch.randn(16, 3000, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16).to(cuda_device)
-    x = base[:, :2992]
+    base = torch.randn(16, 30000, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16).to(cuda_device)
+    x = base[:, :29992]
     y = ops.cumsum(x, out_dtype=torch.float32, tune={"variant": variant})
     np.testing.assert_allclose(_np(y), f64.cumsum(_np(x)), rtol=1e-5, atol=1e-4)
+    ybf = ops.cumsum(x, tune={"variant": variant})  # bf16 out: one rounding of the float64 sum
+    np.testing.assert_allclose(_np(ybf), f64.cumsum(_np(x)), rtol=2 ** -8, atol=1e-2)
     xb = base[:, 1:2990]  # rows off the 16-byte grid: plain loads, no bulk copy
+    if variant == 2:
+        with pytest.raises(N.AxonError) as e:
+            ops.cumsum(xb, out_dtype=torch.float32, tune={"variant": variant})
+        assert e.value.code == N.AXON_E_UNSUPPORTED
+        return
     yb = ops.cumsum(xb, out_dtype=torch.float32, tune={"variant": variant})
     np.testing.assert_allclose(_np(yb), f64.cumsum(_np(xb)), rtol=1e-5, atol=1e-4)
 
