@@ -33,6 +33,8 @@ AXON_EPI_NONE = 0
 AXON_EPI_ROWSCALE = 1
 AXON_EPI_SILU_GATE = 2
 
+AXON_IPC_HANDLE_BYTES = 64
+
 _CODE_NAMES = {
     AXON_E_SHAPE: "AXON_E_SHAPE",
     AXON_E_ALIGN: "AXON_E_ALIGN",
@@ -124,6 +126,14 @@ SIGNATURES: dict[str, tuple] = {
     "axon_row_status": (_I32, [_P]),
     "axon_rmsnorm_matmul": (_I32, [_P, _P, _P, _P, _I64, _I64, _I64, _I32, _I32, _TUNE, _P]),
     "axon_silu_mlp_workspace_bytes": (_I64, [_I64, _I64, _I64, _I32, _TUNE]),
+    "axon_ipc_handle": (_I32, [_P, _P, ctypes.POINTER(_I64)]),
+    "axon_ipc_open": (_I32, [_P, _I64, ctypes.POINTER(_P)]),
+    "axon_ipc_close": (_I32, [_P, _I64]),
+    "axon_tp_down_partial": (_I32, [_P, _P, _P, _I32, _I32, _I64, _I64, _I64, _I64, _I32, _TUNE, _P]),
+    "axon_tp_signal": (_I32, [_P, _I32, _I32, _I32, _P]),
+    "axon_tp_wait": (_I32, [_P, _I32, _I32, _P]),
+    "axon_tp_reduce_gather": (_I32, [_P, _P, _P, _I32, _I32, _I32, _I64, _I64, _I64, _I64, _I32, _I32, _P]),
+    "axon_tp_status": (_I32, [_P]),
     "axon_silu_mlp": (
         _I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I32, _I32, _TUNE, _P]
     ),

@@ -180,8 +180,18 @@ __device__ __forceinline__ void store32(TC* dst, const float* v, int64_t col, in
   }
 }
 
+// Epilogue of the tensor-parallel down projection (internal to
+// axon_tp_down_partial, not an axon_gemm epilogue): output row r goes to the
+// inbox of its owner rank o = r / rows_per_owner, a peer buffer laid out
+// [world][rows_per_owner][ldc], at slot `peer_rank`.
+constexpr int kEpiPeer = 3;
+constexpr int kMaxPeers = 8;
+
 struct GemmParams {
   void* c;
+  void* peers[kMaxPeers];  // kEpiPeer: each owner's inbox for this output
+  int peer_rank;
+  int rows_per_owner;
   const float* row_scale;
   int m, n, k;         // n = output columns
   int64_t ldc;
@@ -192,6 +202,54 @@ struct GemmParams {
   int b_kwrap;         // > 0: B's k coordinate wraps modulo this (B re-read per term)
   int max_ctas;        // > 0: cap on the persistent grid
 };
+
+template <int EPI, typename TC>
+__device__ __forceinline__ TC* out_row(const GemmParams& p, TC* C, int64_t row) {
+  if constexpr (EPI == kEpiPeer) {
+    const int o = static_cast<int>(row / p.rows_per_owner);
+    const int64_t local = static_cast<int64_t>(p.peer_rank) * p.rows_per_owner + (row - static_cast<int64_t>(o) * p.rows_per_owner);
+    return static_cast<TC*>(p.peers[o]) + local * p.ldc;
+  } else {
+    return C + row * p.ldc;
+  }
+}
+
+constexpr int kPeerStageHalves = 72;                              // 64 columns + 8 of padding per row
+constexpr int kPeerStageBytes = 4 * 32 * kPeerStageHalves * 2;    // one 32-row piece per epilogue warp
+
+// kEpiPeer: the warp's 32 accumulator rows leave in 64-column pieces through a
+// shared-memory transpose, so each store instruction writes 4 rows x 128
+// contiguous bytes of an owner's inbox: whole lines cross NVLink instead of
+// 32 scattered 16-byte pieces.
+template <int BN>
+__device__ __forceinline__ void peer_store_tile(const GemmParams& p, __half* stg, uint32_t tbase, int64_t row0,
+                                                int64_t col0, int lane) {
+#pragma unroll 1
+  for (int c = 0; c < BN / 64; ++c) {
+    float v[64];
+    __syncwarp();
+    tmem_ld32(tbase + c * 64, v);
+    tmem_ld32(tbase + c * 64 + 32, v + 32);
+    tmem_wait_ld();
+    __half* mine = stg + lane * kPeerStageHalves;
+#pragma unroll
+    for (int j = 0; j < 64; j += 8) {
+      Vec<__half> pk;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) pk.e[e] = __float2half_rn(v[j + e]);
+      *reinterpret_cast<uint4*>(mine + j) = pk.u;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int r = it * 4 + (lane >> 3), seg = lane & 7;
+      const int64_t row = row0 + r;
+      const int64_t col = col0 + c * 64 + seg * 8;
+      const uint4 val = *reinterpret_cast<const uint4*>(stg + r * kPeerStageHalves + seg * 8);
+      if (row < p.m && col < p.n) *reinterpret_cast<uint4*>(out_row<kEpiPeer, __half>(p, nullptr, row) + col) = val;
+    }
+  }
+}
 
 template <int BN, int EPI, typename TC>
 __global__ void __launch_bounds__(192, 1)
@@ -329,7 +387,7 @@ __global__ void __launch_bounds__(192, 1)
       const int64_t row = static_cast<int64_t>(tm) * BM + q * 32 + lane;
       const bool row_ok = row < p.m;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN);
-      TC* crow = C + (row_ok ? row : 0) * p.ldc;
+      TC* crow = out_row<EPI, TC>(p, C, row_ok ? row : 0);
       float scale = 1.f;
       if constexpr (EPI == AXON_EPI_ROWSCALE) scale = row_ok ? p.row_scale[row] : 0.f;
       if constexpr (EPI == AXON_EPI_SILU_GATE) {
@@ -363,6 +421,10 @@ __global__ void __launch_bounds__(192, 1)
             }
           }
         }
+      } else if constexpr (EPI == kEpiPeer) {
+        __half* stg = reinterpret_cast<__half*>(smem + S * STAGE + 256) + q * 32 * kPeerStageHalves;
+        peer_store_tile<BN>(p, stg, tbase, static_cast<int64_t>(tm) * BM + q * 32, static_cast<int64_t>(tn) * BN,
+                            lane);
       } else {
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
@@ -605,7 +667,7 @@ __global__ void __launch_bounds__(192, 1)
       const int64_t row = static_cast<int64_t>(tm) * 2 * BM + static_cast<int64_t>(rank) * BM + q * 32 + lane;
       const bool row_ok = row < p.m;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN);
-      TC* crow = C + (row_ok ? row : 0) * p.ldc;
+      TC* crow = out_row<EPI, TC>(p, C, row_ok ? row : 0);
       float scale = 1.f;
       if constexpr (EPI == AXON_EPI_ROWSCALE) scale = row_ok ? p.row_scale[row] : 0.f;
       if constexpr (EPI == AXON_EPI_SILU_GATE) {
@@ -636,6 +698,11 @@ __global__ void __launch_bounds__(192, 1)
             }
           }
         }
+      } else if constexpr (EPI == kEpiPeer) {
+        __half* stg = reinterpret_cast<__half*>(smem + S * STAGE + 256) + q * 32 * kPeerStageHalves;
+        peer_store_tile<BN>(p, stg,
+                            tbase, static_cast<int64_t>(tm) * 2 * BM + static_cast<int64_t>(rank) * BM + q * 32,
+                            static_cast<int64_t>(tn) * BN, lane);
       } else {
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
@@ -708,7 +775,7 @@ template <int BN, int EPI, typename TC>
 int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb2, const GemmParams& gp,
                 cudaStream_t s) {
   constexpr int STAGE = A_BYTES + BN * BK * 2;
-  const size_t smem = static_cast<size_t>(gp.stages) * STAGE + 1024 + 256;
+  const size_t smem = static_cast<size_t>(gp.stages) * STAGE + 1024 + 256 + (EPI == kEpiPeer ? kPeerStageBytes : 0);
   auto kern = gemm_tcgen05<BN, EPI, TC>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return fail(AXON_E_LAUNCH, "axon_gemm: smem attribute: %s", cudaGetErrorString(e));
@@ -728,7 +795,7 @@ template <int BN, int EPI, typename TC>
 int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb2, const GemmParams& gp,
                      cudaStream_t s) {
   constexpr int STAGE = A_BYTES + (BN / 2) * BK * 2;
-  const size_t smem = static_cast<size_t>(gp.stages) * STAGE + 1024 + 256;
+  const size_t smem = static_cast<size_t>(gp.stages) * STAGE + 1024 + 256 + (EPI == kEpiPeer ? kPeerStageBytes : 0);
   auto kern = gemm_tcgen05_pair<BN, EPI, TC>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return fail(AXON_E_LAUNCH, "axon_gemm: smem attribute: %s", cudaGetErrorString(e));
@@ -789,9 +856,9 @@ int dispatch_c(int32_t c_dtype, bool pair, const CUtensorMap& ma, const CUtensor
 
 // Deepest ring that fits the 227 KB of shared memory; `b_cols` = B columns
 // staged per CTA (block_n, or block_n / 2 for a CTA pair).
-int max_stages(int b_cols) {
+int max_stages(int b_cols, int extra = 0) {
   const int stage = A_BYTES + b_cols * BK * 2;
-  const int avail = 232448 - 1024 - 256;
+  const int avail = 232448 - 1024 - 256 - extra;
   int s = avail / stage;
   return s > 8 ? 8 : s;
 }
@@ -808,9 +875,13 @@ namespace {
 // the activation as that many split terms, `term_stride` columns apart) and
 // `b_kwrap` (the k coordinate of B wraps modulo b_kwrap, so a K = terms * n
 // contraction re-reads the same [n, p] weight once per term).
+//
+// `peers` (with world, peer_rank, rows_per_owner) switches the epilogue to the
+// tensor-parallel inbox scatter of axon_tp_down_partial; C is then unused.
 int gemm_impl(const void* a, const void* b, const void* b2, void* c, const float* row_scale, int64_t m, int64_t n,
               int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int32_t ab_dtype, int32_t c_dtype, int32_t epilogue,
-              const axon_tune_t* tune, void* stream, int terms, int64_t term_stride, int64_t b_kwrap) {
+              const axon_tune_t* tune, void* stream, int terms, int64_t term_stride, int64_t b_kwrap,
+              void* const* peers = nullptr, int world = 0, int peer_rank = 0, int64_t rows_per_owner = 0) {
   axon_tune_t t = tune_or_default(tune);
   if (m < 0 || n < 0 || k < 0) return fail(AXON_E_SHAPE, "axon_gemm: negative size");
   if (m == 0 || n == 0) return AXON_OK;  // empty output: nothing to launch, pointers may be NULL
@@ -849,7 +920,7 @@ int gemm_impl(const void* a, const void* b, const void* b2, void* c, const float
   // (m % 256 in 1..128) or block_n is 64.
   const bool pair = t.variant == 2 || (t.variant == 0 && bn >= 128 && m >= 256 && (m % 256 == 0 || m % 256 > 128));
   if (pair && bn == 64) return fail(AXON_E_ARG, "axon_gemm: the CTA-pair variant needs block_n >= 128");
-  const int smax = max_stages(pair ? bn / 2 : bn);
+  const int smax = max_stages(pair ? bn / 2 : bn, peers != nullptr ? kPeerStageBytes : 0);
   int stages = t.stages > 0 ? t.stages : smax;
   if (stages < 2 || stages > smax) return fail(AXON_E_ARG, "axon_gemm: stages must be in [2, %d] for block_n %d", smax, bn);
 
@@ -864,7 +935,12 @@ int gemm_impl(const void* a, const void* b, const void* b2, void* c, const float
   } else {
     mb2 = mb;
   }
-  GemmParams gp;
+  GemmParams gp{};
+  if (peers != nullptr) {
+    for (int i = 0; i < world; ++i) gp.peers[i] = peers[i];
+    gp.peer_rank = peer_rank;
+    gp.rows_per_owner = static_cast<int>(rows_per_owner);
+  }
   gp.c = c;
   gp.row_scale = row_scale;
   gp.m = static_cast<int>(m);
@@ -882,6 +958,14 @@ int gemm_impl(const void* a, const void* b, const void* b2, void* c, const float
   gp.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | (0u << 15) | (1u << 16) |
              (static_cast<uint32_t>(bn >> 3) << 17) | ((mma_m >> 4) << 24);
   cudaStream_t s = as_stream(stream);
+  if (peers != nullptr) {
+    if (bn == 64) return fail(AXON_E_ARG, "axon_tp_down_partial: block_n must be 128 or 256");
+    if (bn == 128)
+      return pair ? launch_gemm_pair<128, kEpiPeer, __half>(ma, mb, mb2, gp, s)
+                  : launch_gemm<128, kEpiPeer, __half>(ma, mb, mb2, gp, s);
+    return pair ? launch_gemm_pair<256, kEpiPeer, __half>(ma, mb, mb2, gp, s)
+                : launch_gemm<256, kEpiPeer, __half>(ma, mb, mb2, gp, s);
+  }
   switch (epilogue * 4 + (bn == 64 ? 0 : bn == 128 ? 1 : 2)) {
     case 0: return dispatch_c<64, AXON_EPI_NONE>(c_dtype, pair, ma, mb, mb2, gp, s);
     case 1: return dispatch_c<128, AXON_EPI_NONE>(c_dtype, pair, ma, mb, mb2, gp, s);
@@ -903,6 +987,23 @@ extern "C" int axon_gemm(const void* a, const void* b, const void* b2, void* c, 
                          int32_t c_dtype, int32_t epilogue, const axon_tune_t* tune, void* stream) {
   return gemm_impl(a, b, b2, c, row_scale, m, n, k, lda, ldb, ldc, ab_dtype, c_dtype, epilogue, tune, stream, 1, 0,
                    0);
+}
+
+extern "C" int axon_tp_down_partial(const void* act, const void* w, void* const* inboxes, int32_t world,
+                                    int32_t rank, int64_t m, int64_t n, int64_t k, int64_t rows_per_owner,
+                                    int32_t ab_dtype, const axon_tune_t* tune, void* stream) {
+  if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world)
+    return fail(AXON_E_ARG, "axon_tp_down_partial: world must be 1..%d and 0 <= rank < world", kMaxPeers);
+  if (m < 0 || n < 0 || k < 0) return fail(AXON_E_SHAPE, "axon_tp_down_partial: negative size");
+  if (m == 0 || n == 0) return AXON_OK;
+  if (!inboxes) return fail(AXON_E_ARG, "axon_tp_down_partial: NULL inbox table");
+  if (rows_per_owner <= 0 || rows_per_owner * world != m)
+    return fail(AXON_E_SHAPE, "axon_tp_down_partial: m (%lld) must be world x rows_per_owner", (long long)m);
+  for (int i = 0; i < world; ++i)
+    if (!inboxes[i] || !aligned16(inboxes[i])) return fail(AXON_E_ALIGN, "axon_tp_down_partial: inbox %d NULL or unaligned", i);
+  // C is never written on this path; pass a valid pointer for the argument checks
+  return gemm_impl(act, w, nullptr, inboxes[0], nullptr, m, n, k, k, n, n, ab_dtype, AXON_F16, AXON_EPI_NONE, tune,
+                   stream, 1, 0, 0, inboxes, world, rank, rows_per_owner);
 }
 
 extern "C" int axon_gemm_status(void* stream) {

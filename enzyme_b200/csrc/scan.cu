@@ -495,7 +495,6 @@ __global__ void __launch_bounds__(NW * 32, 2) cumsum_rowstream(const Tin* __rest
     for (int64_t c = 0; c < nchunks && c < kRowStages; ++c) issue(c);
 
   double carry = 0.0;
-  const int64_t wp0 = static_cast<int64_t>(warp) * PPW;
   for (int64_t c = 0; c < nchunks; ++c) {
     const int st = static_cast<int>(c % kRowStages);
     const int b = static_cast<int>(c & 1);

@@ -144,3 +144,202 @@ def adam_shard(total: int, rank: int, world: int) -> slice:
     """The contiguous slice of a flat parameter vector this rank updates."""
     a, b = shard_range(total, rank, world)
     return slice(a, b)
+
+
+# ---- fused path: reduce-scatter in the down GEMM's epilogue, over peer memory ----
+
+
+def fused_slabs(m: int, world: int, slabs: int) -> list[tuple[int, int]]:
+    """Token slabs for the fused path: contiguous, each a multiple of `world`
+    rows so every rank owns the same number of rows of every slab."""
+    if m % world:
+        raise ValueError(f"m={m} must be a multiple of world={world}")
+    slabs = max(1, min(int(slabs), m // world))
+    unit = m // world
+    per = -(-unit // slabs) * world
+    return [(a, min(m, a + per)) for a in range(0, m, per)]
+
+
+@dataclass(frozen=True)
+class PeerLayout:
+    """Byte offsets inside each rank's shared buffer: the f16 inboxes (slab i
+    at its first row: [world][rows_i / world][hidden]), the output [m, hidden]
+    and int32 flags (arrive[i][world], done[i][world])."""
+
+    m: int
+    hidden: int
+    world: int
+    nslabs: int
+    out_itemsize: int
+
+    @property
+    def inbox_bytes(self) -> int:
+        return self.m * self.hidden * 2
+
+    @property
+    def y_offset(self) -> int:
+        return _round_up(self.inbox_bytes, 256)
+
+    @property
+    def flags_offset(self) -> int:
+        return _round_up(self.y_offset + self.m * self.hidden * self.out_itemsize, 256)
+
+    @property
+    def total_bytes(self) -> int:
+        return _round_up(self.flags_offset + 2 * self.nslabs * self.world * 4, 256)
+
+    def inbox_offset(self, slab_start: int) -> int:
+        return slab_start * self.hidden * 2
+
+    def arrive_offset(self, i: int) -> int:
+        return self.flags_offset + (2 * i) * self.world * 4
+
+    def done_offset(self, i: int) -> int:
+        return self.flags_offset + (2 * i + 1) * self.world * 4
+
+
+def _round_up(x: int, a: int) -> int:
+    return -(-x // a) * a
+
+
+class PeerBuffers:
+    """One zeroed device buffer per rank (PeerLayout), mapped into every other
+    rank with CUDA IPC; `bases[d]` is rank d's buffer as seen from this rank."""
+
+    def __init__(self, layout: PeerLayout, device, group=None):
+        import ctypes
+
+        from . import _native as N
+
+        self.layout = layout
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if self.world != layout.world:
+            raise ValueError("layout world size differs from the process group")
+        self.buf = torch.zeros(layout.total_bytes, dtype=torch.uint8, device=device)
+        torch.cuda.synchronize(device)
+        handle = ctypes.create_string_buffer(N.AXON_IPC_HANDLE_BYTES)
+        off = ctypes.c_int64(0)
+        N.check(N.lib().axon_ipc_handle(ctypes.c_void_p(self.buf.data_ptr()), handle, ctypes.byref(off)))
+        mine = (bytes(handle.raw), int(off.value))
+        everyone = [None] * self.world
+        if self.world > 1:
+            dist.all_gather_object(everyone, mine, group=group)
+        else:
+            everyone = [mine]
+        self._opened = []
+        self.bases = []
+        for d, (h, o) in enumerate(everyone):
+            if d == self.rank:
+                self.bases.append(self.buf.data_ptr())
+                continue
+            p = ctypes.c_void_p()
+            N.check(N.lib().axon_ipc_open(h, o, ctypes.byref(p)))
+            self._opened.append((p.value, o))
+            self.bases.append(p.value)
+        if self.world > 1:
+            dist.barrier(group=group)
+
+    def close(self) -> None:
+        from . import _native as N
+
+        for p, o in self._opened:
+            N.lib().axon_ipc_close(p, o)
+        self._opened = []
+
+    def output(self, dtype) -> torch.Tensor:
+        lo = self.layout
+        nbytes = lo.m * lo.hidden * lo.out_itemsize
+        return self.buf[lo.y_offset:lo.y_offset + nbytes].view(dtype).view(lo.m, lo.hidden)
+
+
+class FusedTPSwiGLU:
+    """Tensor-parallel SwiGLU whose down-projection all-reduce is fused into
+    the GEMMs over NVLink peer memory (csrc/tp.cu):
+
+    per slab: SiLU-gate GEMM -> f16 activation; down GEMM whose epilogue
+    stores each f16 partial row into its owner rank's inbox; a release of the
+    slab's arrival flags; on a side stream the owner waits for every rank's
+    partials, sums them in fp32, rounds once to bf16 and pushes its rows into
+    every rank's output, then raises the done flags. forward() ends with a
+    bounded wait on every owner's done flag, so the returned [m, hidden]
+    tensor (a view of the shared buffer, valid until the next forward) holds
+    the full output on every rank. The output is one rounding of the fp32 sum
+    of world f16-rounded partials.
+    """
+
+    def __init__(self, w_gate, w_up, w_down, m: int, *, group=None, slabs: int = 2, tune=None,
+                 reduce_ctas: int = 16, out_dtype=torch.bfloat16):
+        self.w_gate, self.w_up, self.w_down = w_gate, w_up, w_down
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.m = m
+        self.hidden = w_down.shape[1]
+        self.slabs = fused_slabs(m, self.world, slabs)
+        self.tune = dict(tune or {})
+        self.reduce_ctas = int(reduce_ctas)
+        self.out_dtype = out_dtype
+        dev = w_gate.device
+        self.layout = PeerLayout(m, self.hidden, self.world, len(self.slabs), torch.empty(0, dtype=out_dtype).element_size())
+        self.peers = PeerBuffers(self.layout, dev, group)
+        self.y = self.peers.output(out_dtype)
+        self.w_down_h = torch.empty(w_down.shape, dtype=torch.float16, device=dev)
+        self.act = torch.empty((m, w_gate.shape[1]), dtype=torch.float16, device=dev)
+        self.side = torch.cuda.Stream(device=dev)
+        self.epoch = 0
+
+    def close(self) -> None:
+        torch.cuda.synchronize(self.w_gate.device)
+        self.peers.close()
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        import ctypes
+
+        from . import _native as N
+        from . import ops
+
+        if x.shape[0] != self.m:
+            raise ValueError(f"built for {self.m} tokens, got {x.shape[0]}")
+        lib, lo, W = N.lib(), self.layout, self.world
+        self.epoch += 1
+        e = self.epoch
+        main = torch.cuda.current_stream(x.device)
+        ptrs = lambda vals: (ctypes.c_void_p * W)(*vals)  # noqa: E731
+        tune = N.Tune.of(self.tune)
+        out_code = {torch.bfloat16: N.AXON_BF16, torch.float16: N.AXON_F16, torch.float32: N.AXON_F32}[self.out_dtype]
+        ops.cast(self.w_down, torch.float16, out=self.w_down_h)
+        y_ptrs = ptrs([b + lo.y_offset for b in self.peers.bases])
+        for i, (a, b) in enumerate(self.slabs):
+            rows = (b - a) // W
+            ops.gemm(x[a:b], self.w_gate, b2=self.w_up, epilogue=N.AXON_EPI_SILU_GATE, out=self.act[a:b],
+                     tune=self.tune)
+            inboxes = ptrs([base + lo.inbox_offset(a) for base in self.peers.bases])
+            N.check(lib.axon_tp_down_partial(self.act[a:b].data_ptr(), self.w_down_h.data_ptr(), inboxes, W,
+                                             self.rank, b - a, self.hidden, self.act.shape[1], rows, N.AXON_F16,
+                                             tune, main.cuda_stream))
+            N.check(lib.axon_tp_signal(ptrs([base + lo.arrive_offset(i) for base in self.peers.bases]), W,
+                                       self.rank, e, main.cuda_stream))
+            # earlier slabs reduce on a side stream with a small grid, beside
+            # the next slab's GEMMs; the last slab has the whole GPU
+            last = i == len(self.slabs) - 1
+            st = main if last else self.side
+            if not last:
+                self.side.wait_stream(main)
+            mine = self.peers.bases[self.rank]
+            N.check(lib.axon_tp_reduce_gather(mine + lo.inbox_offset(a), y_ptrs, mine + lo.arrive_offset(i), W,
+                                              self.rank, e, rows, self.hidden, a, self.hidden, out_code,
+                                              0 if last else self.reduce_ctas, st.cuda_stream))
+            N.check(lib.axon_tp_signal(ptrs([base + lo.done_offset(i) for base in self.peers.bases]), W,
+                                       self.rank, e, st.cuda_stream))
+        main.wait_stream(self.side)
+        mine = self.peers.bases[self.rank]
+        for i in range(len(self.slabs)):
+            N.check(lib.axon_tp_wait(mine + lo.done_offset(i), W, e, main.cuda_stream))
+        return self.y
+
+    def status(self) -> None:
+        from . import _native as N
+
+        N.check(N.lib().axon_tp_status(torch.cuda.current_stream(self.w_gate.device).cuda_stream))

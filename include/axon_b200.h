@@ -243,6 +243,61 @@ AXON_API int axon_gemm(const void* a, const void* b, const void* b2, void* c,
  * on a bounded pipeline wait (AXON_E_TIMEOUT; the flag is then cleared). */
 AXON_API int axon_gemm_status(void* stream);
 
+/* ---- tensor-parallel SwiGLU over NVLink peer memory ----------------------- */
+
+/* The reference's TP MLP resolves the down projection's Partial(+) output with
+ * a terminal all-reduce (src/axon/sharding.py:380-384, :514-522). These calls
+ * replace that all-reduce with a reduce-scatter fused into the down-projection
+ * GEMM plus an owner-side reduce and all-gather push, all over peer memory
+ * shared by CUDA IPC. The reference has no counterpart entry points (its
+ * collectives are NKI/Neuron runtime calls); the host sequence is
+ * enzyme_b200/tp.py `TPSwiGLU(fused=True)`. */
+
+#define AXON_IPC_HANDLE_BYTES 64
+
+/* IPC handle of the allocation holding dev_ptr, and dev_ptr's byte offset in
+ * it (torch allocations are sub-ranges of larger device allocations). */
+AXON_API int axon_ipc_handle(const void* dev_ptr, void* handle, int64_t* offset);
+/* Map a peer process's allocation; *dev_ptr = its base + offset. A process
+ * cannot open its own handle. */
+AXON_API int axon_ipc_open(const void* handle, int64_t offset, void** dev_ptr);
+AXON_API int axon_ipc_close(void* dev_ptr, int64_t offset);
+
+/* Down projection of one token slab on rank `rank` of `world` (<= 8):
+ * partial = act [m, k] @ w [k, n] (bf16 x bf16 or f16 x f16, fp32
+ * accumulation in TMEM), rounded to f16, with row r written by the GEMM
+ * epilogue straight into owner o = r / rows_per_owner's inbox
+ * inboxes[o] (a peer or local buffer laid out [world][rows_per_owner][n] f16)
+ * at [rank][r - o * rows_per_owner]. m = world * rows_per_owner. tune as
+ * axon_gemm's. */
+AXON_API int axon_tp_down_partial(const void* act, const void* w, void* const* inboxes, int32_t world,
+                         int32_t rank, int64_t m, int64_t n, int64_t k, int64_t rows_per_owner,
+                         int32_t ab_dtype, const axon_tune_t* tune, void* stream);
+
+/* After the work already on `stream`: a system-scope fence, then
+ * flags[d][rank] = epoch (release) for every rank d (flags[d] = int32[world]
+ * on rank d, peer-mapped). */
+AXON_API int axon_tp_signal(int32_t* const* flags, int32_t world, int32_t rank, int32_t epoch,
+                   void* stream);
+
+/* Bounded wait (~2 s) on `stream` until flags[s] >= epoch for every s <
+ * world; a wait that gives up records AXON_E_TIMEOUT for axon_tp_status. */
+AXON_API int axon_tp_wait(const int32_t* flags, int32_t world, int32_t epoch, void* stream);
+
+/* Owner side: wait (bounded) until arrive[s] >= epoch for all s, then
+ * y_i = sum_s inbox[s][i] (fp32, in rank order, one rounding to out_dtype)
+ * for the rows_per_owner x n rows of this rank, stored to every rank's output:
+ * outs[d] + (out_row0 + rank * rows + i) * ld_out. max_ctas caps the grid
+ * (0 = 2 x SMs) so it can run beside a GEMM. */
+AXON_API int axon_tp_reduce_gather(const void* inbox, void* const* outs, const int32_t* arrive,
+                          int32_t world, int32_t rank, int32_t epoch, int64_t rows, int64_t n,
+                          int64_t out_row0, int64_t ld_out, int32_t out_dtype, int32_t max_ctas,
+                          void* stream);
+
+/* Synchronise `stream`; AXON_E_TIMEOUT if a tensor-parallel flag wait gave up
+ * since the last call (the record is then cleared). */
+AXON_API int axon_tp_status(void* stream);
+
 /* dst[i] = src[i] converted from src_dtype to dst_dtype (AXON_F32 / AXON_BF16 /
  * AXON_F16; round to nearest even), n elements, contiguous. No counterpart in
  * Axon's specs: the tensor-parallel SwiGLU step uses it to make the f16 copy

@@ -139,3 +139,24 @@ def test_sharded_adam_two_ranks_equals_unsharded():
         p.join(timeout=120)
     assert all(p.exitcode == 0 for p in procs)
     assert max(q.get(timeout=5) for _ in range(2)) == 0.0
+
+
+def test_fused_slabs_and_layout():
+    assert tp.fused_slabs(4096, 8, 2) == [(0, 2048), (2048, 4096)]
+    assert tp.fused_slabs(1024, 2, 3) == [(0, 342), (342, 684), (684, 1024)]
+    for m, w, s in [(4096, 8, 4), (1000, 4, 3), (64, 8, 16)]:
+        sl = tp.fused_slabs(m, w, s)
+        assert sl[0][0] == 0 and sl[-1][1] == m
+        assert all(b > a and (b - a) % w == 0 for a, b in sl)
+        assert all(sl[i][1] == sl[i + 1][0] for i in range(len(sl) - 1))
+    with pytest.raises(ValueError):
+        tp.fused_slabs(1001, 4, 2)
+    lo = tp.PeerLayout(m=4096, hidden=4096, world=8, nslabs=2, out_itemsize=2)
+    assert lo.inbox_bytes == 4096 * 4096 * 2
+    assert lo.y_offset % 256 == 0 and lo.y_offset >= lo.inbox_bytes
+    assert lo.flags_offset >= lo.y_offset + 4096 * 4096 * 2
+    # slab regions of the inbox do not overlap and end inside it
+    assert lo.inbox_offset(2048) == 2048 * 4096 * 2
+    assert lo.inbox_offset(4096) == lo.inbox_bytes
+    flags = {lo.arrive_offset(0), lo.done_offset(0), lo.arrive_offset(1), lo.done_offset(1)}
+    assert len(flags) == 4 and max(flags) + 8 * 4 <= lo.total_bytes
