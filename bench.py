@@ -20,7 +20,8 @@ pinned host inputs copied in and the result copied back inside the timed loop.
 specs' torch references, restated in oracle/cpu_torch.py) on all host cores.
 Multi-GPU (torchrun): memory-bound configs run as replicas (weak scaling);
 Adam shards the 1e9 parameters across ranks with no collective; the SwiGLU
-MLP runs column/row tensor-parallel with an NCCL all-reduce of its output.
+MLP runs column/row tensor-parallel, its output's reduction fused into the
+down-projection GEMM over NVLink peer memory (enzyme_b200.tp.FusedTPSwiGLU).
 """
 
 from __future__ import annotations
@@ -325,26 +326,42 @@ class SwiGLU(Workload):
         self.tune = {"precision": self.PRECISION}
         ws = ops.silu_mlp_workspace_bytes(m, self.shard, h, 1, self.tune)
         self.act = torch.empty(ws, dtype=torch.uint8, device=dev)
-        self.y = torch.empty(m, h, dtype=torch.bfloat16 if world == 1 else torch.float32, device=dev)
+        self.y = torch.empty(m, h, dtype=torch.bfloat16, device=dev)
         self.nsets = 1
         self.scaling = "strong" if world > 1 else "weak"
         self.use_graph = world == 1
         self.launches_per_step = 3 if self.PRECISION == 4 else 2
         if world > 1:
             # column/row tensor parallel: W_gate/W_up column shard, W_down row
-            # shard, fp32 partials all-reduced per m-slab while the next slab
-            # computes (enzyme_b200.tp)
-            from enzyme_b200.tp import TPSwiGLU, _CudaOps
+            # shard; the down GEMM scatters f16 partial rows to their owner
+            # ranks over NVLink, owners reduce and push bf16 rows to every
+            # rank, slab by slab (enzyme_b200.tp.FusedTPSwiGLU)
+            from enzyme_b200.tp import FusedTPSwiGLU
 
-            self.tp = TPSwiGLU(self.w1, self.w2, self.w3, slabs=self.SLABS, ops=_CudaOps(tune=self.TP_TUNE))
-            self.launches_per_step = 1 + 2 * len(self.tp.slab_bounds(m))
+            self.tp = FusedTPSwiGLU(self.w1, self.w2, self.w3, m=m, slabs=self.SLABS, tune=self.TP_TUNE,
+                                    reduce_ctas=self.REDUCE_CTAS)
+            self.y = self.tp.y
+            # cast, then per slab: gate/up GEMM, down GEMM, signal, reduce, signal; one wait per slab
+            self.launches_per_step = 1 + 6 * len(self.tp.slabs)
 
     PRECISION = 4
-    # measured on 2 B200s: 1 slab 733 us (no overlap: 568 compute + 161
-    # all-reduce), 2 slabs with the GEMM grid capped at 132 CTAs 692 us, 4
-    # slabs slower (ragged last waves)
+    # measured on 2 B200s: NCCL all-reduce of fp32 partials per slab 660-680 us;
+    # fused (2 slabs, GEMM grid capped at 132 CTAs, 32-CTA side reduce) 610 us;
+    # 4 or 8 slabs slower (ragged last waves of the smaller GEMMs)
     SLABS = 2
     TP_TUNE = {"max_ctas": 132}
+    REDUCE_CTAS = 32
+
+    def check(self):
+        if self.world > 1:
+            self.tp.status()
+
+    def close(self):
+        if self.world > 1:
+            torch.cuda.synchronize()
+            dist.barrier()  # no rank unmaps a peer buffer while another still writes it
+            self.tp.close()
+            dist.barrier()
 
     def per_step_work(self):
         m, n, k, p = 4096, self.shard, 4096, 4096
@@ -355,7 +372,7 @@ class SwiGLU(Workload):
 
     def launch(self, i):
         if self.world > 1:
-            self.tp.forward(self.x, out=self.y)
+            self.tp.forward(self.x)
         else:
             ops.silu_mlp(self.x, self.w1, self.w2, self.w3, out=self.y, workspace=self.act, tune=self.tune)
 
@@ -383,7 +400,8 @@ class SwiGLU(Workload):
             f"{rows} of 4096 tokens (fp32 torch, same weights shape)"
 
     def config(self):
-        par = "tp1" if self.world == 1 else f"tp{self.world} (column/row, NCCL all-reduce fp32)"
+        par = "tp1" if self.world == 1 else (f"tp{self.world} (column/row; reduce-scatter fused into the down "
+                                             f"GEMM over NVLink, owner reduce + all-gather push)")
         return {"workload": "silu_mlp_swiglu: m 4096, hidden 4096, inter 14336, bf16, W ~ N(0, 0.02)",
                 "parallelism": par}
 
@@ -535,6 +553,8 @@ def run_workload(name, dev, rank, world, steps, warmup, sampler_gpu, with_e2e=Tr
            "gpu_launches": steps * w.launches_per_step}
     if with_e2e:
         res["e2e"] = measure_e2e(w, steps)
+    if hasattr(w, "close"):
+        w.close()
     return w, res
 
 
