@@ -338,7 +338,8 @@ class SwiGLU(Workload):
             # rank, slab by slab (enzyme_b200.tp.FusedTPSwiGLU)
             from enzyme_b200.tp import FusedTPSwiGLU
 
-            self.tp = FusedTPSwiGLU(self.w1, self.w2, self.w3, m=m, slabs=self.SLABS, tune=self.TP_TUNE,
+            slabs = self.SLABS if world <= 2 else 1
+            self.tp = FusedTPSwiGLU(self.w1, self.w2, self.w3, m=m, slabs=slabs, tune=self.TP_TUNE,
                                     reduce_ctas=self.REDUCE_CTAS)
             self.y = self.tp.y
             # cast, then per slab: gate/up GEMM, down GEMM, signal, reduce, signal; one wait per slab
@@ -347,7 +348,8 @@ class SwiGLU(Workload):
     PRECISION = 4
     # measured on 2 B200s: NCCL all-reduce of fp32 partials per slab 660-680 us;
     # fused (2 slabs, GEMM grid capped at 132 CTAs, 32-CTA side reduce) 610 us;
-    # 4 or 8 slabs slower (ragged last waves of the smaller GEMMs)
+    # 4 or 8 slabs slower (ragged last waves of the smaller GEMMs). On 8: one
+    # slab 274 us, two 307 us (the side reduce slows the shard's small GEMMs).
     SLABS = 2
     TP_TUNE = {"max_ctas": 132}
     REDUCE_CTAS = 32

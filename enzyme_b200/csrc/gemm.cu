@@ -771,6 +771,17 @@ int make_map(CUtensorMap* map, const void* base, int32_t dtype, uint64_t inner, 
   return AXON_OK;
 }
 
+// Persistent grid for `tiles` tiles on at most `cap` workers: the fewest
+// workers that finish in the same number of rounds as `cap` would (224 pair
+// tiles on 74 pairs take 4 rounds either way, so 56 pairs run them and the
+// other SMs stay free for kernels that overlap the GEMM, such as the
+// tensor-parallel reduction).
+int64_t balanced_grid(int64_t tiles, int64_t cap) {
+  if (tiles <= cap) return tiles;
+  const int64_t rounds = (tiles + cap - 1) / cap;
+  return (tiles + rounds - 1) / rounds;
+}
+
 template <int BN, int EPI, typename TC>
 int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mb2, const GemmParams& gp,
                 cudaStream_t s) {
@@ -783,7 +794,7 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
   const int64_t tiles = static_cast<int64_t>((gp.m + BM - 1) / BM) * ((gp.n + BN_OUT - 1) / BN_OUT);
   int64_t cap = sm_count();
   if (gp.max_ctas > 0 && gp.max_ctas < cap) cap = gp.max_ctas;
-  const int grid = static_cast<int>(tiles < cap ? tiles : cap);
+  const int grid = static_cast<int>(balanced_grid(tiles, cap));
   kern<<<grid, 192, smem, s>>>(ma, mb, mb2, gp);
   return launch_status("axon_gemm");
 }
@@ -825,7 +836,7 @@ int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtenso
   const int64_t tiles = static_cast<int64_t>((gp.m + 2 * BM - 1) / (2 * BM)) * ((gp.n + BN_OUT - 1) / BN_OUT);
   int64_t cap = pairs_cap;
   if (gp.max_ctas > 0 && gp.max_ctas / 2 < cap) cap = gp.max_ctas / 2 > 0 ? gp.max_ctas / 2 : 1;
-  const int pairs = static_cast<int>(tiles < cap ? tiles : cap);
+  const int pairs = static_cast<int>(balanced_grid(tiles, cap));
   cfg.gridDim = dim3(2 * pairs, 1, 1);
   e = cudaLaunchKernelEx(&cfg, kern, ma, mb, mb2, gp);
   if (e != cudaSuccess) return fail(AXON_E_LAUNCH, "axon_gemm: %s", cudaGetErrorString(e));
