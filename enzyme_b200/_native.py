@@ -130,6 +130,15 @@ SIGNATURES: dict[str, tuple] = {
     "axon_ipc_open": (_I32, [_P, _I64, ctypes.POINTER(_P)]),
     "axon_ipc_close": (_I32, [_P, _I64]),
     "axon_tp_down_partial": (_I32, [_P, _P, _P, _I32, _I32, _I64, _I64, _I64, _I64, _I32, _TUNE, _P]),
+    "axon_tp_mlp_workspace_bytes": (_I64, [_I64, _I64]),
+    "axon_tp_mlp_partial": (
+        _I32, [_P, _P, _P, _P, _P, _I64, _P, _I32, _I32, _I64, _I64, _I64, _I64, _I64, _TUNE, _P]
+    ),
+    "axon_tp_step_done_per_epoch": (_I64, [_I32, _I64, _I64]),
+    "axon_tp_mlp_step": (
+        _I32, [_P, _P, _P, _P, _P, _I64, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I64, _I64, _I64, _I64, _TUNE, _P]
+    ),
+    "axon_tp_wait_count": (_I32, [_P, _I32, _P]),
     "axon_tp_signal": (_I32, [_P, _I32, _I32, _I32, _P]),
     "axon_tp_wait": (_I32, [_P, _I32, _I32, _P]),
     "axon_tp_reduce_gather": (_I32, [_P, _P, _P, _I32, _I32, _I32, _I64, _I64, _I64, _I64, _I32, _I32, _P]),

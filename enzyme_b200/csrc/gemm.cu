@@ -192,6 +192,8 @@ struct GemmParams {
   void* peers[kMaxPeers];  // kEpiPeer: each owner's inbox for this output
   int peer_rank;
   int rows_per_owner;
+  int world;               // kEpiPeer with interleave: ranks owning 8-row granules in turn
+  int interleave;
   const float* row_scale;
   int m, n, k;         // n = output columns
   int64_t ldc;
@@ -203,12 +205,27 @@ struct GemmParams {
   int max_ctas;        // > 0: cap on the persistent grid
 };
 
+// Ownership of output row r: contiguous blocks of rows_per_owner rows, or
+// (interleave) 8-row granules dealt to the ranks in turn, so every owner's
+// rows are spread over the whole output. `local` is the row's index among
+// its owner's rows.
+__device__ __forceinline__ int row_owner(const GemmParams& p, int64_t row, int64_t& local) {
+  if (p.interleave) {
+    const int o = static_cast<int>((row >> 3) % p.world);
+    local = (row / (8 * p.world)) * 8 + (row & 7);
+    return o;
+  }
+  const int o = static_cast<int>(row / p.rows_per_owner);
+  local = row - static_cast<int64_t>(o) * p.rows_per_owner;
+  return o;
+}
+
 template <int EPI, typename TC>
 __device__ __forceinline__ TC* out_row(const GemmParams& p, TC* C, int64_t row) {
   if constexpr (EPI == kEpiPeer) {
-    const int o = static_cast<int>(row / p.rows_per_owner);
-    const int64_t local = static_cast<int64_t>(p.peer_rank) * p.rows_per_owner + (row - static_cast<int64_t>(o) * p.rows_per_owner);
-    return static_cast<TC*>(p.peers[o]) + local * p.ldc;
+    int64_t local;
+    const int o = row_owner(p, row, local);
+    return static_cast<TC*>(p.peers[o]) + (static_cast<int64_t>(p.peer_rank) * p.rows_per_owner + local) * p.ldc;
   } else {
     return C + row * p.ldc;
   }
@@ -738,6 +755,559 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// ---- fused SwiGLU: both GEMMs (and, for tensor parallelism, the reduction) in one kernel
+//
+// y = (silu(x @ W_gate) * (x @ W_up)) @ W_down with the f16 activation of
+// precision mode 4. Phase-A tiles (256 rows x 128 activation columns: gate and
+// up accumulators side by side in TMEM, as gemm_tcgen05_pair's SiLU-gate
+// epilogue) write the activation to global memory; phase-B tiles (256 x 256
+// of y, K = the intermediate size) read it back through TMA. Pairs claim tiles
+// from one atomic counter, all phase-A tiles before any phase-B tile, so a
+// pair that finishes its part of phase A moves straight on to phase B instead
+// of idling through the last partial wave. A phase-B tile's producers wait
+// (bounded) until every phase-A tile of its 256-row block has been written:
+// each phase-A epilogue warp adds one to its row block's counter after its
+// stores (8 per tile). Tiles are claimed in order by running CTAs and phase-A
+// tiles never wait, so every wait ends without assuming co-residency.
+//
+// Modes: kMlpLocal writes y; kMlpScatter writes each f16 partial row of y to
+// its owner rank's inbox (axon_tp_mlp_partial); kMlpStep (axon_tp_mlp_step)
+// is a whole tensor-parallel step: rows are owned in 8-row granules dealt to
+// the ranks in turn, each phase-B epilogue warp releases its rows' arrival
+// counts into the owners' counters (system scope, over NVLink), and phase-C
+// tiles -- claimed after every phase-B tile -- wait for all ranks' partials of
+// a row block of this rank's rows, sum them in fp32 in rank order, round once
+// to bf16 and store them into every rank's output, then count themselves done
+// on every rank. A phase-C wait depends only on other ranks' phase-B tiles,
+// which depend only on their own phase A: no cycle across GPUs. Arrival and
+// done counts accumulate over steps (epoch * per-step count), so nothing is
+// reset between steps.
+//
+// The leader's producer thread claims each tile and publishes its id to both
+// CTAs through a ring of shared-memory slots (the peer's by a distributed
+// shared-memory store and a remote mbarrier arrival); each consumer role
+// (the peer's producer, the leader's MMA thread, the epilogue warps of both
+// CTAs) frees a slot by arriving on the leader's slot barrier.
+
+constexpr int kSchedRing = 8;
+constexpr int kMlpLocal = 0, kMlpScatter = 1, kMlpStep = 2;
+constexpr int kStepColsPerTile = 1024;  // phase C: output columns per tile
+
+struct MlpParams {
+  void* c;                  // kMlpLocal: y [m, ldc]
+  void* peers[kMaxPeers];   // kMlpScatter / kMlpStep: each owner's inbox [world][m / world][n2] f16
+  int peer_rank;
+  int rows_per_owner;
+  int world;
+  __half* act;              // [m, n1] f16
+  int* ready;               // [row blocks] phase-A epilogue warps done, then the tile counter
+  int m, n1, k1, n2;
+  int64_t ldc;
+  int stages;
+  uint32_t idesc_a, idesc_b;
+  int max_ctas;
+  // kMlpStep
+  int* arrive[kMaxPeers];   // each owner's arrival counts [row blocks]
+  int* done[kMaxPeers];     // each rank's done count
+  const __half* inbox;      // this rank's inbox
+  void* y[kMaxPeers];       // each rank's output [m, n2] bf16
+  int epoch;
+  int group;                // row blocks per group of the tile order
+};
+
+__device__ __forceinline__ int ld_acquire_gpu_s32(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ int ld_acquire_sys_s32(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void red_release_sys_add(int* p, int v) {
+  asm volatile("red.release.sys.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void st_shared_cluster_s32(uint32_t addr, int v) {
+  asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+
+// Bounded wait until *ctr reaches target (wrap-safe); sys: the counter is
+// written by other GPUs.
+template <bool SYS>
+__device__ __forceinline__ bool wait_count(const int* ctr, int target, volatile int* abort_flag) {
+  auto ld = [&]() { return SYS ? ld_acquire_sys_s32(ctr) : ld_acquire_gpu_s32(ctr); };
+  if (ld() - target >= 0) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (ld() - target >= 0) return true;
+    if ((i & 15) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer() - t0 > kTimeoutNs) {
+        *abort_flag = 1;
+        atomicExch(&g_gemm_error, AXON_E_TIMEOUT);
+        return false;
+      }
+    }
+    __nanosleep(64);
+  }
+}
+
+// mbar_wait with cluster-scope acquire: for barriers a thread of the other
+// CTA of the pair arrives on after writing this CTA's shared memory.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  auto try_once = [&]() {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+  };
+  if (try_once()) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (try_once()) return true;
+    if ((i & 127) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer() - t0 > kTimeoutNs) {
+        *abort_flag = 1;
+        atomicExch(&g_gemm_error, AXON_E_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
+struct MlpTile {
+  int kind;    // 0 = phase A (gate/up), 1 = B (down)
+  int r, c;    // 256-row block, column tile
+};
+
+struct MlpGrid {
+  int rb, ta_row, tb_row, tc_row, group;
+  __device__ int tiles() const { return rb * (ta_row + tb_row); }  // phases A and B: the ring's tiles
+  // phase C: units of 8 of this rank's rows x kStepColsPerTile columns, one warp each
+  __device__ int c_units(int world) const { return rb * tc_row * (32 / world); }
+};
+
+// Row groups of `group` 256-row blocks; the tile sequence is A0, A1, B0, A2,
+// B1, ..., A(n-1), B(n-2), B(n-1): a group's down-projection tiles come after
+// the next group's gate/up tiles have been claimed, so their activation rows
+// are complete by the time they are loaded, and the down projection of early
+// groups (and, in a tensor-parallel step, its traffic over NVLink) overlaps
+// later groups' gate/up tiles. Gate/up tiles are column-major inside a group
+// (a wave shares weight columns among the group's row blocks), down tiles
+// row-major.
+__device__ __forceinline__ MlpTile mlp_tile(int t, const MlpGrid& g) {
+  const int GR = g.group;
+  const int ng = (g.rb + GR - 1) / GR;
+  MlpTile x;
+  x.kind = 1;
+  x.r = 0;
+  x.c = 0;
+  for (int k = 0; k <= ng; ++k) {
+    if (k < ng) {
+      const int gr = g.rb - k * GR < GR ? g.rb - k * GR : GR;
+      const int sz = gr * g.ta_row;
+      if (t < sz) {
+        x.kind = 0;
+        x.r = k * GR + t % gr;
+        x.c = t / gr;
+        return x;
+      }
+      t -= sz;
+    }
+    if (k >= 1) {
+      const int j = k - 1;
+      const int gr = g.rb - j * GR < GR ? g.rb - j * GR : GR;
+      const int sz = gr * g.tb_row;
+      if (t < sz) {
+        x.kind = 1;
+        x.r = j * GR + t / g.tb_row;
+        x.c = t % g.tb_row;
+        return x;
+      }
+      t -= sz;
+    }
+  }
+  return x;  // not reached for t < tiles()
+}
+
+template <typename TC, int MODE>
+__global__ void __launch_bounds__(192, 1)
+    swiglu_fused_pair(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmWg,
+                      const __grid_constant__ CUtensorMap tmWu, const __grid_constant__ CUtensorMap tmAct,
+                      const __grid_constant__ CUtensorMap tmWd, MlpParams p) {
+  constexpr int BN = 256, BH = 128;
+  constexpr int B_BYTES = BH * BK * 2;
+  constexpr int STAGE = A_BYTES + B_BYTES;
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int S = p.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * STAGE);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint64_t* sfull = drain + 1;              // schedule ring: tile id published
+  uint64_t* sempty = sfull + kSchedRing;    // leader only: every consumer has read the slot
+  int* sched = reinterpret_cast<int*>(sempty + kSchedRing);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sched + kSchedRing);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  uint32_t rank;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+  const bool leader = rank == 0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  MlpGrid grid;
+  grid.rb = (p.m + 2 * BM - 1) / (2 * BM);
+  grid.ta_row = (p.n1 + BH - 1) / BH;
+  grid.tb_row = (p.n2 + BN - 1) / BN;
+  grid.tc_row = MODE == kMlpStep ? (p.n2 + kStepColsPerTile - 1) / kStepColsPerTile : 0;
+  grid.group = p.group;
+  const int tiles = grid.tiles();
+  const int kb_a = (p.k1 + BK - 1) / BK, kb_b = (p.n1 + BK - 1) / BK;
+  int* counter = p.ready + grid.rb;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 8);
+    }
+    mbar_init(drain, 1);
+    for (int s = 0; s < kSchedRing; ++s) {
+      mbar_init(&sfull[s], 1);
+      mbar_init(&sempty[s], 10);  // leader MMA + 4 + 4 epilogue warps + the peer's producer
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    tc_fence_before();
+  }
+  __syncthreads();
+  cluster_barrier();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  // Consumer side of the schedule ring: the id of this role's i-th tile (-1 = done).
+  auto next_tile = [&](int i, bool arrive_lane) -> int {
+    const int slot = i % kSchedRing;
+    if (!mbar_wait_cluster(&sfull[slot], static_cast<uint32_t>((i / kSchedRing) & 1), abort_flag)) return -1;
+    const int t = *reinterpret_cast<volatile int*>(&sched[slot]);
+    if (arrive_lane) mbar_arrive_cluster(mapa_u32(smem_u32(&sempty[slot]), 0), 1);
+    return t;
+  };
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- producers (the leader's also claims tiles) ----------------
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int i = 0;; ++i) {
+      int t;
+      if (leader) {
+        const int slot = i % kSchedRing;
+        if (!mbar_wait_cluster(&sempty[slot], static_cast<uint32_t>(((i / kSchedRing) & 1) ^ 1), abort_flag)) break;
+        t = atomicAdd(counter, 1);
+        if (t >= tiles) t = -1;
+        sched[slot] = t;
+        st_shared_cluster_s32(mapa_u32(smem_u32(&sched[slot]), 1), t);
+        mbar_arrive(&sfull[slot]);
+        mbar_arrive_cluster(mapa_u32(smem_u32(&sfull[slot]), 1), 1);
+      } else {
+        t = next_tile(i, true);
+      }
+      if (t < 0) break;
+      const MlpTile x = mlp_tile(t, grid);
+      if (x.kind == 1) {
+        if (!wait_count<false>(p.ready + x.r, 8 * grid.ta_row, abort_flag)) break;
+        asm volatile("fence.proxy.async.global;" ::: "memory");  // generic-proxy activation stores -> TMA reads
+      }
+      const int kblocks = x.kind == 0 ? kb_a : kb_b;
+      const int row = x.r * 2 * BM + static_cast<int>(rank) * BM;
+      bool ok = true;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const uint32_t leader_full = mapa_u32(smem_u32(&full[stage]), 0);
+        if (leader) mbar_expect_tx(&full[stage], 2 * STAGE);
+        uint8_t* sa = smem + stage * STAGE;
+        uint8_t* sb = sa + A_BYTES;
+        if (x.kind == 0) {
+          tma_load_2d_pair(&tmX, leader_full, sa, kb * BK, row);
+          const CUtensorMap* mp = leader ? &tmWg : &tmWu;  // gate columns on the leader, up on the peer
+#pragma unroll
+          for (int j = 0; j < BH / 64; ++j) tma_load_2d_pair(mp, leader_full, sb + j * B_CHUNK, x.c * BH + j * 64, kb * BK);
+        } else {
+          tma_load_2d_pair(&tmAct, leader_full, sa, kb * BK, row);
+#pragma unroll
+          for (int j = 0; j < BH / 64; ++j)
+            tma_load_2d_pair(&tmWd, leader_full, sb + j * B_CHUNK, x.c * BN + static_cast<int>(rank) * BH + j * 64,
+                             kb * BK);
+        }
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+    }
+  } else if (warp == 1 && lane == 0 && leader) {
+    // ---------------- MMA issuer (leader only) ----------------
+    int stage = 0;
+    uint32_t phase = 0;
+    int mm = 0;  // tiles that use TMEM (phases A and B)
+    for (int i = 0;; ++i) {
+      const int t = next_tile(i, true);
+      if (t < 0) break;
+      const MlpTile x = mlp_tile(t, grid);
+      const int buf = mm & 1;
+      if (!mbar_wait(&tempty[buf], ((mm >> 1) & 1) ^ 1u, abort_flag)) break;
+      ++mm;
+      tc_fence_after();
+      const uint32_t d = tmem_base + static_cast<uint32_t>(buf * BN);
+      const int kblocks = x.kind == 0 ? kb_a : kb_b;
+      const uint32_t idesc = x.kind == 0 ? p.idesc_a : p.idesc_b;
+      bool ok = true;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!mbar_wait(&full[stage], phase, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + stage * STAGE);
+        const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k) {
+          const uint64_t ad = sdesc(sa + k * 32, 16, 1024);
+          const uint64_t bd = sdesc(sb + k * 2048, B_CHUNK, 1024);
+          tc_mma_pair(d, ad, bd, idesc, (kb | k) != 0);
+        }
+        tc_commit_to(smem_u32(&empty[stage]));
+        tc_commit_to(mapa_u32(smem_u32(&empty[stage]), 1));
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+      tc_commit_to(smem_u32(&tfull[buf]));
+      tc_commit_to(mapa_u32(smem_u32(&tfull[buf]), 1));
+    }
+    tc_commit_to(smem_u32(drain));
+    volatile int never = 0;
+    mbar_wait(drain, 0, &never);
+  } else if (warp >= 2) {
+    // ---------------- epilogue (both CTAs, their own 128 rows) ----------------
+    const int q = warp & 3;
+    int mm = 0;
+    // Phase C (kMlpStep) in units of 8 of this rank's rows x
+    // kStepColsPerTile columns, one warp each, claimed from a counter: sum
+    // the world partials in fp32 in rank order, round once to bf16, store to
+    // every rank's output, count done on every rank. Between its GEMM tiles a
+    // warp takes one unit whose rows have all arrived (no waiting); after the
+    // last tile it takes units until none is left.
+    const int W = p.world > 0 ? p.world : 1;
+    const int upb = 32 / W;                                 // units per row block and column chunk
+    const int c_units = grid.c_units(W);
+    const int c_target = p.epoch * 32 * grid.tb_row;        // arrival count of a complete row block
+    int* c_counter = p.ready + grid.rb + 1;
+    auto c_claim = [&](bool block) -> int {                 // unit, -1 none ready now, -2 none left
+      int u = -2;
+      if (lane == 0) {
+        if (block) {
+          u = *abort_flag ? c_units : atomicAdd(c_counter, 1);
+          if (u >= c_units || !wait_count<true>(p.arrive[p.peer_rank] + u / (grid.tc_row * upb), c_target,
+                                                abort_flag))
+            u = -2;
+        } else {
+          for (int tries = 0; tries < 4; ++tries) {
+            const int v = ld_acquire_gpu_s32(c_counter);
+            if (v >= c_units) break;
+            u = -1;
+            if (ld_acquire_sys_s32(p.arrive[p.peer_rank] + v / (grid.tc_row * upb)) - c_target < 0) break;
+            if (atomicCAS(c_counter, v, v + 1) == v) {
+              u = v;
+              break;
+            }
+          }
+        }
+      }
+      return __shfl_sync(0xffffffffu, u, 0);
+    };
+    auto c_work = [&](int u) {
+      const int r = u / (grid.tc_row * upb);
+      const int rem = u - r * grid.tc_row * upb;
+      const int c = rem / upb, sub = rem - (rem / upb) * upb;
+      const int64_t lr0 = static_cast<int64_t>(r) * (2 * BM / W) + sub * 8;
+      const int col0 = c * kStepColsPerTile;
+      const int ncols = p.n2 - col0 < kStepColsPerTile ? p.n2 - col0 : kStepColsPerTile;
+      const int pkr = ncols / 8;  // 16-byte packets per row
+      const int total = 8 * pkr;
+      const int64_t slot = static_cast<int64_t>(p.rows_per_owner) * p.n2;
+      // two packets per lane per pass, every source's load issued before any sum
+      for (int idx0 = lane; idx0 < total; idx0 += 64) {
+        Vec<__half> v[2][kMaxPeers];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int idx = idx0 + h * 32;
+          const int64_t lr = lr0 + idx / pkr;
+          const int col = col0 + (idx % pkr) * 8;
+#pragma unroll
+          for (int s = 0; s < kMaxPeers; ++s)  // written by other GPUs: loads that skip cached copies
+            if (s < W && idx < total)
+              v[h][s].u = __ldcv(reinterpret_cast<const uint4*>(p.inbox + s * slot + lr * p.n2 + col));
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int idx = idx0 + h * 32;
+          if (idx >= total) break;
+          const int64_t lr = lr0 + idx / pkr;
+          const int col = col0 + (idx % pkr) * 8;
+          float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int s = 0; s < kMaxPeers; ++s)  // fixed rank order
+            if (s < W)
+#pragma unroll
+              for (int e = 0; e < 8; ++e) acc[e] += __half2float(v[h][s].e[e]);
+          Vec<__nv_bfloat16> o;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) o.e[e] = __float2bfloat16_rn(acc[e]);
+          const int64_t grow = ((lr >> 3) * W + p.peer_rank) * 8 + (lr & 7);
+          for (int d = 0; d < W; ++d) st_vec(static_cast<__nv_bfloat16*>(p.y[d]) + grow * p.n2 + col, o);
+        }
+      }
+      __threadfence_system();
+      __syncwarp();
+      if (lane < W) red_release_sys_add(p.done[lane], 1);
+    };
+    (void)c_claim;
+    (void)c_work;
+    (void)c_target;
+    for (int i = 0;; ++i) {
+      const int t = next_tile(i, false);  // every lane reads the slot ...
+      __syncwarp();                       // ... before one arrival frees it for the whole warp
+      if (lane == 0) mbar_arrive_cluster(mapa_u32(smem_u32(&sempty[i % kSchedRing]), 0), 1);
+      if (t < 0) break;
+      const MlpTile x = mlp_tile(t, grid);
+      const int buf = mm & 1;
+      const uint32_t tph = (mm >> 1) & 1;
+      ++mm;
+      if (!mbar_wait(&tfull[buf], tph, abort_flag)) break;
+      tc_fence_after();
+      const int64_t row0 = static_cast<int64_t>(x.r) * 2 * BM + static_cast<int64_t>(rank) * BM + q * 32;
+      const int64_t row = row0 + lane;
+      const bool row_ok = row < p.m;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN);
+      if (x.kind == 0) {
+        __half* arow = p.act + (row_ok ? row : 0) * static_cast<int64_t>(p.n1);
+#pragma unroll 1
+        for (int c = 0; c < BH / 32; ++c) {
+          float g[32], u[32];
+          __syncwarp();
+          tmem_ld32(tbase + c * 32, g);
+          tmem_ld32(tbase + BH + c * 32, u);
+          tmem_wait_ld();
+          const int64_t col = static_cast<int64_t>(x.c) * BH + c * 32;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) g[j] = g[j] / (1.0f + __expf(-g[j])) * u[j];
+          if (row_ok && col < p.n1) store32<__half>(arow + col, g, col, p.n1);
+        }
+        // this warp's rows of the activation are written: publish them to the
+        // phase-B producers (TMA reads them through the async proxy)
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+          __threadfence();
+          atomicAdd(p.ready + x.r, 1);
+        }
+      } else if constexpr (MODE != kMlpLocal) {
+        __half* stg = reinterpret_cast<__half*>(smem + S * STAGE + 512) + q * 32 * kPeerStageHalves;
+        GemmParams gp{};
+        for (int o = 0; o < kMaxPeers; ++o) gp.peers[o] = p.peers[o];
+        gp.peer_rank = p.peer_rank;
+        gp.rows_per_owner = p.rows_per_owner;
+        gp.world = p.world;
+        gp.interleave = MODE == kMlpStep;
+        gp.m = p.m;
+        gp.n = p.n2;
+        gp.ldc = p.ldc;
+        peer_store_tile<BN>(gp, stg, tbase, row0, static_cast<int64_t>(x.c) * BN, lane);
+        if constexpr (MODE == kMlpStep) {
+          // release this warp's 32 rows (4 granules) into their owners' counts
+          __threadfence_system();
+          __syncwarp();
+          if (lane < p.world) {
+            int k = 0;
+#pragma unroll
+            for (int g = 0; g < 4; ++g) k += ((row0 >> 3) + g) % p.world == lane;
+            if (k) red_release_sys_add(p.arrive[lane] + x.r, k);
+          }
+        }
+      } else {
+        TC* crow = static_cast<TC*>(p.c) + (row_ok ? row : 0) * p.ldc;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          __syncwarp();
+          tmem_ld32(tbase + c * 32, v);
+          tmem_wait_ld();
+          const int64_t col = static_cast<int64_t>(x.c) * BN + c * 32;
+          if (row_ok && col < p.n2) store32<TC>(crow + col, v, col, p.n2);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_u32(smem_u32(&tempty[buf]), 0), 1);
+      if constexpr (MODE == kMlpStep) {
+        const int u = c_claim(false);
+        if (u >= 0) c_work(u);
+      }
+    }
+    if constexpr (MODE == kMlpStep) {
+      // ---- phase C, the rest: claim units until none is left, waiting
+      // (bounded) for each unit's rows to arrive from every rank
+      for (;;) {
+        const int u = c_claim(true);
+        if (u < 0) break;
+        c_work(u);
+      }
+    }
+  }
+
+  __syncthreads();
+  if (threadIdx.x == 0 && *abort_flag) {
+    // copies issued by this CTA may still be landing (failure path only)
+    for (int k = 0; k < 1000; ++k) __nanosleep(1000);
+  }
+  cluster_barrier();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                 : "memory");
+  }
+}
+
 // ---- host side -------------------------------------------------------------------
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -872,6 +1442,135 @@ int max_stages(int b_cols, int extra = 0) {
   const int avail = 232448 - 1024 - 256 - extra;
   int s = avail / stage;
   return s > 8 ? 8 : s;
+}
+
+template <typename TC, int MODE>
+int launch_swiglu_fused(const CUtensorMap& mx, const CUtensorMap& mg, const CUtensorMap& mu, const CUtensorMap& ma,
+                        const CUtensorMap& md, const MlpParams& mp, cudaStream_t s) {
+  constexpr int STAGE = A_BYTES + 128 * BK * 2;
+  const size_t smem =
+      static_cast<size_t>(mp.stages) * STAGE + 1024 + 512 + (MODE != kMlpLocal ? kPeerStageBytes : 0);
+  auto kern = swiglu_fused_pair<TC, MODE>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return fail(AXON_E_LAUNCH, "axon_silu_mlp: smem attribute: %s", cudaGetErrorString(e));
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(192, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  static int cached_pairs[9] = {0};
+  int& pairs_cap = cached_pairs[mp.stages > 8 ? 8 : mp.stages];
+  if (pairs_cap == 0) {
+    cfg.gridDim = dim3(2, 1, 1);
+    int clusters = 0;
+    e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+    if (e != cudaSuccess || clusters <= 0)
+      return fail(AXON_E_LAUNCH, "axon_silu_mlp: no room for a CTA pair (%s)", cudaGetErrorString(e));
+    pairs_cap = clusters;
+  }
+  const int64_t rb = (mp.m + 2 * BM - 1) / (2 * BM);
+  const int64_t tiles = rb * ((mp.n1 + 127) / 128 + (mp.n2 + 255) / 256);
+  int64_t pairs = pairs_cap;
+  if (mp.max_ctas > 0 && mp.max_ctas / 2 < pairs) pairs = mp.max_ctas / 2 > 0 ? mp.max_ctas / 2 : 1;
+  if (tiles < pairs) pairs = tiles;
+  // row-block counters and the tile counter start at zero every call
+  e = cudaMemsetAsync(mp.ready, 0, static_cast<size_t>(rb + 2) * sizeof(int), s);
+  if (e != cudaSuccess) return fail(AXON_E_CUDA, "axon_silu_mlp: counter reset: %s", cudaGetErrorString(e));
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
+  e = cudaLaunchKernelEx(&cfg, kern, mx, mg, mu, ma, md, mp);
+  if (e != cudaSuccess) return fail(AXON_E_LAUNCH, "axon_silu_mlp: %s", cudaGetErrorString(e));
+  return launch_status("axon_silu_mlp");
+}
+
+// Bytes of the fused kernel's counters: one per 256-row block, the tile
+// counter and the phase-C counter.
+int64_t swiglu_counter_bytes(int64_t m) { return ((m + 255) / 256 + 2) * 4; }
+
+// The fused SwiGLU (precision 4): x [m, k1] bf16, w1/w2 [k1, n1] bf16, w3h [n1, n2]
+// f16 (the caller's f16 copy of W_down), act [m, n1] f16 and counters from the
+// caller's workspace; the output goes to c [m, ldc] (c_dtype) or, with
+// `peers`, to the owners' inboxes as axon_tp_down_partial lays them out.
+// `step` (with peers) selects the whole tensor-parallel step (kMlpStep).
+struct StepArgs {
+  int32_t* const* arrive;
+  int32_t* const* done;
+  const void* inbox;
+  void* const* ys;
+  int epoch;
+};
+
+int swiglu_fused_impl(const void* x, const void* w1, const void* w2, const void* w3h, __half* act, int* counters,
+                      void* c, int64_t ldc, int32_t c_dtype, int64_t m, int64_t n1, int64_t k1, int64_t n2,
+                      const axon_tune_t& t, void* stream, void* const* peers = nullptr, int world = 0,
+                      int peer_rank = 0, int64_t rows_per_owner = 0, const StepArgs* step = nullptr) {
+  if (m > 0x7fffffff || n1 > 0x7fffffff || k1 > 0x7fffffff || n2 > 0x7fffffff)
+    return fail(AXON_E_SHAPE, "axon_silu_mlp: sizes out of range");
+  if (n1 % 8 || k1 % 8 || n2 % 8) return fail(AXON_E_SHAPE, "axon_silu_mlp: n, k and p must be multiples of 8");
+  if (!aligned16(x) || !aligned16(w1) || !aligned16(w2) || !aligned16(w3h) || !aligned16(act) ||
+      (c != nullptr && !aligned16(c)))
+    return fail(AXON_E_ALIGN, "axon_silu_mlp: operands must be 16-byte aligned");
+  const int extra = peers != nullptr ? kPeerStageBytes : 0;
+  const int smax = (232448 - 1024 - 512 - extra) / (A_BYTES + 128 * BK * 2) > 8
+                       ? 8
+                       : (232448 - 1024 - 512 - extra) / (A_BYTES + 128 * BK * 2);
+  const int stages = t.stages > 0 ? t.stages : smax;
+  if (stages < 2 || stages > smax) return fail(AXON_E_ARG, "axon_silu_mlp: stages must be in [2, %d]", smax);
+  CUtensorMap mx, mg, mu, ma, md;
+  int rc = make_map(&mx, x, AXON_BF16, k1, m, k1, BK, BM, "x");
+  if (!rc) rc = make_map(&mg, w1, AXON_BF16, n1, k1, n1, 64, BK, "w1");
+  if (!rc) rc = make_map(&mu, w2, AXON_BF16, n1, k1, n1, 64, BK, "w2");
+  if (!rc) rc = make_map(&ma, act, AXON_F16, n1, m, n1, BK, BM, "activation");
+  if (!rc) rc = make_map(&md, w3h, AXON_F16, n2, n1, n2, 64, BK, "w3");
+  if (rc) return rc;
+  MlpParams mp{};
+  mp.c = c;
+  if (peers != nullptr) {
+    for (int i = 0; i < world; ++i) mp.peers[i] = peers[i];
+    mp.peer_rank = peer_rank;
+    mp.rows_per_owner = static_cast<int>(rows_per_owner);
+    mp.world = world;
+  }
+  if (step != nullptr) {
+    for (int i = 0; i < world; ++i) {
+      mp.arrive[i] = step->arrive[i];
+      mp.done[i] = step->done[i];
+      mp.y[i] = step->ys[i];
+    }
+    mp.inbox = static_cast<const __half*>(step->inbox);
+    mp.epoch = step->epoch;
+  }
+  mp.act = act;
+  mp.ready = counters;
+  // tile order: two groups for one GPU (the weights are read twice), groups
+  // of four row blocks for a tensor-parallel step (more overlap of the down
+  // projection's traffic with gate/up tiles; the shard's weights are small)
+  mp.group = step != nullptr ? 4 : 8;
+  mp.m = static_cast<int>(m);
+  mp.n1 = static_cast<int>(n1);
+  mp.k1 = static_cast<int>(k1);
+  mp.n2 = static_cast<int>(n2);
+  mp.ldc = ldc;
+  mp.stages = stages;
+  mp.max_ctas = t.max_ctas;
+  // M = 256 (pair), N = 256; A/B bf16 in phase A, f16 in phase B
+  const uint32_t shape = (static_cast<uint32_t>(256 >> 3) << 17) | (static_cast<uint32_t>(256 >> 4) << 24);
+  mp.idesc_a = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | shape;
+  mp.idesc_b = (1u << 4) | (1u << 16) | shape;
+  cudaStream_t s = as_stream(stream);
+  if (step != nullptr) return launch_swiglu_fused<__half, kMlpStep>(mx, mg, mu, ma, md, mp, s);
+  if (peers != nullptr) return launch_swiglu_fused<__half, kMlpScatter>(mx, mg, mu, ma, md, mp, s);
+  switch (c_dtype) {
+    case AXON_BF16: return launch_swiglu_fused<__nv_bfloat16, kMlpLocal>(mx, mg, mu, ma, md, mp, s);
+    case AXON_F16: return launch_swiglu_fused<__half, kMlpLocal>(mx, mg, mu, ma, md, mp, s);
+    case AXON_F32: return launch_swiglu_fused<float, kMlpLocal>(mx, mg, mu, ma, md, mp, s);
+    default: return fail(AXON_E_UNSUPPORTED, "axon_silu_mlp: unsupported output dtype %d", c_dtype);
+  }
 }
 
 }  // namespace
@@ -1017,6 +1716,66 @@ extern "C" int axon_tp_down_partial(const void* act, const void* w, void* const*
                    stream, 1, 0, 0, inboxes, world, rank, rows_per_owner);
 }
 
+extern "C" int64_t axon_tp_mlp_workspace_bytes(int64_t m, int64_t n) {
+  if (m < 0 || n < 0) return fail(AXON_E_SHAPE, "axon_tp_mlp_workspace_bytes: negative size");
+  return m * n * 2 + swiglu_counter_bytes(m);
+}
+
+extern "C" int axon_tp_mlp_partial(const void* x, const void* w_gate, const void* w_up, const void* w_down_h,
+                                   void* workspace, int64_t workspace_bytes, void* const* inboxes, int32_t world,
+                                   int32_t rank, int64_t m, int64_t n, int64_t k, int64_t p, int64_t rows_per_owner,
+                                   const axon_tune_t* tune, void* stream) {
+  if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world)
+    return fail(AXON_E_ARG, "axon_tp_mlp_partial: world must be 1..%d and 0 <= rank < world", kMaxPeers);
+  if (m < 0 || n < 0 || k < 0 || p < 0) return fail(AXON_E_SHAPE, "axon_tp_mlp_partial: negative size");
+  if (m == 0 || p == 0) return AXON_OK;
+  if (!x || !w_gate || !w_up || !w_down_h || !inboxes) return fail(AXON_E_ARG, "axon_tp_mlp_partial: NULL operand");
+  if (rows_per_owner <= 0 || rows_per_owner * world != m)
+    return fail(AXON_E_SHAPE, "axon_tp_mlp_partial: m (%lld) must be world x rows_per_owner", (long long)m);
+  const int64_t need = m * n * 2 + swiglu_counter_bytes(m);
+  if (!workspace || workspace_bytes < need)
+    return fail(AXON_E_ARG, "axon_tp_mlp_partial: workspace of %lld bytes needed", (long long)need);
+  for (int i = 0; i < world; ++i)
+    if (!inboxes[i] || !aligned16(inboxes[i]))
+      return fail(AXON_E_ALIGN, "axon_tp_mlp_partial: inbox %d NULL or unaligned", i);
+  __half* act = static_cast<__half*>(workspace);
+  int* counters = reinterpret_cast<int*>(static_cast<unsigned char*>(workspace) + m * n * 2);
+  return swiglu_fused_impl(x, w_gate, w_up, w_down_h, act, counters, nullptr, p, AXON_F16, m, n, k, p,
+                           tune_or_default(tune), stream, inboxes, world, rank, rows_per_owner);
+}
+
+extern "C" int64_t axon_tp_step_done_per_epoch(int32_t world, int64_t m, int64_t p) {
+  if (world < 1 || m < 0 || p < 0) return fail(AXON_E_ARG, "axon_tp_step_done_per_epoch: bad argument");
+  // every phase-C unit (8 rows of an owner x kStepColsPerTile columns) counts
+  // once on every rank: world owners x (m / 256 row blocks x chunks x 32 / world)
+  return static_cast<int64_t>(32) * ((m + 255) / 256) * ((p + kStepColsPerTile - 1) / kStepColsPerTile);
+}
+
+extern "C" int axon_tp_mlp_step(const void* x, const void* w_gate, const void* w_up, const void* w_down_h,
+                                void* workspace, int64_t workspace_bytes, const void* inbox, void* const* inboxes,
+                                int32_t* const* arrive, int32_t* const* done, void* const* ys, int32_t world,
+                                int32_t rank, int32_t epoch, int64_t m, int64_t n, int64_t k, int64_t p,
+                                const axon_tune_t* tune, void* stream) {
+  if (world < 1 || world > kMaxPeers || (world & (world - 1)) || rank < 0 || rank >= world)
+    return fail(AXON_E_ARG, "axon_tp_mlp_step: world must be 1, 2, 4 or 8 and 0 <= rank < world");
+  if (m <= 0 || n <= 0 || k <= 0 || p <= 0) return fail(AXON_E_SHAPE, "axon_tp_mlp_step: sizes must be positive");
+  if (m % 256) return fail(AXON_E_SHAPE, "axon_tp_mlp_step: m (%lld) must be a multiple of 256", (long long)m);
+  if (!x || !w_gate || !w_up || !w_down_h || !inbox || !inboxes || !arrive || !done || !ys)
+    return fail(AXON_E_ARG, "axon_tp_mlp_step: NULL argument");
+  const int64_t need = m * n * 2 + swiglu_counter_bytes(m);
+  if (!workspace || workspace_bytes < need)
+    return fail(AXON_E_ARG, "axon_tp_mlp_step: workspace of %lld bytes needed", (long long)need);
+  for (int i = 0; i < world; ++i)
+    if (!inboxes[i] || !aligned16(inboxes[i]) || !ys[i] || !aligned16(ys[i]) || !arrive[i] || !done[i])
+      return fail(AXON_E_ALIGN, "axon_tp_mlp_step: buffers of rank %d NULL or unaligned", i);
+  if (!aligned16(inbox)) return fail(AXON_E_ALIGN, "axon_tp_mlp_step: inbox unaligned");
+  __half* act = static_cast<__half*>(workspace);
+  int* counters = reinterpret_cast<int*>(static_cast<unsigned char*>(workspace) + m * n * 2);
+  StepArgs sa{arrive, done, inbox, ys, epoch};
+  return swiglu_fused_impl(x, w_gate, w_up, w_down_h, act, counters, nullptr, p, AXON_F16, m, n, k, p,
+                           tune_or_default(tune), stream, inboxes, world, rank, m / world, &sa);
+}
+
 extern "C" int axon_gemm_status(void* stream) {
   int v = 0;
   cudaStream_t s = as_stream(stream);
@@ -1052,7 +1811,7 @@ static int silu_terms(const axon_tune_t* tune) {
 static bool silu_mode_ok(int terms) { return (terms >= 1 && terms <= 3) || terms == kF16Act; }
 
 static int64_t silu_ws_bytes(int64_t m, int64_t n, int64_t p, int terms) {
-  return terms == kF16Act ? m * n * 2 + n * p * 2 : m * n * 2 * terms;
+  return terms == kF16Act ? m * n * 2 + n * p * 2 + (swiglu_counter_bytes(m) + 255) / 256 * 256 : m * n * 2 * terms;
 }
 
 extern "C" int64_t axon_silu_mlp_workspace_bytes(int64_t m, int64_t n, int64_t p, int32_t ab_dtype,
@@ -1089,8 +1848,13 @@ extern "C" int axon_silu_mlp(const void* x, const void* w1, const void* w2, cons
     // a tcgen05 f16-kind MMA takes both operands in one type.
     __half* act = static_cast<__half*>(workspace);
     __half* w3h = reinterpret_cast<__half*>(static_cast<unsigned char*>(workspace) + m * n * 2);
+    int* counters = reinterpret_cast<int*>(static_cast<unsigned char*>(workspace) + m * n * 2 + n * p * 2);
     int rc = cast_impl(w3, w3h, n * p, AXON_BF16, AXON_F16, as_stream(stream));
     if (rc) return rc;
+    // variant 0 (default): both GEMMs in one CTA-pair kernel; 1 / 2: two
+    // launches of the one-CTA / CTA-pair GEMM
+    if (t.variant == 0 && m >= 256)
+      return swiglu_fused_impl(x, w1, w2, w3h, act, counters, y, p, c_dtype, m, n, k, p, t, stream);
     rc = gemm_impl(x, w1, w2, act, nullptr, m, n, k, k, n, n, ab_dtype, AXON_F16, AXON_EPI_SILU_GATE, &up, stream, 1,
                    0, 0);
     if (rc) return rc;

@@ -81,6 +81,10 @@ __global__ void tp_wait_kernel(const int* flags, int world, int epoch) {
   if (threadIdx.x == 0 && !wait_flags(flags, world, epoch)) atomicExch(&g_tp_error, AXON_E_TIMEOUT);
 }
 
+__global__ void tp_wait_count_kernel(const int* counter, int target) {
+  if (threadIdx.x == 0 && !wait_flags(counter, 1, target)) atomicExch(&g_tp_error, AXON_E_TIMEOUT);
+}
+
 template <typename Tout>
 __device__ __forceinline__ void store8(Tout* dst, const float* v) {
   if constexpr (sizeof(Tout) == 4) {
@@ -221,6 +225,12 @@ extern "C" int axon_tp_wait(const int32_t* flags, int32_t world, int32_t epoch, 
   if (!flags) return fail(AXON_E_ARG, "axon_tp_wait: NULL flags");
   tp_wait_kernel<<<1, 32, 0, as_stream(stream)>>>(flags, world, epoch);
   return launch_status("axon_tp_wait");
+}
+
+extern "C" int axon_tp_wait_count(const int32_t* counter, int32_t target, void* stream) {
+  if (!counter) return fail(AXON_E_ARG, "axon_tp_wait_count: NULL counter");
+  tp_wait_count_kernel<<<1, 32, 0, as_stream(stream)>>>(counter, target);
+  return launch_status("axon_tp_wait_count");
 }
 
 extern "C" int axon_tp_reduce_gather(const void* inbox, void* const* outs, const int32_t* arrive, int32_t world,

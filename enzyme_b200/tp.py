@@ -185,8 +185,17 @@ class PeerLayout:
         return _round_up(self.y_offset + self.m * self.hidden * self.out_itemsize, 256)
 
     @property
-    def total_bytes(self) -> int:
+    def counts_offset(self) -> int:
+        """Whole-step kernel: arrival counts [m / 256] then the done count."""
         return _round_up(self.flags_offset + 2 * self.nslabs * self.world * 4, 256)
+
+    @property
+    def done_count_offset(self) -> int:
+        return self.counts_offset + _round_up(-(-self.m // 256) * 4, 16)
+
+    @property
+    def total_bytes(self) -> int:
+        return _round_up(self.done_count_offset + 16, 256)
 
     def inbox_offset(self, slab_start: int) -> int:
         return slab_start * self.hidden * 2
@@ -259,7 +268,8 @@ class FusedTPSwiGLU:
     the GEMMs over NVLink peer memory (csrc/tp.cu):
 
     per slab: SiLU-gate GEMM -> f16 activation; down GEMM whose epilogue
-    stores each f16 partial row into its owner rank's inbox; a release of the
+    stores each f16 partial row into its owner rank's inbox (with one slab,
+    both GEMMs run as one kernel, axon_tp_mlp_partial); a release of the
     slab's arrival flags; on a side stream the owner waits for every rank's
     partials, sums them in fp32, rounds once to bf16 and pushes its rows into
     every rank's output, then raises the done flags. forward() ends with a
@@ -267,10 +277,16 @@ class FusedTPSwiGLU:
     tensor (a view of the shared buffer, valid until the next forward) holds
     the full output on every rank. The output is one rounding of the fp32 sum
     of world f16-rounded partials.
+
+    whole_step=True runs the step as one kernel (axon_tp_mlp_step): rows are
+    owned in 8-row granules dealt to the ranks in turn, so every owner's rows
+    complete while the down projection is still running, and the reduction
+    and all-gather push run as the kernel's last tiles; one wait for the done
+    count ends the step.
     """
 
     def __init__(self, w_gate, w_up, w_down, m: int, *, group=None, slabs: int = 2, tune=None,
-                 reduce_ctas: int = 16, out_dtype=torch.bfloat16):
+                 reduce_ctas: int = 16, out_dtype=torch.bfloat16, whole_step: bool = False):
         self.w_gate, self.w_up, self.w_down = w_gate, w_up, w_down
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -286,9 +302,20 @@ class FusedTPSwiGLU:
         self.peers = PeerBuffers(self.layout, dev, group)
         self.y = self.peers.output(out_dtype)
         self.w_down_h = torch.empty(w_down.shape, dtype=torch.float16, device=dev)
-        self.act = torch.empty((m, w_gate.shape[1]), dtype=torch.float16, device=dev)
+        from . import _native as N
+
+        # activation [m, n] f16 followed by the fused kernel's counters
+        n = w_gate.shape[1]
+        self.ws = torch.empty(int(N.lib().axon_tp_mlp_workspace_bytes(m, n)), dtype=torch.uint8, device=dev)
+        self.act = self.ws[:m * n * 2].view(torch.float16).view(m, n)
         self.side = torch.cuda.Stream(device=dev)
         self.epoch = 0
+        # one kernel per step (axon_tp_mlp_step): both GEMMs and the reduction
+        self.whole_step = bool(whole_step)
+        if self.whole_step:
+            if out_dtype != torch.bfloat16 or m % 256 or self.world not in (1, 2, 4, 8):
+                raise ValueError("whole_step needs bf16 output, m % 256 == 0 and 1, 2, 4 or 8 ranks")
+            self.done_per_epoch = int(N.lib().axon_tp_step_done_per_epoch(self.world, m, self.hidden))
 
     def close(self) -> None:
         torch.cuda.synchronize(self.w_gate.device)
@@ -311,6 +338,36 @@ class FusedTPSwiGLU:
         out_code = {torch.bfloat16: N.AXON_BF16, torch.float16: N.AXON_F16, torch.float32: N.AXON_F32}[self.out_dtype]
         ops.cast(self.w_down, torch.float16, out=self.w_down_h)
         y_ptrs = ptrs([b + lo.y_offset for b in self.peers.bases])
+        mine = self.peers.bases[self.rank]
+        if self.whole_step:
+            bases = self.peers.bases
+            N.check(lib.axon_tp_mlp_step(
+                x.data_ptr(), self.w_gate.data_ptr(), self.w_up.data_ptr(), self.w_down_h.data_ptr(),
+                self.ws.data_ptr(), self.ws.numel(), mine + lo.inbox_offset(0),
+                ptrs([b + lo.inbox_offset(0) for b in bases]), ptrs([b + lo.counts_offset for b in bases]),
+                ptrs([b + lo.done_count_offset for b in bases]), y_ptrs, W, self.rank, e, self.m,
+                self.act.shape[1], x.shape[1], self.hidden, tune, main.cuda_stream))
+            target = (e * self.done_per_epoch + 2 ** 31) % 2 ** 32 - 2 ** 31  # int32 wrap, as the counters
+            N.check(lib.axon_tp_wait_count(mine + lo.done_count_offset, target, main.cuda_stream))
+            return self.y
+        if len(self.slabs) == 1:
+            # one slab: both GEMMs in one kernel, the down projection's rows
+            # scattered to the owners as its tiles finish
+            rows = self.m // W
+            inboxes = ptrs([base + lo.inbox_offset(0) for base in self.peers.bases])
+            N.check(lib.axon_tp_mlp_partial(x.data_ptr(), self.w_gate.data_ptr(), self.w_up.data_ptr(),
+                                            self.w_down_h.data_ptr(), self.ws.data_ptr(), self.ws.numel(), inboxes,
+                                            W, self.rank, self.m, self.act.shape[1], x.shape[1], self.hidden, rows,
+                                            tune, main.cuda_stream))
+            N.check(lib.axon_tp_signal(ptrs([base + lo.arrive_offset(0) for base in self.peers.bases]), W,
+                                       self.rank, e, main.cuda_stream))
+            N.check(lib.axon_tp_reduce_gather(mine + lo.inbox_offset(0), y_ptrs, mine + lo.arrive_offset(0), W,
+                                              self.rank, e, rows, self.hidden, 0, self.hidden, out_code, 0,
+                                              main.cuda_stream))
+            N.check(lib.axon_tp_signal(ptrs([base + lo.done_offset(0) for base in self.peers.bases]), W,
+                                       self.rank, e, main.cuda_stream))
+            N.check(lib.axon_tp_wait(mine + lo.done_offset(0), W, e, main.cuda_stream))
+            return self.y
         for i, (a, b) in enumerate(self.slabs):
             rows = (b - a) // W
             ops.gemm(x[a:b], self.w_gate, b2=self.w_up, epilogue=N.AXON_EPI_SILU_GATE, out=self.act[a:b],
@@ -327,14 +384,12 @@ class FusedTPSwiGLU:
             st = main if last else self.side
             if not last:
                 self.side.wait_stream(main)
-            mine = self.peers.bases[self.rank]
             N.check(lib.axon_tp_reduce_gather(mine + lo.inbox_offset(a), y_ptrs, mine + lo.arrive_offset(i), W,
                                               self.rank, e, rows, self.hidden, a, self.hidden, out_code,
                                               0 if last else self.reduce_ctas, st.cuda_stream))
             N.check(lib.axon_tp_signal(ptrs([base + lo.done_offset(i) for base in self.peers.bases]), W,
                                        self.rank, e, st.cuda_stream))
         main.wait_stream(self.side)
-        mine = self.peers.bases[self.rank]
         for i in range(len(self.slabs)):
             N.check(lib.axon_tp_wait(mine + lo.done_offset(i), W, e, main.cuda_stream))
         return self.y

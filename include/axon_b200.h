@@ -274,6 +274,44 @@ AXON_API int axon_tp_down_partial(const void* act, const void* w, void* const* i
                          int32_t rank, int64_t m, int64_t n, int64_t k, int64_t rows_per_owner,
                          int32_t ab_dtype, const axon_tune_t* tune, void* stream);
 
+/* Both GEMMs of one rank's SwiGLU shard in one CTA-pair kernel (the fused
+ * kernel axon_silu_mlp runs at precision 4): act = silu(x @ w_gate) *
+ * (x @ w_up) as f16 in `workspace`, then act @ w_down_h (f16 [n, p], the
+ * caller's f16 copy of W_down) with the down projection's f16 partial rows
+ * scattered to the owners' inboxes as axon_tp_down_partial does.
+ * x [m, k] bf16, w_gate/w_up [k, n] bf16; m = world * rows_per_owner. */
+AXON_API int64_t axon_tp_mlp_workspace_bytes(int64_t m, int64_t n);
+AXON_API int axon_tp_mlp_partial(const void* x, const void* w_gate, const void* w_up,
+                        const void* w_down_h, void* workspace, int64_t workspace_bytes,
+                        void* const* inboxes, int32_t world, int32_t rank, int64_t m, int64_t n,
+                        int64_t k, int64_t p, int64_t rows_per_owner, const axon_tune_t* tune,
+                        void* stream);
+
+/* One whole tensor-parallel SwiGLU step of rank `rank` in one kernel (world
+ * 1, 2, 4 or 8; m a multiple of 256): the two GEMMs as axon_tp_mlp_partial,
+ * with output rows owned in 8-row granules dealt to the ranks in turn (row r
+ * belongs to rank (r / 8) % world), each phase-B warp releasing its rows into
+ * the owners' arrival counts arrive[o][r / 256] (system scope), and then the
+ * owner-side reduction inside the same kernel: for each 256-row block, once
+ * all ranks' partials of this rank's rows have arrived, they are summed in
+ * fp32 in rank order, rounded once to bf16 and stored to every rank's output
+ * ys[d] [m, p] bf16, and done[d] is incremented on every rank. Counts
+ * accumulate: step `epoch` (1, 2, ...) is complete on a rank when its done
+ * count reaches epoch * axon_tp_step_done_per_epoch(world, m, p)
+ * (axon_tp_wait_count). inbox = this rank's inbox, inboxes[o] = rank o's,
+ * each [world][m / world][p] f16; workspace as axon_tp_mlp_partial's. */
+AXON_API int64_t axon_tp_step_done_per_epoch(int32_t world, int64_t m, int64_t p);
+AXON_API int axon_tp_mlp_step(const void* x, const void* w_gate, const void* w_up,
+                     const void* w_down_h, void* workspace, int64_t workspace_bytes,
+                     const void* inbox, void* const* inboxes, int32_t* const* arrive,
+                     int32_t* const* done, void* const* ys, int32_t world, int32_t rank,
+                     int32_t epoch, int64_t m, int64_t n, int64_t k, int64_t p,
+                     const axon_tune_t* tune, void* stream);
+
+/* Bounded wait (~2 s) on `stream` until *counter >= target (wrap-safe); a
+ * wait that gives up records AXON_E_TIMEOUT for axon_tp_status. */
+AXON_API int axon_tp_wait_count(const int32_t* counter, int32_t target, void* stream);
+
 /* After the work already on `stream`: a system-scope fence, then
  * flags[d][rank] = epoch (release) for every rank d (flags[d] = int32[world]
  * on rank d, peer-mapped). */

@@ -159,4 +159,8 @@ def test_fused_slabs_and_layout():
     assert lo.inbox_offset(2048) == 2048 * 4096 * 2
     assert lo.inbox_offset(4096) == lo.inbox_bytes
     flags = {lo.arrive_offset(0), lo.done_offset(0), lo.arrive_offset(1), lo.done_offset(1)}
-    assert len(flags) == 4 and max(flags) + 8 * 4 <= lo.total_bytes
+    assert len(flags) == 4 and max(flags) + 8 * 4 <= lo.counts_offset
+    # whole-step counts: one per 256-row block, then the done count
+    assert lo.counts_offset % 256 == 0
+    assert lo.done_count_offset >= lo.counts_offset + 16 * 4
+    assert lo.done_count_offset + 4 <= lo.total_bytes

@@ -115,7 +115,7 @@ def _swiglu_case(m, h, inter, seed):
     return x, wg, wu, wd
 
 
-def _fused_rank(rank, world, port, q):
+def _fused_rank(rank, world, port, q, whole_step=False):
     import datetime
 
     import torch.distributed as dist
@@ -130,7 +130,7 @@ def _fused_rank(rank, world, port, q):
         dev = torch.device("cuda", rank)
         x, wg, wu, wd = _swiglu_case(1024, 1024, 2048, 3)
         shards = [s.to(dev) for s in tp.shard_swiglu(wg, wu, wd, rank, world)]
-        f = tp.FusedTPSwiGLU(*shards, m=1024, slabs=2, tune={"max_ctas": 132})
+        f = tp.FusedTPSwiGLU(*shards, m=1024, slabs=2, tune={"max_ctas": 132}, whole_step=whole_step)
         xd = x.to(dev)
         y1 = f.forward(xd).clone()
         y2 = f.forward(xd).clone()  # second epoch reuses inboxes, output and flags
@@ -144,7 +144,8 @@ def _fused_rank(rank, world, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_fused_tp_swiglu_two_gpus():
+@pytest.mark.parametrize("whole_step", [False, True])
+def test_fused_tp_swiglu_two_gpus(whole_step):
     import torch.multiprocessing as mp
 
     from oracle import f64
@@ -152,7 +153,7 @@ def test_fused_tp_swiglu_two_gpus():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_fused_rank, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_fused_rank, args=(r, 2, port, q, whole_step)) for r in range(2)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in range(2)]
@@ -168,17 +169,22 @@ def test_fused_tp_swiglu_two_gpus():
     np.testing.assert_array_equal(res[0][1], res[1][1])
 
 
-def test_fused_tp_single_rank(cuda_device):
-    """world = 1: the same kernels with the inbox and output local."""
+@pytest.mark.parametrize("slabs,whole_step", [(2, False), (1, False), (1, True)])
+def test_fused_tp_single_rank(slabs, whole_step, cuda_device):
+    """world = 1: the same kernels with the inbox and output local; twice, so
+    the whole-step kernel's accumulating counts are exercised."""
     from enzyme_b200 import ops, tp
     from oracle import f64
 
     x, wg, wu, wd = _swiglu_case(512, 512, 1024, 4)
-    f = tp.FusedTPSwiGLU(wg.to(cuda_device), wu.to(cuda_device), wd.to(cuda_device), m=512, slabs=2)
+    f = tp.FusedTPSwiGLU(wg.to(cuda_device), wu.to(cuda_device), wd.to(cuda_device), m=512, slabs=slabs,
+                         whole_step=whole_step)
+    y1 = f.forward(x.to(cuda_device)).clone()
     y = f.forward(x.to(cuda_device))
     torch.cuda.synchronize()
     f.status()
     ops.gemm_status()
+    assert torch.equal(y1, y)
     rows = np.arange(0, 512, 3)
     want = f64.silu_mlp(*(t.float().numpy() for t in (x[rows], wg, wu, wd)))
     np.testing.assert_allclose(y.float().cpu().numpy()[rows], want, rtol=1e-2, atol=1e-2)
