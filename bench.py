@@ -338,20 +338,21 @@ class SwiGLU(Workload):
             # rank, slab by slab (enzyme_b200.tp.FusedTPSwiGLU)
             from enzyme_b200.tp import FusedTPSwiGLU
 
-            slabs = self.SLABS if world <= 2 else 1
-            self.tp = FusedTPSwiGLU(self.w1, self.w2, self.w3, m=m, slabs=slabs, tune=self.TP_TUNE,
+            self.tp = FusedTPSwiGLU(self.w1, self.w2, self.w3, m=m, slabs=self.SLABS, tune=self.TP_TUNE,
                                     reduce_ctas=self.REDUCE_CTAS)
             self.y = self.tp.y
-            # cast, then per slab: gate/up GEMM, down GEMM, signal, reduce, signal; one wait per slab
-            self.launches_per_step = 1 + 6 * len(self.tp.slabs)
+            # cast, fused SwiGLU kernel (both GEMMs, partial rows scattered to
+            # their owners), signal, reduce + all-gather push, signal, wait
+            self.launches_per_step = 6
 
     PRECISION = 4
-    # measured on 2 B200s: NCCL all-reduce of fp32 partials per slab 660-680 us;
-    # fused (2 slabs, GEMM grid capped at 132 CTAs, 32-CTA side reduce) 610 us;
-    # 4 or 8 slabs slower (ragged last waves of the smaller GEMMs). On 8: one
-    # slab 274 us, two 307 us (the side reduce slows the shard's small GEMMs).
-    SLABS = 2
-    TP_TUNE = {"max_ctas": 132}
+    # measured per step on 2 B200s: NCCL all-reduce of fp32 partials per
+    # slab 653-680 us; fused SwiGLU kernel with the scatter, then the owner
+    # reduce + push, 595 us; two slabs of separate GEMMs 605 us; the
+    # whole-step kernel (reduction inside the GEMM kernel) 713 us. On 8:
+    # 270 us one slab vs 308 two slabs vs 430 NCCL.
+    SLABS = 1
+    TP_TUNE = None
     REDUCE_CTAS = 32
 
     def check(self):

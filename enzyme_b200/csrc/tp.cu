@@ -145,6 +145,76 @@ __global__ void __launch_bounds__(256) tp_reduce_gather_kernel(const __half* __r
   }
 }
 
+// The same reduction for contiguous outputs (ld_out == n), pushed by the bulk
+// copy engine: a CTA sums a chunk of whole rows into shared memory, then one
+// thread issues a 1-D bulk copy of the chunk to every rank's output
+// (cp.async.bulk global <- shared, no multicast), so the all-gather crosses
+// NVLink in long bursts instead of per-thread 16-byte stores. Two chunk
+// buffers alternate: a buffer is refilled once its copies have read it.
+template <typename Tout>
+__global__ void __launch_bounds__(256) tp_reduce_push_kernel(const __half* __restrict__ inbox, OutPtrs outs,
+                                                             const int* arrive, int world, int rank, int epoch,
+                                                             int64_t rows, int64_t n, int64_t out_row0,
+                                                             int chunk_rows) {
+  extern __shared__ __align__(128) unsigned char cbuf[];
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    ok = wait_flags(arrive, world, epoch);
+    if (!ok) atomicExch(&g_tp_error, AXON_E_TIMEOUT);
+  }
+  __syncthreads();
+  if (!ok) return;
+  const int64_t slot = rows * n;
+  const int64_t nchunks = (rows + chunk_rows - 1) / chunk_rows;
+  const int64_t chunk_bytes = static_cast<int64_t>(chunk_rows) * n * sizeof(Tout);
+  const int64_t first_row = out_row0 + static_cast<int64_t>(rank) * rows;
+  int it = 0;
+  for (int64_t ch = blockIdx.x; ch < nchunks; ch += gridDim.x, ++it) {
+    Tout* buf = reinterpret_cast<Tout*>(cbuf + (it & 1) * chunk_bytes);
+    if (threadIdx.x == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");  // buffer's copies have read it
+    __syncthreads();
+    const int64_t r0 = ch * chunk_rows;
+    const int64_t nr = rows - r0 < chunk_rows ? rows - r0 : chunk_rows;
+    const int64_t packets = nr * n / 8;
+    const __half* src = inbox + r0 * n;
+    for (int64_t pk0 = threadIdx.x; pk0 < packets; pk0 += 2 * blockDim.x) {
+      Vec<__half> v[2][kMaxWorld];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int64_t pk = pk0 + u * blockDim.x;
+#pragma unroll
+        for (int s = 0; s < kMaxWorld; ++s)
+          if (s < world && pk < packets) v[u][s].u = __ldcv(reinterpret_cast<const uint4*>(src + s * slot + pk * 8));
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int64_t pk = pk0 + u * blockDim.x;
+        if (pk >= packets) break;
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int s = 0; s < kMaxWorld; ++s)  // fixed rank order
+          if (s < world)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[e] += __half2float(v[u][s].e[e]);
+        store8(buf + pk * 8, acc);
+      }
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // shared-memory writes -> bulk copy reads
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const uint32_t bytes = static_cast<uint32_t>(nr * n * sizeof(Tout));
+      const uint32_t saddr = static_cast<uint32_t>(__cvta_generic_to_shared(buf));
+      for (int d = 0; d < world; ++d) {
+        Tout* dst = static_cast<Tout*>(outs.p[d]) + (first_row + r0) * n;
+        asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(saddr), "r"(bytes)
+                     : "memory");
+      }
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    }
+  }
+  if (threadIdx.x == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // every copy complete
+}
+
 PFN_cuMemGetAddressRange_v3020 address_range_fn() {
   static PFN_cuMemGetAddressRange_v3020 fn = nullptr;
   static bool tried = false;
@@ -257,6 +327,39 @@ extern "C" int axon_tp_reduce_gather(const void* inbox, void* const* outs, const
   if (grid < 1) grid = 1;  // still waits for the arrivals, so the done flags keep their meaning
   cudaStream_t s = as_stream(stream);
   const __half* in = static_cast<const __half*>(inbox);
+  // contiguous outputs: whole-row chunks of about 32 KB pushed by bulk copies
+  const int osize = out_dtype == AXON_F32 ? 4 : 2;
+  if (ld_out == n && n * osize <= 32768) {
+    const int chunk_rows = static_cast<int>(32768 / (n * osize));
+    const int64_t nchunks = (rows + chunk_rows - 1) / chunk_rows;
+    int64_t g2 = nchunks < cap ? nchunks : cap;
+    if (g2 < 1) g2 = 1;
+    const size_t smem = 2 * static_cast<size_t>(chunk_rows) * n * osize;
+    switch (out_dtype) {
+      case AXON_BF16: {
+        auto k = tp_reduce_push_kernel<__nv_bfloat16>;
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        k<<<static_cast<unsigned>(g2), 256, smem, s>>>(in, o, arrive, world, rank, epoch, rows, n, out_row0,
+                                                        chunk_rows);
+        break;
+      }
+      case AXON_F16: {
+        auto k = tp_reduce_push_kernel<__half>;
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        k<<<static_cast<unsigned>(g2), 256, smem, s>>>(in, o, arrive, world, rank, epoch, rows, n, out_row0,
+                                                        chunk_rows);
+        break;
+      }
+      default: {
+        auto k = tp_reduce_push_kernel<float>;
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        k<<<static_cast<unsigned>(g2), 256, smem, s>>>(in, o, arrive, world, rank, epoch, rows, n, out_row0,
+                                                        chunk_rows);
+        break;
+      }
+    }
+    return launch_status("axon_tp_reduce_gather");
+  }
   switch (out_dtype) {
     case AXON_BF16:
       tp_reduce_gather_kernel<__nv_bfloat16><<<static_cast<unsigned>(grid), 256, 0, s>>>(in, o, arrive, world, rank,
