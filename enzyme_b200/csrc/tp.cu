@@ -327,10 +327,11 @@ extern "C" int axon_tp_reduce_gather(const void* inbox, void* const* outs, const
   if (grid < 1) grid = 1;  // still waits for the arrivals, so the done flags keep their meaning
   cudaStream_t s = as_stream(stream);
   const __half* in = static_cast<const __half*>(inbox);
-  // contiguous outputs: whole-row chunks of about 32 KB pushed by bulk copies
+  // contiguous outputs: whole-row chunks of about 8 KB pushed by bulk copies
+  // (small chunks: every SM gets several, its loads and pushes overlap)
   const int osize = out_dtype == AXON_F32 ? 4 : 2;
   if (ld_out == n && n * osize <= 32768) {
-    const int chunk_rows = static_cast<int>(32768 / (n * osize));
+    const int chunk_rows = n * osize >= 8192 ? 1 : static_cast<int>(8192 / (n * osize));
     const int64_t nchunks = (rows + chunk_rows - 1) / chunk_rows;
     int64_t g2 = nchunks < cap ? nchunks : cap;
     if (g2 < 1) g2 = 1;
