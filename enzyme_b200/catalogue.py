@@ -26,7 +26,8 @@ Tile knob meaning (the CUDA counterpart of TILES_IN_BLOCK_*):
                         K -> stages, P -> down-projection BLOCK_N = 64*v
                         (recorded; the down GEMM picks its own tile today).
                         hw_variant 0/1/2 stores the activation as 1/2/3 bf16
-                        terms (see axon_silu_mlp).
+                        terms, 3 as f16, 4 as f16 with both GEMMs in one
+                        kernel (see axon_silu_mlp).
 """
 
 from __future__ import annotations
@@ -73,7 +74,7 @@ def variants(spec_name: str) -> list[Variant]:
         return [Variant(0, "tcgen05_ws_persistent"), Variant(1, "tcgen05_cta_pair")]
     if spec_name in MLP_SPECS:
         return [Variant(0, "tcgen05_act_1term"), Variant(1, "tcgen05_act_2term"), Variant(2, "tcgen05_act_3term"),
-                Variant(3, "tcgen05_act_f16")]
+                Variant(3, "tcgen05_act_f16"), Variant(4, "tcgen05_act_f16_fused")]
     raise KeyError(f"no CUDA variants for spec '{spec_name}'")
 
 
@@ -162,6 +163,8 @@ def tune_for(spec_name: str, hw_variant: int, tiles: dict[str, int]) -> dict | l
         bn = 64 * t["N"]
         return {"variant": hw_variant + 1, "block_n": bn, "stages": min(t["K"], gemm_max_stages(hw_variant == 1, bn))}
     if spec_name in MLP_SPECS:
+        if hw_variant == 4:  # both GEMMs in one kernel (256-column tiles; N and P are recorded only)
+            return {"variant": 3, "stages": t["K"], "precision": 4, "down_block_n": 64 * t["P"]}
         precision = 4 if hw_variant == 3 else hw_variant + 1
         return {"block_n": 128 * t["N"], "stages": t["K"], "precision": precision, "down_block_n": 64 * t["P"]}
     raise KeyError(spec_name)

@@ -1802,6 +1802,7 @@ extern "C" int axon_rmsnorm_matmul(const void* x, const void* w, void* y, void* 
 }
 
 constexpr int kF16Act = 4;  // tune.precision value of the f16-activation mode
+constexpr int64_t kFusedMaxTiles = 1024;  // see axon_silu_mlp
 
 static int silu_terms(const axon_tune_t* tune) {
   const int p = tune ? tune->precision : 0;
@@ -1851,10 +1852,18 @@ extern "C" int axon_silu_mlp(const void* x, const void* w1, const void* w2, cons
     int* counters = reinterpret_cast<int*>(static_cast<unsigned char*>(workspace) + m * n * 2 + n * p * 2);
     int rc = cast_impl(w3, w3h, n * p, AXON_BF16, AXON_F16, as_stream(stream));
     if (rc) return rc;
-    // variant 0 (default): both GEMMs in one CTA-pair kernel; 1 / 2: two
-    // launches of the one-CTA / CTA-pair GEMM
-    if (t.variant == 0 && m >= 256)
+    // variant 3: both GEMMs in one CTA-pair kernel; 1 / 2: two launches of
+    // the one-CTA / CTA-pair GEMM; 0 (default): the fused kernel while the
+    // gate/up GEMM has fewer than 1024 pair tiles (about 14 waves on 74
+    // pairs), where filling the first GEMM's last partial wave with the
+    // second's tiles pays; two launches above that. Measured on B200: the
+    // 8-way shard of the BASELINE config (224 + 256 tiles) 151 us fused vs
+    // 175 us in two launches; the full config (1792 + 256 tiles) 1.06 ms
+    // fused vs 0.98 ms (the fused order reads the gate/up weights twice).
+    const int64_t tiles_a = (m + 255) / 256 * ((n + 127) / 128);
+    if (m >= 256 && (t.variant == 3 || (t.variant == 0 && tiles_a < kFusedMaxTiles)))
       return swiglu_fused_impl(x, w1, w2, w3h, act, counters, y, p, c_dtype, m, n, k, p, t, stream);
+    if (t.variant == 3) return fail(AXON_E_SHAPE, "axon_silu_mlp: the fused variant needs m >= 256");
     rc = gemm_impl(x, w1, w2, act, nullptr, m, n, k, k, n, n, ab_dtype, AXON_F16, AXON_EPI_SILU_GATE, &up, stream, 1,
                    0, 0);
     if (rc) return rc;

@@ -365,8 +365,8 @@ AXON_API int axon_rmsnorm_matmul(const void* x, const void* w, void* y, void* wo
                         int32_t c_dtype, const axon_tune_t* tune, void* stream);
 
 /* Bytes of scratch axon_silu_mlp needs: the [m, n] activation in ab_dtype
- * times tune->precision terms, or for precision 4 an f16 activation plus an
- * f16 copy of w3 ([n, p]). */
+ * times tune->precision terms, or for precision 4 an f16 activation, an f16
+ * copy of w3 ([n, p]) and the fused kernel's counters. */
 AXON_API int64_t axon_silu_mlp_workspace_bytes(int64_t m, int64_t n, int64_t p, int32_t ab_dtype,
                                                const axon_tune_t* tune);
 
@@ -385,7 +385,11 @@ AXON_API int64_t axon_silu_mlp_workspace_bytes(int64_t m, int64_t n, int64_t p, 
  *                than bf16 for ~3% extra traffic, finite only while |a| < 65504.
  * An fp32 reference at 1e-2 needs precision >= 2 (or 4) at the SwiGLU config
  * and 3 for N(0, 1) weights. In the column/row tensor-parallel form each rank
- * passes its shard (n = inter / G) and sums the fp32 partial outputs. */
+ * passes its shard (n = inter / G) and sums the fp32 partial outputs.
+ * tune->variant at precision 4: 1 / 2 = two launches of the one-CTA / CTA-pair
+ * GEMM, 3 = both GEMMs in one CTA-pair kernel (m >= 256), 0 (default) = 3
+ * while the gate/up GEMM has fewer than 1024 256 x 128 tiles, else 2. Other
+ * precisions run two launches (variant as axon_gemm's). */
 AXON_API int axon_silu_mlp(const void* x, const void* w1, const void* w2, const void* w3,
                   void* y, void* workspace, int64_t workspace_bytes, int64_t m,
                   int64_t n, int64_t k, int64_t p, int32_t ab_dtype, int32_t c_dtype,

@@ -464,7 +464,7 @@ def test_silu_precision_ladder(cuda_device):
     assert errs[0] > 100 * errs[1] > 0 and errs[2] <= errs[1] * 1.5, errs
 
 
-@pytest.mark.parametrize("terms,variant", [(2, 0), (4, 0), (4, 1), (4, 2)])
+@pytest.mark.parametrize("terms,variant", [(2, 0), (4, 0), (4, 1), (4, 2), (4, 3)])
 def test_silu_mlp_config_sampled_rows(terms, variant, cuda_device):
     """The BASELINE SwiGLU config at full size, checked on sampled rows. A
     one-term bf16 activation is not enough here: over the whole output about
@@ -483,7 +483,7 @@ def test_silu_mlp_config_sampled_rows(terms, variant, cuda_device):
 @pytest.mark.parametrize("shape", [(300, 264, 200, 136), (256, 128, 64, 256), (1024, 1792, 4096, 4096),
                                    (777, 520, 136, 264)])
 def test_silu_mlp_fused_kernel_matches_two_launches(shape, cuda_device):
-    """Precision 4, variant 0 runs both GEMMs in one kernel (dynamic tiles,
+    """Precision 4, variant 3 runs both GEMMs in one kernel (dynamic tiles,
     row-block readiness counters); variant 2 runs the same CTA-pair tiles as
     two launches. Same MMAs in the same k order: the results are identical.
     Both are checked against the float64 oracle."""
@@ -492,7 +492,7 @@ def test_silu_mlp_fused_kernel_matches_two_launches(shape, cuda_device):
     x = torch.randn(m, k, generator=g, device=cuda_device).bfloat16()
     w1, w2 = ((torch.randn(k, n, generator=g, device=cuda_device) / k ** 0.5).bfloat16() for _ in range(2))
     w3 = (torch.randn(n, p, generator=g, device=cuda_device) / n ** 0.5).bfloat16()
-    fused = ops.silu_mlp(x, w1, w2, w3, out_dtype=torch.float32, tune={"precision": 4})
+    fused = ops.silu_mlp(x, w1, w2, w3, out_dtype=torch.float32, tune={"precision": 4, "variant": 3})
     two = ops.silu_mlp(x, w1, w2, w3, out_dtype=torch.float32, tune={"precision": 4, "variant": 2})
     ops.gemm_status()
     assert torch.equal(fused, two)
