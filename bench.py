@@ -341,16 +341,17 @@ class SwiGLU(Workload):
             self.tp = FusedTPSwiGLU(self.w1, self.w2, self.w3, m=m, slabs=self.SLABS, tune=self.TP_TUNE,
                                     reduce_ctas=self.REDUCE_CTAS)
             self.y = self.tp.y
-            # cast, fused SwiGLU kernel (both GEMMs, partial rows scattered to
-            # their owners), signal, reduce + all-gather push, signal, wait
-            self.launches_per_step = 6
+            # cast, the GEMMs (one fused kernel, or gate/up + scattering down
+            # projection), signal, reduce + all-gather push, signal, wait
+            self.launches_per_step = 6 if self.tp.fused_kernel else 7
 
     PRECISION = 4
     # measured per step on 2 B200s: NCCL all-reduce of fp32 partials per
-    # slab 653-680 us; fused SwiGLU kernel with the scatter, then the owner
-    # reduce + push, 595 us; two slabs of separate GEMMs 605 us; the
-    # whole-step kernel (reduction inside the GEMM kernel) 713 us. On 8:
-    # 270 us one slab vs 308 two slabs vs 430 NCCL.
+    # slab 653-680 us; one slab of two launches (gate/up, scattering down
+    # projection) then the owner reduce + push 576 us, with the fused SwiGLU
+    # kernel 602 us, two slabs 639 us; the whole-step kernel 713 us. On 8
+    # (fused kernel, the shard is small): 270 us one slab vs 308 two slabs
+    # vs 430 NCCL.
     SLABS = 1
     TP_TUNE = None
     REDUCE_CTAS = 32

@@ -1802,7 +1802,7 @@ extern "C" int axon_rmsnorm_matmul(const void* x, const void* w, void* y, void* 
 }
 
 constexpr int kF16Act = 4;  // tune.precision value of the f16-activation mode
-constexpr int64_t kFusedMaxTiles = 1024;  // see axon_silu_mlp
+constexpr int64_t kFusedMaxTiles = 320;  // see axon_silu_mlp
 
 static int silu_terms(const axon_tune_t* tune) {
   const int p = tune ? tune->precision : 0;
@@ -1854,12 +1854,13 @@ extern "C" int axon_silu_mlp(const void* x, const void* w1, const void* w2, cons
     if (rc) return rc;
     // variant 3: both GEMMs in one CTA-pair kernel; 1 / 2: two launches of
     // the one-CTA / CTA-pair GEMM; 0 (default): the fused kernel while the
-    // gate/up GEMM has fewer than 1024 pair tiles (about 14 waves on 74
-    // pairs), where filling the first GEMM's last partial wave with the
-    // second's tiles pays; two launches above that. Measured on B200: the
-    // 8-way shard of the BASELINE config (224 + 256 tiles) 151 us fused vs
-    // 175 us in two launches; the full config (1792 + 256 tiles) 1.06 ms
-    // fused vs 0.98 ms (the fused order reads the gate/up weights twice).
+    // gate/up GEMM has fewer than 320 pair tiles (about 4 waves on 74 pairs),
+    // where filling the first GEMM's last partial wave with the second's
+    // tiles pays; two launches above that. Measured on one B200, m = k = p =
+    // 4096: n = 1792 (the 8-way shard of the BASELINE config, 224 tiles)
+    // 156-169 us fused vs 182-194 us in two launches; n = 3584: 316-324 vs
+    // 305-314; n = 7168: 631 vs 520-580; n = 14336: 1240 vs 1149-1185 (the
+    // fused order reads the gate/up weights once per row group).
     const int64_t tiles_a = (m + 255) / 256 * ((n + 127) / 128);
     if (m >= 256 && (t.variant == 3 || (t.variant == 0 && tiles_a < kFusedMaxTiles)))
       return swiglu_fused_impl(x, w1, w2, w3h, act, counters, y, p, c_dtype, m, n, k, p, t, stream);

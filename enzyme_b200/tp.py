@@ -286,7 +286,8 @@ class FusedTPSwiGLU:
     """
 
     def __init__(self, w_gate, w_up, w_down, m: int, *, group=None, slabs: int = 2, tune=None,
-                 reduce_ctas: int = 16, out_dtype=torch.bfloat16, whole_step: bool = False):
+                 reduce_ctas: int = 16, out_dtype=torch.bfloat16, whole_step: bool = False,
+                 fused_kernel: bool | None = None):
         self.w_gate, self.w_up, self.w_down = w_gate, w_up, w_down
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -310,6 +311,11 @@ class FusedTPSwiGLU:
         self.act = self.ws[:m * n * 2].view(torch.float16).view(m, n)
         self.side = torch.cuda.Stream(device=dev)
         self.epoch = 0
+        # Both GEMMs in one kernel pays while the shard's gate/up GEMM is a
+        # few waves of 256 x 128 tiles (the rule axon_silu_mlp's default
+        # applies: fewer than 320 tiles, e.g. 8 ranks at the BASELINE config);
+        # larger shards run the two GEMMs as separate launches.
+        self.fused_kernel = (-(-m // 256) * -(-n // 128) < 320) if fused_kernel is None else bool(fused_kernel)
         # one kernel per step (axon_tp_mlp_step): both GEMMs and the reduction
         self.whole_step = bool(whole_step)
         if self.whole_step:
@@ -350,7 +356,7 @@ class FusedTPSwiGLU:
             target = (e * self.done_per_epoch + 2 ** 31) % 2 ** 32 - 2 ** 31  # int32 wrap, as the counters
             N.check(lib.axon_tp_wait_count(mine + lo.done_count_offset, target, main.cuda_stream))
             return self.y
-        if len(self.slabs) == 1:
+        if len(self.slabs) == 1 and self.fused_kernel:
             # one slab: both GEMMs in one kernel, the down projection's rows
             # scattered to the owners as its tiles finish
             rows = self.m // W

@@ -388,7 +388,7 @@ AXON_API int64_t axon_silu_mlp_workspace_bytes(int64_t m, int64_t n, int64_t p, 
  * passes its shard (n = inter / G) and sums the fp32 partial outputs.
  * tune->variant at precision 4: 1 / 2 = two launches of the one-CTA / CTA-pair
  * GEMM, 3 = both GEMMs in one CTA-pair kernel (m >= 256), 0 (default) = 3
- * while the gate/up GEMM has fewer than 1024 256 x 128 tiles, else 2. Other
+ * while the gate/up GEMM has fewer than 320 256 x 128 tiles, else 2. Other
  * precisions run two launches (variant as axon_gemm's). */
 AXON_API int axon_silu_mlp(const void* x, const void* w1, const void* w2, const void* w3,
                   void* y, void* workspace, int64_t workspace_bytes, int64_t m,

@@ -169,8 +169,9 @@ def test_fused_tp_swiglu_two_gpus(whole_step):
     np.testing.assert_array_equal(res[0][1], res[1][1])
 
 
-@pytest.mark.parametrize("slabs,whole_step", [(2, False), (1, False), (1, True)])
-def test_fused_tp_single_rank(slabs, whole_step, cuda_device):
+@pytest.mark.parametrize("slabs,whole_step,fused_kernel", [(2, False, None), (1, False, True), (1, False, False),
+                                                        (1, True, None)])
+def test_fused_tp_single_rank(slabs, whole_step, fused_kernel, cuda_device):
     """world = 1: the same kernels with the inbox and output local; twice, so
     the whole-step kernel's accumulating counts are exercised."""
     from enzyme_b200 import ops, tp
@@ -178,7 +179,7 @@ def test_fused_tp_single_rank(slabs, whole_step, cuda_device):
 
     x, wg, wu, wd = _swiglu_case(512, 512, 1024, 4)
     f = tp.FusedTPSwiGLU(wg.to(cuda_device), wu.to(cuda_device), wd.to(cuda_device), m=512, slabs=slabs,
-                         whole_step=whole_step)
+                         whole_step=whole_step, fused_kernel=fused_kernel)
     y1 = f.forward(x.to(cuda_device)).clone()
     y = f.forward(x.to(cuda_device))
     torch.cuda.synchronize()
