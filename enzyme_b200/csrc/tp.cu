@@ -102,8 +102,8 @@ __device__ __forceinline__ void store8(Tout* dst, const float* v) {
 // this rank goes to outs.p[d] + (out_row0 + rank * rows + i) * ld_out on every d.
 template <typename Tout>
 __global__ void __launch_bounds__(256) tp_reduce_gather_kernel(const __half* __restrict__ inbox, OutPtrs outs,
-                                                               const int* arrive, int world, int rank, int epoch,
-                                                               int64_t rows, int64_t n, int64_t out_row0,
+                                                               int n_outs, const int* arrive, int world, int rank,
+                                                               int epoch, int64_t rows, int64_t n, int64_t out_row0,
                                                                int64_t ld_out) {
   __shared__ int ok;
   if (threadIdx.x == 0) {
@@ -140,7 +140,7 @@ __global__ void __launch_bounds__(256) tp_reduce_gather_kernel(const __half* __r
           for (int e = 0; e < 8; ++e) acc[e] += __half2float(v[u][s].e[e]);
       const int64_t e0 = pk * 8;
       const int64_t i = e0 / n, j = e0 - i * n;
-      for (int d = 0; d < world; ++d) store8(static_cast<Tout*>(outs.p[d]) + (first_row + i) * ld_out + j, acc);
+      for (int d = 0; d < n_outs; ++d) store8(static_cast<Tout*>(outs.p[d]) + (first_row + i) * ld_out + j, acc);
     }
   }
 }
@@ -153,8 +153,8 @@ __global__ void __launch_bounds__(256) tp_reduce_gather_kernel(const __half* __r
 // buffers alternate: a buffer is refilled once its copies have read it.
 template <typename Tout>
 __global__ void __launch_bounds__(256) tp_reduce_push_kernel(const __half* __restrict__ inbox, OutPtrs outs,
-                                                             const int* arrive, int world, int rank, int epoch,
-                                                             int64_t rows, int64_t n, int64_t out_row0,
+                                                             int n_outs, const int* arrive, int world, int rank,
+                                                             int epoch, int64_t rows, int64_t n, int64_t out_row0,
                                                              int chunk_rows) {
   extern __shared__ __align__(128) unsigned char cbuf[];
   __shared__ int ok;
@@ -204,7 +204,7 @@ __global__ void __launch_bounds__(256) tp_reduce_push_kernel(const __half* __res
     if (threadIdx.x == 0) {
       const uint32_t bytes = static_cast<uint32_t>(nr * n * sizeof(Tout));
       const uint32_t saddr = static_cast<uint32_t>(__cvta_generic_to_shared(buf));
-      for (int d = 0; d < world; ++d) {
+      for (int d = 0; d < n_outs; ++d) {
         Tout* dst = static_cast<Tout*>(outs.p[d]) + (first_row + r0) * n;
         asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(saddr), "r"(bytes)
                      : "memory");
@@ -303,9 +303,13 @@ extern "C" int axon_tp_wait_count(const int32_t* counter, int32_t target, void* 
   return launch_status("axon_tp_wait_count");
 }
 
-extern "C" int axon_tp_reduce_gather(const void* inbox, void* const* outs, const int32_t* arrive, int32_t world,
-                                     int32_t rank, int32_t epoch, int64_t rows, int64_t n, int64_t out_row0,
-                                     int64_t ld_out, int32_t out_dtype, int32_t max_ctas, void* stream) {
+namespace axon {
+namespace {
+
+// The body of axon_tp_reduce_gather (n_outs = world) and axon_tp_reduce_local (n_outs = 1).
+int reduce_impl(const void* inbox, void* const* outs, int n_outs, const int32_t* arrive, int32_t world,
+                int32_t rank, int32_t epoch, int64_t rows, int64_t n, int64_t out_row0, int64_t ld_out,
+                int32_t out_dtype, int32_t max_ctas, void* stream) {
   int rc = check_world(world, rank, "axon_tp_reduce_gather");
   if (rc) return rc;
   if (rows < 0 || n < 0 || out_row0 < 0) return fail(AXON_E_SHAPE, "axon_tp_reduce_gather: negative size");
@@ -316,7 +320,7 @@ extern "C" int axon_tp_reduce_gather(const void* inbox, void* const* outs, const
     return fail(AXON_E_UNSUPPORTED, "axon_tp_reduce_gather: unsupported output dtype %d", out_dtype);
   if (!aligned16(inbox)) return fail(AXON_E_ALIGN, "axon_tp_reduce_gather: inbox must be 16-byte aligned");
   OutPtrs o{};
-  for (int d = 0; d < world; ++d) {
+  for (int d = 0; d < n_outs; ++d) {
     if (!outs[d] || !aligned16(outs[d])) return fail(AXON_E_ALIGN, "axon_tp_reduce_gather: output %d NULL or unaligned", d);
     o.p[d] = outs[d];
   }
@@ -340,22 +344,22 @@ extern "C" int axon_tp_reduce_gather(const void* inbox, void* const* outs, const
       case AXON_BF16: {
         auto k = tp_reduce_push_kernel<__nv_bfloat16>;
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-        k<<<static_cast<unsigned>(g2), 256, smem, s>>>(in, o, arrive, world, rank, epoch, rows, n, out_row0,
-                                                        chunk_rows);
+        k<<<static_cast<unsigned>(g2), 256, smem, s>>>(in, o, n_outs, arrive, world, rank, epoch, rows, n,
+                                                        out_row0, chunk_rows);
         break;
       }
       case AXON_F16: {
         auto k = tp_reduce_push_kernel<__half>;
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-        k<<<static_cast<unsigned>(g2), 256, smem, s>>>(in, o, arrive, world, rank, epoch, rows, n, out_row0,
-                                                        chunk_rows);
+        k<<<static_cast<unsigned>(g2), 256, smem, s>>>(in, o, n_outs, arrive, world, rank, epoch, rows, n,
+                                                        out_row0, chunk_rows);
         break;
       }
       default: {
         auto k = tp_reduce_push_kernel<float>;
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-        k<<<static_cast<unsigned>(g2), 256, smem, s>>>(in, o, arrive, world, rank, epoch, rows, n, out_row0,
-                                                        chunk_rows);
+        k<<<static_cast<unsigned>(g2), 256, smem, s>>>(in, o, n_outs, arrive, world, rank, epoch, rows, n,
+                                                        out_row0, chunk_rows);
         break;
       }
     }
@@ -363,20 +367,55 @@ extern "C" int axon_tp_reduce_gather(const void* inbox, void* const* outs, const
   }
   switch (out_dtype) {
     case AXON_BF16:
-      tp_reduce_gather_kernel<__nv_bfloat16><<<static_cast<unsigned>(grid), 256, 0, s>>>(in, o, arrive, world, rank,
+      tp_reduce_gather_kernel<__nv_bfloat16><<<static_cast<unsigned>(grid), 256, 0, s>>>(in, o, n_outs, arrive, world, rank,
                                                                                           epoch, rows, n, out_row0,
                                                                                           ld_out);
       break;
     case AXON_F16:
-      tp_reduce_gather_kernel<__half><<<static_cast<unsigned>(grid), 256, 0, s>>>(in, o, arrive, world, rank, epoch,
+      tp_reduce_gather_kernel<__half><<<static_cast<unsigned>(grid), 256, 0, s>>>(in, o, n_outs, arrive, world, rank, epoch,
                                                                                    rows, n, out_row0, ld_out);
       break;
     default:
-      tp_reduce_gather_kernel<float><<<static_cast<unsigned>(grid), 256, 0, s>>>(in, o, arrive, world, rank, epoch,
+      tp_reduce_gather_kernel<float><<<static_cast<unsigned>(grid), 256, 0, s>>>(in, o, n_outs, arrive, world, rank, epoch,
                                                                                   rows, n, out_row0, ld_out);
       break;
   }
   return launch_status("axon_tp_reduce_gather");
+}
+
+}  // namespace
+}  // namespace axon
+
+extern "C" int axon_tp_reduce_gather(const void* inbox, void* const* outs, const int32_t* arrive, int32_t world,
+                                     int32_t rank, int32_t epoch, int64_t rows, int64_t n, int64_t out_row0,
+                                     int64_t ld_out, int32_t out_dtype, int32_t max_ctas, void* stream) {
+  return reduce_impl(inbox, outs, world, arrive, world, rank, epoch, rows, n, out_row0, ld_out, out_dtype, max_ctas,
+                     stream);
+}
+
+extern "C" int axon_tp_reduce_local(const void* inbox, void* out, const int32_t* arrive, int32_t world,
+                                    int32_t rank, int32_t epoch, int64_t rows, int64_t n, int64_t out_row0,
+                                    int64_t ld_out, int32_t out_dtype, int32_t max_ctas, void* stream) {
+  void* one[1] = {out};
+  return reduce_impl(inbox, one, 1, arrive, world, rank, epoch, rows, n, out_row0, ld_out, out_dtype, max_ctas,
+                     stream);
+}
+
+extern "C" int axon_tp_push_rows(const void* src, void* const* dsts, int64_t bytes, int32_t world, int32_t rank,
+                                 void* stream) {
+  int rc = check_world(world, rank, "axon_tp_push_rows");
+  if (rc) return rc;
+  if (bytes < 0 || !src || !dsts) return fail(AXON_E_ARG, "axon_tp_push_rows: bad argument");
+  cudaStream_t s = as_stream(stream);
+  // one copy per peer, in ring order from the next rank so that the ranks'
+  // copies spread over the peers instead of all hitting rank 0 first
+  for (int i = 1; i < world; ++i) {
+    const int d = (rank + i) % world;
+    if (!dsts[d]) return fail(AXON_E_ARG, "axon_tp_push_rows: NULL destination for rank %d", d);
+    cudaError_t e = cudaMemcpyAsync(dsts[d], src, static_cast<size_t>(bytes), cudaMemcpyDeviceToDevice, s);
+    if (e != cudaSuccess) return fail(AXON_E_CUDA, "axon_tp_push_rows: %s", cudaGetErrorString(e));
+  }
+  return AXON_OK;
 }
 
 extern "C" int axon_tp_status(void* stream) {

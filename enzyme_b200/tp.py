@@ -287,7 +287,7 @@ class FusedTPSwiGLU:
 
     def __init__(self, w_gate, w_up, w_down, m: int, *, group=None, slabs: int = 2, tune=None,
                  reduce_ctas: int = 16, out_dtype=torch.bfloat16, whole_step: bool = False,
-                 fused_kernel: bool | None = None):
+                 fused_kernel: bool | None = None, copy_engine_gather: bool = False):
         self.w_gate, self.w_up, self.w_down = w_gate, w_up, w_down
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -316,6 +316,9 @@ class FusedTPSwiGLU:
         # applies: fewer than 320 tiles, e.g. 8 ranks at the BASELINE config);
         # larger shards run the two GEMMs as separate launches.
         self.fused_kernel = (-(-m // 256) * -(-n // 128) < 320) if fused_kernel is None else bool(fused_kernel)
+        # all-gather by the copy engines (cudaMemcpyAsync to each peer) instead
+        # of bulk copies issued by the reducing SMs
+        self.copy_engine_gather = bool(copy_engine_gather)
         # one kernel per step (axon_tp_mlp_step): both GEMMs and the reduction
         self.whole_step = bool(whole_step)
         if self.whole_step:
@@ -367,9 +370,8 @@ class FusedTPSwiGLU:
                                             tune, main.cuda_stream))
             N.check(lib.axon_tp_signal(ptrs([base + lo.arrive_offset(0) for base in self.peers.bases]), W,
                                        self.rank, e, main.cuda_stream))
-            N.check(lib.axon_tp_reduce_gather(mine + lo.inbox_offset(0), y_ptrs, mine + lo.arrive_offset(0), W,
-                                              self.rank, e, rows, self.hidden, 0, self.hidden, out_code, 0,
-                                              main.cuda_stream))
+            self._reduce(lib, mine + lo.inbox_offset(0), y_ptrs, mine + lo.arrive_offset(0), e, rows, 0, out_code,
+                         0, main)
             N.check(lib.axon_tp_signal(ptrs([base + lo.done_offset(0) for base in self.peers.bases]), W,
                                        self.rank, e, main.cuda_stream))
             N.check(lib.axon_tp_wait(mine + lo.done_offset(0), W, e, main.cuda_stream))
@@ -390,15 +392,35 @@ class FusedTPSwiGLU:
             st = main if last else self.side
             if not last:
                 self.side.wait_stream(main)
-            N.check(lib.axon_tp_reduce_gather(mine + lo.inbox_offset(a), y_ptrs, mine + lo.arrive_offset(i), W,
-                                              self.rank, e, rows, self.hidden, a, self.hidden, out_code,
-                                              0 if last else self.reduce_ctas, st.cuda_stream))
+            self._reduce(lib, mine + lo.inbox_offset(a), y_ptrs, mine + lo.arrive_offset(i), e, rows, a, out_code,
+                         0 if last else self.reduce_ctas, st)
             N.check(lib.axon_tp_signal(ptrs([base + lo.done_offset(i) for base in self.peers.bases]), W,
                                        self.rank, e, st.cuda_stream))
         main.wait_stream(self.side)
         for i in range(len(self.slabs)):
             N.check(lib.axon_tp_wait(mine + lo.done_offset(i), W, e, main.cuda_stream))
         return self.y
+
+    def _reduce(self, lib, inbox, y_ptrs, arrive, e, rows, row0, out_code, ctas, stream) -> None:
+        """Owner side of a slab: sum this rank's rows and put them into every
+        rank's output (bulk copies from the reducing SMs, or a local write
+        and then one copy-engine transfer per peer)."""
+        import ctypes
+
+        from . import _native as N
+
+        W = self.world
+        if not self.copy_engine_gather:
+            N.check(lib.axon_tp_reduce_gather(inbox, y_ptrs, arrive, W, self.rank, e, rows, self.hidden, row0,
+                                              self.hidden, out_code, ctas, stream.cuda_stream))
+            return
+        first = (row0 + self.rank * rows) * self.hidden * self.y.element_size()
+        nbytes = rows * self.hidden * self.y.element_size()
+        N.check(lib.axon_tp_reduce_local(inbox, ctypes.c_void_p(y_ptrs[self.rank]), arrive, W, self.rank, e, rows,
+                                         self.hidden, row0, self.hidden, out_code, ctas, stream.cuda_stream))
+        dsts = (ctypes.c_void_p * W)(*[y_ptrs[d] + first for d in range(W)])
+        N.check(lib.axon_tp_push_rows(ctypes.c_void_p(y_ptrs[self.rank] + first), dsts, nbytes, W, self.rank,
+                                      stream.cuda_stream))
 
     def status(self) -> None:
         from . import _native as N

@@ -332,6 +332,19 @@ AXON_API int axon_tp_reduce_gather(const void* inbox, void* const* outs, const i
                           int64_t out_row0, int64_t ld_out, int32_t out_dtype, int32_t max_ctas,
                           void* stream);
 
+/* The same reduction with this rank's rows written to its own output only
+ * (`out`, laid out as one of axon_tp_reduce_gather's outs) ... */
+AXON_API int axon_tp_reduce_local(const void* inbox, void* out, const int32_t* arrive, int32_t world,
+                         int32_t rank, int32_t epoch, int64_t rows, int64_t n, int64_t out_row0,
+                         int64_t ld_out, int32_t out_dtype, int32_t max_ctas, void* stream);
+
+/* ... and then copied to the other ranks by the copy engines: one
+ * cudaMemcpyAsync of `bytes` from src (this rank's rows in its own output) to
+ * dsts[d] (the same rows in rank d's output) for every d != rank, on
+ * `stream`, in ring order from rank + 1. No SM runs the all-gather. */
+AXON_API int axon_tp_push_rows(const void* src, void* const* dsts, int64_t bytes, int32_t world,
+                      int32_t rank, void* stream);
+
 /* Synchronise `stream`; AXON_E_TIMEOUT if a tensor-parallel flag wait gave up
  * since the last call (the record is then cleared). */
 AXON_API int axon_tp_status(void* stream);

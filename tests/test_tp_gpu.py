@@ -115,7 +115,7 @@ def _swiglu_case(m, h, inter, seed):
     return x, wg, wu, wd
 
 
-def _fused_rank(rank, world, port, q, whole_step=False):
+def _fused_rank(rank, world, port, q, whole_step=False, ce=False):
     import datetime
 
     import torch.distributed as dist
@@ -130,7 +130,8 @@ def _fused_rank(rank, world, port, q, whole_step=False):
         dev = torch.device("cuda", rank)
         x, wg, wu, wd = _swiglu_case(1024, 1024, 2048, 3)
         shards = [s.to(dev) for s in tp.shard_swiglu(wg, wu, wd, rank, world)]
-        f = tp.FusedTPSwiGLU(*shards, m=1024, slabs=2, tune={"max_ctas": 132}, whole_step=whole_step)
+        f = tp.FusedTPSwiGLU(*shards, m=1024, slabs=2, tune={"max_ctas": 132}, whole_step=whole_step,
+                             copy_engine_gather=ce)
         xd = x.to(dev)
         y1 = f.forward(xd).clone()
         y2 = f.forward(xd).clone()  # second epoch reuses inboxes, output and flags
@@ -144,8 +145,8 @@ def _fused_rank(rank, world, port, q, whole_step=False):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("whole_step", [False, True])
-def test_fused_tp_swiglu_two_gpus(whole_step):
+@pytest.mark.parametrize("whole_step,ce", [(False, False), (True, False), (False, True)])
+def test_fused_tp_swiglu_two_gpus(whole_step, ce):
     import torch.multiprocessing as mp
 
     from oracle import f64
@@ -153,7 +154,7 @@ def test_fused_tp_swiglu_two_gpus(whole_step):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_fused_rank, args=(r, 2, port, q, whole_step)) for r in range(2)]
+    procs = [ctx.Process(target=_fused_rank, args=(r, 2, port, q, whole_step, ce)) for r in range(2)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in range(2)]
