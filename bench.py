@@ -548,7 +548,9 @@ def run_workload(name, dev, rank, world, steps, warmup, sampler_gpu, with_e2e=Tr
     per_step_ms = ms / steps
     value = w.job_work() / (per_step_ms / 1e3) / (1e9 if w.kind == "hbm" else 1e12)
     # per rank: the step's algorithmic work over the step's device time
-    roof = roofline.fraction(w.kind, w.per_step_work(), per_step_ms / 1e3)
+    # the timed loop follows a soak of the same steps, so a tensor-bound
+    # step runs at the power-capped (sustained) clock
+    roof = roofline.fraction(w.kind, w.per_step_work(), per_step_ms / 1e3, sustained=w.kind == "tensor")
     tr = load_traffic().get(w.spec)
     roof["traffic"] = tr.get("bytes_per_launch") if tr else None
     roof["traffic_source"] = tr.get("source") if tr else None
