@@ -83,9 +83,9 @@ static const char* kVariants[][2] = {
     {"gemm",
      "{\"op\":\"gemm\",\"variants\":[{\"id\":0,\"name\":\"auto\",\"knobs\":{}},"
      "{\"id\":1,\"name\":\"tcgen05_ws_persistent\",\"knobs\":{\"block_m\":[0,128],"
-     "\"block_n\":[0,64,128,256],\"block_k\":[0,64],\"stages\":[0,2,3,4,5,6,7,8],\"max_ctas\":[0]}},"
+     "\"block_n\":[0,64,128,256],\"block_k\":[0,64],\"stages\":[0,2,3,4,5,6,7,8],\"max_ctas\":[0],\"split\":[0,4,8,16]}},"
      "{\"id\":2,\"name\":\"tcgen05_cta_pair\",\"knobs\":{\"block_m\":[0,128],"
-     "\"block_n\":[0,128,256],\"block_k\":[0,64],\"stages\":[0,2,3,4,5,6,7,8],\"max_ctas\":[0]}}]}"},
+     "\"block_n\":[0,128,256],\"block_k\":[0,64],\"stages\":[0,2,3,4,5,6,7,8],\"max_ctas\":[0],\"split\":[0,4,8,16]}}]}"},
 };
 
 extern "C" {

@@ -203,6 +203,7 @@ struct GemmParams {
   int64_t term_stride; // columns between the terms in C
   int b_kwrap;         // > 0: B's k coordinate wraps modulo this (B re-read per term)
   int max_ctas;        // > 0: cap on the persistent grid
+  int raster;          // > 0: tiles ordered in bands of this many row tiles (see tile_coords)
 };
 
 // Ownership of output row r: contiguous blocks of rows_per_owner rows, or
@@ -218,6 +219,23 @@ __device__ __forceinline__ int row_owner(const GemmParams& p, int64_t row, int64
   const int o = static_cast<int>(row / p.rows_per_owner);
   local = row - static_cast<int64_t>(o) * p.rows_per_owner;
   return o;
+}
+
+// Tile t of the persistent loop: column-major over the whole grid of tiles
+// (raster 0), or in bands of `raster` row tiles, each band column-major, so
+// the tiles in flight share fewer A rows and B columns and more of both stay
+// in L2.
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int raster, int& tm, int& tn) {
+  if (raster <= 0 || raster >= num_m) {
+    tm = t % num_m;
+    tn = t / num_m;
+    return;
+  }
+  const int band = t / (raster * num_n);
+  const int within = t - band * raster * num_n;
+  const int rows = num_m - band * raster < raster ? num_m - band * raster : raster;
+  tm = band * raster + within % rows;
+  tn = within / rows;
 }
 
 template <int EPI, typename TC>
@@ -328,7 +346,8 @@ __global__ void __launch_bounds__(192, 1)
     int stage = 0;
     uint32_t phase = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
-      const int tm = t % num_m, tn = t / num_m;
+      int tm, tn;
+      tile_coords(t, num_m, num_n, p.raster, tm, tn);
       for (int kb = 0; kb < kblocks; ++kb) {
         if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) goto producer_done;
         mbar_expect_tx(&full[stage], STAGE);
@@ -397,7 +416,8 @@ __global__ void __launch_bounds__(192, 1)
     int local = 0;
     TC* C = static_cast<TC*>(p.c);
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++local) {
-      const int tm = t % num_m, tn = t / num_m;
+      int tm, tn;
+      tile_coords(t, num_m, num_n, p.raster, tm, tn);
       const int buf = local & 1;
       if (!mbar_wait(&tfull[buf], (local >> 1) & 1, abort_flag)) break;
       tc_fence_after();
@@ -603,7 +623,8 @@ __global__ void __launch_bounds__(192, 1)
     int stage = 0;
     uint32_t phase = 0;
     for (int t = pair_id; t < tiles; t += num_pairs) {
-      const int tm = t % num_m, tn = t / num_m;
+      int tm, tn;
+      tile_coords(t, num_m, num_n, p.raster, tm, tn);
       for (int kb = 0; kb < kblocks; ++kb) {
         if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) goto producer_done;
         const uint32_t leader_full = mapa_u32(smem_u32(&full[stage]), 0);
@@ -677,7 +698,8 @@ __global__ void __launch_bounds__(192, 1)
     int local = 0;
     TC* C = static_cast<TC*>(p.c);
     for (int t = pair_id; t < tiles; t += num_pairs, ++local) {
-      const int tm = t % num_m, tn = t / num_m;
+      int tm, tn;
+      tile_coords(t, num_m, num_n, p.raster, tm, tn);
       const int buf = local & 1;
       if (!mbar_wait(&tfull[buf], (local >> 1) & 1, abort_flag)) break;
       tc_fence_after();
@@ -1662,6 +1684,8 @@ int gemm_impl(const void* a, const void* b, const void* b2, void* c, const float
   gp.term_stride = term_stride;
   gp.b_kwrap = static_cast<int>(b_kwrap);
   gp.max_ctas = t.max_ctas;
+  gp.raster = t.split;  // tune.split: row tiles per raster band (0 = column-major)
+  if (t.split < 0) return fail(AXON_E_ARG, "axon_gemm: split (raster band) must be >= 0");
   if (t.max_ctas < 0) return fail(AXON_E_ARG, "axon_gemm: max_ctas must be >= 0");
   const uint32_t fmt = ab_dtype == AXON_BF16 ? 1u : 0u;
   const uint32_t mma_m = pair ? 2 * BM : BM;  // a CTA pair issues M = 256

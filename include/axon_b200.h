@@ -233,7 +233,11 @@ AXON_API int axon_adam(const void* param, const void* grad, const void* exp_avg,
  * (cta_group::2, block_n 128 or 256); 0 (default) = 2 unless m < 256, the
  * 256-row tiling would add a mostly empty tile, or block_n is 64.
  * tune->stages: shared-memory ring depth (0 = deepest that fits);
- * tune->max_ctas caps the persistent grid (CTAs, pairs count as two). */
+ * tune->max_ctas caps the persistent grid (CTAs, pairs count as two);
+ * tune->split > 0 orders the persistent tiles in bands of that many row tiles
+ * (each band column by column) instead of column-major over all of them --
+ * same tiles, same bits; on B200 it was within run-to-run noise (about 15%)
+ * of the default at 8192^3 and the SwiGLU shapes, so the default stays 0. */
 AXON_API int axon_gemm(const void* a, const void* b, const void* b2, void* c,
               const float* row_scale, int64_t m, int64_t n, int64_t k, int64_t lda,
               int64_t ldb, int64_t ldc, int32_t ab_dtype, int32_t c_dtype,

@@ -390,6 +390,22 @@ def test_gemm_tiles_and_ragged(variant, bn, shape, cuda_device):
 
 
 @pytest.mark.parametrize("variant", GEMM_VARIANTS)
+@pytest.mark.parametrize("raster", [1, 3, 4])
+def test_gemm_raster_bands_same_result(variant, raster, cuda_device):
+    """tune.split orders the persistent tiles in bands of row tiles; the
+    tiles and their k order do not change, so neither do the bits."""
+    g = torch.Generator(device=cuda_device).manual_seed(26)
+    a = (torch.randn(1800, 512, generator=g, device=cuda_device) / 22).bfloat16()
+    b = torch.randn(512, 1400, generator=g, device=cuda_device).bfloat16()
+    c0 = ops.gemm(a, b, out_dtype=torch.float32, tune={"variant": variant})
+    c1 = ops.gemm(a, b, out_dtype=torch.float32, tune={"variant": variant, "split": raster})
+    ops.gemm_status()
+    assert torch.equal(c0, c1)
+    rows = np.arange(0, 1800, 37)
+    _close(_np(c1)[rows], f64.matmul(_np(a)[rows], _np(b)), 1e-4, 1e-4, f"raster {raster}")
+
+
+@pytest.mark.parametrize("variant", GEMM_VARIANTS)
 @pytest.mark.parametrize("stages", [2, 3, 4, 7])
 def test_gemm_pipeline_depths(variant, stages, cuda_device):
     if variant == 1 and stages == 7:
