@@ -143,6 +143,7 @@ SIGNATURES: dict[str, tuple] = {
     "axon_tp_wait": (_I32, [_P, _I32, _I32, _P]),
     "axon_tp_reduce_gather": (_I32, [_P, _P, _P, _I32, _I32, _I32, _I64, _I64, _I64, _I64, _I32, _I32, _P]),
     "axon_tp_reduce_local": (_I32, [_P, _P, _P, _I32, _I32, _I32, _I64, _I64, _I64, _I64, _I32, _I32, _P]),
+    "axon_tp_reduce_multicast": (_I32, [_P, _P, _P, _I32, _I32, _I32, _I64, _I64, _I64, _I64, _I32, _I32, _P]),
     "axon_tp_push_rows": (_I32, [_P, _P, _I64, _I32, _I32, _P]),
     "axon_tp_status": (_I32, [_P]),
     "axon_silu_mlp": (

@@ -78,7 +78,10 @@ __global__ void tp_signal_kernel(FlagPtrs flags, int world, int rank, int epoch)
 }
 
 __global__ void tp_wait_kernel(const int* flags, int world, int epoch) {
-  if (threadIdx.x == 0 && !wait_flags(flags, world, epoch)) atomicExch(&g_tp_error, AXON_E_TIMEOUT);
+  if (threadIdx.x != 0) return;
+  if (!wait_flags(flags, world, epoch)) atomicExch(&g_tp_error, AXON_E_TIMEOUT);
+  // outputs may have arrived through a multicast alias of this rank's buffer
+  asm volatile("fence.proxy.alias;" ::: "memory");
 }
 
 __global__ void tp_wait_count_kernel(const int* counter, int target) {
@@ -98,9 +101,39 @@ __device__ __forceinline__ void store8(Tout* dst, const float* v) {
   }
 }
 
+// Eight outputs as 16-byte multimem stores to a multicast address: the
+// NVLink switch writes each store into every GPU bound to the multicast
+// object, so one rank's output rows reach all ranks for one crossing of its
+// own links. A store carries bits only (the .f32 vector form is the
+// 16-byte store; no arithmetic is done on the values).
+__device__ __forceinline__ void multimem_st16(void* mc, uint4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+template <typename Tout>
+__device__ __forceinline__ void store8_multicast(Tout* dst, const float* v) {
+  if constexpr (sizeof(Tout) == 4) {
+    multimem_st16(dst, make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]),
+                                  __float_as_uint(v[3])));
+    multimem_st16(dst + 4, make_uint4(__float_as_uint(v[4]), __float_as_uint(v[5]), __float_as_uint(v[6]),
+                                      __float_as_uint(v[7])));
+  } else {
+    Vec<Tout> o;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o.e[e] = from_f<Tout>(v[e]);
+    multimem_st16(dst, o.u);
+  }
+}
+
 // inbox: [world][rows][n] f16 partials of this rank's rows; out row i of
 // this rank goes to outs.p[d] + (out_row0 + rank * rows + i) * ld_out on every d.
-template <typename Tout>
+// MC: outs.p[0] is a multicast address and n_outs is 1; the rows reach every
+// rank through multimem stores, and each thread ends with an alias-proxy and a
+// system-scope fence so the stores are ordered before the done flags that a
+// later launch raises.
+template <typename Tout, bool MC = false>
 __global__ void __launch_bounds__(256) tp_reduce_gather_kernel(const __half* __restrict__ inbox, OutPtrs outs,
                                                                int n_outs, const int* arrive, int world, int rank,
                                                                int epoch, int64_t rows, int64_t n, int64_t out_row0,
@@ -140,8 +173,16 @@ __global__ void __launch_bounds__(256) tp_reduce_gather_kernel(const __half* __r
           for (int e = 0; e < 8; ++e) acc[e] += __half2float(v[u][s].e[e]);
       const int64_t e0 = pk * 8;
       const int64_t i = e0 / n, j = e0 - i * n;
-      for (int d = 0; d < n_outs; ++d) store8(static_cast<Tout*>(outs.p[d]) + (first_row + i) * ld_out + j, acc);
+      if constexpr (MC) {
+        store8_multicast(static_cast<Tout*>(outs.p[0]) + (first_row + i) * ld_out + j, acc);
+      } else {
+        for (int d = 0; d < n_outs; ++d) store8(static_cast<Tout*>(outs.p[d]) + (first_row + i) * ld_out + j, acc);
+      }
     }
+  }
+  if constexpr (MC) {
+    asm volatile("fence.proxy.alias;" ::: "memory");
+    __threadfence_system();
   }
 }
 
@@ -306,10 +347,11 @@ extern "C" int axon_tp_wait_count(const int32_t* counter, int32_t target, void* 
 namespace axon {
 namespace {
 
-// The body of axon_tp_reduce_gather (n_outs = world) and axon_tp_reduce_local (n_outs = 1).
+// The body of axon_tp_reduce_gather (n_outs = world), axon_tp_reduce_local
+// (n_outs = 1) and axon_tp_reduce_multicast (n_outs = 1, multicast = true).
 int reduce_impl(const void* inbox, void* const* outs, int n_outs, const int32_t* arrive, int32_t world,
                 int32_t rank, int32_t epoch, int64_t rows, int64_t n, int64_t out_row0, int64_t ld_out,
-                int32_t out_dtype, int32_t max_ctas, void* stream) {
+                int32_t out_dtype, int32_t max_ctas, void* stream, bool multicast = false) {
   int rc = check_world(world, rank, "axon_tp_reduce_gather");
   if (rc) return rc;
   if (rows < 0 || n < 0 || out_row0 < 0) return fail(AXON_E_SHAPE, "axon_tp_reduce_gather: negative size");
@@ -333,6 +375,23 @@ int reduce_impl(const void* inbox, void* const* outs, int n_outs, const int32_t*
   const __half* in = static_cast<const __half*>(inbox);
   // contiguous outputs: whole-row chunks of about 8 KB pushed by bulk copies
   // (small chunks: every SM gets several, its loads and pushes overlap)
+  if (multicast) {
+    switch (out_dtype) {
+      case AXON_BF16:
+        tp_reduce_gather_kernel<__nv_bfloat16, true><<<static_cast<unsigned>(grid), 256, 0, s>>>(
+            in, o, 1, arrive, world, rank, epoch, rows, n, out_row0, ld_out);
+        break;
+      case AXON_F16:
+        tp_reduce_gather_kernel<__half, true><<<static_cast<unsigned>(grid), 256, 0, s>>>(
+            in, o, 1, arrive, world, rank, epoch, rows, n, out_row0, ld_out);
+        break;
+      default:
+        tp_reduce_gather_kernel<float, true><<<static_cast<unsigned>(grid), 256, 0, s>>>(
+            in, o, 1, arrive, world, rank, epoch, rows, n, out_row0, ld_out);
+        break;
+    }
+    return launch_status("axon_tp_reduce_multicast");
+  }
   const int osize = out_dtype == AXON_F32 ? 4 : 2;
   if (ld_out == n && n * osize <= 32768) {
     const int chunk_rows = n * osize >= 8192 ? 1 : static_cast<int>(8192 / (n * osize));
@@ -399,6 +458,14 @@ extern "C" int axon_tp_reduce_local(const void* inbox, void* out, const int32_t*
   void* one[1] = {out};
   return reduce_impl(inbox, one, 1, arrive, world, rank, epoch, rows, n, out_row0, ld_out, out_dtype, max_ctas,
                      stream);
+}
+
+extern "C" int axon_tp_reduce_multicast(const void* inbox, void* out_mc, const int32_t* arrive, int32_t world,
+                                        int32_t rank, int32_t epoch, int64_t rows, int64_t n, int64_t out_row0,
+                                        int64_t ld_out, int32_t out_dtype, int32_t max_ctas, void* stream) {
+  void* one[1] = {out_mc};
+  return reduce_impl(inbox, one, 1, arrive, world, rank, epoch, rows, n, out_row0, ld_out, out_dtype, max_ctas,
+                     stream, true);
 }
 
 extern "C" int axon_tp_push_rows(const void* src, void* const* dsts, int64_t bytes, int32_t world, int32_t rank,

@@ -263,6 +263,39 @@ class PeerBuffers:
         return self.buf[lo.y_offset:lo.y_offset + nbytes].view(dtype).view(lo.m, lo.hidden)
 
 
+def multicast_supported(device) -> bool:
+    """True where symmetric memory on this CUDA device can be bound to an
+    NVLink multicast object (GPUs behind an NVSwitch with multicast enabled)."""
+    from torch._C._distributed_c10d import _SymmetricMemory
+
+    dev = torch.device(device)
+    try:
+        return bool(_SymmetricMemory.has_multicast_support(torch._C._autograd.DeviceType.CUDA, dev.index or 0))
+    except (RuntimeError, AttributeError):
+        return False
+
+
+def multicast_output(m: int, hidden: int, dtype, device, group=None):
+    """An [m, hidden] output in symmetric memory whose ranks' copies are bound
+    to one NVLink multicast object: returns (this rank's tensor, the multicast
+    address of its first element, the symmetric-memory handle that keeps the
+    mapping alive). Raises RuntimeError where the GPUs or the group give no
+    multicast address (no NVSwitch multicast support)."""
+    from torch.distributed import _symmetric_memory as symm
+
+    y = symm.empty((m, hidden), dtype=dtype, device=device)
+    handle = symm.rendezvous(y, group if group is not None else dist.group.WORLD)
+    mc = int(handle.multicast_ptr or 0)
+    if not mc:
+        raise RuntimeError("no NVLink multicast address for this group's symmetric memory")
+    # the tensor's offset inside the rank's mapping, applied to the multicast
+    # mapping of the same allocation
+    off = y.data_ptr() - int(handle.buffer_ptrs[handle.rank])
+    if not 0 <= off <= int(handle.buffer_size) - y.numel() * y.element_size():
+        raise RuntimeError("symmetric-memory output lies outside its handle's buffer")
+    return y, mc + off, handle
+
+
 class FusedTPSwiGLU:
     """Tensor-parallel SwiGLU whose down-projection all-reduce is fused into
     the GEMMs over NVLink peer memory (csrc/tp.cu):
@@ -283,11 +316,19 @@ class FusedTPSwiGLU:
     complete while the down projection is still running, and the reduction
     and all-gather push run as the kernel's last tiles; one wait for the done
     count ends the step.
+
+    multicast_gather=True puts the output in symmetric memory bound to an
+    NVLink multicast object and has each owner store its summed rows once, to
+    the multicast address (axon_tp_reduce_multicast): the switch writes them
+    into every rank's output, so the all-gather leaves each GPU once instead
+    of world - 1 times. The returned tensor is then that symmetric-memory
+    output.
     """
 
     def __init__(self, w_gate, w_up, w_down, m: int, *, group=None, slabs: int = 2, tune=None,
                  reduce_ctas: int = 16, out_dtype=torch.bfloat16, whole_step: bool = False,
-                 fused_kernel: bool | None = None, copy_engine_gather: bool = False):
+                 fused_kernel: bool | None = None, copy_engine_gather: bool = False,
+                 multicast_gather: bool = False):
         self.w_gate, self.w_up, self.w_down = w_gate, w_up, w_down
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -319,6 +360,13 @@ class FusedTPSwiGLU:
         # all-gather by the copy engines (cudaMemcpyAsync to each peer) instead
         # of bulk copies issued by the reducing SMs
         self.copy_engine_gather = bool(copy_engine_gather)
+        # all-gather through one multicast store per output packet
+        self.multicast_gather = bool(multicast_gather)
+        self._y_mc, self._symm = 0, None
+        if self.multicast_gather:
+            if copy_engine_gather or whole_step:
+                raise ValueError("multicast_gather replaces the copy-engine and whole-step all-gathers")
+            self.y, self._y_mc, self._symm = multicast_output(m, self.hidden, out_dtype, dev, group)
         # one kernel per step (axon_tp_mlp_step): both GEMMs and the reduction
         self.whole_step = bool(whole_step)
         if self.whole_step:
@@ -329,6 +377,11 @@ class FusedTPSwiGLU:
     def close(self) -> None:
         torch.cuda.synchronize(self.w_gate.device)
         self.peers.close()
+        if self._symm is not None:
+            # every rank done with the multicast output before any unmaps it
+            if self.world > 1:
+                dist.barrier(group=self.group)
+            self.y, self._symm, self._y_mc = None, None, 0
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         import ctypes
@@ -410,6 +463,10 @@ class FusedTPSwiGLU:
         from . import _native as N
 
         W = self.world
+        if self._y_mc:
+            N.check(lib.axon_tp_reduce_multicast(inbox, ctypes.c_void_p(self._y_mc), arrive, W, self.rank, e, rows,
+                                                 self.hidden, row0, self.hidden, out_code, ctas, stream.cuda_stream))
+            return
         if not self.copy_engine_gather:
             N.check(lib.axon_tp_reduce_gather(inbox, y_ptrs, arrive, W, self.rank, e, rows, self.hidden, row0,
                                               self.hidden, out_code, ctas, stream.cuda_stream))

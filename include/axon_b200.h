@@ -349,6 +349,19 @@ AXON_API int axon_tp_reduce_local(const void* inbox, void* out, const int32_t* a
 AXON_API int axon_tp_push_rows(const void* src, void* const* dsts, int64_t bytes, int32_t world,
                       int32_t rank, void* stream);
 
+/* The same reduction with the rows stored once, through out_mc: a multicast
+ * address (an NVLink multicast object bound to every rank's output buffer,
+ * e.g. a symmetric-memory allocation's multicast pointer), laid out as one of
+ * axon_tp_reduce_gather's outs. The switch writes each 16-byte multimem store
+ * into every rank's copy, so the all-gather leaves this GPU once instead of
+ * world - 1 times. Each storing thread ends with an alias-proxy and a
+ * system-scope fence; axon_tp_signal afterwards publishes the rows, and
+ * axon_tp_wait on the reader orders them before its later reads. */
+AXON_API int axon_tp_reduce_multicast(const void* inbox, void* out_mc, const int32_t* arrive,
+                             int32_t world, int32_t rank, int32_t epoch, int64_t rows,
+                             int64_t n, int64_t out_row0, int64_t ld_out, int32_t out_dtype,
+                             int32_t max_ctas, void* stream);
+
 /* Synchronise `stream`; AXON_E_TIMEOUT if a tensor-parallel flag wait gave up
  * since the last call (the record is then cleared). */
 AXON_API int axon_tp_status(void* stream);

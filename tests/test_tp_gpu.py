@@ -7,8 +7,10 @@
   gathered result equals a one-GPU update of the whole vector.
 * Fused tensor-parallel SwiGLU: the down GEMM's epilogue scatters f16
   partial rows into the owners' inboxes over peer memory, owners reduce and
-  push bf16 rows to every rank; checked against the oracle, across ranks and
-  over repeated steps (epoch flags), and on one rank without a process group.
+  push bf16 rows to every rank (bulk copies, copy engines, or one multicast
+  store per packet through the NVLink switch); checked against the oracle,
+  across ranks and over repeated steps (epoch flags), and on one rank
+  without a process group.
 * A flag wait that nobody satisfies gives up with AXON_E_TIMEOUT and the
   context stays usable.
 NVLS is off (NCCL_NVLS_ENABLE=0) and the process group has a short timeout.
@@ -115,7 +117,7 @@ def _swiglu_case(m, h, inter, seed):
     return x, wg, wu, wd
 
 
-def _fused_rank(rank, world, port, q, whole_step=False, ce=False):
+def _fused_rank(rank, world, port, q, whole_step=False, ce=False, mc=False):
     import datetime
 
     import torch.distributed as dist
@@ -130,23 +132,34 @@ def _fused_rank(rank, world, port, q, whole_step=False, ce=False):
         dev = torch.device("cuda", rank)
         x, wg, wu, wd = _swiglu_case(1024, 1024, 2048, 3)
         shards = [s.to(dev) for s in tp.shard_swiglu(wg, wu, wd, rank, world)]
-        f = tp.FusedTPSwiGLU(*shards, m=1024, slabs=2, tune={"max_ctas": 132}, whole_step=whole_step,
-                             copy_engine_gather=ce)
         xd = x.to(dev)
-        y1 = f.forward(xd).clone()
-        y2 = f.forward(xd).clone()  # second epoch reuses inboxes, output and flags
-        torch.cuda.synchronize()
+        if mc and not tp.multicast_supported(dev):
+            q.put((rank, None, None))  # every rank sees the same GPUs, so all skip
+            return
+        f = tp.FusedTPSwiGLU(*shards, m=1024, slabs=2, tune={"max_ctas": 132}, whole_step=whole_step,
+                             copy_engine_gather=ce, multicast_gather=mc)
+        try:
+            y1 = f.forward(xd).clone()
+            y2 = f.forward(xd).clone()  # second epoch reuses inboxes, output and flags
+            torch.cuda.synchronize()
+        finally:
+            f.close()  # with multicast: a barrier first, so no rank unmaps while another still stores
         f.status()
         ops.gemm_status()
-        f.close()
-        q.put((rank, y1.float().cpu().numpy(), bool(torch.equal(y1, y2))))
+        same = bool(torch.equal(y1, y2))
+        if mc:  # the multicast all-gather carries the bits of the bulk-copy push
+            plain = tp.FusedTPSwiGLU(*shards, m=1024, slabs=2, tune={"max_ctas": 132})
+            same = same and bool(torch.equal(y1, plain.forward(xd)))
+            plain.close()
+        q.put((rank, y1.float().cpu().numpy(), same))
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("whole_step,ce", [(False, False), (True, False), (False, True)])
-def test_fused_tp_swiglu_two_gpus(whole_step, ce):
+@pytest.mark.parametrize("whole_step,ce,mc", [(False, False, False), (True, False, False), (False, True, False),
+                                              (False, False, True)])
+def test_fused_tp_swiglu_two_gpus(whole_step, ce, mc):
     import torch.multiprocessing as mp
 
     from oracle import f64
@@ -154,13 +167,15 @@ def test_fused_tp_swiglu_two_gpus(whole_step, ce):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_fused_rank, args=(r, 2, port, q, whole_step, ce)) for r in range(2)]
+    procs = [ctx.Process(target=_fused_rank, args=(r, 2, port, q, whole_step, ce, mc)) for r in range(2)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in range(2)]
     for p in procs:
         p.join(timeout=120)
     assert all(p.exitcode == 0 for p in procs)
+    if any(y is None for _, y, _ in res):
+        pytest.skip("no NVLink multicast on these GPUs")
     x, wg, wu, wd = (t.float().numpy() for t in _swiglu_case(1024, 1024, 2048, 3))
     rows = np.arange(0, 1024, 5)
     want = f64.silu_mlp(x[rows], wg, wu, wd)
