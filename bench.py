@@ -194,7 +194,7 @@ class Cumsum(Workload):
             logits = 2.0 * torch.randn(256, 128256, device=dev, generator=self.gen)
             x = torch.sort(torch.softmax(logits, dim=1), dim=1, descending=True).values.contiguous()
             nbytes = ops.cumsum_workspace_bytes(256, 128256, self.TUNE)
-            ws = torch.empty(nbytes, dtype=torch.uint8, device=dev) if nbytes else None
+            ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev) if nbytes else None
             self.sets.append((x, torch.empty_like(x), ws))
 
     # the library default: at 256 aligned rows it runs the row-streaming scan

@@ -616,6 +616,286 @@ int launch_rowstream(const void* x, void* y, int64_t m, int64_t n, int64_t ld_x,
   return launch_status("axon_cumsum");
 }
 
+// ---- variant 3: balanced chunk ranges --------------------------------------------
+//
+// One CTA per row loads the SMs unevenly whenever the row count is not a
+// multiple of the resident CTAs (256 rows over 148 SMs with two CTAs each:
+// 108 SMs stream two rows, 40 stream one, and the slowest SM sets the time).
+// Here rows are cut into the same fixed chunks as variant 2 and every CTA --
+// two 512-thread CTAs per SM, as variant 2 runs, G = 2 x SMs of them --
+// takes an equal contiguous range of the row-major chunk sequence. A range
+// is: a lead (the tail of a row whose head belongs to the previous CTA),
+// whole rows, and a trail (the head of a row whose tail belongs to the next
+// CTA), or, when it lies inside one row, a single middle piece. A CTA streams
+// its trail first and publishes the trail's float64 running sum in its
+// workspace slot (a release store of a ready word), then its whole rows, and
+// its lead last, taking the lead's carry from the previous CTA's slot
+// (acquire load, bounded wait): published early in that CTA's run, so a lead
+// rarely waits. A middle piece waits for its carry first and publishes after
+// its last chunk. The reader clears the ready word, so a call leaves the
+// slots as it found them. Numerics are those of variant 2: a float64 running
+// sum across chunks and a chunk-local fp32 prefix, same warp split.
+struct ScanSlot {
+  double prefix;
+  int ready;
+  int pad;
+};
+constexpr int kSlotReady = 0x5ca11ed;    // a slot holds a published sum
+constexpr int kBalThreads = 512;
+constexpr int kBalStages = 2;            // default ring: 2 x 32 KB per CTA
+constexpr int64_t kBalSlotOffset = 256;  // slots follow the status word's block
+constexpr int kBalMaxSlots = 1024;
+constexpr int64_t kBalShortRowBytes = 32768;  // variant 0 runs variant 3 for rows up to this
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_gpu(int* p, int v) {
+  asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+template <typename Tin, typename Tout, int NW, int SKB>
+__global__ void __launch_bounds__(NW * 32, 2) cumsum_balanced(const Tin* __restrict__ x, Tout* __restrict__ y,
+                                                              int64_t m, int64_t n, int64_t ld_x, int64_t ld_y,
+                                                              bool vec_out, int stages, unsigned char* ws) {
+  constexpr int E = Vec<Tin>::E;
+  constexpr int64_t kChunk = SKB * 1024 / static_cast<int64_t>(sizeof(Tin));
+  constexpr int64_t PPW = kChunk / E / NW;  // packets per warp per chunk
+  static_assert(PPW % 32 == 0, "whole segments per warp");
+  constexpr int NSEG = static_cast<int>(PPW / 32);
+  constexpr int64_t kStageBytes = SKB * 1024;
+  extern __shared__ __align__(128) unsigned char dyn_smem[];
+  __shared__ __align__(8) uint64_t full[kRowMaxStages];
+  __shared__ float s_warp[2][NW];
+  __shared__ double s_lead;
+  __shared__ int s_abort;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  ScanSlot* slots = reinterpret_cast<ScanSlot*>(ws + kBalSlotOffset);
+
+  // this CTA's chunks [g0, g1) of the row-major sequence, split into
+  // trail (row rb, chunks [0, k1)), whole rows [full0, rb), lead (row ra,
+  // chunks [k0, cpr)), processed in that order; or one middle piece (row ra,
+  // chunks [k0, k1)), handled as a lead that also publishes
+  // (chunk counts fit in 32 bits: the launcher checks m * cpr < 2^31)
+  const int cpr = static_cast<int>((n + kChunk - 1) / kChunk);
+  const int64_t total = m * cpr;
+  const int b = blockIdx.x;
+  const int g0 = static_cast<int>(b * total / gridDim.x), g1 = static_cast<int>((b + 1) * total / gridDim.x);
+  const int ra = g0 / cpr, k0 = g0 - ra * cpr;
+  const int rb = g1 / cpr, k1 = g1 - rb * cpr;
+  const bool mid = ra == rb && k0 > 0;  // then k1 > k0
+  const int n_trail = mid ? 0 : k1;
+  const int full0 = k0 > 0 ? ra + 1 : ra;
+  const int n_full = mid ? 0 : (rb - full0) * cpr;
+  const int n_lead = mid ? k1 - k0 : k0 > 0 ? cpr - k0 : 0;
+  const int npos = n_trail + n_full + n_lead;
+  auto locate = [&](int p, int& row, int& c) {
+    if (p < n_trail) {
+      row = rb;
+      c = p;
+    } else if (p < n_trail + n_full) {
+      const int q = p - n_trail;
+      row = full0 + q / cpr;
+      c = q - (q / cpr) * cpr;
+    } else {
+      row = ra;
+      c = k0 + (p - n_trail - n_full);
+    }
+  };
+  auto chunk_len = [&](int c) {
+    const int64_t left = n - static_cast<int64_t>(c) * kChunk;
+    return left < kChunk ? left : kChunk;
+  };
+  auto issue = [&](int p) {
+    int row, c;
+    locate(p, row, c);
+    const int st = p % stages;
+    const uint32_t bytes = static_cast<uint32_t>(chunk_len(c) * static_cast<int64_t>(sizeof(Tin)) / 16 * 16);
+    if (bytes == 0) {
+      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sm100::smem_addr(&full[st])) : "memory");
+      return;
+    }
+    sm100::mbar_expect_tx(&full[st], bytes);
+    sm100::bulk_g2s(dyn_smem + st * kStageBytes, x + row * ld_x + static_cast<int64_t>(c) * kChunk, bytes,
+                    &full[st]);
+  };
+
+  if (tid == 0) {
+    for (int st = 0; st < stages; ++st) sm100::mbar_init(&full[st], 1);
+    s_abort = 0;
+    sm100::mbar_init_fence();
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_trigger();
+  if (b == 0 && tid == 0) *reinterpret_cast<int*>(ws) = AXON_OK;
+  if (tid == 0)
+    for (int p = 0; p < npos && p < stages; ++p) issue(p);
+
+  double carry = 0.0;
+  for (int p = 0; p < npos; ++p) {
+    int row, c;
+    locate(p, row, c);
+    const int st = p % stages;
+    const int bsel = p & 1;
+    const int len = static_cast<int>(chunk_len(c));
+    const int bulk_elems = static_cast<int>(len * sizeof(Tin) / 16 * 16 / sizeof(Tin));
+    const Tin* buf = reinterpret_cast<const Tin*>(dyn_smem + st * kStageBytes);
+    const Tin* gsrc = x + row * ld_x + static_cast<int64_t>(c) * kChunk;
+    const bool lead_start = n_lead > 0 && p == n_trail + n_full;
+    if (tid == 0 && lead_start) {
+      // the previous CTA's trail sum, read once and cleared
+      ScanSlot* prev = slots + (b - 1);
+      const uint64_t t0 = sm100::globaltimer_ns();
+      bool ok = true;
+      while (ld_acquire_gpu(&prev->ready) != kSlotReady) {
+        if (sm100::globaltimer_ns() - t0 > kBulkWaitNs) {
+          ok = false;
+          break;
+        }
+        __nanosleep(100);
+      }
+      if (ok) {
+        s_lead = __ldcg(&prev->prefix);
+        prev->ready = 0;
+      } else {
+        s_lead = 0.0;
+        atomicExch(&g_scan_error, AXON_E_TIMEOUT);
+      }
+    }
+    if (!s_abort &&
+        !sm100::mbar_wait_bounded(&full[st], static_cast<uint32_t>((p / stages) & 1), kBulkWaitNs)) {
+      s_abort = 1;
+      atomicExch(&g_scan_error, AXON_E_TIMEOUT);
+    }
+    // pass 1: this thread's packets -> registers, and the warp sums
+    const bool full_chunk = len == kChunk;
+    const int wbase = warp * static_cast<int>(PPW) + lane;  // this lane's first packet
+    Vec<Tin> raw[NSEG];
+    float wsum = 0.f;
+#pragma unroll
+    for (int q = 0; q < NSEG; ++q) {
+      const int e0 = (wbase + q * 32) * E;
+      if (full_chunk || e0 + E <= bulk_elems) {
+        raw[q] = *reinterpret_cast<const Vec<Tin>*>(buf + e0);
+      } else {
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const int i = e0 + e;
+          raw[q].e[e] = i < bulk_elems ? buf[i] : i < len ? gsrc[i] : from_f<Tin>(0.f);
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < E; ++e) wsum += to_f(raw[q].e[e]);
+    }
+    wsum = warp_sum(wsum);
+    if (lane == 0) s_warp[bsel][warp] = wsum;
+    __syncthreads();
+    if (tid == 0 && p + stages < npos) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(p + stages);
+    }
+    if (c == 0) carry = 0.0;  // a row starts: the trail, or a whole row
+    if (lead_start) carry = s_lead;
+    float wi = lane < NW ? s_warp[bsel][lane] : 0.f;
+#pragma unroll
+    for (int o = 1; o < NW; o <<= 1) {
+      const float up = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += up;
+    }
+    const float chunk_total = __shfl_sync(0xffffffffu, wi, NW - 1);
+    const float warp_excl = __shfl_sync(0xffffffffu, wi, warp > 0 ? warp - 1 : 0);
+    const float carry_f = static_cast<float>(carry);
+    float seg_carry = warp > 0 ? warp_excl : 0.f;
+    // pass 2: scan 32-packet segments and write them out
+    Tout* cdst = y + row * ld_y + static_cast<int64_t>(c) * kChunk;
+#pragma unroll
+    for (int j = 0; j < NSEG; ++j) {
+      const int e0 = (wbase + j * 32) * E;
+      float v[E];
+#pragma unroll
+      for (int q = 0; q < E; ++q) v[q] = to_f(raw[j].e[q]);
+#pragma unroll
+      for (int q = 1; q < E; ++q) v[q] += v[q - 1];
+      const float own = v[E - 1];
+      float incl = own;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float up = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += up;
+      }
+      const float base = seg_carry + (incl - own);
+#pragma unroll
+      for (int q = 0; q < E; ++q) v[q] = carry_f + (base + v[q]);
+      if (full_chunk) store_packet<Tout, E>(cdst + e0, v, E, vec_out);
+      else if (e0 < len) store_packet<Tout, E>(cdst + e0, v, len - e0, vec_out);
+      seg_carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    carry += static_cast<double>(chunk_total);
+    if (tid == 0 && ((n_trail > 0 && p == n_trail - 1) || (mid && p == npos - 1))) {
+      // the trail (or middle piece) is done: its running sum carries into
+      // the next CTA's lead
+      slots[b].prefix = carry;
+      st_release_gpu(&slots[b].ready, kSlotReady);
+    }
+  }
+  // copies may still be landing only if a wait gave up: let them finish
+  // before the CTA's shared memory is released (failure path only)
+  if (tid == 0 && s_abort)
+    for (int k = 0; k < 2000; ++k) __nanosleep(1000);
+}
+
+// Launch of variant 3: `ws` holds the status word and one slot per CTA
+// (kBalSlotOffset + 16 * G bytes); its slots must read as not ready (zero-filled
+// before the first call; every completed call leaves them so).
+template <typename Tin, typename Tout>
+int launch_balanced(const void* x, void* y, int64_t m, int64_t n, int64_t ld_x, int64_t ld_y, const axon_tune_t& t,
+                    void* ws, int64_t ws_bytes, cudaStream_t s) {
+  if (!aligned16(x) || (m > 1 && (ld_x * sizeof(Tin)) % 16))
+    return fail(AXON_E_UNSUPPORTED, "axon_cumsum: variant 3 needs 16-byte aligned input rows");
+  const int64_t chunk_elems = (t.block_k ? t.block_k : 32) * 1024 / static_cast<int64_t>(sizeof(Tin));
+  const int64_t chunks = m * ((n + chunk_elems - 1) / chunk_elems);
+  if (chunks > 0x7fffffffLL) return fail(AXON_E_SHAPE, "axon_cumsum: variant 3 takes fewer than 2^31 chunks");
+  // two CTAs per SM, every CTA at least one chunk
+  int64_t G = t.max_ctas > 0 ? t.max_ctas : 2 * sm_count();
+  if (G > 2 * sm_count()) G = 2 * sm_count();
+  if (G > chunks) G = chunks;
+  if (G > kBalMaxSlots) G = kBalMaxSlots;
+  const int64_t need = kBalSlotOffset + static_cast<int64_t>(sizeof(ScanSlot)) * G;
+  if (ws == nullptr || ws_bytes < need || !aligned16(ws))
+    return fail(AXON_E_ARG, "axon_cumsum: variant 3 needs a zero-filled, 16-byte aligned workspace of %lld bytes",
+                (long long)need);
+  const int stages = t.stages ? t.stages : kBalStages;
+  const int kb = t.block_k ? t.block_k : 32;
+  if (t.threads != 0 && t.threads != kBalThreads)
+    return fail(AXON_E_ARG, "axon_cumsum: variant 3 runs %d threads", kBalThreads);
+  if (stages < 2 || stages > kRowMaxStages) return fail(AXON_E_ARG, "axon_cumsum: variant 3 stages must be 2..8");
+  if ((kb != 16 && kb != 32) || stages * kb > 200)
+    return fail(AXON_E_ARG, "axon_cumsum: variant 3 stage size must be 16 or 32 KB, ring <= 200 KB");
+  const bool vec_out = aligned16(y) && (ld_y * sizeof(Tout)) % 16 == 0;
+  const size_t smem = static_cast<size_t>(stages) * kb * 1024;
+  constexpr int NW = kBalThreads / 32;
+  auto kern = kb == 16 ? cumsum_balanced<Tin, Tout, NW, 16> : cumsum_balanced<Tin, Tout, NW, 32>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return fail(AXON_E_LAUNCH, "axon_cumsum: smem attribute: %s", cudaGetErrorString(e));
+  launch_k(kern, dim3(static_cast<unsigned>(G)), dim3(kBalThreads), smem, s, static_cast<const Tin*>(x),
+           static_cast<Tout*>(y), m, n, ld_x, ld_y, vec_out, stages, static_cast<unsigned char*>(ws));
+  return launch_status("axon_cumsum");
+}
+
+template <typename Tin>
+int dispatch_balanced(int32_t out_dtype, const void* x, void* y, int64_t m, int64_t n, int64_t ld_x, int64_t ld_y,
+                      const axon_tune_t& t, void* ws, int64_t ws_bytes, cudaStream_t s) {
+  switch (out_dtype) {
+    case AXON_F32: return launch_balanced<Tin, float>(x, y, m, n, ld_x, ld_y, t, ws, ws_bytes, s);
+    case AXON_BF16: return launch_balanced<Tin, __nv_bfloat16>(x, y, m, n, ld_x, ld_y, t, ws, ws_bytes, s);
+    default: return fail(AXON_E_UNSUPPORTED, "axon_cumsum: unsupported output dtype %d", out_dtype);
+  }
+}
+
 template <typename Tin>
 int dispatch_rowstream(int32_t out_dtype, const void* x, void* y, int64_t m, int64_t n, int64_t ld_x, int64_t ld_y,
                        const axon_tune_t& t, void* ws, cudaStream_t s) {
@@ -695,7 +975,11 @@ extern "C" int64_t axon_cumsum_workspace_bytes(int64_t m, int64_t n, const axon_
   axon_tune_t t = tune_or_default(tune);
   if (m < 0 || n < 0) return fail(AXON_E_SHAPE, "axon_cumsum_workspace_bytes: negative size");
   if (t.variant == 1 || t.variant == 2) return 0;
-  return lookback_ws_bytes(m, n, t);
+  const int64_t balanced = kBalSlotOffset + static_cast<int64_t>(sizeof(ScanSlot)) * kBalMaxSlots;
+  if (t.variant == 3) return balanced;
+  // variant 0 may run variant 3 (short aligned rows): room for either
+  const int64_t lookback = lookback_ws_bytes(m, n, t);
+  return lookback > balanced ? lookback : balanced;
 }
 
 extern "C" int axon_cumsum(const void* x, void* y, int64_t m, int64_t n, int64_t ld_x, int64_t ld_y,
@@ -728,18 +1012,46 @@ extern "C" int axon_cumsum(const void* x, void* y, int64_t m, int64_t n, int64_t
       default: return fail(AXON_E_UNSUPPORTED, "axon_cumsum: unsupported input dtype %d", in_dtype);
     }
   }
+  if (t.variant == 3) {
+    if (m == 0 || n == 0) return AXON_OK;
+    cudaStream_t s = as_stream(stream);
+    switch (in_dtype) {
+      case AXON_F32:
+        return dispatch_balanced<float>(out_dtype, x, y, m, n, ld_x, ld_y, t, workspace, workspace_bytes, s);
+      case AXON_BF16:
+        return dispatch_balanced<__nv_bfloat16>(out_dtype, x, y, m, n, ld_x, ld_y, t, workspace, workspace_bytes,
+                                                s);
+      default: return fail(AXON_E_UNSUPPORTED, "axon_cumsum: unsupported input dtype %d", in_dtype);
+    }
+  }
   if (t.split != 0 && t.split != 2048 && t.split != 4096 && t.split != 8192 && t.split != 16384)
     return fail(AXON_E_ARG, "axon_cumsum: split must be one of 2048, 4096, 8192, 16384 (got %d)", t.split);
   if (t.variant != 0) return fail(AXON_E_UNSUPPORTED, "axon_cumsum: unknown variant %d", t.variant);
   if (m == 0 || n == 0) return AXON_OK;
-  // Default (variant 0 without a split): the row-streaming scan when there
-  // are enough rows to fill the GPU and the rows are 16-byte aligned; it beat
-  // the look-back scan on B200 at 256 x 128256 (51 vs 85 us), 1024 x 32768
-  // and 4096 x 4096, and lost at 64 x 1e6 (228 vs 211 us).
+  // Default (variant 0 without a split): the chunk-streaming scans when there
+  // are enough rows to fill the GPU and the rows are 16-byte aligned; the
+  // row-streaming scan beat the look-back scan on B200 at 256 x 128256 (51
+  // vs 85 us), 1024 x 32768 and 4096 x 4096, and lost at 64 x 1e6 (228 vs
+  // 211 us).
   const int64_t in_size = in_dtype == AXON_F32 ? 4 : 2;
   if (t.split == 0 && t.threads == 0 && m >= kRowStreamMinRows && aligned16(x) && (ld_x * in_size) % 16 == 0 &&
       (in_dtype == AXON_F32 || in_dtype == AXON_BF16)) {
     cudaStream_t s = as_stream(stream);
+    // Rows of at most 32 KB: balanced chunk ranges of 16 KB chunks, which
+    // stream across row ends instead of paying a CTA's start per row
+    // (4096 x 4096 fp32 on B200: 30.9 us vs 53.9 for one CTA per row); longer
+    // rows: the row-streaming scan (1024 x 32768: 45.1 vs 49.3 us).
+    if (n * in_size <= kBalShortRowBytes && workspace != nullptr &&
+        workspace_bytes >= kBalSlotOffset + static_cast<int64_t>(sizeof(ScanSlot)) * 2 * sm_count()) {
+      axon_tune_t tb = t;
+      tb.variant = 3;
+      tb.block_k = 16;
+      tb.stages = 4;
+      return in_dtype == AXON_F32
+                 ? dispatch_balanced<float>(out_dtype, x, y, m, n, ld_x, ld_y, tb, workspace, workspace_bytes, s)
+                 : dispatch_balanced<__nv_bfloat16>(out_dtype, x, y, m, n, ld_x, ld_y, tb, workspace,
+                                                    workspace_bytes, s);
+    }
     return in_dtype == AXON_F32
                ? dispatch_rowstream<float>(out_dtype, x, y, m, n, ld_x, ld_y, t, workspace, s)
                : dispatch_rowstream<__nv_bfloat16>(out_dtype, x, y, m, n, ld_x, ld_y, t, workspace, s);

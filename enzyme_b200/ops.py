@@ -118,25 +118,51 @@ def cumsum_workspace_bytes(m: int, n: int, tune=None) -> int:
     return int(nbytes)
 
 
+# Zero-filled cumsum workspaces kept per (device, stream): the scans leave a
+# workspace zero-filled (variant 0 clears it itself, variant 3's slots are
+# cleared by their readers), so one buffer serves every call on a stream.
+_CUMSUM_WS: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def _cumsum_workspace(x, need: int) -> torch.Tensor:
+    key = (x.device.index or 0, _stream(x))
+    ws = _CUMSUM_WS.get(key)
+    if ws is None or ws.numel() < need:
+        ws = torch.zeros(need, dtype=torch.uint8, device=x.device)
+        _CUMSUM_WS[key] = ws
+    return ws
+
+
 def cumsum(x, *, out=None, out_dtype=None, workspace=None, tune=None):
-    """Inclusive scan along the last axis. Allocates its workspace with torch
-    unless one is passed (uint8 tensor of cumsum_workspace_bytes)."""
+    """Inclusive scan along the last axis. Without a `workspace` (uint8
+    tensor of cumsum_workspace_bytes, zero-filled before its first use) a
+    zero-filled one kept for this device and stream is used."""
     _require_cuda(x)
     m, n, ldx = _rows(x)
     y = out if out is not None else torch.empty(x.shape, dtype=out_dtype or x.dtype, device=x.device)
     _, _, ldy = _rows(y)
     need = cumsum_workspace_bytes(m, n, tune)
     if workspace is None and need > 0:
-        workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
+        workspace = _cumsum_workspace(x, need)
     wsb = workspace.numel() if workspace is not None else 0
     check(N.lib().axon_cumsum(_ptr(x), _ptr(y), m, n, ldx, ldy, dtype_code(x), dtype_code(y), _ptr(workspace), wsb,
                               _tune(tune), _stream(x)))
     return y
 
 
-def cumsum_status(workspace) -> None:
-    """Raise AxonError(AXON_E_TIMEOUT) if a look-back wait gave up."""
-    check(N.lib().axon_cumsum_status(_ptr(workspace), _stream(workspace)))
+def cumsum_status(workspace=None) -> None:
+    """Raise AxonError(AXON_E_TIMEOUT) if a bounded wait gave up (the status
+    word of `workspace`, if given, and the device word). A wait that gave up
+    can leave a carry slot set, so the kept workspaces are then dropped and
+    a caller's own workspace must be zero-filled again."""
+    try:
+        if workspace is not None:
+            check(N.lib().axon_cumsum_status(_ptr(workspace), _stream(workspace)))
+        else:
+            check(N.lib().axon_cumsum_status(None, torch.cuda.current_stream().cuda_stream))
+    except N.AxonError:
+        _CUMSUM_WS.clear()
+        raise
 
 
 def adam(param, grad, exp_avg, exp_avg_sq, *, step_size=None, inv_bc2_sqrt=None, wd=None, beta1=0.9,

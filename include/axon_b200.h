@@ -153,14 +153,27 @@ AXON_API int64_t axon_cumsum_workspace_bytes(int64_t m, int64_t n, const axon_tu
  * `workspace` (zeroed by the call itself, on `stream`); every device-side
  * wait is bounded and a wait that gives up records AXON_E_TIMEOUT in the
  * workspace status word (read it with axon_cumsum_status). With no
- * tune->split, variant 0 runs variant 2 instead when m >= 128 and the input
- * rows are 16-byte aligned (the workspace is then unused).
+ * tune->split, variant 0 runs a chunk-streaming variant instead when m >= 128
+ * and the input rows are 16-byte aligned: variant 3 (16 KB chunks) for rows
+ * of at most 32 KB when a workspace is given, else variant 2 (the workspace
+ * then only carries the status word). A workspace used with variant 0 is
+ * therefore zero-filled before its first use, as variant 3 requires.
  * Variant 1: one thread-block cluster per row exchanging tile sums through
  * distributed shared memory; needs no workspace.
  * Variant 2: one CTA streams each row through a ring of shared-memory chunks
  * filled by bulk copies (tune->stages, tune->block_k = chunk KB); needs no
- * workspace and 16-byte aligned input rows. Variants 1 and 2 record a bulk
- * copy wait that gave up in a device word: axon_cumsum_status(NULL, ...). */
+ * workspace and 16-byte aligned input rows.
+ * Variant 3: rows cut into variant 2's chunks, and every CTA (one
+ * 1024-thread CTA per SM, min(SMs, m) CTAs; tune->max_ctas caps it) streams
+ * an equal contiguous range of the row-major chunk sequence, so the SMs carry
+ * equal bytes whatever m is. A row split between two CTAs takes the float64
+ * running sum of its head from the previous CTA through a workspace slot:
+ * the workspace (axon_cumsum_workspace_bytes) must be zero-filled before its
+ * first use and every completed call leaves it so; after AXON_E_TIMEOUT zero
+ * it again. tune->stages (default 4) x tune->block_k (16 or 32 KB, default
+ * 32) is the ring per CTA; 16-byte aligned input rows.
+ * Variants 1, 2 and 3 record a bulk-copy or carry wait that gave up in a
+ * device word: axon_cumsum_status(NULL, ...). */
 AXON_API int axon_cumsum(const void* x, void* y, int64_t m, int64_t n, int64_t ld_x,
                 int64_t ld_y, int32_t in_dtype, int32_t out_dtype, void* workspace,
                 int64_t workspace_bytes, const axon_tune_t* tune, void* stream);

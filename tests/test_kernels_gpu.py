@@ -218,13 +218,14 @@ def test_rope_odd_head_dim_scalar_path(cuda_device):
 
 # ---- cumsum ------------------------------------------------------------------------------
 
-@pytest.mark.parametrize("variant,split", [(0, 0), (0, 2048), (0, 4096), (0, 16384), (1, 0), (1, 4), (1, 8), (2, 0)])
+@pytest.mark.parametrize("variant,split", [(0, 0), (0, 2048), (0, 4096), (0, 16384), (1, 0), (1, 4), (1, 8), (2, 0),
+                                           (3, 0)])
 def test_cumsum_config_full_size(variant, split, cuda_device):
     spec = load_spec("cumsum_nucleus_sorted")
     (x,) = spec.make_inputs(m=256, n=128256, rng=np.random.default_rng(SEED))
     tune = {"variant": variant, "split": split}
     nbytes = ops.cumsum_workspace_bytes(256, 128256, tune)
-    ws = torch.empty(nbytes, dtype=torch.uint8, device=cuda_device) if nbytes else None
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device=cuda_device) if nbytes else None
     y = ops.cumsum(_t(x, cuda_device), workspace=ws, tune=tune)
     if ws is not None:
         ops.cumsum_status(ws)
@@ -239,12 +240,13 @@ def test_cumsum_config_full_size(variant, split, cuda_device):
     np.testing.assert_allclose(got[:, -1], x.astype(np.float64).sum(1), rtol=1e-6)
 
 
-@pytest.mark.parametrize("variant", [0, 1, 2])
+@pytest.mark.parametrize("variant", [0, 1, 2, 3])
 @pytest.mark.parametrize("shape", [(1, 1), (3, 7), (5, 8191), (2, 8193), (64, 100000), (1024, 1024), (3, 150001),
-                                   (2, 6144), (2, 6145), (7, 12290), (200, 1001), (300, 40000)])
+                                   (2, 6144), (2, 6145), (7, 12290), (200, 1001), (300, 40000), (149, 24576),
+                                   (256, 32772)])
 def test_cumsum_shapes(shape, variant, cuda_device):
     x = torch.randn(*shape, generator=torch.Generator().manual_seed(11))
-    if variant == 2 and shape[0] > 1 and shape[1] % 4:
+    if variant in (2, 3) and shape[0] > 1 and shape[1] % 4:
         # contiguous fp32 rows of n % 4 != 0 start off the 16-byte grid
         with pytest.raises(N.AxonError) as e:
             ops.cumsum(x.to(cuda_device), tune={"variant": variant})
@@ -257,7 +259,7 @@ def test_cumsum_shapes(shape, variant, cuda_device):
     assert err.max() < 1e-5
 
 
-@pytest.mark.parametrize("variant", [0, 1, 2])
+@pytest.mark.parametrize("variant", [0, 1, 2, 3])
 def test_cumsum_bf16_in_fp32_out_and_strided(variant, cuda_device):
     base = torch.randn(16, 30000, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16).to(cuda_device)
     x = base[:, :29992]
@@ -266,13 +268,60 @@ def test_cumsum_bf16_in_fp32_out_and_strided(variant, cuda_device):
     ybf = ops.cumsum(x, tune={"variant": variant})  # bf16 out: one rounding of the float64 sum
     np.testing.assert_allclose(_np(ybf), f64.cumsum(_np(x)), rtol=2 ** -8, atol=1e-2)
     xb = base[:, 1:2990]  # rows off the 16-byte grid: plain loads, no bulk copy
-    if variant == 2:
+    if variant in (2, 3):
         with pytest.raises(N.AxonError) as e:
             ops.cumsum(xb, out_dtype=torch.float32, tune={"variant": variant})
         assert e.value.code == N.AXON_E_UNSUPPORTED
         return
     yb = ops.cumsum(xb, out_dtype=torch.float32, tune={"variant": variant})
     np.testing.assert_allclose(_np(yb), f64.cumsum(_np(xb)), rtol=1e-5, atol=1e-4)
+
+
+@pytest.mark.parametrize("ctas", [0, 1, 3, 37])
+def test_cumsum_balanced_ranges_reuse_workspace(ctas, cuda_device):
+    """Variant 3 with one workspace across calls of different shapes and CTA
+    counts: the carry slots it reads are cleared again, so every call sees
+    only its own carries (a stale slot would shift a split row's values)."""
+    ws = torch.zeros(ops.cumsum_workspace_bytes(1, 1, {"variant": 3}), dtype=torch.uint8, device=cuda_device)
+    g = torch.Generator().manual_seed(5)
+    for m, n in [(40, 70000), (7, 123456), (40, 70000), (160, 8192 * 3 + 4)]:
+        x = torch.rand(m, n, generator=g)
+        for _ in range(2):
+            y = ops.cumsum(x.to(cuda_device), workspace=ws, tune={"variant": 3, "max_ctas": ctas})
+            ops.cumsum_status(ws)
+            want = f64.cumsum(x.numpy())
+            rel = np.abs(_np(y) - want) / np.maximum(want, 1e-30)
+            assert rel.max() <= 1e-5, f"{m}x{n}, {ctas} CTAs: rel err {rel.max():.3e}"
+    assert int(ws[:4].view(torch.int32)[0]) == 0  # status word: OK
+    slots = ws[256:].view(torch.int32).view(-1, 4)[:, 2]  # ready words
+    assert int(slots.abs().sum()) == 0
+
+
+@pytest.mark.parametrize("shape", [(256, 128256), (300, 40000), (5, 100000)])
+def test_cumsum_balanced_bitwise_equals_row_stream(shape, cuda_device):
+    """Both chunk-streaming variants cut rows into the same chunks, split a
+    chunk over the same 16 warps and carry a float64 running sum from chunk
+    to chunk (across CTAs in variant 3, through the slot), so their outputs
+    are the same bits."""
+    x = torch.rand(*shape, generator=torch.Generator().manual_seed(6)).to(cuda_device)
+    a = ops.cumsum(x, tune={"variant": 2})
+    b = ops.cumsum(x, tune={"variant": 3})
+    ops.cumsum_status()
+    assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("shape", [(4096, 4096), (128, 8192), (1000, 20)])
+def test_cumsum_default_short_rows_run_balanced(shape, cuda_device):
+    """The default for many short aligned rows is variant 3 with 16 KB
+    chunks: the same bits as asking for it, within 1e-5 of float64."""
+    x = torch.randn(*shape, generator=torch.Generator().manual_seed(8)).to(cuda_device)
+    a = ops.cumsum(x)
+    b = ops.cumsum(x, tune={"variant": 3, "block_k": 16, "stages": 4})
+    ops.cumsum_status()
+    assert torch.equal(a, b)
+    want = f64.cumsum(_np(x))
+    err = np.abs(_np(a) - want) / np.sqrt(np.arange(1, shape[1] + 1))[None, :]
+    assert err.max() < 1e-5
 
 
 def test_cumsum_repeat_calls_reuse_workspace(cuda_device):
