@@ -32,6 +32,7 @@ AXON_F16 = 2
 AXON_EPI_NONE = 0
 AXON_EPI_ROWSCALE = 1
 AXON_EPI_SILU_GATE = 2
+AXON_EPI_EXP = 3
 
 AXON_IPC_HANDLE_BYTES = 64
 
@@ -125,6 +126,13 @@ SIGNATURES: dict[str, tuple] = {
     "axon_row_rsqrt": (_I32, [_P, _P, _I64, _I64, _I64, _I32, _F, _F, _P]),
     "axon_row_status": (_I32, [_P]),
     "axon_rmsnorm_matmul": (_I32, [_P, _P, _P, _P, _I64, _I64, _I64, _I32, _I32, _TUNE, _P]),
+    "axon_gemm_exp": (_I32, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _I32, _TUNE, _P]),
+    "axon_qkv_cte_workspace_bytes": (_I64, [_I64, _I64]),
+    "axon_qkv_cte": (_I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I32, _I32, _TUNE, _P]),
+    "axon_softmax_mm_workspace_bytes": (_I64, [_I64, _I64]),
+    "axon_softmax_mm": (_I32, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I32, _I32, _TUNE, _P]),
+    "axon_attention_workspace_bytes": (_I64, [_I64, _I64]),
+    "axon_attention": (_I32, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I32, _I32, _TUNE, _P]),
     "axon_silu_mlp_workspace_bytes": (_I64, [_I64, _I64, _I64, _I32, _TUNE]),
     "axon_ipc_handle": (_I32, [_P, _P, ctypes.POINTER(_I64)]),
     "axon_ipc_open": (_I32, [_P, _I64, ctypes.POINTER(_P)]),

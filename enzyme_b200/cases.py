@@ -62,6 +62,25 @@ CASES: dict[str, dict[str, dict]] = {
     },
     "silu_mlp": {"sq1k": {"sizes": [1024, 1024, 1024, 1024]}},
     "softmax": {"sq1k": {"sizes": [1024, 1024]}, "roofline": {"sizes": [4096, 32768]}},
+    # the GEMM-backed neighbours of the hot path (eval/sizes.json:47-74, :96)
+    "qkv_cte": {
+        "llama405b_1k": {"sizes": [1024, 512, 16384], "rtol": 5e-2, "atol": 1.5e-1},
+        "llama405b_8k": {"sizes": [8192, 512, 16384], "rtol": 5e-2, "atol": 1.5e-1},
+        "llama70b": {"sizes": [16384, 512, 8192], "rtol": 5e-2, "atol": 1.5e-1},
+        "llama70b_l2": {"sizes": [16384, 512, 8192], "lnc": 2, "rtol": 5e-2, "atol": 1.5e-1},
+        "mistral123b": {"sizes": [16384, 640, 12288], "rtol": 5e-2, "atol": 1.5e-1},
+        "vision_l4": {"sizes": [578, 264, 1408], "rtol": 5e-2, "atol": 1.5e-1},
+        # fp32 operands: no fp32 tensor-core GEMM here, the rows record AXON_E_UNSUPPORTED
+        "llama405b_1k_fp32": {"sizes": [1024, 512, 16384], "dtype": "float32", "rtol": 1e-3, "atol": 1e-3},
+        "vision_l4_fp32": {"sizes": [578, 264, 1408], "dtype": "float32", "rtol": 1e-3, "atol": 1e-3},
+    },
+    "softmax_mm": {"sq1k": {"sizes": [1024, 1024, 1024]}},
+    "attention_nkilib": {
+        "d128": {"sizes": [1024, 128], "rtol": 5e-2, "atol": 5e-2},
+        "s2k_d128": {"sizes": [2048, 128], "rtol": 5e-2, "atol": 5e-2},
+        "s4k_d128": {"sizes": [4096, 128], "rtol": 5e-2, "atol": 5e-2},
+        "s8k_d128": {"sizes": [8192, 128], "rtol": 5e-2, "atol": 5e-2},
+    },
     # the BASELINE configs (sibling specs)
     "rmsnorm_llama": {"config": {"sizes": [2048, 4096], "rtol": 1e-2, "atol": 1e-2}},
     "rope_gqa": {"config": {"sizes": [4096, 32, 8, 64], "rtol": 1e-2, "atol": 1e-2}},

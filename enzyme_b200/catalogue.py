@@ -18,11 +18,14 @@ Tile knob meaning (the CUDA counterpart of TILES_IN_BLOCK_*):
   cumsum                TILES_IN_BLOCK_N = v -> 1024*v elements per scan tile
                         (cluster_dsmem: v CTAs per row; row_stream and
                         balanced_ranges: v = 1).
-  GEMM specs            TILES_IN_BLOCK_M must be 1 (128-row tcgen05 tiles per CTA),
+  GEMM specs            (matmul, rmsnorm_matmul, qkv_cte, softmax_mm)
+                        TILES_IN_BLOCK_M must be 1 (128-row tcgen05 tiles per CTA),
                         TILES_IN_BLOCK_N = v -> BLOCK_N = 64*v,
                         TILES_IN_BLOCK_K = v -> min(v, deepest that fits)
                         shared-memory pipeline stages. hw_variant 0 = one CTA
                         per tile, 1 = CTA pairs (cta_group::2, 256-row tiles).
+  attention_nkilib      N -> BLOCK_N = 64*v of the exp(q @ k_t) GEMM, K -> its
+                        stages; M and P must be 1 (the second GEMM picks its tile).
   silu_mlp              N -> gate/up BLOCK_N = 128*v (64*v output columns),
                         K -> stages, P -> down-projection BLOCK_N = 64*v
                         (recorded; the down GEMM picks its own tile today).
@@ -46,9 +49,12 @@ ROW_SPECS = ("rmsnorm", "rmsnorm_llama", "layernorm", "softmax")
 ROPE_SPECS = ("rope", "rope_gqa")
 SCAN_SPECS = ("cumsum", "cumsum_nucleus_sorted")
 ADAM_SPECS = ("fused_adam", "fused_adam_cfg")
-GEMM_SPECS = ("matmul", "rmsnorm_matmul")
+# GEMM-backed specs: a row pass (or the first GEMM's epilogue) and a
+# row-scaled tcgen05 GEMM; their tile knobs are the GEMM's
+GEMM_SPECS = ("matmul", "rmsnorm_matmul", "qkv_cte", "softmax_mm")
+ATTN_SPECS = ("attention_nkilib",)
 MLP_SPECS = ("silu_mlp", "silu_mlp_swiglu")
-ALL_SPECS = ROW_SPECS + ROPE_SPECS + SCAN_SPECS + ADAM_SPECS + GEMM_SPECS + MLP_SPECS
+ALL_SPECS = ROW_SPECS + ROPE_SPECS + SCAN_SPECS + ADAM_SPECS + GEMM_SPECS + ATTN_SPECS + MLP_SPECS
 
 ADAM_BETAS = {"fused_adam": (0.9, 0.999), "fused_adam_cfg": (0.9, 0.95)}
 
@@ -74,6 +80,10 @@ def variants(spec_name: str) -> list[Variant]:
     if spec_name in GEMM_SPECS:
         # hw_variant i runs axon_gemm variant i + 1 (0 is the library's auto pick)
         return [Variant(0, "tcgen05_ws_persistent"), Variant(1, "tcgen05_cta_pair")]
+    if spec_name in ATTN_SPECS:
+        # both GEMMs at the library's pick (pairs from 256 rows); the exp GEMM's
+        # column tile is the knob
+        return [Variant(0, "tcgen05_exp_rowsum")]
     if spec_name in MLP_SPECS:
         return [Variant(0, "tcgen05_act_1term"), Variant(1, "tcgen05_act_2term"), Variant(2, "tcgen05_act_3term"),
                 Variant(3, "tcgen05_act_f16"), Variant(4, "tcgen05_act_f16_fused")]
@@ -140,6 +150,12 @@ def constraints(spec_name: str, hw_variant: int, dims: dict, itemsize: int,
         out.append(TileConstraint(args[1], extent=256, tile_size=64, require_divisible=True,
                                   allowed=(1, 2, 4) if hw_variant == 0 else (2, 4)))
         out.append(TileConstraint(args[2], extent=8, tile_size=1, require_divisible=True, allowed=(2, 4, 8)))
+    elif spec_name in ATTN_SPECS:
+        # N -> column tile of the exp GEMM (64 * v); K -> stages; M, P fixed
+        out.append(_one(args[0]))
+        out.append(TileConstraint(args[1], extent=256, tile_size=64, require_divisible=True, allowed=(1, 2, 4)))
+        out.append(TileConstraint(args[2], extent=8, tile_size=1, require_divisible=True, allowed=(2, 4)))
+        out.append(_one(args[3]))
     elif spec_name in MLP_SPECS:
         out.append(_one(args[0]))
         out.append(TileConstraint(args[1], extent=256, tile_size=128, require_divisible=True, allowed=(1, 2)))
@@ -164,6 +180,9 @@ def tune_for(spec_name: str, hw_variant: int, tiles: dict[str, int]) -> dict | l
     if spec_name in GEMM_SPECS:
         bn = 64 * t["N"]
         return {"variant": hw_variant + 1, "block_n": bn, "stages": min(t["K"], gemm_max_stages(hw_variant == 1, bn))}
+    if spec_name in ATTN_SPECS:
+        bn = 64 * t["N"]
+        return {"block_n": bn, "stages": min(t["K"], gemm_max_stages(False, bn))}
     if spec_name in MLP_SPECS:
         if hw_variant == 4:  # both GEMMs in one kernel (256-column tiles; N and P are recorded only)
             return {"variant": 3, "stages": t["K"], "precision": 4, "down_block_n": 64 * t["P"]}
@@ -218,6 +237,12 @@ def launch(spec_name: str, hw_variant: int, tiles: dict[str, int], inputs: Seque
         return (ops.gemm(t[0], t[1], tune=tune, out=out and out[0]),)
     if spec_name == "rmsnorm_matmul":
         return (ops.rmsnorm_matmul(t[0], t[1], tune=tune, out=out and out[0]),)
+    if spec_name == "qkv_cte":
+        return (ops.qkv_cte(*t, tune=tune, out=out and out[0]),)
+    if spec_name == "softmax_mm":
+        return (ops.softmax_mm(*t, tune=tune, out=out and out[0]),)
+    if spec_name in ATTN_SPECS:
+        return (ops.attention(*t, tune=tune, out=out and out[0]),)
     if spec_name in MLP_SPECS:
         tune = dict(tune)
         tune.pop("down_block_n")

@@ -184,7 +184,7 @@ __device__ __forceinline__ void store32(TC* dst, const float* v, int64_t col, in
 // axon_tp_down_partial, not an axon_gemm epilogue): output row r goes to the
 // inbox of its owner rank o = r / rows_per_owner, a peer buffer laid out
 // [world][rows_per_owner][ldc], at slot `peer_rank`.
-constexpr int kEpiPeer = 3;
+constexpr int kEpiPeer = 7;
 constexpr int kMaxPeers = 8;
 
 struct GemmParams {
@@ -204,6 +204,8 @@ struct GemmParams {
   int b_kwrap;         // > 0: B's k coordinate wraps modulo this (B re-read per term)
   int max_ctas;        // > 0: cap on the persistent grid
   int raster;          // > 0: tiles ordered in bands of this many row tiles (see tile_coords)
+  float* row_part;     // EXP: sums of the stored values per (column tile, row), or NULL
+  int64_t part_ld;     // row_part stride between column tiles (>= m)
 };
 
 // Ownership of output row r: contiguous blocks of rows_per_owner rows, or
@@ -463,6 +465,7 @@ __global__ void __launch_bounds__(192, 1)
         peer_store_tile<BN>(p, stg, tbase, static_cast<int64_t>(tm) * BM + q * 32, static_cast<int64_t>(tn) * BN,
                             lane);
       } else {
+        float psum = 0.f;  // EXP: this row's sum over the tile, of the values as stored
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           float v[32];
@@ -474,7 +477,17 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] *= scale;
           }
+          if constexpr (EPI == AXON_EPI_EXP) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              v[j] = to_f(from_f<TC>(__expf(v[j])));
+              if (col + j < p.n) psum += v[j];
+            }
+          }
           if (row_ok && col < p.n) store32<TC>(crow + col, v, col, p.n);
+        }
+        if constexpr (EPI == AXON_EPI_EXP) {
+          if (row_ok && p.row_part != nullptr) p.row_part[tn * p.part_ld + row] = psum;
         }
       }
       tc_fence_before();
@@ -743,6 +756,7 @@ __global__ void __launch_bounds__(192, 1)
                             tbase, static_cast<int64_t>(tm) * 2 * BM + static_cast<int64_t>(rank) * BM + q * 32,
                             static_cast<int64_t>(tn) * BN, lane);
       } else {
+        float psum = 0.f;  // EXP: this row's sum over the tile, of the values as stored
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           float v[32];
@@ -754,7 +768,17 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] *= scale;
           }
+          if constexpr (EPI == AXON_EPI_EXP) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              v[j] = to_f(from_f<TC>(__expf(v[j])));
+              if (col + j < p.n) psum += v[j];
+            }
+          }
           if (row_ok && col < p.n) store32<TC>(crow + col, v, col, p.n);
+        }
+        if constexpr (EPI == AXON_EPI_EXP) {
+          if (row_ok && p.row_part != nullptr) p.row_part[tn * p.part_ld + row] = psum;
         }
       }
       tc_fence_before();
@@ -1613,14 +1637,15 @@ namespace {
 int gemm_impl(const void* a, const void* b, const void* b2, void* c, const float* row_scale, int64_t m, int64_t n,
               int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int32_t ab_dtype, int32_t c_dtype, int32_t epilogue,
               const axon_tune_t* tune, void* stream, int terms, int64_t term_stride, int64_t b_kwrap,
-              void* const* peers = nullptr, int world = 0, int peer_rank = 0, int64_t rows_per_owner = 0) {
+              void* const* peers = nullptr, int world = 0, int peer_rank = 0, int64_t rows_per_owner = 0,
+              float* row_part = nullptr, int64_t part_ld = 0) {
   axon_tune_t t = tune_or_default(tune);
   if (m < 0 || n < 0 || k < 0) return fail(AXON_E_SHAPE, "axon_gemm: negative size");
   if (m == 0 || n == 0) return AXON_OK;  // empty output: nothing to launch, pointers may be NULL
   if (!a || !b || !c) return fail(AXON_E_ARG, "axon_gemm: NULL operand");
   if (ab_dtype != AXON_BF16 && ab_dtype != AXON_F16)
     return fail(AXON_E_UNSUPPORTED, "axon_gemm: A/B dtype must be bf16 or f16 (got %d)", ab_dtype);
-  if (epilogue < AXON_EPI_NONE || epilogue > AXON_EPI_SILU_GATE)
+  if (epilogue < AXON_EPI_NONE || epilogue > AXON_EPI_EXP)
     return fail(AXON_E_ARG, "axon_gemm: unknown epilogue %d", epilogue);
   if (epilogue == AXON_EPI_SILU_GATE && !b2) return fail(AXON_E_ARG, "axon_gemm: SILU_GATE needs b2");
   if (epilogue == AXON_EPI_ROWSCALE && !row_scale) return fail(AXON_E_ARG, "axon_gemm: ROWSCALE needs row_scale");
@@ -1675,6 +1700,10 @@ int gemm_impl(const void* a, const void* b, const void* b2, void* c, const float
   }
   gp.c = c;
   gp.row_scale = row_scale;
+  gp.row_part = row_part;
+  gp.part_ld = part_ld;
+  if (row_part != nullptr && (epilogue != AXON_EPI_EXP || part_ld < m))
+    return fail(AXON_E_ARG, "axon_gemm: row sums need the EXP epilogue and a tile stride of >= m");
   gp.m = static_cast<int>(m);
   gp.n = static_cast<int>(n);
   gp.k = static_cast<int>(k);
@@ -1709,12 +1738,22 @@ int gemm_impl(const void* a, const void* b, const void* b2, void* c, const float
     case 6: return dispatch_c<256, AXON_EPI_ROWSCALE>(c_dtype, pair, ma, mb, mb2, gp, s);
     case 9: return dispatch_c<128, AXON_EPI_SILU_GATE>(c_dtype, pair, ma, mb, mb2, gp, s);
     case 10: return dispatch_c<256, AXON_EPI_SILU_GATE>(c_dtype, pair, ma, mb, mb2, gp, s);
+    case 12: return dispatch_c<64, AXON_EPI_EXP>(c_dtype, pair, ma, mb, mb2, gp, s);
+    case 13: return dispatch_c<128, AXON_EPI_EXP>(c_dtype, pair, ma, mb, mb2, gp, s);
+    case 14: return dispatch_c<256, AXON_EPI_EXP>(c_dtype, pair, ma, mb, mb2, gp, s);
     default: return fail(AXON_E_ARG, "axon_gemm: unsupported tile/epilogue combination");
   }
 }
 
 }  // namespace
 }  // namespace axon
+
+extern "C" int axon_gemm_exp(const void* a, const void* b, void* c, float* row_part, int64_t part_ld, int64_t m,
+                             int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int32_t ab_dtype,
+                             int32_t c_dtype, const axon_tune_t* tune, void* stream) {
+  return gemm_impl(a, b, nullptr, c, nullptr, m, n, k, lda, ldb, ldc, ab_dtype, c_dtype, AXON_EPI_EXP, tune, stream,
+                   1, 0, 0, nullptr, 0, 0, 0, row_part, part_ld);
+}
 
 extern "C" int axon_gemm(const void* a, const void* b, const void* b2, void* c, const float* row_scale, int64_t m,
                          int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int32_t ab_dtype,

@@ -257,6 +257,88 @@ def rmsnorm_matmul(x, w, *, out=None, out_dtype=None, workspace=None, tune=None)
     return y
 
 
+def _workspace(nbytes: int, device, workspace=None) -> torch.Tensor:
+    if workspace is not None:
+        if workspace.numel() < nbytes:
+            raise N.AxonError(N.AXON_E_ARG, f"workspace of {nbytes} bytes needed")
+        return workspace
+    return torch.empty(nbytes, dtype=torch.uint8, device=device)
+
+
+def _check_ws_bytes(nbytes: int) -> int:
+    if nbytes < 0:
+        check(int(nbytes))
+    return int(nbytes)
+
+
+def gemm_exp(a, b, *, row_part=None, out=None, out_dtype=None, tune=None):
+    """C = exp(A @ B); with `row_part` (fp32 [tiles, m], tiles = ceil(n /
+    block_n)) also each row's sum of the stored values per column tile."""
+    _require_cuda(a, b, row_part)
+    m, k, lda = _rows(a)
+    kb, n, ldb = _rows(b)
+    if kb != k:
+        raise N.AxonError(N.AXON_E_SHAPE, f"gemm_exp: inner dims differ ({k} vs {kb})")
+    c = out if out is not None else torch.empty((m, n), dtype=out_dtype or a.dtype, device=a.device)
+    _, _, ldc = _rows(c)
+    part_ld = row_part.stride(0) if row_part is not None else 0
+    check(N.lib().axon_gemm_exp(_ptr(a), _ptr(b), _ptr(c), _ptr(row_part), part_ld, m, n, k, lda, ldb, ldc,
+                                dtype_code(a), dtype_code(c), _tune(tune), _stream(a)))
+    return c
+
+
+def qkv_cte(x, mlp_prev, attention_prev, w, *, out=None, out_dtype=None, workspace=None, tune=None):
+    """(h / sqrt(mean(h^2) + 1e-6)) @ w with h = x + mlp_prev + attention_prev."""
+    _require_cuda(x, mlp_prev, attention_prev, w)
+    for t in (x, mlp_prev, attention_prev, w):
+        if not t.is_contiguous():
+            raise N.AxonError(N.AXON_E_SHAPE, "qkv_cte: tensors must be contiguous")
+    m, k = x.shape
+    n = w.shape[1]
+    if mlp_prev.shape != x.shape or attention_prev.shape != x.shape or w.shape[0] != k:
+        raise N.AxonError(N.AXON_E_SHAPE, "qkv_cte: x, mlp_prev, attention_prev [m, k] and w [k, n]")
+    y = out if out is not None else torch.empty((m, n), dtype=out_dtype or x.dtype, device=x.device)
+    nbytes = _check_ws_bytes(N.lib().axon_qkv_cte_workspace_bytes(m, k))
+    ws = _workspace(nbytes, x.device, workspace)
+    check(N.lib().axon_qkv_cte(_ptr(x), _ptr(mlp_prev), _ptr(attention_prev), _ptr(w), _ptr(y), _ptr(ws), ws.numel(),
+                               m, n, k, dtype_code(x), dtype_code(y), _tune(tune), _stream(x)))
+    return y
+
+
+def softmax_mm(x, w, *, out=None, out_dtype=None, workspace=None, tune=None):
+    """(exp(x) / sum(exp(x))) @ w, the bare exponential of the spec."""
+    _require_cuda(x, w)
+    if not x.is_contiguous() or not w.is_contiguous():
+        raise N.AxonError(N.AXON_E_SHAPE, "softmax_mm: x and w must be contiguous")
+    m, k = x.shape
+    if w.shape[0] != k:
+        raise N.AxonError(N.AXON_E_SHAPE, "softmax_mm: x [m, k] and w [k, n]")
+    n = w.shape[1]
+    y = out if out is not None else torch.empty((m, n), dtype=out_dtype or x.dtype, device=x.device)
+    nbytes = _check_ws_bytes(N.lib().axon_softmax_mm_workspace_bytes(m, k))
+    ws = _workspace(nbytes, x.device, workspace)
+    check(N.lib().axon_softmax_mm(_ptr(x), _ptr(w), _ptr(y), _ptr(ws), ws.numel(), m, n, k, dtype_code(x),
+                                  dtype_code(y), _tune(tune), _stream(x)))
+    return y
+
+
+def attention(q, k_t, v, *, out=None, out_dtype=None, workspace=None, tune=None):
+    """softmax(q @ k_t) @ v (bare exponential), q [s, d], k_t [d, s], v [s, d]."""
+    _require_cuda(q, k_t, v)
+    for t in (q, k_t, v):
+        if not t.is_contiguous():
+            raise N.AxonError(N.AXON_E_SHAPE, "attention: tensors must be contiguous")
+    s, d = q.shape
+    if k_t.shape != (d, s) or v.shape != (s, d):
+        raise N.AxonError(N.AXON_E_SHAPE, "attention: q [s, d], k_t [d, s], v [s, d]")
+    y = out if out is not None else torch.empty((s, d), dtype=out_dtype or q.dtype, device=q.device)
+    nbytes = _check_ws_bytes(N.lib().axon_attention_workspace_bytes(s, d))
+    ws = _workspace(nbytes, q.device, workspace)
+    check(N.lib().axon_attention(_ptr(q), _ptr(k_t), _ptr(v), _ptr(y), _ptr(ws), ws.numel(), s, d, dtype_code(q),
+                                 dtype_code(y), _tune(tune), _stream(q)))
+    return y
+
+
 def silu_mlp_workspace_bytes(m: int, n: int, p: int, dtype_code_: int, tune=None) -> int:
     nbytes = int(N.lib().axon_silu_mlp_workspace_bytes(m, n, p, dtype_code_, _tune(tune)))
     if nbytes < 0:

@@ -54,8 +54,10 @@ def work(spec: str, dims: dict, itemsize: int = 2) -> tuple[str, float]:
         return "hbm", 7 * d["p"] * d["f"] * itemsize + 3 * d["p"] * itemsize
     if spec == "fused_adam_cfg":
         return "hbm", 26 * d["p"] * d["f"] + 3 * 4 * d["p"]
-    if spec in ("matmul", "rmsnorm_matmul"):
+    if spec in ("matmul", "rmsnorm_matmul", "qkv_cte", "softmax_mm"):
         return "tensor", 2.0 * d["m"] * d["n"] * d["k"]
+    if spec == "attention_nkilib":
+        return "tensor", 4.0 * d["s"] * d["s"] * d["d"]
     if spec in ("silu_mlp", "silu_mlp_swiglu"):
         return "tensor", 2.0 * d["m"] * d["k"] * d["n"] * 2 + 2.0 * d["m"] * d["n"] * d["p"]
     raise KeyError(spec)

@@ -233,6 +233,7 @@ AXON_API int axon_adam(const void* param, const void* grad, const void* exp_avg,
 #define AXON_EPI_NONE 0      /* C = A @ B                                        */
 #define AXON_EPI_ROWSCALE 1  /* C = row_scale[i] * (A @ B)                       */
 #define AXON_EPI_SILU_GATE 2 /* C = silu(A @ B) * (A @ B2)  (B2 = up weight)     */
+#define AXON_EPI_EXP 3       /* C = exp(A @ B)  (bare exponential, no shift)      */
 
 /* tcgen05 / TMEM GEMM: A [m, k] row-major (lda), B [k, n] row-major (ldb) --
  * the layout Axon's specs pass (kernels/matmul/refs.py:24-25) -- C [m, n]
@@ -406,6 +407,50 @@ AXON_API int axon_row_rsqrt(const void* x, float* r, int64_t m, int64_t n, int64
 AXON_API int axon_rmsnorm_matmul(const void* x, const void* w, void* y, void* workspace,
                         int64_t m, int64_t n, int64_t k, int32_t ab_dtype,
                         int32_t c_dtype, const axon_tune_t* tune, void* stream);
+
+/* C = exp(A @ B) (AXON_EPI_EXP) and, when row_part is not NULL, the sum of
+ * each row's stored values over each column tile of the GEMM:
+ * row_part[t * part_ld + i] for row i and tile t < ceil(n / block_n)
+ * (part_ld >= m; block_n as tune->block_n, or axon_gemm's default for n).
+ * Shapes and alignment as axon_gemm. The softmax denominator of
+ * axon_attention comes from these sums. */
+AXON_API int axon_gemm_exp(const void* a, const void* b, void* c, float* row_part, int64_t part_ld,
+                  int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc,
+                  int32_t ab_dtype, int32_t c_dtype, const axon_tune_t* tune, void* stream);
+
+/* qkv_cte (Axon kernels/qkv_cte/kernel.py:18-27; refs.py:23-36):
+ * h = x + mlp_prev + attention_prev, y = (h / sqrt(mean(h^2) + 1e-6)) @ w.
+ * x, mlp_prev, attention_prev [m, k] and w [k, n] contiguous, bf16 or f16;
+ * y [m, n] (c_dtype). One row pass writes h (input dtype) and the per-row
+ * scale; the GEMM applies the scale in its epilogue. k a multiple of 8.
+ * workspace: axon_qkv_cte_workspace_bytes(m, k) bytes, 16-byte aligned. */
+AXON_API int64_t axon_qkv_cte_workspace_bytes(int64_t m, int64_t k);
+AXON_API int axon_qkv_cte(const void* x, const void* mlp_prev, const void* attention_prev,
+                 const void* w, void* y, void* workspace, int64_t workspace_bytes, int64_t m,
+                 int64_t n, int64_t k, int32_t ab_dtype, int32_t c_dtype,
+                 const axon_tune_t* tune, void* stream);
+
+/* softmax_mm (Axon kernels/softmax_mm/kernel.py:7-11; refs.py:16-19):
+ * y = (exp(x) / sum(exp(x))) @ w, a bare exponential as in the spec.
+ * x [m, k], w [k, n] contiguous bf16 or f16; one row pass writes exp(x) in
+ * the input dtype and 1 / (its row sum, over the stored values); the GEMM
+ * applies that in its epilogue. workspace: axon_softmax_mm_workspace_bytes. */
+AXON_API int64_t axon_softmax_mm_workspace_bytes(int64_t m, int64_t k);
+AXON_API int axon_softmax_mm(const void* x, const void* w, void* y, void* workspace,
+                    int64_t workspace_bytes, int64_t m, int64_t n, int64_t k, int32_t ab_dtype,
+                    int32_t c_dtype, const axon_tune_t* tune, void* stream);
+
+/* attention_nkilib (Axon kernels/attention_nkilib/kernel.py:14-21; refs.py:36-47):
+ * y = softmax(q @ k_t) @ v with a bare exponential, q [s, d], k_t [d, s]
+ * (pre-transposed), v [s, d], contiguous bf16 or f16; y [s, d] (c_dtype).
+ * The first GEMM stores e = exp(q @ k_t) [s, s] in the input dtype with
+ * per-tile row sums (axon_gemm_exp, tune->block_n), a small pass forms
+ * 1 / row sum, and the second GEMM applies it: y = r * (e @ v).
+ * s and d multiples of 8. workspace: axon_attention_workspace_bytes(s, d). */
+AXON_API int64_t axon_attention_workspace_bytes(int64_t s, int64_t d);
+AXON_API int axon_attention(const void* q, const void* k_t, const void* v, void* y, void* workspace,
+                   int64_t workspace_bytes, int64_t s, int64_t d, int32_t ab_dtype,
+                   int32_t c_dtype, const axon_tune_t* tune, void* stream);
 
 /* Bytes of scratch axon_silu_mlp needs: the [m, n] activation in ab_dtype
  * times tune->precision terms, or for precision 4 an f16 activation, an f16

@@ -90,6 +90,25 @@ def rmsnorm_matmul(x, w):
     return rmsnorm_sum(x) @ _f(w)
 
 
+def qkv_cte(x, mlp_prev, attention_prev, w, eps=1e-6):
+    """Axon kernels/qkv_cte/refs.py:23-27: residual add, mean-RMS norm, projection."""
+    h = _f(x) + _f(mlp_prev) + _f(attention_prev)
+    return (h / np.sqrt(np.mean(h * h, axis=1, keepdims=True) + eps)) @ _f(w)
+
+
+def softmax_mm(x, w):
+    """Axon kernels/softmax_mm/refs.py:16-19: bare-exponential softmax, then @ w."""
+    e = np.exp(_f(x))
+    return (e / e.sum(axis=1, keepdims=True)) @ _f(w)
+
+
+def attention(q, k_t, v):
+    """Axon kernels/attention_nkilib/refs.py:36-40: softmax(q @ k_t) @ v with a
+    bare exponential (q @ k_t stays below the exponential's float64 limit)."""
+    e = np.exp(_f(q) @ _f(k_t))
+    return (e / e.sum(axis=1, keepdims=True)) @ _f(v)
+
+
 # spec name -> oracle over the spec's positional inputs
 ORACLES = {
     "rmsnorm": rmsnorm_sum,
@@ -106,6 +125,9 @@ ORACLES = {
     "silu_mlp": silu_mlp,
     "silu_mlp_swiglu": silu_mlp,
     "rmsnorm_matmul": rmsnorm_matmul,
+    "qkv_cte": qkv_cte,
+    "softmax_mm": softmax_mm,
+    "attention_nkilib": attention,
 }
 
 

@@ -51,6 +51,9 @@ CASES = [
     ("matmul", "tiles", dict(m=160, n=320, k=96), None),
     ("silu_mlp", "small", dict(m=128, n=256, k=128, p=128), None),
     ("rmsnorm_matmul", "small", dict(m=128, n=192, k=384), None),
+    ("qkv_cte", "small", dict(m=96, n=160, k=256), None),
+    ("softmax_mm", "small", dict(m=64, n=96, k=192), None),
+    ("attention_nkilib", "small", dict(s=128, d=64), None),
 ]
 
 

@@ -36,6 +36,11 @@ TOL = {
     "matmul": (2e-2, 2e-2),
     "silu_mlp": (2e-2, 2e-2),
     "rmsnorm_matmul": (2e-2, 2e-2),
+    # the north star's bf16 bar, tighter than these specs' case tolerances
+    # (eval/sizes.json: qkv_cte 5e-2 / 1.5e-1, attention_nkilib 5e-2 / 5e-2)
+    "qkv_cte": (1e-2, 1e-2),
+    "softmax_mm": (1e-2, 1e-2),
+    "attention_nkilib": (1e-2, 1e-2),
 }
 
 
@@ -82,6 +87,12 @@ def _run_spec(spec_name, inputs, dev):
         return (ops.silu_mlp(*t, tune={"precision": 3}),)
     if spec_name == "rmsnorm_matmul":
         return (ops.rmsnorm_matmul(t[0], t[1]),)
+    if spec_name == "qkv_cte":
+        return (ops.qkv_cte(*t),)
+    if spec_name == "softmax_mm":
+        return (ops.softmax_mm(*t),)
+    if spec_name == "attention_nkilib":
+        return (ops.attention(*t),)
     raise KeyError(spec_name)
 
 
@@ -89,6 +100,7 @@ GOLDEN = [
     "rmsnorm_small", "rmsnorm_ragged", "layernorm_small", "layernorm_ragged", "softmax_small", "softmax_ragged",
     "rope_small", "rope_ragged", "cumsum_long", "cumsum_ragged", "cumsum_bf16", "fused_adam_bf16",
     "fused_adam_fp32", "matmul_small", "matmul_tiles", "silu_mlp_small", "rmsnorm_matmul_small",
+    "qkv_cte_small", "softmax_mm_small", "attention_nkilib_small",
 ]
 
 
@@ -105,6 +117,58 @@ def test_golden_parity(case, cuda_device):
     # and against the float64 oracle, one output rounding away
     for g, w in zip(got, f64.evaluate(spec_name, *inputs)):
         _close(g, w, rtol, atol, case + " vs oracle")
+
+
+# ---- GEMM-backed neighbours: qkv_cte, softmax_mm, attention_nkilib --------------------
+
+def _spec_inputs(name, dims, dev):
+    spec = load_spec(name)
+    ins = spec.make_inputs(**dims, rng=np.random.default_rng(SEED))
+    return ins, [_t(a, dev) for a in ins]
+
+
+@pytest.mark.parametrize("dims,tune", [(dict(m=578, n=264, k=1408), None), (dict(m=1024, n=512, k=2048), None),
+                                       (dict(m=1024, n=512, k=2048), {"variant": 1, "block_n": 128}),
+                                       (dict(m=300, n=640, k=512), {"variant": 2})])
+def test_qkv_cte(dims, tune, cuda_device):
+    ins, t = _spec_inputs("qkv_cte", dims, cuda_device)
+    y = ops.qkv_cte(*t, tune=tune)
+    torch.cuda.synchronize()
+    _close(y, f64.qkv_cte(*ins), 1e-2, 1e-2, f"qkv_cte {dims}")
+
+
+@pytest.mark.parametrize("dims", [dict(m=1024, n=1024, k=1024), dict(m=200, n=72, k=4104)])
+def test_softmax_mm(dims, cuda_device):
+    ins, t = _spec_inputs("softmax_mm", dims, cuda_device)
+    y = ops.softmax_mm(*t)
+    torch.cuda.synchronize()
+    _close(y, f64.softmax_mm(*ins), 1e-2, 1e-2, f"softmax_mm {dims}")
+
+
+@pytest.mark.parametrize("s,d,block_n", [(1024, 128, 0), (1000, 128, 0), (2048, 128, 128), (2048, 64, 64),
+                                         (512, 512, 0)])
+def test_attention(s, d, block_n, cuda_device):
+    ins, t = _spec_inputs("attention_nkilib", dict(s=s, d=d), cuda_device)
+    y = ops.attention(*t, tune={"block_n": block_n} if block_n else None)
+    torch.cuda.synchronize()
+    _close(y, f64.attention(*ins), 1e-2, 1e-2, f"attention s={s} d={d}")
+
+
+@pytest.mark.parametrize("n,block_n", [(1000, 256), (512, 128), (200, 64)])
+def test_gemm_exp_row_sums(n, block_n, cuda_device):
+    """exp(A @ B) rounded once to bf16, and per column tile the sum of the
+    stored values of each row."""
+    g = torch.Generator().manual_seed(3)
+    a = (0.1 * torch.randn(300, 64, generator=g)).bfloat16().to(cuda_device)
+    b = (0.1 * torch.randn(64, n, generator=g)).bfloat16().to(cuda_device)
+    tiles = -(-n // block_n)
+    part = torch.full((tiles, 300), float("nan"), device=cuda_device)
+    c = ops.gemm_exp(a, b, row_part=part, tune={"block_n": block_n})
+    torch.cuda.synchronize()
+    want = torch.exp(a.double() @ b.double())
+    _close(c, want.cpu().numpy(), 2 ** -8, 0, "exp")
+    sums = torch.stack([c[:, i * block_n:(i + 1) * block_n].double().sum(1) for i in range(tiles)])
+    np.testing.assert_allclose(part.double().cpu().numpy(), sums.cpu().numpy(), rtol=1e-5)
 
 
 # ---- row kernels ---------------------------------------------------------------
