@@ -127,7 +127,9 @@ SIGNATURES: dict[str, tuple] = {
     "axon_row_status": (_I32, [_P]),
     "axon_rmsnorm_matmul": (_I32, [_P, _P, _P, _P, _I64, _I64, _I64, _I32, _I32, _TUNE, _P]),
     "axon_gemm_exp": (_I32, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I32, _I32, _TUNE, _P]),
-    "axon_qkv_cte_workspace_bytes": (_I64, [_I64, _I64]),
+    "axon_gemm_resid3_workspace_bytes": (_I64, [_I64, _I64, _I64, _TUNE]),
+    "axon_gemm_resid3": (_I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I32, _I32, _F, _TUNE, _P]),
+    "axon_qkv_cte_workspace_bytes": (_I64, [_I64, _I64, _I64, _TUNE]),
     "axon_qkv_cte": (_I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I32, _I32, _TUNE, _P]),
     "axon_softmax_mm_workspace_bytes": (_I64, [_I64, _I64]),
     "axon_softmax_mm": (_I32, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I32, _I32, _TUNE, _P]),

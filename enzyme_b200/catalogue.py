@@ -51,10 +51,11 @@ SCAN_SPECS = ("cumsum", "cumsum_nucleus_sorted")
 ADAM_SPECS = ("fused_adam", "fused_adam_cfg")
 # GEMM-backed specs: a row pass (or the first GEMM's epilogue) and a
 # row-scaled tcgen05 GEMM; their tile knobs are the GEMM's
-GEMM_SPECS = ("matmul", "rmsnorm_matmul", "qkv_cte", "softmax_mm")
+GEMM_SPECS = ("matmul", "rmsnorm_matmul", "softmax_mm")
+QKV_SPECS = ("qkv_cte",)
 ATTN_SPECS = ("attention_nkilib",)
 MLP_SPECS = ("silu_mlp", "silu_mlp_swiglu")
-ALL_SPECS = ROW_SPECS + ROPE_SPECS + SCAN_SPECS + ADAM_SPECS + GEMM_SPECS + ATTN_SPECS + MLP_SPECS
+ALL_SPECS = ROW_SPECS + ROPE_SPECS + SCAN_SPECS + ADAM_SPECS + GEMM_SPECS + QKV_SPECS + ATTN_SPECS + MLP_SPECS
 
 ADAM_BETAS = {"fused_adam": (0.9, 0.999), "fused_adam_cfg": (0.9, 0.95)}
 
@@ -84,6 +85,10 @@ def variants(spec_name: str) -> list[Variant]:
         # both GEMMs at the library's pick (pairs from 256 rows); the exp GEMM's
         # column tile is the knob
         return [Variant(0, "tcgen05_exp_rowsum")]
+    if spec_name in QKV_SPECS:
+        # 0: residual sum formed while staging the GEMM operand (one kernel);
+        # 1 / 2: a row pass writing h, then the one-CTA / CTA-pair GEMM
+        return [Variant(0, "tcgen05_resid3_fused"), Variant(1, "rowpass_tcgen05"), Variant(2, "rowpass_tcgen05_pair")]
     if spec_name in MLP_SPECS:
         return [Variant(0, "tcgen05_act_1term"), Variant(1, "tcgen05_act_2term"), Variant(2, "tcgen05_act_3term"),
                 Variant(3, "tcgen05_act_f16"), Variant(4, "tcgen05_act_f16_fused")]
@@ -150,6 +155,11 @@ def constraints(spec_name: str, hw_variant: int, dims: dict, itemsize: int,
         out.append(TileConstraint(args[1], extent=256, tile_size=64, require_divisible=True,
                                   allowed=(1, 2, 4) if hw_variant == 0 else (2, 4)))
         out.append(TileConstraint(args[2], extent=8, tile_size=1, require_divisible=True, allowed=(2, 4, 8)))
+    elif spec_name in QKV_SPECS:
+        out.append(_one(args[0]))
+        out.append(TileConstraint(args[1], extent=256, tile_size=64, require_divisible=True,
+                                  allowed=(2, 4) if hw_variant != 1 else (1, 2, 4)))
+        out.append(TileConstraint(args[2], extent=8, tile_size=1, require_divisible=True, allowed=(2, 4)))
     elif spec_name in ATTN_SPECS:
         # N -> column tile of the exp GEMM (64 * v); K -> stages; M, P fixed
         out.append(_one(args[0]))
@@ -183,6 +193,12 @@ def tune_for(spec_name: str, hw_variant: int, tiles: dict[str, int]) -> dict | l
     if spec_name in ATTN_SPECS:
         bn = 64 * t["N"]
         return {"block_n": bn, "stages": min(t["K"], gemm_max_stages(False, bn))}
+    if spec_name in QKV_SPECS:
+        bn = 64 * t["N"]
+        if hw_variant == 0:  # stages of x, r1, r2 and the B slab
+            return {"variant": 0, "block_n": bn, "stages": min(t["K"], (232448 - 3584) // (3 * 16384 + bn * 128))}
+        return {"variant": hw_variant, "block_n": bn,
+                "stages": min(t["K"], gemm_max_stages(hw_variant == 2, bn))}
     if spec_name in MLP_SPECS:
         if hw_variant == 4:  # both GEMMs in one kernel (256-column tiles; N and P are recorded only)
             return {"variant": 3, "stages": t["K"], "precision": 4, "down_block_n": 64 * t["P"]}

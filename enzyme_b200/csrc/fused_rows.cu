@@ -3,8 +3,10 @@
 // row-wise map feeding a tcgen05 GEMM whose epilogue applies a per-row
 // scale, so the normalisation costs no pass of its own:
 //
-//   qkv_cte     h = x + mlp_prev + attention_prev, r = rsqrt(mean(h^2) + eps)
-//               (one row pass writing h), then y = r * (h @ w)
+//   qkv_cte     h = x + mlp_prev + attention_prev, r = rsqrt(mean(h^2) + eps),
+//               y = r * (h @ w): by default one kernel (axon_gemm_resid3,
+//               gemm.cu) that forms h while staging the GEMM's A operand;
+//               variants 1 / 2 run a row pass writing h, then the GEMM
 //   softmax_mm  e = exp(x), r = 1 / sum(e) (one row pass writing e), then
 //               y = r * (e @ w)
 //   attention   e = exp(q @ k_t) written by the first GEMM's epilogue, which
@@ -114,9 +116,16 @@ int default_block_n(int64_t n) { return n <= 64 ? 64 : n <= 128 ? 128 : 256; }
 
 using namespace axon;
 
-extern "C" int64_t axon_qkv_cte_workspace_bytes(int64_t m, int64_t k) {
-  if (m < 0 || k < 0) return fail(AXON_E_SHAPE, "axon_qkv_cte_workspace_bytes: negative size");
-  return round256(m * k * 2) + 4 * m;
+namespace axon {
+namespace {
+int64_t qkv_rowpass_bytes(int64_t m, int64_t k) { return round256(m * k * 2) + 4 * m; }
+}  // namespace
+}  // namespace axon
+
+extern "C" int64_t axon_qkv_cte_workspace_bytes(int64_t m, int64_t n, int64_t k, const axon_tune_t* tune) {
+  if (m < 0 || n < 0 || k < 0) return fail(AXON_E_SHAPE, "axon_qkv_cte_workspace_bytes: negative size");
+  if (tune_or_default(tune).variant == 0) return axon_gemm_resid3_workspace_bytes(m, n, k, tune);
+  return qkv_rowpass_bytes(m, k);
 }
 
 extern "C" int axon_qkv_cte(const void* x, const void* mlp_prev, const void* attention_prev, const void* w, void* y,
@@ -130,7 +139,12 @@ extern "C" int axon_qkv_cte(const void* x, const void* mlp_prev, const void* att
   if (!x || !mlp_prev || !attention_prev || !w || !y) return fail(AXON_E_ARG, "axon_qkv_cte: NULL tensor");
   if (!aligned16(x) || !aligned16(mlp_prev) || !aligned16(attention_prev))
     return fail(AXON_E_ALIGN, "axon_qkv_cte: inputs must be 16-byte aligned");
-  const int64_t need = axon_qkv_cte_workspace_bytes(m, k);
+  const axon_tune_t t = tune_or_default(tune);
+  if (t.variant == 0)
+    return axon_gemm_resid3(x, mlp_prev, attention_prev, w, y, workspace, workspace_bytes, m, n, k, ab_dtype, c_dtype,
+                            1e-6f, tune, stream);
+  if (t.variant != 1 && t.variant != 2) return fail(AXON_E_ARG, "axon_qkv_cte: variant must be 0, 1 or 2");
+  const int64_t need = qkv_rowpass_bytes(m, k);
   if (!workspace || workspace_bytes < need || !aligned16(workspace))
     return fail(AXON_E_ARG, "axon_qkv_cte: workspace of %lld bytes needed", (long long)need);
   void* h = workspace;

@@ -513,6 +513,330 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// ---- qkv_cte in one pass: the residual sum staged as the A operand ----------------
+//
+// C = rsqrt(sum_k h^2 / k + eps)[i] * (h @ B), h = x + r1 + r2 (the qkv_cte
+// spec's residual add, norm and projection), without h reaching global
+// memory. The three [m, k] inputs arrive by TMA into three buffers of a
+// stage with the same 128-byte swizzle, so their elementwise sum is formed
+// in place without undoing the swizzle: a transform group of 8 warps (two
+// threads per row of the 128-row tile, four 16-byte chunks each) adds them in
+// fp32 in the spec's order, writes h rounded to the operand type over the x
+// buffer, accumulates the row's sum of h^2 and hands the stage to the MMA
+// warp. A tile is up to 512 columns wide -- the whole fused QKV width of the
+// reference's cases -- as two MMAs per k-step (N = 256 and BN - 256) into
+// the 512 TMEM columns, so each row block's inputs are read and summed once.
+// When the row blocks cannot fill the GPU, k is split: each unit writes its
+// fp32 partial tile and partial sums of h^2, and resid3_reduce_kernel adds
+// the splits in a fixed order and applies the scale. Roles: warp 0 TMA,
+// warp 1 TMEM + MMA, warps 2..5 epilogue, warps 6..13 transform; every wait
+// is bounded.
+constexpr int kResidXformWarps = 8;
+constexpr int kResidThreads = (6 + kResidXformWarps) * 32;
+
+struct Resid3Params {
+  void* c;          // [m, ldc] output (splits == 1)
+  float* part;      // [splits][m][n] fp32 partial tiles (splits > 1)
+  float* ss_part;   // [splits][m] partial sums of h^2 (splits > 1)
+  int m, n, k;
+  int64_t ldc;
+  int stages;
+  uint32_t idesc_lo;  // N = min(BN, 256)
+  uint32_t idesc_hi;  // N = BN - 256 (BN > 256)
+  int splits;
+  int kb_per_split;
+  int raster;
+  float inv_k, eps;
+};
+
+template <typename T>
+__device__ __forceinline__ Vec<T> ld_smem16(const uint8_t* p) {
+  Vec<T> v;
+  v.u = *reinterpret_cast<const uint4*>(p);
+  return v;
+}
+
+template <int BN, typename TA, typename TC>
+__global__ void __launch_bounds__(kResidThreads, 1)
+    gemm_resid3(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmR1,
+                const __grid_constant__ CUtensorMap tmR2, const __grid_constant__ CUtensorMap tmB, Resid3Params p) {
+  constexpr int B_BYTES = BN * BK * 2;
+  constexpr int STAGE = 3 * A_BYTES + B_BYTES;
+  constexpr int NBUF = 2 * BN <= 512 ? 2 : 1;  // accumulator buffers in TMEM
+  constexpr uint32_t TMEM_COLS = 512;
+  constexpr int XT = kResidXformWarps * 32;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int S = p.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * STAGE);  // TMA landed
+  uint64_t* hready = full + S;                                      // h formed
+  uint64_t* empty = hready + S;                                     // MMAs retired
+  uint64_t* tfull = empty + S;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* rsfull = tempty + 2;
+  uint64_t* rsempty = rsfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rsempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* issued = reinterpret_cast<int*>(tmem_slot + 2);
+  int* consumed = issued + S;
+  float* rs = reinterpret_cast<float*>(smem + S * STAGE + 512);  // [2][BM] row scales
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_m = (p.m + BM - 1) / BM;
+  const int num_n = (p.n + BN - 1) / BN;
+  const int units = num_m * num_n * p.splits;
+  const int kblocks = (p.k + BK - 1) / BK;
+  auto unit_k = [&](int u, int& kb0, int& kb1) {
+    kb0 = (u % p.splits) * p.kb_per_split;
+    kb1 = kb0 + p.kb_per_split < kblocks ? kb0 + p.kb_per_split : kblocks;
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&hready[s], XT);
+      mbar_init(&empty[s], 1);
+      issued[s] = 0;
+      consumed[s] = 0;
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], EPI_THREADS);
+      mbar_init(&rsfull[b], XT);
+      mbar_init(&rsempty[b], EPI_THREADS);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer: x, r1, r2 slabs and the B slab ----------------
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+      int tm, tn, kb0, kb1;
+      tile_coords(u / p.splits, num_m, num_n, p.raster, tm, tn);
+      unit_k(u, kb0, kb1);
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) goto producer_done;
+        mbar_expect_tx(&full[stage], STAGE);
+        uint8_t* sx = smem + stage * STAGE;
+        tma_load_2d(&tmX, &full[stage], sx, kb * BK, tm * BM);
+        tma_load_2d(&tmR1, &full[stage], sx + A_BYTES, kb * BK, tm * BM);
+        tma_load_2d(&tmR2, &full[stage], sx + 2 * A_BYTES, kb * BK, tm * BM);
+        uint8_t* sb = sx + 3 * A_BYTES;
+#pragma unroll
+        for (int j = 0; j < BN / 64; ++j) tma_load_2d(&tmB, &full[stage], sb + j * B_CHUNK, tn * BN + j * 64, kb * BK);
+        issued[stage] += 1;
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  producer_done:;
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer: A = the h slab formed over x ----------------
+    int stage = 0;
+    uint32_t phase = 0;
+    int local = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
+      const int buf = local % NBUF;
+      const uint32_t use = static_cast<uint32_t>(local / NBUF);
+      if (!mbar_wait(&tempty[buf], (use & 1) ^ 1u, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t d = tmem_base + static_cast<uint32_t>(buf * BN);
+      int kb0, kb1;
+      unit_k(u, kb0, kb1);
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&hready[stage], phase, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + stage * STAGE);
+        const uint32_t sb = sa + 3 * A_BYTES;
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k) {
+          const uint64_t ad = sdesc(sa + k * 32, 16, 1024);
+          const uint32_t acc = (kb != kb0 || k != 0) ? 1u : 0u;
+          tc_mma(d, ad, sdesc(sb + k * 2048, B_CHUNK, 1024), p.idesc_lo, acc);
+          if constexpr (BN > 256)
+            tc_mma(d + 256, ad, sdesc(sb + 4 * B_CHUNK + k * 2048, B_CHUNK, 1024), p.idesc_hi, acc);
+        }
+        tc_commit(&empty[stage]);
+        consumed[stage] += 1;
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+      tc_commit(&tfull[buf]);
+    }
+  } else if (warp >= 2 && warp < 6) {
+    // ---------------- epilogue: C = rs[row] * acc, or the fp32 partial ----------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int local = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
+      int tm, tn;
+      tile_coords(u / p.splits, num_m, num_n, p.raster, tm, tn);
+      const int buf = local % NBUF;
+      const uint32_t use = static_cast<uint32_t>(local / NBUF);
+      if (!mbar_wait(&tfull[buf], use & 1, abort_flag)) break;
+      if (!mbar_wait(&rsfull[buf], use & 1, abort_flag)) break;
+      tc_fence_after();
+      const float scale = rs[buf * BM + q * 32 + lane];
+      mbar_arrive(&rsempty[buf]);
+      const int64_t row = static_cast<int64_t>(tm) * BM + q * 32 + lane;
+      const bool row_ok = row < p.m;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN);
+      const int64_t r = row_ok ? row : 0;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        __syncwarp();
+        tmem_ld32(tbase + c * 32, v);
+        tmem_wait_ld();
+        const int64_t col = static_cast<int64_t>(tn) * BN + c * 32;
+        if (p.splits == 1) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] *= scale;
+          if (row_ok && col < p.n) store32<TC>(static_cast<TC*>(p.c) + r * p.ldc + col, v, col, p.n);
+        } else if (row_ok && col < p.n) {
+          float* dst = p.part + (static_cast<int64_t>(u % p.splits) * p.m + r) * p.n + col;
+          store32<float>(dst, v, col, p.n);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[buf]);
+    }
+  } else if (warp >= 6) {
+    // ---------------- transform: h = (x + r1) + r2, row sums of h^2 ----------------
+    const int xt = threadIdx.x - 192;
+    const int row = xt >> 1, half = xt & 1;  // two threads per row, four chunks each
+    int stage = 0;
+    uint32_t phase = 0;
+    int local = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
+      int kb0, kb1;
+      unit_k(u, kb0, kb1);
+      const int buf = local % NBUF;
+      const uint32_t use = static_cast<uint32_t>(local / NBUF);
+      float ss = 0.f;
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&full[stage], phase, abort_flag)) {
+          ok = false;
+          break;
+        }
+        // the row's 128-byte line in each buffer (the swizzle permutes its
+        // 16-byte chunks alike in all three); chunk order rotated by the row
+        // so the eight threads of a shared-memory phase hit eight banks groups
+        uint8_t* lx = smem + stage * STAGE + row * 128;
+        Vec<TA> a[4], b[4], d[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int c = ((half * 4 + j + row) & 7) * 16;
+          a[j] = ld_smem16<TA>(lx + c);
+          b[j] = ld_smem16<TA>(lx + A_BYTES + c);
+          d[j] = ld_smem16<TA>(lx + 2 * A_BYTES + c);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int c = ((half * 4 + j + row) & 7) * 16;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float h = (to_f(a[j].e[e]) + to_f(b[j].e[e])) + to_f(d[j].e[e]);
+            ss = fmaf(h, h, ss);
+            a[j].e[e] = from_f<TA>(h);
+          }
+          *reinterpret_cast<uint4*>(lx + c) = a[j].u;
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // h -> the tensor cores' reads
+        mbar_arrive(&hready[stage]);
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (__any_sync(0xffffffffu, !ok)) break;  // warp-uniform exit before the shuffle
+      ss += __shfl_xor_sync(0xffffffffu, ss, 1);  // the row's two halves
+      if (!mbar_wait(&rsempty[buf], (use & 1) ^ 1u, abort_flag)) break;
+      if (half == 0) {
+        rs[buf * BM + row] = rsqrtf(ss * p.inv_k + p.eps);
+        if (p.splits > 1) {  // the split's partial sum, added up by the reduce pass
+          int tm, tn;
+          tile_coords(u / p.splits, num_m, num_n, p.raster, tm, tn);
+          const int64_t grow = static_cast<int64_t>(tm) * BM + row;
+          if (tn == 0 && grow < p.m) p.ss_part[static_cast<int64_t>(u % p.splits) * p.m + grow] = ss;
+        }
+      }
+      mbar_arrive(&rsfull[buf]);
+    }
+  }
+
+  __syncthreads();
+  if (threadIdx.x == 0 && *abort_flag) {
+    for (int s = 0; s < S; ++s) {
+      if (issued[s] > consumed[s]) {
+        volatile int never = 0;
+        mbar_wait(&full[s], static_cast<uint32_t>((issued[s] - 1) & 1), &never);
+      }
+    }
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// Split-k finish of gemm_resid3: c[i, j] = rsqrt(sum_s ss[s][i] / k + eps) *
+// sum_s part[s][i][j], splits added in order (deterministic). Four outputs
+// per thread; n a multiple of 8.
+template <typename TC>
+__global__ void __launch_bounds__(256) resid3_reduce_kernel(const float* __restrict__ part,
+                                                            const float* __restrict__ ss_part, TC* __restrict__ c,
+                                                            int64_t m, int64_t n, int64_t ldc, int splits, float inv_k,
+                                                            float eps) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  pdl_wait();
+  pdl_trigger();
+  const int64_t per_row = n / 4;
+  if (idx >= m * per_row) return;
+  const int64_t i = idx / per_row, j = (idx - i * per_row) * 4;
+  float ss = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int s = 0; s < splits; ++s) {
+    ss += ss_part[static_cast<int64_t>(s) * m + i];
+    const float4 v = *reinterpret_cast<const float4*>(part + (static_cast<int64_t>(s) * m + i) * n + j);
+    acc.x += v.x;
+    acc.y += v.y;
+    acc.z += v.z;
+    acc.w += v.w;
+  }
+  const float r = rsqrtf(ss * inv_k + eps);
+  TC* dst = c + i * ldc + j;
+  dst[0] = from_f<TC>(acc.x * r);
+  dst[1] = from_f<TC>(acc.y * r);
+  dst[2] = from_f<TC>(acc.z * r);
+  dst[3] = from_f<TC>(acc.w * r);
+}
+
 // ---- variant 2: CTA pairs (tcgen05 cta_group::2) ------------------------------------
 //
 // A cluster of two CTAs on two SMs computes a 256 x BN tile with one
@@ -1747,6 +2071,178 @@ int gemm_impl(const void* a, const void* b, const void* b2, void* c, const float
 
 }  // namespace
 }  // namespace axon
+
+namespace axon {
+namespace {
+
+// Tile width, k split and pipeline depth of gemm_resid3 for a shape.
+struct Resid3Plan {
+  int bn, splits, kb_per_split, stages;
+  int64_t ws_bytes;
+};
+
+int resid3_plan(int64_t m, int64_t n, int64_t k, const axon_tune_t& t, Resid3Plan& pl) {
+  int bn = t.block_n;
+  if (bn == 0) {
+    // the narrowest of 128 / 256 / 384 / 512 that covers n; wider outputs take
+    // the width that wastes the fewest columns, then the fewest tiles
+    bn = 512;
+    for (int c : {128, 256, 384, 512})
+      if (n <= c) {
+        bn = c;
+        break;
+      }
+    if (n > 512) {
+      int64_t best = -1;
+      for (int c : {512, 384, 256}) {
+        const int64_t cols = (n + c - 1) / c * c;
+        if (best < 0 || cols < best) {
+          best = cols;
+          bn = c;
+        }
+      }
+    }
+  }
+  if (bn != 128 && bn != 256 && bn != 384 && bn != 512)
+    return fail(AXON_E_ARG, "axon_gemm_resid3: block_n must be 128, 256, 384 or 512");
+  const int64_t stage_bytes = 3 * A_BYTES + static_cast<int64_t>(bn) * BK * 2;
+  int smax = static_cast<int>((232448 - 1024 - 512 - 2 * BM * 4) / stage_bytes);
+  if (smax > 4) smax = 4;
+  const int stages = t.stages > 0 ? t.stages : smax;
+  if (stages < 2 || stages > smax)
+    return fail(AXON_E_ARG, "axon_gemm_resid3: stages must be in [2, %d] for block_n %d", smax, bn);
+  const int64_t kblocks = (k + BK - 1) / BK;
+  const int64_t tiles = (m + BM - 1) / BM * ((n + bn - 1) / bn);
+  int64_t splits = t.split;
+  if (splits < 0) return fail(AXON_E_ARG, "axon_gemm_resid3: split (k splits) must be >= 0");
+  if (splits == 0) {
+    // split k only while the tiles leave SMs idle, keeping >= 8 k-blocks a split
+    splits = tiles >= sm_count() ? 1 : sm_count() / tiles;
+    if (splits > kblocks / 8) splits = kblocks / 8;
+    if (splits < 1) splits = 1;
+  }
+  if (splits > kblocks) splits = kblocks;
+  const int64_t kbps = (kblocks + splits - 1) / splits;
+  splits = (kblocks + kbps - 1) / kbps;  // no empty split
+  pl.bn = bn;
+  pl.splits = static_cast<int>(splits);
+  pl.kb_per_split = static_cast<int>(kbps);
+  pl.stages = stages;
+  pl.ws_bytes = splits > 1 ? (splits * m * n * 4 + 255) / 256 * 256 + splits * m * 4 : 0;
+  return AXON_OK;
+}
+
+template <int BN, typename TA, typename TC>
+int launch_resid3(const CUtensorMap& mx, const CUtensorMap& m1, const CUtensorMap& m2, const CUtensorMap& mb,
+                  const Resid3Params& rp, int64_t cap, cudaStream_t s) {
+  constexpr int STAGE = 3 * A_BYTES + BN * BK * 2;
+  const size_t smem = static_cast<size_t>(rp.stages) * STAGE + 1024 + 512 + 2 * BM * 4;
+  auto kern = gemm_resid3<BN, TA, TC>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return fail(AXON_E_LAUNCH, "axon_gemm_resid3: smem attribute: %s", cudaGetErrorString(e));
+  const int64_t units = static_cast<int64_t>((rp.m + BM - 1) / BM) * ((rp.n + BN - 1) / BN) * rp.splits;
+  const int grid = static_cast<int>(balanced_grid(units, cap));
+  kern<<<grid, kResidThreads, smem, s>>>(mx, m1, m2, mb, rp);
+  int rc = launch_status("axon_gemm_resid3");
+  if (rc || rp.splits == 1) return rc;
+  const int64_t packets = static_cast<int64_t>(rp.m) * (rp.n / 4);
+  launch_k(resid3_reduce_kernel<TC>, dim3(static_cast<unsigned>((packets + 255) / 256)), dim3(256), 0, s,
+           static_cast<const float*>(rp.part), static_cast<const float*>(rp.ss_part), static_cast<TC*>(rp.c),
+           static_cast<int64_t>(rp.m), static_cast<int64_t>(rp.n), rp.ldc, rp.splits, rp.inv_k, rp.eps);
+  return launch_status("axon_gemm_resid3");
+}
+
+template <int BN, typename TA>
+int dispatch_resid3(int32_t c_dtype, const CUtensorMap& mx, const CUtensorMap& m1, const CUtensorMap& m2,
+                    const CUtensorMap& mb, const Resid3Params& rp, int64_t cap, cudaStream_t s) {
+  switch (c_dtype) {
+    case AXON_BF16: return launch_resid3<BN, TA, __nv_bfloat16>(mx, m1, m2, mb, rp, cap, s);
+    case AXON_F16: return launch_resid3<BN, TA, __half>(mx, m1, m2, mb, rp, cap, s);
+    case AXON_F32: return launch_resid3<BN, TA, float>(mx, m1, m2, mb, rp, cap, s);
+    default: return fail(AXON_E_UNSUPPORTED, "axon_gemm_resid3: unsupported output dtype %d", c_dtype);
+  }
+}
+
+template <typename TA>
+int dispatch_resid3_bn(int bn, int32_t c_dtype, const CUtensorMap& mx, const CUtensorMap& m1, const CUtensorMap& m2,
+                       const CUtensorMap& mb, const Resid3Params& rp, int64_t cap, cudaStream_t s) {
+  switch (bn) {
+    case 128: return dispatch_resid3<128, TA>(c_dtype, mx, m1, m2, mb, rp, cap, s);
+    case 256: return dispatch_resid3<256, TA>(c_dtype, mx, m1, m2, mb, rp, cap, s);
+    case 384: return dispatch_resid3<384, TA>(c_dtype, mx, m1, m2, mb, rp, cap, s);
+    default: return dispatch_resid3<512, TA>(c_dtype, mx, m1, m2, mb, rp, cap, s);
+  }
+}
+
+uint32_t resid3_idesc(int32_t ab_dtype, int n) {
+  const uint32_t fmt = ab_dtype == AXON_BF16 ? 1u : 0u;
+  return (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 16) | (static_cast<uint32_t>(n >> 3) << 17) |
+         ((static_cast<uint32_t>(BM) >> 4) << 24);
+}
+
+}  // namespace
+}  // namespace axon
+
+extern "C" int64_t axon_gemm_resid3_workspace_bytes(int64_t m, int64_t n, int64_t k, const axon_tune_t* tune) {
+  if (m < 0 || n < 0 || k < 0) return fail(AXON_E_SHAPE, "axon_gemm_resid3_workspace_bytes: negative size");
+  if (m == 0 || n == 0 || k == 0) return 0;
+  Resid3Plan pl;
+  const int rc = resid3_plan(m, n, k, tune_or_default(tune), pl);
+  return rc ? rc : pl.ws_bytes;
+}
+
+extern "C" int axon_gemm_resid3(const void* x, const void* r1, const void* r2, const void* w, void* c,
+                                void* workspace, int64_t workspace_bytes, int64_t m, int64_t n, int64_t k,
+                                int32_t ab_dtype, int32_t c_dtype, float eps, const axon_tune_t* tune, void* stream) {
+  const axon_tune_t t = tune_or_default(tune);
+  if (m < 0 || n < 0 || k < 0) return fail(AXON_E_SHAPE, "axon_gemm_resid3: negative size");
+  if (m == 0 || n == 0) return AXON_OK;
+  if (!x || !r1 || !r2 || !w || !c) return fail(AXON_E_ARG, "axon_gemm_resid3: NULL operand");
+  if (ab_dtype != AXON_BF16 && ab_dtype != AXON_F16)
+    return fail(AXON_E_UNSUPPORTED, "axon_gemm_resid3: inputs must be bf16 or f16 (got %d)", ab_dtype);
+  if (m > 0x7fffffff || n > 0x7fffffff || k > 0x7fffffff || k == 0)
+    return fail(AXON_E_SHAPE, "axon_gemm_resid3: sizes out of range");
+  if (k % 8 || n % 8) return fail(AXON_E_SHAPE, "axon_gemm_resid3: k and n must be multiples of 8");
+  if (!aligned16(x) || !aligned16(r1) || !aligned16(r2) || !aligned16(w) || !aligned16(c))
+    return fail(AXON_E_ALIGN, "axon_gemm_resid3: operands must be 16-byte aligned");
+  if (t.max_ctas < 0) return fail(AXON_E_ARG, "axon_gemm_resid3: max_ctas must be >= 0");
+  Resid3Plan pl;
+  int rc = resid3_plan(m, n, k, t, pl);
+  if (rc) return rc;
+  if (pl.ws_bytes > 0 && (!workspace || workspace_bytes < pl.ws_bytes || !aligned16(workspace)))
+    return fail(AXON_E_ARG, "axon_gemm_resid3: %d k splits need a 16-byte aligned workspace of %lld bytes",
+                pl.splits, (long long)pl.ws_bytes);
+  CUtensorMap mx, m1, m2, mb;
+  rc = make_map(&mx, x, ab_dtype, k, m, k, BK, BM, "x");
+  if (!rc) rc = make_map(&m1, r1, ab_dtype, k, m, k, BK, BM, "r1");
+  if (!rc) rc = make_map(&m2, r2, ab_dtype, k, m, k, BK, BM, "r2");
+  if (!rc) rc = make_map(&mb, w, ab_dtype, n, k, n, 64, BK, "w");
+  if (rc) return rc;
+  Resid3Params rp{};
+  rp.c = c;
+  if (pl.splits > 1) {
+    rp.part = static_cast<float*>(workspace);
+    rp.ss_part = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) +
+                                          (static_cast<int64_t>(pl.splits) * m * n * 4 + 255) / 256 * 256);
+  }
+  rp.m = static_cast<int>(m);
+  rp.n = static_cast<int>(n);
+  rp.k = static_cast<int>(k);
+  rp.ldc = n;
+  rp.stages = pl.stages;
+  rp.idesc_lo = resid3_idesc(ab_dtype, pl.bn < 256 ? pl.bn : 256);
+  rp.idesc_hi = resid3_idesc(ab_dtype, pl.bn > 256 ? pl.bn - 256 : 256);
+  rp.splits = pl.splits;
+  rp.kb_per_split = pl.kb_per_split;
+  rp.raster = 1;  // a row block's column tiles side by side: its inputs come from L2 the second time
+  rp.inv_k = 1.0f / static_cast<float>(k);
+  rp.eps = eps;
+  int64_t cap = sm_count();
+  if (t.max_ctas > 0 && t.max_ctas < cap) cap = t.max_ctas;
+  cudaStream_t s = as_stream(stream);
+  return ab_dtype == AXON_BF16 ? dispatch_resid3_bn<__nv_bfloat16>(pl.bn, c_dtype, mx, m1, m2, mb, rp, cap, s)
+                               : dispatch_resid3_bn<__half>(pl.bn, c_dtype, mx, m1, m2, mb, rp, cap, s);
+}
 
 extern "C" int axon_gemm_exp(const void* a, const void* b, void* c, float* row_part, int64_t part_ld, int64_t m,
                              int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int32_t ab_dtype,

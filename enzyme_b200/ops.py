@@ -288,7 +288,9 @@ def gemm_exp(a, b, *, row_part=None, out=None, out_dtype=None, tune=None):
 
 
 def qkv_cte(x, mlp_prev, attention_prev, w, *, out=None, out_dtype=None, workspace=None, tune=None):
-    """(h / sqrt(mean(h^2) + 1e-6)) @ w with h = x + mlp_prev + attention_prev."""
+    """(h / sqrt(mean(h^2) + 1e-6)) @ w with h = x + mlp_prev + attention_prev:
+    one kernel by default (tune variant 0); variants 1 / 2 run a row pass and
+    the one-CTA / CTA-pair GEMM."""
     _require_cuda(x, mlp_prev, attention_prev, w)
     for t in (x, mlp_prev, attention_prev, w):
         if not t.is_contiguous():
@@ -298,10 +300,13 @@ def qkv_cte(x, mlp_prev, attention_prev, w, *, out=None, out_dtype=None, workspa
     if mlp_prev.shape != x.shape or attention_prev.shape != x.shape or w.shape[0] != k:
         raise N.AxonError(N.AXON_E_SHAPE, "qkv_cte: x, mlp_prev, attention_prev [m, k] and w [k, n]")
     y = out if out is not None else torch.empty((m, n), dtype=out_dtype or x.dtype, device=x.device)
-    nbytes = _check_ws_bytes(N.lib().axon_qkv_cte_workspace_bytes(m, k))
-    ws = _workspace(nbytes, x.device, workspace)
-    check(N.lib().axon_qkv_cte(_ptr(x), _ptr(mlp_prev), _ptr(attention_prev), _ptr(w), _ptr(y), _ptr(ws), ws.numel(),
-                               m, n, k, dtype_code(x), dtype_code(y), _tune(tune), _stream(x)))
+    ws = workspace
+    nbytes = _check_ws_bytes(N.lib().axon_qkv_cte_workspace_bytes(m, n, k, _tune(tune)))
+    if nbytes > 0:  # k-split partials (variant 0) or the staged h (variants 1, 2)
+        ws = _workspace(nbytes, x.device, workspace)
+    check(N.lib().axon_qkv_cte(_ptr(x), _ptr(mlp_prev), _ptr(attention_prev), _ptr(w), _ptr(y), _ptr(ws),
+                               ws.numel() if ws is not None else 0, m, n, k, dtype_code(x), dtype_code(y),
+                               _tune(tune), _stream(x)))
     return y
 
 

@@ -418,13 +418,34 @@ AXON_API int axon_gemm_exp(const void* a, const void* b, void* c, float* row_par
                   int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb, int64_t ldc,
                   int32_t ab_dtype, int32_t c_dtype, const axon_tune_t* tune, void* stream);
 
+/* C = rsqrt(sum_k h^2 / k + eps)[i] * (h @ w) with h = x + r1 + r2, in one
+ * kernel: the three [m, k] inputs (contiguous, bf16 or f16) are summed in
+ * fp32 while the A operand is staged in shared memory, the row sums of h^2
+ * accumulate beside it, and the scale is applied in the epilogue; h never
+ * reaches global memory. w [k, n] (row-major), C [m, n] contiguous (c_dtype).
+ * tune: block_n 128 / 256 / 384 / 512 (default: the narrowest covering n, so
+ * a row block's inputs are read once up to n = 512), stages, split = k
+ * splits (0: split while the tiles leave SMs idle; splits > 1 write fp32
+ * partials to the workspace and a second pass adds them in order and applies
+ * the scale), max_ctas. k and n multiples of 8. workspace:
+ * axon_gemm_resid3_workspace_bytes(m, n, k, tune) bytes (0 without splits). */
+AXON_API int64_t axon_gemm_resid3_workspace_bytes(int64_t m, int64_t n, int64_t k,
+                                         const axon_tune_t* tune);
+AXON_API int axon_gemm_resid3(const void* x, const void* r1, const void* r2, const void* w, void* c,
+                     void* workspace, int64_t workspace_bytes, int64_t m, int64_t n, int64_t k,
+                     int32_t ab_dtype, int32_t c_dtype, float eps, const axon_tune_t* tune,
+                     void* stream);
+
 /* qkv_cte (Axon kernels/qkv_cte/kernel.py:18-27; refs.py:23-36):
  * h = x + mlp_prev + attention_prev, y = (h / sqrt(mean(h^2) + 1e-6)) @ w.
  * x, mlp_prev, attention_prev [m, k] and w [k, n] contiguous, bf16 or f16;
- * y [m, n] (c_dtype). One row pass writes h (input dtype) and the per-row
- * scale; the GEMM applies the scale in its epilogue. k a multiple of 8.
- * workspace: axon_qkv_cte_workspace_bytes(m, k) bytes, 16-byte aligned. */
-AXON_API int64_t axon_qkv_cte_workspace_bytes(int64_t m, int64_t k);
+ * y [m, n] (c_dtype). tune->variant 0 (default): one kernel
+ * (axon_gemm_resid3, the other tune fields as there); 1 / 2: a row pass
+ * writes h (input dtype) and the per-row scale into the workspace and the
+ * GEMM (its variant 1 / 2) applies the scale in its epilogue. k a multiple
+ * of 8. workspace: axon_qkv_cte_workspace_bytes(m, n, k, tune) bytes,
+ * 16-byte aligned (may be 0 for variant 0). */
+AXON_API int64_t axon_qkv_cte_workspace_bytes(int64_t m, int64_t n, int64_t k, const axon_tune_t* tune);
 AXON_API int axon_qkv_cte(const void* x, const void* mlp_prev, const void* attention_prev,
                  const void* w, void* y, void* workspace, int64_t workspace_bytes, int64_t m,
                  int64_t n, int64_t k, int32_t ab_dtype, int32_t c_dtype,

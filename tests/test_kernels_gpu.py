@@ -127,7 +127,16 @@ def _spec_inputs(name, dims, dev):
     return ins, [_t(a, dev) for a in ins]
 
 
+# the one-kernel default at: split k with a 384-column tile (578 x 264), split
+# k at 512 columns, no split at 512 columns, two 384-column tiles, 128-column
+# tiles, explicit splits / CTA cap / stages; then the two-pass variants
 @pytest.mark.parametrize("dims,tune", [(dict(m=578, n=264, k=1408), None), (dict(m=1024, n=512, k=2048), None),
+                                       (dict(m=2048, n=512, k=1024), {"split": 1}),
+                                       (dict(m=300, n=640, k=520), None),
+                                       (dict(m=1024, n=512, k=2048), {"block_n": 128}),
+                                       (dict(m=1024, n=512, k=2048), {"split": 3, "max_ctas": 7}),
+                                       (dict(m=256, n=256, k=4096), {"stages": 2, "split": 5}),
+                                       (dict(m=578, n=264, k=1408), {"variant": 1}),
                                        (dict(m=1024, n=512, k=2048), {"variant": 1, "block_n": 128}),
                                        (dict(m=300, n=640, k=512), {"variant": 2})])
 def test_qkv_cte(dims, tune, cuda_device):
