@@ -517,20 +517,21 @@ __global__ void __launch_bounds__(192, 1)
 //
 // C = rsqrt(sum_k h^2 / k + eps)[i] * (h @ B), h = x + r1 + r2 (the qkv_cte
 // spec's residual add, norm and projection), without h reaching global
-// memory. The three [m, k] inputs arrive by TMA into three buffers of a
-// stage with the same 128-byte swizzle, so their elementwise sum is formed
-// in place without undoing the swizzle: a transform group of 8 warps (two
-// threads per row of the 128-row tile, four 16-byte chunks each) adds them in
-// fp32 in the spec's order, writes h rounded to the operand type over the x
-// buffer, accumulates the row's sum of h^2 and hands the stage to the MMA
-// warp. A tile is up to 512 columns wide -- the whole fused QKV width of the
-// reference's cases -- as two MMAs per k-step (N = 256 and BN - 256) into
-// the 512 TMEM columns, so each row block's inputs are read and summed once.
-// When the row blocks cannot fill the GPU, k is split: each unit writes its
-// fp32 partial tile and partial sums of h^2, and resid3_reduce_kernel adds
-// the splits in a fixed order and applies the scale. Roles: warp 0 TMA,
-// warp 1 TMEM + MMA, warps 2..5 epilogue, warps 6..13 transform; every wait
-// is bounded.
+// memory. A transform group of 8 warps is the A producer: per k-block each
+// thread loads its four 16-byte chunks of each input straight from global
+// memory (a warp's load covers four whole 128-byte row segments; two
+// k-blocks stay in flight in registers), adds them in fp32 in the spec's
+// order, accumulates the rows' sums of h^2 and writes h, rounded to the
+// operand type, into a ring of 128-byte-swizzled A slabs -- the layout TMA's
+// swizzle would produce -- for the MMA warp. TMA streams only B. A tile is up
+// to 512 columns wide -- the whole fused QKV width of the reference's
+// cases -- as two MMAs per k-step (N = 256 and BN - 256) into the 512 TMEM
+// columns, so each row block's inputs are read and summed once. When the
+// row blocks cannot fill the GPU, k is split: each unit writes its fp32
+// partial tile and partial sums of h^2, and resid3_reduce_kernel adds the
+// splits in a fixed order and applies the scale. Roles: warp 0 TMA, warp 1
+// TMEM + MMA, warps 2..5 epilogue, warps 6..13 transform; every wait is
+// bounded.
 constexpr int kResidXformWarps = 8;
 constexpr int kResidThreads = (6 + kResidXformWarps) * 32;
 
@@ -549,30 +550,78 @@ struct Resid3Params {
   float inv_k, eps;
 };
 
-template <typename T>
-__device__ __forceinline__ Vec<T> ld_smem16(const uint8_t* p) {
-  Vec<T> v;
-  v.u = *reinterpret_cast<const uint4*>(p);
-  return v;
+constexpr int kResidHSlots = 4;  // h ring depth (16 KB each)
+
+// One k-block of this transform thread's share of the three inputs: chunk
+// (t & 7) of rows (t >> 3) + 32 i, i < 4, so each load instruction of a warp
+// reads four whole 128-byte row segments. Rows past m and k-blocks past k
+// read as zero.
+template <typename TA>
+struct Resid3Regs {
+  uint4 x[4], r1[4], r2[4];
+};
+
+template <typename TA>
+__device__ __forceinline__ void resid3_load(Resid3Regs<TA>& g, const TA* x, const TA* r1, const TA* r2,
+                                            int64_t row0, int m, int k, int kb, int t) {
+  const int c = t & 7;
+  const int64_t col = static_cast<int64_t>(kb) * BK + c * 8;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t row = row0 + (t >> 3) + 32 * i;
+    if (row < m && col < k) {
+      const int64_t off = row * k + col;
+      g.x[i] = __ldcs(reinterpret_cast<const uint4*>(x + off));
+      g.r1[i] = __ldcs(reinterpret_cast<const uint4*>(r1 + off));
+      g.r2[i] = __ldcs(reinterpret_cast<const uint4*>(r2 + off));
+    } else {
+      g.x[i] = g.r1[i] = g.r2[i] = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+}
+
+// h = (x + r1) + r2 in fp32 into the 128-byte-swizzled A slab (chunk c of row
+// r at r * 128 + ((c ^ (r & 7)) * 16), the layout TMA's 128-byte swizzle
+// writes), and the rows' sums of h^2.
+template <typename TA>
+__device__ __forceinline__ void resid3_store(const Resid3Regs<TA>& g, uint8_t* slab, float* ss, int t) {
+  const int c = t & 7;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = (t >> 3) + 32 * i;
+    Vec<TA> a, b, d;
+    a.u = g.x[i];
+    b.u = g.r1[i];
+    d.u = g.r2[i];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float h = (to_f(a.e[e]) + to_f(b.e[e])) + to_f(d.e[e]);
+      ss[i] = fmaf(h, h, ss[i]);
+      a.e[e] = from_f<TA>(h);
+    }
+    *reinterpret_cast<uint4*>(slab + r * 128 + ((c ^ (r & 7)) * 16)) = a.u;
+  }
 }
 
 template <int BN, typename TA, typename TC>
 __global__ void __launch_bounds__(kResidThreads, 1)
-    gemm_resid3(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmR1,
-                const __grid_constant__ CUtensorMap tmR2, const __grid_constant__ CUtensorMap tmB, Resid3Params p) {
+    gemm_resid3(const TA* __restrict__ x, const TA* __restrict__ r1, const TA* __restrict__ r2,
+                const __grid_constant__ CUtensorMap tmB, Resid3Params p) {
   constexpr int B_BYTES = BN * BK * 2;
-  constexpr int STAGE = 3 * A_BYTES + B_BYTES;
   constexpr int NBUF = 2 * BN <= 512 ? 2 : 1;  // accumulator buffers in TMEM
   constexpr uint32_t TMEM_COLS = 512;
   constexpr int XT = kResidXformWarps * 32;
+  constexpr int H = kResidHSlots;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int S = p.stages;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * STAGE);  // TMA landed
-  uint64_t* hready = full + S;                                      // h formed
-  uint64_t* empty = hready + S;                                     // MMAs retired
-  uint64_t* tfull = empty + S;
+  const int S = p.stages;                                   // B ring depth
+  uint8_t* hbase = smem + S * B_BYTES;                      // h ring: H slabs of A_BYTES
+  uint64_t* bfull = reinterpret_cast<uint64_t*>(hbase + H * A_BYTES);
+  uint64_t* bempty = bfull + S;
+  uint64_t* hfull = bempty + S;
+  uint64_t* hempty = hfull + H;
+  uint64_t* tfull = hempty + H;
   uint64_t* tempty = tfull + 2;
   uint64_t* rsfull = tempty + 2;
   uint64_t* rsempty = rsfull + 2;
@@ -580,7 +629,7 @@ __global__ void __launch_bounds__(kResidThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* issued = reinterpret_cast<int*>(tmem_slot + 2);
   int* consumed = issued + S;
-  float* rs = reinterpret_cast<float*>(smem + S * STAGE + 512);  // [2][BM] row scales
+  float* rs = reinterpret_cast<float*>(hbase + H * A_BYTES + 512);  // [2][BM] row scales
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_m = (p.m + BM - 1) / BM;
@@ -594,11 +643,14 @@ __global__ void __launch_bounds__(kResidThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&hready[s], XT);
-      mbar_init(&empty[s], 1);
+      mbar_init(&bfull[s], 1);
+      mbar_init(&bempty[s], 1);
       issued[s] = 0;
       consumed[s] = 0;
+    }
+    for (int h = 0; h < H; ++h) {
+      mbar_init(&hfull[h], XT);
+      mbar_init(&hempty[h], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
@@ -622,7 +674,7 @@ __global__ void __launch_bounds__(kResidThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0 && lane == 0) {
-    // ---------------- TMA producer: x, r1, r2 slabs and the B slab ----------------
+    // ---------------- TMA producer: the B slabs ----------------
     int stage = 0;
     uint32_t phase = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
@@ -630,15 +682,12 @@ __global__ void __launch_bounds__(kResidThreads, 1)
       tile_coords(u / p.splits, num_m, num_n, p.raster, tm, tn);
       unit_k(u, kb0, kb1);
       for (int kb = kb0; kb < kb1; ++kb) {
-        if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) goto producer_done;
-        mbar_expect_tx(&full[stage], STAGE);
-        uint8_t* sx = smem + stage * STAGE;
-        tma_load_2d(&tmX, &full[stage], sx, kb * BK, tm * BM);
-        tma_load_2d(&tmR1, &full[stage], sx + A_BYTES, kb * BK, tm * BM);
-        tma_load_2d(&tmR2, &full[stage], sx + 2 * A_BYTES, kb * BK, tm * BM);
-        uint8_t* sb = sx + 3 * A_BYTES;
+        if (!mbar_wait(&bempty[stage], phase ^ 1u, abort_flag)) goto producer_done;
+        mbar_expect_tx(&bfull[stage], B_BYTES);
+        uint8_t* sb = smem + stage * B_BYTES;
 #pragma unroll
-        for (int j = 0; j < BN / 64; ++j) tma_load_2d(&tmB, &full[stage], sb + j * B_CHUNK, tn * BN + j * 64, kb * BK);
+        for (int j = 0; j < BN / 64; ++j)
+          tma_load_2d(&tmB, &bfull[stage], sb + j * B_CHUNK, tn * BN + j * 64, kb * BK);
         issued[stage] += 1;
         if (++stage == S) {
           stage = 0;
@@ -648,9 +697,9 @@ __global__ void __launch_bounds__(kResidThreads, 1)
     }
   producer_done:;
   } else if (warp == 1 && lane == 0) {
-    // ---------------- MMA issuer: A = the h slab formed over x ----------------
-    int stage = 0;
-    uint32_t phase = 0;
+    // ---------------- MMA issuer: A = an h slab, B = a B slab ----------------
+    int stage = 0, hs = 0;
+    uint32_t phase = 0, hphase = 0;
     int local = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
       const int buf = local % NBUF;
@@ -662,13 +711,13 @@ __global__ void __launch_bounds__(kResidThreads, 1)
       unit_k(u, kb0, kb1);
       bool ok = true;
       for (int kb = kb0; kb < kb1; ++kb) {
-        if (!mbar_wait(&hready[stage], phase, abort_flag)) {
+        if (!mbar_wait(&bfull[stage], phase, abort_flag) || !mbar_wait(&hfull[hs], hphase, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t sa = smem_u32(smem + stage * STAGE);
-        const uint32_t sb = sa + 3 * A_BYTES;
+        const uint32_t sa = smem_u32(hbase + hs * A_BYTES);
+        const uint32_t sb = smem_u32(smem + stage * B_BYTES);
 #pragma unroll
         for (int k = 0; k < BK / 16; ++k) {
           const uint64_t ad = sdesc(sa + k * 32, 16, 1024);
@@ -677,11 +726,16 @@ __global__ void __launch_bounds__(kResidThreads, 1)
           if constexpr (BN > 256)
             tc_mma(d + 256, ad, sdesc(sb + 4 * B_CHUNK + k * 2048, B_CHUNK, 1024), p.idesc_hi, acc);
         }
-        tc_commit(&empty[stage]);
+        tc_commit(&bempty[stage]);
+        tc_commit(&hempty[hs]);
         consumed[stage] += 1;
         if (++stage == S) {
           stage = 0;
           phase ^= 1u;
+        }
+        if (++hs == H) {
+          hs = 0;
+          hphase ^= 1u;
         }
       }
       if (!ok) break;
@@ -725,64 +779,65 @@ __global__ void __launch_bounds__(kResidThreads, 1)
       mbar_arrive(&tempty[buf]);
     }
   } else if (warp >= 6) {
-    // ---------------- transform: h = (x + r1) + r2, row sums of h^2 ----------------
-    const int xt = threadIdx.x - 192;
-    const int row = xt >> 1, half = xt & 1;  // two threads per row, four chunks each
-    int stage = 0;
-    uint32_t phase = 0;
+    // ---------------- transform: loads x, r1, r2, forms h into the h ring ----------------
+    const int t = threadIdx.x - 192;
+    int hs = 0;
+    uint32_t hphase = 0;
     int local = 0;
-    for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
-      int kb0, kb1;
+    bool ok = true;
+    // one k-block: wait for the slot, write h, hand it to the MMA warp
+    auto put = [&](const Resid3Regs<TA>& g, float* ss) {
+      if (!mbar_wait(&hempty[hs], hphase ^ 1u, abort_flag)) {
+        ok = false;
+        return;
+      }
+      resid3_store<TA>(g, hbase + hs * A_BYTES, ss, t);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // h -> the tensor cores' reads
+      mbar_arrive(&hfull[hs]);
+      if (++hs == H) {
+        hs = 0;
+        hphase ^= 1u;
+      }
+    };
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++local) {
+      int tm, tn, kb0, kb1;
+      tile_coords(u / p.splits, num_m, num_n, p.raster, tm, tn);
       unit_k(u, kb0, kb1);
+      const int64_t row0 = static_cast<int64_t>(tm) * BM;
       const int buf = local % NBUF;
       const uint32_t use = static_cast<uint32_t>(local / NBUF);
-      float ss = 0.f;
-      bool ok = true;
-      for (int kb = kb0; kb < kb1; ++kb) {
-        if (!mbar_wait(&full[stage], phase, abort_flag)) {
-          ok = false;
-          break;
-        }
-        // the row's 128-byte line in each buffer (the swizzle permutes its
-        // 16-byte chunks alike in all three); chunk order rotated by the row
-        // so the eight threads of a shared-memory phase hit eight banks groups
-        uint8_t* lx = smem + stage * STAGE + row * 128;
-        Vec<TA> a[4], b[4], d[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int c = ((half * 4 + j + row) & 7) * 16;
-          a[j] = ld_smem16<TA>(lx + c);
-          b[j] = ld_smem16<TA>(lx + A_BYTES + c);
-          d[j] = ld_smem16<TA>(lx + 2 * A_BYTES + c);
-        }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int c = ((half * 4 + j + row) & 7) * 16;
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float h = (to_f(a[j].e[e]) + to_f(b[j].e[e])) + to_f(d[j].e[e]);
-            ss = fmaf(h, h, ss);
-            a[j].e[e] = from_f<TA>(h);
-          }
-          *reinterpret_cast<uint4*>(lx + c) = a[j].u;
-        }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // h -> the tensor cores' reads
-        mbar_arrive(&hready[stage]);
-        if (++stage == S) {
-          stage = 0;
-          phase ^= 1u;
+      float ss[4] = {0.f, 0.f, 0.f, 0.f};
+      Resid3Regs<TA> g0, g1;  // two k-blocks in flight
+      resid3_load<TA>(g0, x, r1, r2, row0, p.m, p.k, kb0, t);
+      if (kb0 + 1 < kb1) resid3_load<TA>(g1, x, r1, r2, row0, p.m, p.k, kb0 + 1, t);
+      for (int kb = kb0; kb < kb1 && ok; kb += 2) {
+        put(g0, ss);
+        if (kb + 2 < kb1) resid3_load<TA>(g0, x, r1, r2, row0, p.m, p.k, kb + 2, t);
+        if (kb + 1 < kb1 && ok) {
+          put(g1, ss);
+          if (kb + 3 < kb1) resid3_load<TA>(g1, x, r1, r2, row0, p.m, p.k, kb + 3, t);
         }
       }
-      if (__any_sync(0xffffffffu, !ok)) break;  // warp-uniform exit before the shuffle
-      ss += __shfl_xor_sync(0xffffffffu, ss, 1);  // the row's two halves
+      if (__any_sync(0xffffffffu, !ok)) {  // warp-uniform exit before the shuffles
+        ok = false;
+        break;
+      }
+      // a row's eight chunks sit in eight consecutive lanes
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        ss[i] += __shfl_xor_sync(0xffffffffu, ss[i], 1);
+        ss[i] += __shfl_xor_sync(0xffffffffu, ss[i], 2);
+        ss[i] += __shfl_xor_sync(0xffffffffu, ss[i], 4);
+      }
       if (!mbar_wait(&rsempty[buf], (use & 1) ^ 1u, abort_flag)) break;
-      if (half == 0) {
-        rs[buf * BM + row] = rsqrtf(ss * p.inv_k + p.eps);
-        if (p.splits > 1) {  // the split's partial sum, added up by the reduce pass
-          int tm, tn;
-          tile_coords(u / p.splits, num_m, num_n, p.raster, tm, tn);
-          const int64_t grow = static_cast<int64_t>(tm) * BM + row;
-          if (tn == 0 && grow < p.m) p.ss_part[static_cast<int64_t>(u % p.splits) * p.m + grow] = ss;
+      if ((t & 7) == 0) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int row = (t >> 3) + 32 * i;
+          rs[buf * BM + row] = rsqrtf(ss[i] * p.inv_k + p.eps);
+          const int64_t grow = row0 + row;
+          // a split's partial sum, added up by the reduce pass
+          if (p.splits > 1 && tn == 0 && grow < p.m) p.ss_part[static_cast<int64_t>(u % p.splits) * p.m + grow] = ss[i];
         }
       }
       mbar_arrive(&rsfull[buf]);
@@ -794,7 +849,7 @@ __global__ void __launch_bounds__(kResidThreads, 1)
     for (int s = 0; s < S; ++s) {
       if (issued[s] > consumed[s]) {
         volatile int never = 0;
-        mbar_wait(&full[s], static_cast<uint32_t>((issued[s] - 1) & 1), &never);
+        mbar_wait(&bfull[s], static_cast<uint32_t>((issued[s] - 1) & 1), &never);
       }
     }
   }
@@ -2105,8 +2160,8 @@ int resid3_plan(int64_t m, int64_t n, int64_t k, const axon_tune_t& t, Resid3Pla
   }
   if (bn != 128 && bn != 256 && bn != 384 && bn != 512)
     return fail(AXON_E_ARG, "axon_gemm_resid3: block_n must be 128, 256, 384 or 512");
-  const int64_t stage_bytes = 3 * A_BYTES + static_cast<int64_t>(bn) * BK * 2;
-  int smax = static_cast<int>((232448 - 1024 - 512 - 2 * BM * 4) / stage_bytes);
+  const int64_t stage_bytes = static_cast<int64_t>(bn) * BK * 2;  // B slab; the h ring is fixed
+  int smax = static_cast<int>((232448 - 1024 - 512 - 2 * BM * 4 - kResidHSlots * A_BYTES) / stage_bytes);
   if (smax > 4) smax = 4;
   const int stages = t.stages > 0 ? t.stages : smax;
   if (stages < 2 || stages > smax)
@@ -2116,9 +2171,9 @@ int resid3_plan(int64_t m, int64_t n, int64_t k, const axon_tune_t& t, Resid3Pla
   int64_t splits = t.split;
   if (splits < 0) return fail(AXON_E_ARG, "axon_gemm_resid3: split (k splits) must be >= 0");
   if (splits == 0) {
-    // split k only while the tiles leave SMs idle, keeping >= 8 k-blocks a split
+    // split k only while the tiles leave SMs idle, keeping >= 4 k-blocks a split
     splits = tiles >= sm_count() ? 1 : sm_count() / tiles;
-    if (splits > kblocks / 8) splits = kblocks / 8;
+    if (splits > kblocks / 4) splits = kblocks / 4;
     if (splits < 1) splits = 1;
   }
   if (splits > kblocks) splits = kblocks;
@@ -2133,16 +2188,17 @@ int resid3_plan(int64_t m, int64_t n, int64_t k, const axon_tune_t& t, Resid3Pla
 }
 
 template <int BN, typename TA, typename TC>
-int launch_resid3(const CUtensorMap& mx, const CUtensorMap& m1, const CUtensorMap& m2, const CUtensorMap& mb,
-                  const Resid3Params& rp, int64_t cap, cudaStream_t s) {
-  constexpr int STAGE = 3 * A_BYTES + BN * BK * 2;
-  const size_t smem = static_cast<size_t>(rp.stages) * STAGE + 1024 + 512 + 2 * BM * 4;
+int launch_resid3(const void* x, const void* r1, const void* r2, const CUtensorMap& mb, const Resid3Params& rp,
+                  int64_t cap, cudaStream_t s) {
+  constexpr int STAGE = BN * BK * 2;
+  const size_t smem = static_cast<size_t>(rp.stages) * STAGE + kResidHSlots * A_BYTES + 1024 + 512 + 2 * BM * 4;
   auto kern = gemm_resid3<BN, TA, TC>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return fail(AXON_E_LAUNCH, "axon_gemm_resid3: smem attribute: %s", cudaGetErrorString(e));
   const int64_t units = static_cast<int64_t>((rp.m + BM - 1) / BM) * ((rp.n + BN - 1) / BN) * rp.splits;
   const int grid = static_cast<int>(balanced_grid(units, cap));
-  kern<<<grid, kResidThreads, smem, s>>>(mx, m1, m2, mb, rp);
+  kern<<<grid, kResidThreads, smem, s>>>(static_cast<const TA*>(x), static_cast<const TA*>(r1),
+                                         static_cast<const TA*>(r2), mb, rp);
   int rc = launch_status("axon_gemm_resid3");
   if (rc || rp.splits == 1) return rc;
   const int64_t packets = static_cast<int64_t>(rp.m) * (rp.n / 4);
@@ -2153,8 +2209,8 @@ int launch_resid3(const CUtensorMap& mx, const CUtensorMap& m1, const CUtensorMa
 }
 
 template <int BN, typename TA>
-int dispatch_resid3(int32_t c_dtype, const CUtensorMap& mx, const CUtensorMap& m1, const CUtensorMap& m2,
-                    const CUtensorMap& mb, const Resid3Params& rp, int64_t cap, cudaStream_t s) {
+int dispatch_resid3(int32_t c_dtype, const void* mx, const void* m1, const void* m2, const CUtensorMap& mb,
+                    const Resid3Params& rp, int64_t cap, cudaStream_t s) {
   switch (c_dtype) {
     case AXON_BF16: return launch_resid3<BN, TA, __nv_bfloat16>(mx, m1, m2, mb, rp, cap, s);
     case AXON_F16: return launch_resid3<BN, TA, __half>(mx, m1, m2, mb, rp, cap, s);
@@ -2164,7 +2220,7 @@ int dispatch_resid3(int32_t c_dtype, const CUtensorMap& mx, const CUtensorMap& m
 }
 
 template <typename TA>
-int dispatch_resid3_bn(int bn, int32_t c_dtype, const CUtensorMap& mx, const CUtensorMap& m1, const CUtensorMap& m2,
+int dispatch_resid3_bn(int bn, int32_t c_dtype, const void* mx, const void* m1, const void* m2,
                        const CUtensorMap& mb, const Resid3Params& rp, int64_t cap, cudaStream_t s) {
   switch (bn) {
     case 128: return dispatch_resid3<128, TA>(c_dtype, mx, m1, m2, mb, rp, cap, s);
@@ -2212,11 +2268,8 @@ extern "C" int axon_gemm_resid3(const void* x, const void* r1, const void* r2, c
   if (pl.ws_bytes > 0 && (!workspace || workspace_bytes < pl.ws_bytes || !aligned16(workspace)))
     return fail(AXON_E_ARG, "axon_gemm_resid3: %d k splits need a 16-byte aligned workspace of %lld bytes",
                 pl.splits, (long long)pl.ws_bytes);
-  CUtensorMap mx, m1, m2, mb;
-  rc = make_map(&mx, x, ab_dtype, k, m, k, BK, BM, "x");
-  if (!rc) rc = make_map(&m1, r1, ab_dtype, k, m, k, BK, BM, "r1");
-  if (!rc) rc = make_map(&m2, r2, ab_dtype, k, m, k, BK, BM, "r2");
-  if (!rc) rc = make_map(&mb, w, ab_dtype, n, k, n, 64, BK, "w");
+  CUtensorMap mb;
+  rc = make_map(&mb, w, ab_dtype, n, k, n, 64, BK, "w");
   if (rc) return rc;
   Resid3Params rp{};
   rp.c = c;
@@ -2240,8 +2293,8 @@ extern "C" int axon_gemm_resid3(const void* x, const void* r1, const void* r2, c
   int64_t cap = sm_count();
   if (t.max_ctas > 0 && t.max_ctas < cap) cap = t.max_ctas;
   cudaStream_t s = as_stream(stream);
-  return ab_dtype == AXON_BF16 ? dispatch_resid3_bn<__nv_bfloat16>(pl.bn, c_dtype, mx, m1, m2, mb, rp, cap, s)
-                               : dispatch_resid3_bn<__half>(pl.bn, c_dtype, mx, m1, m2, mb, rp, cap, s);
+  return ab_dtype == AXON_BF16 ? dispatch_resid3_bn<__nv_bfloat16>(pl.bn, c_dtype, x, r1, r2, mb, rp, cap, s)
+                               : dispatch_resid3_bn<__half>(pl.bn, c_dtype, x, r1, r2, mb, rp, cap, s);
 }
 
 extern "C" int axon_gemm_exp(const void* a, const void* b, void* c, float* row_part, int64_t part_ld, int64_t m,
