@@ -4,8 +4,10 @@
 
 One JSON line on rank 0. The headline workload is the rope config (Llama-3-8B
 GQA rotary embedding); the other BASELINE configs
-(rmsnorm, nucleus cumsum, 1e9-parameter Adam, SwiGLU MLP) are measured in the
-same run and reported under "workloads" unless --no-extra is given.
+(rmsnorm, nucleus cumsum, 1e9-parameter Adam, SwiGLU MLP) and the GEMM-backed
+neighbour specs at reference eval cases (qkv_cte, softmax_mm, attention_nkilib)
+are measured in the same run and reported under "workloads" unless --no-extra
+is given.
 
 A step is one pass of the hot path over one batch of synthetic input: one
 launch of the config's kernel (two tcgen05 GEMMs for the SwiGLU MLP). Timing:
@@ -40,6 +42,7 @@ import torch.distributed as dist
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
+from enzyme_b200 import _native as N  # noqa: E402
 from enzyme_b200 import ops, roofline, timing  # noqa: E402
 
 THETA = 500000.0
@@ -410,7 +413,160 @@ class SwiGLU(Workload):
                 "parallelism": par}
 
 
-WORKLOADS = {"rope": Rope, "rmsnorm": RmsNorm, "cumsum": Cumsum, "fused_adam": Adam, "silu_mlp": SwiGLU}
+class QkvCte(Workload):
+    """qkv_cte at its eval/sizes.json llama70b case: residual add, norm and
+    fused QKV projection in one kernel; HBM-bound (the three inputs)."""
+
+    name, spec = "qkv_cte", "qkv_cte"
+    M, N, K = 16384, 512, 8192
+
+    def __init__(self, dev, rank, world):
+        super().__init__(dev, rank, world)
+        m, n, k = self.M, self.N, self.K
+        self.dims = dict(m=m, n=n, k=k)
+        self.nsets = 1  # 830 MB per step: well past L2 with one set
+        self.ins = [torch.randn(m, k, device=dev, generator=self.gen).to(torch.bfloat16) for _ in range(3)]
+        self.w = (torch.randn(k, n, device=dev, generator=self.gen) / k ** 0.5).to(torch.bfloat16)
+        self.y = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+        nbytes = int(N.lib().axon_qkv_cte_workspace_bytes(m, n, k, None))
+        self.ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=dev)
+
+    def launch(self, i):
+        ops.qkv_cte(*self.ins, self.w, out=self.y, workspace=self.ws)
+
+    def e2e_setup(self):
+        self.h = [t.cpu().pin_memory() for t in (*self.ins, self.w)]
+        self.ho = torch.empty(self.y.shape, dtype=self.y.dtype).pin_memory()
+        self.h2d = sum(t.numel() * t.element_size() for t in self.h)
+        self.d2h = self.ho.numel() * 2
+
+    def e2e_step(self, i):
+        for d, h in zip((*self.ins, self.w), self.h):
+            d.copy_(h, non_blocking=True)
+        self.launch(i)
+        self.ho.copy_(self.y, non_blocking=True)
+
+    def cpu_step(self):
+        from oracle import cpu_torch
+
+        rows = 256
+        if not hasattr(self, "_cpu"):
+            g = torch.Generator().manual_seed(1)
+            self._cpu = [torch.randn(rows, self.K, generator=g) for _ in range(3)] + \
+                [torch.randn(self.K, self.N, generator=g) / self.K ** 0.5]
+        cpu_torch.qkv_cte(*self._cpu)
+        return self.per_step_work() * rows / self.M, f"{rows} of {self.M} rows (fp32 torch_ref)"
+
+    def config(self):
+        return {"workload": "qkv_cte llama70b (eval/sizes.json): m 16384, n 512, k 8192 bf16, one kernel",
+                "l2": "inputs 805 MB >> L2"}
+
+
+class SoftmaxMM(Workload):
+    """softmax_mm at 4096^3: exp row pass, then the row-scaled GEMM."""
+
+    name, spec = "softmax_mm", "softmax_mm"
+    kind = "tensor"
+    launches_per_step = 2
+    M = N = K = 4096
+
+    def __init__(self, dev, rank, world):
+        super().__init__(dev, rank, world)
+        m, n, k = self.M, self.N, self.K
+        self.dims = dict(m=m, n=n, k=k)
+        self.nsets = 2  # 2 x 128 MB (x, w, exp(x), y) rotate past L2
+        self.sets = []
+        for _ in range(self.nsets):
+            x = torch.randn(m, k, device=dev, generator=self.gen).to(torch.bfloat16)
+            w = torch.randn(k, n, device=dev, generator=self.gen).to(torch.bfloat16)
+            ws = torch.empty(int(N.lib().axon_softmax_mm_workspace_bytes(m, k)), dtype=torch.uint8, device=dev)
+            self.sets.append((x, w, torch.empty(m, n, dtype=torch.bfloat16, device=dev), ws))
+
+    def launch(self, i):
+        x, w, y, ws = self.sets[i % self.nsets]
+        ops.softmax_mm(x, w, out=y, workspace=ws)
+
+    def e2e_setup(self):
+        x, w, y, _ = self.sets[0]
+        self.h = [x.cpu().pin_memory(), w.cpu().pin_memory()]
+        self.ho = torch.empty(y.shape, dtype=y.dtype).pin_memory()
+        self.h2d = sum(t.numel() * 2 for t in self.h)
+        self.d2h = self.ho.numel() * 2
+
+    def e2e_step(self, i):
+        x, w, y, ws = self.sets[i % self.nsets]
+        x.copy_(self.h[0], non_blocking=True)
+        w.copy_(self.h[1], non_blocking=True)
+        ops.softmax_mm(x, w, out=y, workspace=ws)
+        self.ho.copy_(y, non_blocking=True)
+
+    def cpu_step(self):
+        from oracle import cpu_torch
+
+        rows = 256
+        if not hasattr(self, "_cpu"):
+            g = torch.Generator().manual_seed(1)
+            self._cpu = (torch.randn(rows, self.K, generator=g), torch.randn(self.K, self.N, generator=g))
+        cpu_torch.softmax_mm(*self._cpu)
+        return self.per_step_work() * rows / self.M, f"{rows} of {self.M} rows (fp32 baseline_op in torch)"
+
+    def config(self):
+        return {"workload": "softmax_mm: m = n = k = 4096 bf16 (exp row pass + row-scaled tcgen05 GEMM)",
+                "rotating_sets": self.nsets, "l2": "inputs rotate over 256 MB > 2 x L2"}
+
+
+class Attention(Workload):
+    """attention_nkilib at its s8k_d128 case (eval/sizes.json)."""
+
+    name, spec = "attention", "attention_nkilib"
+    kind = "tensor"
+    launches_per_step = 3
+    S, D = 8192, 128
+
+    def __init__(self, dev, rank, world):
+        super().__init__(dev, rank, world)
+        s, d = self.S, self.D
+        self.dims = dict(s=s, d=d)
+        self.nsets = 1
+        self.q = torch.rand(s, d, device=dev, generator=self.gen).to(torch.bfloat16)
+        self.kt = torch.rand(d, s, device=dev, generator=self.gen).to(torch.bfloat16)
+        self.v = torch.rand(s, d, device=dev, generator=self.gen).to(torch.bfloat16)
+        self.y = torch.empty(s, d, dtype=torch.bfloat16, device=dev)
+        self.ws = torch.empty(int(N.lib().axon_attention_workspace_bytes(s, d)), dtype=torch.uint8, device=dev)
+
+    def launch(self, i):
+        ops.attention(self.q, self.kt, self.v, out=self.y, workspace=self.ws)
+
+    def e2e_setup(self):
+        self.h = [t.cpu().pin_memory() for t in (self.q, self.kt, self.v)]
+        self.ho = torch.empty(self.y.shape, dtype=self.y.dtype).pin_memory()
+        self.h2d = sum(t.numel() * 2 for t in self.h)
+        self.d2h = self.ho.numel() * 2
+
+    def e2e_step(self, i):
+        for d, h in zip((self.q, self.kt, self.v), self.h):
+            d.copy_(h, non_blocking=True)
+        self.launch(i)
+        self.ho.copy_(self.y, non_blocking=True)
+
+    def cpu_step(self):
+        from oracle import cpu_torch
+
+        rows = 256
+        if not hasattr(self, "_cpu"):
+            g = torch.Generator().manual_seed(1)
+            self._cpu = (torch.rand(rows, self.D, generator=g), torch.rand(self.D, self.S, generator=g),
+                         torch.rand(self.S, self.D, generator=g))
+        cpu_torch.attention(*self._cpu)
+        return self.per_step_work() * rows / self.S, f"{rows} of {self.S} query rows (fp32 torch_ref)"
+
+    def config(self):
+        return {"workload": "attention_nkilib s8k_d128 (eval/sizes.json): s 8192, d 128 bf16, uniform [0, 1)",
+                "l2": "each step writes and re-reads the 134 MB score matrix (> L2), which evicts the rest"}
+
+
+WORKLOADS = {"rope": Rope, "rmsnorm": RmsNorm, "cumsum": Cumsum, "fused_adam": Adam, "silu_mlp": SwiGLU,
+             "qkv_cte": QkvCte, "softmax_mm": SoftmaxMM, "attention": Attention}
 
 
 # ---------------------------------------------------------------------------------
@@ -639,7 +795,7 @@ def main():
         for name in WORKLOADS:
             if name == args.workload:
                 continue
-            w, r = run_workload(name, dev, rank, world, max(3, min(args.steps, 20 if name in ("fused_adam", "silu_mlp") else args.steps)),
+            w, r = run_workload(name, dev, rank, world, max(3, min(args.steps, 20 if name in ("fused_adam", "silu_mlp", "qkv_cte", "softmax_mm", "attention") else args.steps)),
                                 args.warmup, None, with_e2e=False)
             extra[name] = {k: r[k] for k in ("metric", "value", "unit", "ms_per_step", "roofline", "scaling",
                                              "gpu_launches")}
@@ -678,6 +834,10 @@ def _prepare_cpu_only(w):
     elif name == "SwiGLU":
         w.dims = dict(m=4096, n=14336, k=4096, p=4096)
         w.shard = 14336
+    elif name in ("QkvCte", "SoftmaxMM"):
+        w.dims = dict(m=w.M, n=w.N, k=w.K)
+    elif name == "Attention":
+        w.dims = dict(s=w.S, d=w.D)
 
 
 if __name__ == "__main__":

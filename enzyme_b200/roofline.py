@@ -54,8 +54,13 @@ def work(spec: str, dims: dict, itemsize: int = 2) -> tuple[str, float]:
         return "hbm", 7 * d["p"] * d["f"] * itemsize + 3 * d["p"] * itemsize
     if spec == "fused_adam_cfg":
         return "hbm", 26 * d["p"] * d["f"] + 3 * 4 * d["p"]
-    if spec in ("matmul", "rmsnorm_matmul", "qkv_cte", "softmax_mm"):
+    if spec in ("matmul", "rmsnorm_matmul", "softmax_mm"):
         return "tensor", 2.0 * d["m"] * d["n"] * d["k"]
+    if spec == "qkv_cte":
+        # three [m, k] inputs read, w read, y written: HBM-bound at the
+        # reference's shapes (n = 512: 2n/6 ~ 170 FLOP per byte, below B200's
+        # ridge of ~250)
+        return "hbm", (3 * d["m"] * d["k"] + d["k"] * d["n"] + d["m"] * d["n"]) * itemsize
     if spec == "attention_nkilib":
         return "tensor", 4.0 * d["s"] * d["s"] * d["d"]
     if spec in ("silu_mlp", "silu_mlp_swiglu"):

@@ -50,3 +50,18 @@ def adam(p, g, m, v, step_size, inv_bc2_sqrt, wd, beta1=0.9, beta2=0.999, eps=1e
 
 def silu_mlp(x, w1, w2, w3):
     return (torch.nn.functional.silu(x @ w1) * (x @ w2)) @ w3
+
+
+def qkv_cte(x, mlp_prev, attention_prev, w, eps=1e-6):
+    h = x + mlp_prev + attention_prev
+    return (h / torch.sqrt(torch.mean(h * h, dim=1, keepdim=True) + eps)) @ w
+
+
+def softmax_mm(x, w):
+    e = torch.exp(x)
+    return (e / torch.sum(e, dim=1, keepdim=True)) @ w
+
+
+def attention(q, k_t, v):
+    e = torch.exp(q @ k_t)
+    return (e / torch.sum(e, dim=1, keepdim=True)) @ v
