@@ -520,7 +520,7 @@ class Attention(Workload):
 
     name, spec = "attention", "attention_nkilib"
     kind = "tensor"
-    launches_per_step = 3
+    launches_per_step = 2  # the fused kernel and its split-key reduce
     S, D = 8192, 128
 
     def __init__(self, dev, rank, world):
@@ -532,7 +532,8 @@ class Attention(Workload):
         self.kt = torch.rand(d, s, device=dev, generator=self.gen).to(torch.bfloat16)
         self.v = torch.rand(s, d, device=dev, generator=self.gen).to(torch.bfloat16)
         self.y = torch.empty(s, d, dtype=torch.bfloat16, device=dev)
-        self.ws = torch.empty(int(N.lib().axon_attention_workspace_bytes(s, d)), dtype=torch.uint8, device=dev)
+        nbytes = int(N.lib().axon_attention_workspace_bytes(s, d, None))
+        self.ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=dev)
 
     def launch(self, i):
         ops.attention(self.q, self.kt, self.v, out=self.y, workspace=self.ws)
@@ -561,8 +562,9 @@ class Attention(Workload):
         return self.per_step_work() * rows / self.S, f"{rows} of {self.S} query rows (fp32 torch_ref)"
 
     def config(self):
-        return {"workload": "attention_nkilib s8k_d128 (eval/sizes.json): s 8192, d 128 bf16, uniform [0, 1)",
-                "l2": "each step writes and re-reads the 134 MB score matrix (> L2), which evicts the rest"}
+        return {"workload": "attention_nkilib s8k_d128 (eval/sizes.json): s 8192, d 128 bf16, uniform [0, 1), "
+                            "one kernel (scores stay on chip)",
+                "l2": "q, k_t, v (6 MB) stay L2-resident across steps: the kernel is tensor-bound, not HBM-bound"}
 
 
 WORKLOADS = {"rope": Rope, "rmsnorm": RmsNorm, "cumsum": Cumsum, "fused_adam": Adam, "silu_mlp": SwiGLU,

@@ -133,7 +133,9 @@ SIGNATURES: dict[str, tuple] = {
     "axon_qkv_cte": (_I32, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I32, _I32, _TUNE, _P]),
     "axon_softmax_mm_workspace_bytes": (_I64, [_I64, _I64]),
     "axon_softmax_mm": (_I32, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I32, _I32, _TUNE, _P]),
-    "axon_attention_workspace_bytes": (_I64, [_I64, _I64]),
+    "axon_attention_workspace_bytes": (_I64, [_I64, _I64, _TUNE]),
+    "axon_attention_fused_workspace_bytes": (_I64, [_I64, _I64, _TUNE]),
+    "axon_attention_fused": (_I32, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I32, _I32, _TUNE, _P]),
     "axon_attention": (_I32, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I32, _I32, _TUNE, _P]),
     "axon_silu_mlp_workspace_bytes": (_I64, [_I64, _I64, _I64, _I32, _TUNE]),
     "axon_ipc_handle": (_I32, [_P, _P, ctypes.POINTER(_I64)]),

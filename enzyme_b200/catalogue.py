@@ -82,9 +82,9 @@ def variants(spec_name: str) -> list[Variant]:
         # hw_variant i runs axon_gemm variant i + 1 (0 is the library's auto pick)
         return [Variant(0, "tcgen05_ws_persistent"), Variant(1, "tcgen05_cta_pair")]
     if spec_name in ATTN_SPECS:
-        # both GEMMs at the library's pick (pairs from 256 rows); the exp GEMM's
-        # column tile is the knob
-        return [Variant(0, "tcgen05_exp_rowsum")]
+        # 0: one kernel, scores in TMEM / shared memory (head dim 64, 128);
+        # 1: exp GEMM with row sums + row-scaled GEMM (its column tile is the knob)
+        return [Variant(0, "tcgen05_fused_attention"), Variant(1, "tcgen05_exp_rowsum")]
     if spec_name in QKV_SPECS:
         # 0: residual sum formed while staging the GEMM operand (one kernel);
         # 1 / 2: a row pass writing h, then the one-CTA / CTA-pair GEMM
@@ -160,6 +160,9 @@ def constraints(spec_name: str, hw_variant: int, dims: dict, itemsize: int,
         out.append(TileConstraint(args[1], extent=256, tile_size=64, require_divisible=True,
                                   allowed=(2, 4) if hw_variant != 1 else (1, 2, 4)))
         out.append(TileConstraint(args[2], extent=8, tile_size=1, require_divisible=True, allowed=(2, 4)))
+    elif spec_name in ATTN_SPECS and hw_variant == 0:
+        for a in args:  # the fused kernel's tiles are fixed (128 queries x 128 keys)
+            out.append(_one(a))
     elif spec_name in ATTN_SPECS:
         # N -> column tile of the exp GEMM (64 * v); K -> stages; M, P fixed
         out.append(_one(args[0]))
@@ -191,8 +194,10 @@ def tune_for(spec_name: str, hw_variant: int, tiles: dict[str, int]) -> dict | l
         bn = 64 * t["N"]
         return {"variant": hw_variant + 1, "block_n": bn, "stages": min(t["K"], gemm_max_stages(hw_variant == 1, bn))}
     if spec_name in ATTN_SPECS:
+        if hw_variant == 0:
+            return {"variant": 0}
         bn = 64 * t["N"]
-        return {"block_n": bn, "stages": min(t["K"], gemm_max_stages(False, bn))}
+        return {"variant": 1, "block_n": bn, "stages": min(t["K"], gemm_max_stages(False, bn))}
     if spec_name in QKV_SPECS:
         bn = 64 * t["N"]
         if hw_variant == 0:  # stages of x, r1, r2 and the B slab

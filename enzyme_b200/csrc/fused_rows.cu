@@ -9,7 +9,9 @@
 //               variants 1 / 2 run a row pass writing h, then the GEMM
 //   softmax_mm  e = exp(x), r = 1 / sum(e) (one row pass writing e), then
 //               y = r * (e @ w)
-//   attention   e = exp(q @ k_t) written by the first GEMM's epilogue, which
+//   attention   by default (head dim 64 or 128) one kernel that keeps the
+//               scores on chip (axon_attention_fused, gemm.cu); variant 1:
+//               e = exp(q @ k_t) written by the first GEMM's epilogue, which
 //               also leaves each row's sum per 256-column tile; r = 1 / sum
 //               of those (a tiny pass over s x tiles floats), then
 //               y = r * (e @ v)
@@ -181,10 +183,21 @@ extern "C" int axon_softmax_mm(const void* x, const void* w, void* y, void* work
   return axon_gemm(e, w, nullptr, y, r, m, n, k, k, n, n, ab_dtype, c_dtype, AXON_EPI_ROWSCALE, tune, stream);
 }
 
-extern "C" int64_t axon_attention_workspace_bytes(int64_t s, int64_t d) {
-  if (s < 0 || d < 0) return fail(AXON_E_SHAPE, "axon_attention_workspace_bytes: negative size");
+namespace axon {
+namespace {
+// scores [s, s], per-tile row sums, 1 / row sums: the two-GEMM form
+int64_t attention_composed_bytes(int64_t s) {
   const int64_t tiles = (s + 63) / 64;  // the most column tiles the first GEMM can use
   return round256(s * s * 2) + round256(tiles * s * 4) + 4 * s;
+}
+bool attention_fused_ok(int64_t d, const axon_tune_t& t) { return t.variant == 0 && (d == 64 || d == 128); }
+}  // namespace
+}  // namespace axon
+
+extern "C" int64_t axon_attention_workspace_bytes(int64_t s, int64_t d, const axon_tune_t* tune) {
+  if (s < 0 || d < 0) return fail(AXON_E_SHAPE, "axon_attention_workspace_bytes: negative size");
+  if (attention_fused_ok(d, tune_or_default(tune))) return axon_attention_fused_workspace_bytes(s, d, tune);
+  return attention_composed_bytes(s);
 }
 
 extern "C" int axon_attention(const void* q, const void* k_t, const void* v, void* y, void* workspace,
@@ -196,12 +209,16 @@ extern "C" int axon_attention(const void* q, const void* k_t, const void* v, voi
   if (s == 0 || d == 0) return AXON_OK;
   if (s % 8 || d % 8) return fail(AXON_E_SHAPE, "axon_attention: s and d must be multiples of 8");
   if (!q || !k_t || !v || !y) return fail(AXON_E_ARG, "axon_attention: NULL tensor");
-  const int64_t need = axon_attention_workspace_bytes(s, d);
+  const axon_tune_t t = tune_or_default(tune);
+  if (t.variant != 0 && t.variant != 1) return fail(AXON_E_ARG, "axon_attention: variant must be 0 or 1");
+  if (attention_fused_ok(d, t))
+    return axon_attention_fused(q, k_t, v, y, workspace, workspace_bytes, s, d, ab_dtype, c_dtype, tune, stream);
+  const int64_t need = attention_composed_bytes(s);
   if (!workspace || workspace_bytes < need || !aligned16(workspace))
     return fail(AXON_E_ARG, "axon_attention: workspace of %lld bytes needed", (long long)need);
-  const axon_tune_t t = tune_or_default(tune);
   // scores: e = exp(q @ k_t) [s, s], row sums per column tile of the first GEMM
   axon_tune_t t1 = t;
+  t1.variant = 0;  // the GEMMs' own automatic choice
   if (t1.block_n == 0) t1.block_n = default_block_n(s);
   if (t1.block_n != 64 && t1.block_n != 128 && t1.block_n != 256)
     return fail(AXON_E_ARG, "axon_attention: block_n must be 64, 128 or 256");
@@ -219,6 +236,7 @@ extern "C" int axon_attention(const void* q, const void* k_t, const void* v, voi
   if (rc) return rc;
   // output: y = r * (e @ v), the second GEMM with its own default tile
   axon_tune_t t2 = t;
+  t2.variant = 0;
   t2.block_n = 0;
   return axon_gemm(e, v, nullptr, y, r, s, d, s, s, d, d, ab_dtype, c_dtype, AXON_EPI_ROWSCALE, &t2, stream);
 }

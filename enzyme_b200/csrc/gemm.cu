@@ -892,6 +892,409 @@ __global__ void __launch_bounds__(256) resid3_reduce_kernel(const float* __restr
   dst[3] = from_f<TC>(acc.w * r);
 }
 
+// ---- attention_nkilib in one kernel: softmax(q @ k_t) @ v, bare exponential ----------
+//
+// The spec's softmax has no max shift, so no running maximum and no
+// rescaling are needed: P = exp(S) feeds the second product directly and the
+// row sums add up. One CTA (576 threads) owns 128 query rows and a range of
+// 128-key blocks:
+//   warp 0     TMA: the Q tile once per unit, then per key block the k_t slab
+//              [D, 128 keys] and the v slab [128 keys, D] (both consumed as
+//              MN-major B operands, as the GEMM consumes weights), two stages
+//              each, a k_t stage freed as soon as its scores are computed;
+//   warp 1     TMEM + MMA: S_j = Q @ k_t_j (M 128, N 128, K D) into one of two
+//              TMEM score buffers, then O += P_{j-1} @ v_{j-1} (N = D) into the
+//              TMEM output, so the next block's scores overlap this block's
+//              softmax;
+//   warps 2-17 softmax: four warps per TMEM lane quarter, each on 32 of the
+//              block's 128 keys (thread = query row = TMEM lane): tcgen05.ld
+//              the 32 scores, e = exp(s) rounded to bf16 (keys past s are 0),
+//              l += e as stored, and e written into a 128-byte-swizzled P
+//              slab (the A operand of the second product; two slabs); after
+//              the last block the four partial row sums meet in shared
+//              memory and the key-quarter-0 warps add them in a fixed order
+//              and store O / l, or, when the keys are split over CTAs, the
+//              fp32 partial O and l.
+// Scores never reach global memory. Split keys are combined by
+// attn_reduce_kernel in a fixed order. Every wait is bounded.
+// Two floats rounded to the operand type by one packed conversion
+// (cvt.rn.bf16x2.f32 / cvt.rn.f16x2.f32); `sum` gains the rounded values.
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float a, float b, float& sum);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b, float& sum) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  sum += __low2float(h) + __high2float(h);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float a, float b, float& sum) {
+  const __half2 h = __floats2half2_rn(a, b);
+  sum += __low2float(h) + __high2float(h);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+constexpr int kAttnSoftmaxWarps = 16;
+constexpr int kAttnThreads = (2 + kAttnSoftmaxWarps) * 32;
+constexpr int kAttnSoftmaxThreads = kAttnSoftmaxWarps * 32;
+
+struct AttnParams {
+  void* y;        // [s, D] output (splits == 1)
+  float* part;    // [splits][s][D] partial O (splits > 1)
+  float* lpart;   // [splits][s] partial row sums
+  int s;
+  int splits, kblk_per_split;  // key blocks (128 keys) per split
+  uint32_t idesc_s, idesc_o;
+};
+
+template <int D, typename TA, typename TC>
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    attn_fused(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+               const __grid_constant__ CUtensorMap tmV, AttnParams p) {
+  constexpr int KA = D / 64;                 // 64-wide k-atoms of the head dim
+  constexpr int Q_BYTES = KA * A_BYTES;      // [128, D]
+  constexpr int KT_BYTES = KA * 2 * B_CHUNK;  // [D, 128 keys]: per k-atom two 64-key chunks
+  constexpr int V_BYTES = 2 * KA * B_CHUNK;   // [128 keys, D]: per 64-key block KA chunks
+  constexpr int KV_STAGE = KT_BYTES + V_BYTES;
+  constexpr int P_BYTES = 2 * A_BYTES;        // [128, 128 keys] as two k-atoms
+  constexpr uint32_t TMEM_COLS = 512;         // S0 | S1 | O
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sq = smem;
+  uint8_t* skv = sq + Q_BYTES;                // 2 stages
+  uint8_t* sp = skv + 2 * KV_STAGE;           // 2 P slabs
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sp + 2 * P_BYTES);
+  uint64_t* qfull = bars;
+  uint64_t* qempty = bars + 1;
+  uint64_t* kfull = bars + 2;    // [2] k_t stages
+  uint64_t* kempty = bars + 4;   // [2]
+  uint64_t* vfull = bars + 6;    // [2] v stages
+  uint64_t* vempty = bars + 8;   // [2]
+  uint64_t* sfull = bars + 10;   // [2] TMEM score buffers
+  uint64_t* sempty = bars + 12;  // [2]
+  uint64_t* pfull = bars + 14;   // [2] P slabs
+  uint64_t* pempty = bars + 16;  // [2]
+  uint64_t* ofull = bars + 18;
+  uint64_t* oempty = bars + 19;
+  uint64_t* lbar = bars + 20;    // a unit's partial row sums are in place
+  uint64_t* lfree = bars + 21;   // ... and have been read
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 22);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* issued = reinterpret_cast<int*>(tmem_slot + 2);  // [4]: k_t stages, v stages
+  int* consumed = issued + 4;                           // [4]
+  int* q_issued = consumed + 4;
+  float* lred = reinterpret_cast<float*>(bars + 32);  // [key quarters 1..3][128 rows]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nq = (p.s + 127) / 128;
+  const int nkb = (p.s + 127) / 128;
+  const int units = nq * p.splits;
+  auto unit_range = [&](int u, int& qb, int& j0, int& j1) {
+    qb = u / p.splits;
+    j0 = (u % p.splits) * p.kblk_per_split;
+    j1 = j0 + p.kblk_per_split < nkb ? j0 + p.kblk_per_split : nkb;
+  };
+
+  if (threadIdx.x == 0) {
+    mbar_init(qfull, 1);
+    mbar_init(qempty, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&kfull[b], 1);
+      mbar_init(&kempty[b], 1);
+      mbar_init(&vfull[b], 1);
+      mbar_init(&vempty[b], 1);
+      mbar_init(&sfull[b], 1);
+      mbar_init(&sempty[b], kAttnSoftmaxThreads);
+      mbar_init(&pfull[b], kAttnSoftmaxThreads);
+      mbar_init(&pempty[b], 1);
+    }
+    for (int i = 0; i < 4; ++i) issued[i] = consumed[i] = 0;
+    mbar_init(ofull, 1);
+    mbar_init(oempty, 128);
+    mbar_init(lbar, kAttnSoftmaxThreads);
+    mbar_init(lfree, 128);
+    *q_issued = 0;
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t t_s0 = tmem_base, t_o = tmem_base + 256;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer ----------------
+    int stage = 0;
+    uint32_t ph = 0;
+    int uq = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++uq) {
+      int qb, j0, j1;
+      unit_range(u, qb, j0, j1);
+      if (!mbar_wait(qempty, (uq & 1) ^ 1u, abort_flag)) break;
+      mbar_expect_tx(qfull, Q_BYTES);
+#pragma unroll
+      for (int a = 0; a < KA; ++a) tma_load_2d(&tmQ, qfull, sq + a * A_BYTES, a * 64, qb * 128);
+      *q_issued += 1;
+      bool ok = true;
+      for (int j = j0; j < j1; ++j) {
+        uint8_t* st = skv + stage * KV_STAGE;
+        if (!mbar_wait(&kempty[stage], ph ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        mbar_expect_tx(&kfull[stage], KT_BYTES);
+#pragma unroll
+        for (int a = 0; a < KA; ++a)
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+            tma_load_2d(&tmK, &kfull[stage], st + (a * 2 + c) * B_CHUNK, j * 128 + c * 64, a * 64);
+        issued[stage] += 1;
+        if (!mbar_wait(&vempty[stage], ph ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        mbar_expect_tx(&vfull[stage], V_BYTES);
+#pragma unroll
+        for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+          for (int c = 0; c < KA; ++c)
+            tma_load_2d(&tmV, &vfull[stage], st + KT_BYTES + (kb * KA + c) * B_CHUNK, c * 64, j * 128 + kb * 64);
+        issued[2 + stage] += 1;
+        if (++stage == 2) {
+          stage = 0;
+          ph ^= 1u;
+        }
+      }
+      if (!ok) break;
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer ----------------
+    int stage = 0, sb = 0, pb = 0;
+    uint32_t ph = 0, sph = 0, pph = 0;
+    int uq = 0;
+    bool ok = true;
+    // O += P @ v for the block whose v sits in stage `st` (phase `vp`)
+    auto mma2 = [&](int st, uint32_t vp, bool first) {
+      if (!mbar_wait(&pfull[pb], pph, abort_flag) || !mbar_wait(&vfull[st], vp, abort_flag)) {
+        ok = false;
+        return;
+      }
+      if (first && !mbar_wait(oempty, (uq & 1) ^ 1u, abort_flag)) {
+        ok = false;
+        return;
+      }
+      tc_fence_after();
+      const uint32_t pa = smem_u32(sp + pb * P_BYTES);
+      const uint32_t vb = smem_u32(skv + st * KV_STAGE + KT_BYTES);
+#pragma unroll
+      for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          tc_mma(t_o, sdesc(pa + kb * A_BYTES + k * 32, 16, 1024), sdesc(vb + kb * KA * B_CHUNK + k * 2048, B_CHUNK, 1024),
+                 p.idesc_o, (first && kb == 0 && k == 0) ? 0u : 1u);
+      tc_commit(&pempty[pb]);
+      tc_commit(&vempty[st]);
+      consumed[2 + st] += 1;
+      if (++pb == 2) {
+        pb = 0;
+        pph ^= 1u;
+      }
+    };
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++uq) {
+      int qb, j0, j1;
+      unit_range(u, qb, j0, j1);
+      if (!mbar_wait(qfull, uq & 1, abort_flag)) break;
+      int prev = -1;
+      uint32_t prev_ph = 0;
+      for (int j = j0; j < j1 && ok; ++j) {
+        if (!mbar_wait(&kfull[stage], ph, abort_flag) || !mbar_wait(&sempty[sb], sph ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t qa = smem_u32(sq);
+        const uint32_t kt = smem_u32(skv + stage * KV_STAGE);
+#pragma unroll
+        for (int a = 0; a < KA; ++a)
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            tc_mma(t_s0 + sb * 128, sdesc(qa + a * A_BYTES + k * 32, 16, 1024),
+                   sdesc(kt + a * 2 * B_CHUNK + k * 2048, B_CHUNK, 1024), p.idesc_s, (a | k) != 0 ? 1u : 0u);
+        tc_commit(&sfull[sb]);
+        tc_commit(&kempty[stage]);            // this k_t slab is read
+        consumed[stage] += 1;
+        if (j == j1 - 1) tc_commit(qempty);  // the unit's last read of Q
+        if (++sb == 2) {
+          sb = 0;
+          sph ^= 1u;
+        }
+        if (prev >= 0) mma2(prev, prev_ph, j == j0 + 1);
+        prev = stage;
+        prev_ph = ph;
+        if (++stage == 2) {
+          stage = 0;
+          ph ^= 1u;
+        }
+      }
+      if (!ok) break;
+      mma2(prev, prev_ph, j1 - j0 == 1);
+      if (!ok) break;
+      tc_commit(ofull);
+    }
+  } else if (warp >= 2) {
+    // ---------------- softmax and output ----------------
+    const int q = warp & 3;             // TMEM lane quarter this warp may access
+    const int kq = (warp - 2) >> 2;     // its quarter of the block's keys / O's columns
+    const int row = q * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    int sb = 0, pb = 0;
+    uint32_t sph = 0, pph = 0;
+    int uq = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++uq) {
+      int qb, j0, j1;
+      unit_range(u, qb, j0, j1);
+      float l = 0.f;
+      bool ok = true;
+      for (int j = j0; j < j1; ++j) {
+        if (!mbar_wait(&sfull[sb], sph, abort_flag) || !mbar_wait(&pempty[pb], pph ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        float v[32];
+        __syncwarp();
+        tmem_ld32(t_s0 + sb * 128 + lane_off + kq * 32, v);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&sempty[sb]);
+        const int key0 = j * 128 + kq * 32;
+        uint4 pk[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 8; e += 2) {
+            const int kk = t * 8 + e;
+            // two exponentials rounded by one packed conversion
+            w[e / 2] = pack2<TA>(key0 + kk < p.s ? __expf(v[kk]) : 0.f,
+                                 key0 + kk + 1 < p.s ? __expf(v[kk + 1]) : 0.f, l);
+          }
+          pk[t] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        uint8_t* line = sp + pb * P_BYTES + (kq >> 1) * A_BYTES + row * 128;
+        const int cb = (kq & 1) * 4;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) *reinterpret_cast<uint4*>(line + (((cb + t) ^ (row & 7)) * 16)) = pk[t];
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P -> the tensor cores' reads
+        mbar_arrive(&pfull[pb]);
+        if (++sb == 2) {
+          sb = 0;
+          sph ^= 1u;
+        }
+        if (++pb == 2) {
+          pb = 0;
+          pph ^= 1u;
+        }
+      }
+      if (!ok) break;
+      // the row's four partial sums meet in shared memory; the key-quarter 0
+      // warps add them in key order and write the output
+      if (kq != 0) {
+        if (!mbar_wait(lfree, (uq & 1) ^ 1u, abort_flag)) break;  // the last unit's sums were read
+        lred[(kq - 1) * 128 + row] = l;
+      }
+      mbar_arrive(lbar);
+      if (kq != 0) continue;
+      if (!mbar_wait(lbar, uq & 1, abort_flag)) break;
+      l = ((l + lred[row]) + lred[128 + row]) + lred[256 + row];
+      mbar_arrive(lfree);
+      if (!mbar_wait(ofull, uq & 1, abort_flag)) break;
+      tc_fence_after();
+      const int64_t grow = static_cast<int64_t>(qb) * 128 + row;
+      const bool row_ok = grow < p.s;
+      const int split = u % p.splits;
+      const float inv_l = 1.0f / l;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        float v[32];
+        __syncwarp();
+        tmem_ld32(t_o + lane_off + c * 32, v);
+        tmem_wait_ld();
+        if (!row_ok) continue;
+        if (p.splits == 1) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[e] *= inv_l;
+          store32<TC>(static_cast<TC*>(p.y) + grow * D + c * 32, v, c * 32, D);
+        } else {
+          store32<float>(p.part + (static_cast<int64_t>(split) * p.s + grow) * D + c * 32, v, c * 32, D);
+        }
+      }
+      if (p.splits > 1 && row_ok) p.lpart[static_cast<int64_t>(split) * p.s + grow] = l;
+      tc_fence_before();
+      mbar_arrive(oempty);
+    }
+  }
+
+  __syncthreads();
+  if (threadIdx.x == 0 && *abort_flag) {
+    // copies issued but not consumed may still land: wait for them (bounded)
+    for (int s = 0; s < 4; ++s) {
+      if (issued[s] > consumed[s]) {
+        volatile int never = 0;
+        mbar_wait(s < 2 ? &kfull[s] : &vfull[s - 2], static_cast<uint32_t>((issued[s] - 1) & 1), &never);
+      }
+    }
+    if (*q_issued > 0) {
+      volatile int never = 0;
+      mbar_wait(qfull, static_cast<uint32_t>((*q_issued - 1) & 1), &never);
+    }
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// Split keys of attn_fused: y[i, :] = sum_s part[s][i, :] / sum_s l[s][i],
+// splits added in order. Four outputs per thread.
+template <typename TC>
+__global__ void __launch_bounds__(256) attn_reduce_kernel(const float* __restrict__ part,
+                                                          const float* __restrict__ lpart, TC* __restrict__ y,
+                                                          int64_t s, int64_t d, int splits) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  pdl_wait();
+  pdl_trigger();
+  const int64_t per_row = d / 4;
+  if (idx >= s * per_row) return;
+  const int64_t i = idx / per_row, j = (idx - i * per_row) * 4;
+  float l = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int k = 0; k < splits; ++k) {
+    l += lpart[static_cast<int64_t>(k) * s + i];
+    const float4 v = *reinterpret_cast<const float4*>(part + (static_cast<int64_t>(k) * s + i) * d + j);
+    acc.x += v.x;
+    acc.y += v.y;
+    acc.z += v.z;
+    acc.w += v.w;
+  }
+  const float r = 1.0f / l;
+  TC* dst = y + i * d + j;
+  dst[0] = from_f<TC>(acc.x * r);
+  dst[1] = from_f<TC>(acc.y * r);
+  dst[2] = from_f<TC>(acc.z * r);
+  dst[3] = from_f<TC>(acc.w * r);
+}
+
 // ---- variant 2: CTA pairs (tcgen05 cta_group::2) ------------------------------------
 //
 // A cluster of two CTAs on two SMs computes a 256 x BN tile with one
@@ -2295,6 +2698,122 @@ extern "C" int axon_gemm_resid3(const void* x, const void* r1, const void* r2, c
   cudaStream_t s = as_stream(stream);
   return ab_dtype == AXON_BF16 ? dispatch_resid3_bn<__nv_bfloat16>(pl.bn, c_dtype, x, r1, r2, mb, rp, cap, s)
                                : dispatch_resid3_bn<__half>(pl.bn, c_dtype, x, r1, r2, mb, rp, cap, s);
+}
+
+namespace axon {
+namespace {
+
+struct AttnPlan {
+  int splits, kblk_per_split;
+  int64_t ws_bytes;
+};
+
+// Key splits: while the 128-row query blocks leave SMs idle, at least two
+// key blocks a split.
+AttnPlan attn_plan(int64_t s, int64_t d, const axon_tune_t& t) {
+  const int64_t nb = (s + 127) / 128;
+  int64_t splits = t.split;
+  if (splits <= 0) {
+    splits = nb >= sm_count() ? 1 : sm_count() / nb;
+    if (splits > nb / 2) splits = nb / 2;
+    if (splits < 1) splits = 1;
+  }
+  if (splits > nb) splits = nb;
+  const int64_t per = (nb + splits - 1) / splits;
+  splits = (nb + per - 1) / per;
+  AttnPlan pl;
+  pl.splits = static_cast<int>(splits);
+  pl.kblk_per_split = static_cast<int>(per);
+  pl.ws_bytes = splits > 1 ? (splits * s * d * 4 + 255) / 256 * 256 + splits * s * 4 : 0;
+  return pl;
+}
+
+template <int D, typename TA, typename TC>
+int launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const AttnParams& ap,
+                int64_t cap, cudaStream_t st) {
+  constexpr int KA = D / 64;
+  constexpr size_t smem = static_cast<size_t>(KA) * A_BYTES + 2 * (KA * 2 * B_CHUNK + 2 * KA * B_CHUNK) +
+                          2 * 2 * A_BYTES + 32 * 8 + 3 * 128 * 4 + 1024;
+  auto kern = attn_fused<D, TA, TC>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return fail(AXON_E_LAUNCH, "axon_attention: smem attribute: %s", cudaGetErrorString(e));
+  const int64_t units = static_cast<int64_t>((ap.s + 127) / 128) * ap.splits;
+  const int grid = static_cast<int>(balanced_grid(units, cap));
+  kern<<<grid, kAttnThreads, smem, st>>>(mq, mk, mv, ap);
+  int rc = launch_status("axon_attention");
+  if (rc || ap.splits == 1) return rc;
+  const int64_t packets = static_cast<int64_t>(ap.s) * (D / 4);
+  launch_k(attn_reduce_kernel<TC>, dim3(static_cast<unsigned>((packets + 255) / 256)), dim3(256), 0, st,
+           static_cast<const float*>(ap.part), static_cast<const float*>(ap.lpart), static_cast<TC*>(ap.y),
+           static_cast<int64_t>(ap.s), static_cast<int64_t>(D), ap.splits);
+  return launch_status("axon_attention");
+}
+
+template <int D, typename TA>
+int dispatch_attn(int32_t c_dtype, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                  const AttnParams& ap, int64_t cap, cudaStream_t st) {
+  switch (c_dtype) {
+    case AXON_BF16: return launch_attn<D, TA, __nv_bfloat16>(mq, mk, mv, ap, cap, st);
+    case AXON_F16: return launch_attn<D, TA, __half>(mq, mk, mv, ap, cap, st);
+    case AXON_F32: return launch_attn<D, TA, float>(mq, mk, mv, ap, cap, st);
+    default: return fail(AXON_E_UNSUPPORTED, "axon_attention: unsupported output dtype %d", c_dtype);
+  }
+}
+
+}  // namespace
+}  // namespace axon
+
+extern "C" int64_t axon_attention_fused_workspace_bytes(int64_t s, int64_t d, const axon_tune_t* tune) {
+  if (s < 0 || d < 0) return fail(AXON_E_SHAPE, "axon_attention_fused_workspace_bytes: negative size");
+  if (s == 0 || d == 0) return 0;
+  return attn_plan(s, d, tune_or_default(tune)).ws_bytes;
+}
+
+extern "C" int axon_attention_fused(const void* q, const void* k_t, const void* v, void* y, void* workspace,
+                                    int64_t workspace_bytes, int64_t s, int64_t d, int32_t ab_dtype,
+                                    int32_t c_dtype, const axon_tune_t* tune, void* stream) {
+  const axon_tune_t t = tune_or_default(tune);
+  if (s < 0 || d < 0) return fail(AXON_E_SHAPE, "axon_attention_fused: negative size");
+  if (s == 0 || d == 0) return AXON_OK;
+  if (d != 64 && d != 128) return fail(AXON_E_UNSUPPORTED, "axon_attention_fused: head dim must be 64 or 128");
+  if (s % 8 || s > 0x7fffffff) return fail(AXON_E_SHAPE, "axon_attention_fused: s must be a multiple of 8");
+  if (ab_dtype != AXON_BF16 && ab_dtype != AXON_F16)
+    return fail(AXON_E_UNSUPPORTED, "axon_attention_fused: inputs must be bf16 or f16 (got %d)", ab_dtype);
+  if (!q || !k_t || !v || !y) return fail(AXON_E_ARG, "axon_attention_fused: NULL tensor");
+  if (!aligned16(q) || !aligned16(k_t) || !aligned16(v) || !aligned16(y))
+    return fail(AXON_E_ALIGN, "axon_attention_fused: tensors must be 16-byte aligned");
+  if (t.split < 0 || t.max_ctas < 0) return fail(AXON_E_ARG, "axon_attention_fused: negative tune field");
+  const AttnPlan pl = attn_plan(s, d, t);
+  if (pl.ws_bytes > 0 && (!workspace || workspace_bytes < pl.ws_bytes || !aligned16(workspace)))
+    return fail(AXON_E_ARG, "axon_attention_fused: %d key splits need a 16-byte aligned workspace of %lld bytes",
+                pl.splits, (long long)pl.ws_bytes);
+  CUtensorMap mq, mk, mv;
+  int rc = make_map(&mq, q, ab_dtype, d, s, d, 64, 128, "q");  // [s, d]: 128 rows x 64 of the head dim
+  if (!rc) rc = make_map(&mk, k_t, ab_dtype, s, d, s, 64, 64, "k_t");  // [d, s]: 64 keys x 64 of the head dim
+  if (!rc) rc = make_map(&mv, v, ab_dtype, d, s, d, 64, 64, "v");      // [s, d]: 64 of the head dim x 64 keys
+  if (rc) return rc;
+  AttnParams ap{};
+  ap.y = y;
+  if (pl.splits > 1) {
+    ap.part = static_cast<float*>(workspace);
+    ap.lpart = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) +
+                                        (static_cast<int64_t>(pl.splits) * s * d * 4 + 255) / 256 * 256);
+  }
+  ap.s = static_cast<int>(s);
+  ap.splits = pl.splits;
+  ap.kblk_per_split = pl.kblk_per_split;
+  const uint32_t fmt = ab_dtype == AXON_BF16 ? 1u : 0u;
+  const uint32_t base = (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 16) | ((128u >> 4) << 24);
+  ap.idesc_s = base | ((128u >> 3) << 17);
+  ap.idesc_o = base | (static_cast<uint32_t>(d >> 3) << 17);
+  int64_t cap = sm_count();
+  if (t.max_ctas > 0 && t.max_ctas < cap) cap = t.max_ctas;
+  cudaStream_t st = as_stream(stream);
+  if (ab_dtype == AXON_BF16)
+    return d == 64 ? dispatch_attn<64, __nv_bfloat16>(c_dtype, mq, mk, mv, ap, cap, st)
+                   : dispatch_attn<128, __nv_bfloat16>(c_dtype, mq, mk, mv, ap, cap, st);
+  return d == 64 ? dispatch_attn<64, __half>(c_dtype, mq, mk, mv, ap, cap, st)
+                 : dispatch_attn<128, __half>(c_dtype, mq, mk, mv, ap, cap, st);
 }
 
 extern "C" int axon_gemm_exp(const void* a, const void* b, void* c, float* row_part, int64_t part_ld, int64_t m,

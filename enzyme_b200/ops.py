@@ -328,7 +328,9 @@ def softmax_mm(x, w, *, out=None, out_dtype=None, workspace=None, tune=None):
 
 
 def attention(q, k_t, v, *, out=None, out_dtype=None, workspace=None, tune=None):
-    """softmax(q @ k_t) @ v (bare exponential), q [s, d], k_t [d, s], v [s, d]."""
+    """softmax(q @ k_t) @ v (bare exponential), q [s, d], k_t [d, s], v [s, d]:
+    one kernel by default for head dim 64 / 128 (tune variant 0), the
+    exp-GEMM + row-scaled GEMM form as variant 1."""
     _require_cuda(q, k_t, v)
     for t in (q, k_t, v):
         if not t.is_contiguous():
@@ -337,10 +339,10 @@ def attention(q, k_t, v, *, out=None, out_dtype=None, workspace=None, tune=None)
     if k_t.shape != (d, s) or v.shape != (s, d):
         raise N.AxonError(N.AXON_E_SHAPE, "attention: q [s, d], k_t [d, s], v [s, d]")
     y = out if out is not None else torch.empty((s, d), dtype=out_dtype or q.dtype, device=q.device)
-    nbytes = _check_ws_bytes(N.lib().axon_attention_workspace_bytes(s, d))
-    ws = _workspace(nbytes, q.device, workspace)
-    check(N.lib().axon_attention(_ptr(q), _ptr(k_t), _ptr(v), _ptr(y), _ptr(ws), ws.numel(), s, d, dtype_code(q),
-                                 dtype_code(y), _tune(tune), _stream(q)))
+    nbytes = _check_ws_bytes(N.lib().axon_attention_workspace_bytes(s, d, _tune(tune)))
+    ws = _workspace(nbytes, q.device, workspace) if nbytes > 0 else workspace
+    check(N.lib().axon_attention(_ptr(q), _ptr(k_t), _ptr(v), _ptr(y), _ptr(ws), ws.numel() if ws is not None else 0,
+                                 s, d, dtype_code(q), dtype_code(y), _tune(tune), _stream(q)))
     return y
 
 

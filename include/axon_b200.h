@@ -461,14 +461,28 @@ AXON_API int axon_softmax_mm(const void* x, const void* w, void* y, void* worksp
                     int64_t workspace_bytes, int64_t m, int64_t n, int64_t k, int32_t ab_dtype,
                     int32_t c_dtype, const axon_tune_t* tune, void* stream);
 
+/* attention in one kernel, head dim d = 64 or 128: per 128 query rows,
+ * S = q @ k_t_j per 128-key block into tensor memory, P = exp(S) (bf16, keys
+ * past s zero) written by four softmax warps into a swizzled shared-memory
+ * slab with the row sums kept in registers, O += P @ v_j in tensor memory,
+ * y = O / l; scores never reach global memory. Key blocks are split over
+ * CTAs while the query blocks leave SMs idle (tune->split: splits, 0 = auto;
+ * max_ctas caps the grid), the fp32 partials added in order by a second
+ * pass. workspace: axon_attention_fused_workspace_bytes (0 without splits). */
+AXON_API int64_t axon_attention_fused_workspace_bytes(int64_t s, int64_t d, const axon_tune_t* tune);
+AXON_API int axon_attention_fused(const void* q, const void* k_t, const void* v, void* y, void* workspace,
+                         int64_t workspace_bytes, int64_t s, int64_t d, int32_t ab_dtype,
+                         int32_t c_dtype, const axon_tune_t* tune, void* stream);
+
 /* attention_nkilib (Axon kernels/attention_nkilib/kernel.py:14-21; refs.py:36-47):
  * y = softmax(q @ k_t) @ v with a bare exponential, q [s, d], k_t [d, s]
  * (pre-transposed), v [s, d], contiguous bf16 or f16; y [s, d] (c_dtype).
- * The first GEMM stores e = exp(q @ k_t) [s, s] in the input dtype with
- * per-tile row sums (axon_gemm_exp, tune->block_n), a small pass forms
- * 1 / row sum, and the second GEMM applies it: y = r * (e @ v).
- * s and d multiples of 8. workspace: axon_attention_workspace_bytes(s, d). */
-AXON_API int64_t axon_attention_workspace_bytes(int64_t s, int64_t d);
+ * tune->variant 0 (default): axon_attention_fused for d = 64 or 128; variant
+ * 1 (and other d): the first GEMM stores e = exp(q @ k_t) [s, s] in the
+ * input dtype with per-tile row sums (axon_gemm_exp, tune->block_n), a small
+ * pass forms 1 / row sum, and the second GEMM applies it: y = r * (e @ v).
+ * s and d multiples of 8. workspace: axon_attention_workspace_bytes(s, d, tune). */
+AXON_API int64_t axon_attention_workspace_bytes(int64_t s, int64_t d, const axon_tune_t* tune);
 AXON_API int axon_attention(const void* q, const void* k_t, const void* v, void* y, void* workspace,
                    int64_t workspace_bytes, int64_t s, int64_t d, int32_t ab_dtype,
                    int32_t c_dtype, const axon_tune_t* tune, void* stream);
