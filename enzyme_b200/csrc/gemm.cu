@@ -100,6 +100,25 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// mbar_wait for threads with slack: after a few failed tries it sleeps
+// between polls, leaving the issue slots to the warps doing the work.
+__device__ __forceinline__ bool mbar_wait_backoff(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (i > 4) __nanosleep(64);
+    if ((i & 31) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer() - t0 > kTimeoutNs) {
+        *abort_flag = 1;
+        atomicExch(&g_gemm_error, AXON_E_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
 __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst, int c0, int c1) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
@@ -1165,7 +1184,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       float l = 0.f;
       bool ok = true;
       for (int j = j0; j < j1; ++j) {
-        if (!mbar_wait(&sfull[sb], sph, abort_flag) || !mbar_wait(&pempty[pb], pph ^ 1u, abort_flag)) {
+        if (!mbar_wait_backoff(&sfull[sb], sph, abort_flag) ||
+            !mbar_wait_backoff(&pempty[pb], pph ^ 1u, abort_flag)) {
           ok = false;
           break;
         }
@@ -1177,17 +1197,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tc_fence_before();
         mbar_arrive(&sempty[sb]);
         const int key0 = j * 128 + kq * 32;
+        if (key0 + 32 > p.s) {  // the ragged last block: keys past s weigh nothing
+#pragma unroll
+          for (int kk = 0; kk < 32; ++kk)
+            if (key0 + kk >= p.s) v[kk] = -INFINITY;
+        }
         uint4 pk[4];
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
           uint32_t w[4];
 #pragma unroll
-          for (int e = 0; e < 8; e += 2) {
-            const int kk = t * 8 + e;
-            // two exponentials rounded by one packed conversion
-            w[e / 2] = pack2<TA>(key0 + kk < p.s ? __expf(v[kk]) : 0.f,
-                                 key0 + kk + 1 < p.s ? __expf(v[kk + 1]) : 0.f, l);
-          }
+          for (int e = 0; e < 8; e += 2)  // two exponentials rounded by one packed conversion
+            w[e / 2] = pack2<TA>(__expf(v[t * 8 + e]), __expf(v[t * 8 + e + 1]), l);
           pk[t] = make_uint4(w[0], w[1], w[2], w[3]);
         }
         uint8_t* line = sp + pb * P_BYTES + (kq >> 1) * A_BYTES + row * 128;
@@ -1214,10 +1235,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       mbar_arrive(lbar);
       if (kq != 0) continue;
-      if (!mbar_wait(lbar, uq & 1, abort_flag)) break;
+      if (!mbar_wait_backoff(lbar, uq & 1, abort_flag)) break;
       l = ((l + lred[row]) + lred[128 + row]) + lred[256 + row];
       mbar_arrive(lfree);
-      if (!mbar_wait(ofull, uq & 1, abort_flag)) break;
+      if (!mbar_wait_backoff(ofull, uq & 1, abort_flag)) break;
       tc_fence_after();
       const int64_t grow = static_cast<int64_t>(qb) * 128 + row;
       const bool row_ok = grow < p.s;
