@@ -769,8 +769,9 @@ __global__ void __launch_bounds__(kResidThreads, 1)
       tile_coords(u / p.splits, num_m, num_n, p.raster, tm, tn);
       const int buf = local % NBUF;
       const uint32_t use = static_cast<uint32_t>(local / NBUF);
-      if (!mbar_wait(&tfull[buf], use & 1, abort_flag)) break;
-      if (!mbar_wait(&rsfull[buf], use & 1, abort_flag)) break;
+      // the epilogue idles through a tile's mainloop: poll with sleeps
+      if (!mbar_wait_backoff(&tfull[buf], use & 1, abort_flag)) break;
+      if (!mbar_wait_backoff(&rsfull[buf], use & 1, abort_flag)) break;
       tc_fence_after();
       const float scale = rs[buf * BM + q * 32 + lane];
       mbar_arrive(&rsempty[buf]);
@@ -806,7 +807,7 @@ __global__ void __launch_bounds__(kResidThreads, 1)
     bool ok = true;
     // one k-block: wait for the slot, write h, hand it to the MMA warp
     auto put = [&](const Resid3Regs<TA>& g, float* ss) {
-      if (!mbar_wait(&hempty[hs], hphase ^ 1u, abort_flag)) {
+      if (!mbar_wait_backoff(&hempty[hs], hphase ^ 1u, abort_flag)) {
         ok = false;
         return;
       }
