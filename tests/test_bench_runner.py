@@ -234,3 +234,25 @@ def test_baseline_timing_writes_csv(tmp_path):
     out = br.run_baseline(spec, {"m": 16, "n": 128}, warmup=1, bench=2, paths=paths)
     rows = _rows(out)
     assert rows[0]["ref"] == "torch_ref" and int(rows[0]["cores"]) >= 1 and float(rows[0]["median_ms"]) > 0
+
+
+@pytest.mark.parametrize("name,dims", [("qkv_cte", {"m": 578, "n": 264, "k": 1408}),
+                                       ("softmax_mm", {"m": 1024, "n": 1024, "k": 1024}),
+                                       ("attention_nkilib", {"s": 1024, "d": 128})])
+def test_neighbour_specs_emit_every_variant(tmp_path, name, dims):
+    """The GEMM-backed neighbour specs emit one loadable module per catalogue
+    variant, each with a manifest whose feasible tile key maps to a tune."""
+    import importlib.util
+
+    spec = load_spec(name)
+    paths = run_paths(spec, str(tmp_path / f"out/{name}_t"))
+    mods = catalogue.emit_variant_modules(spec, dims, 2, paths)
+    assert len(mods) == len(catalogue.variants(name))
+    for var, mod in zip(catalogue.variants(name), mods):
+        m = importlib.util.module_from_spec(importlib.util.spec_from_file_location(f"_m_{name}_{var.hw_variant}", mod))
+        m.__spec__.loader.exec_module(m)
+        assert callable(getattr(m, safe_name(name)))
+        cons = catalogue.constraints(name, var.hw_variant, dims, 2, spec.tile_args)
+        tiles = {c.tile_arg: (c.allowed[-1] if c.allowed else 1) for c in cons}
+        tune = catalogue.tune_for(name, var.hw_variant, tiles)
+        assert isinstance(tune, dict) and tune.get("variant", 0) in (0, 1, 2, 3)
