@@ -82,3 +82,29 @@ def test_error_is_thread_local():
     t.join()
     assert seen == [""]
     assert "NULL" in N.last_error()
+
+
+def test_split_plans_without_a_gpu():
+    """Workspace queries of the one-kernel qkv_cte and attention paths (on a
+    host without a GPU the SM count reads as B200's 148): no k split once the
+    row blocks fill the GPU, splits (fp32 partials + row sums) when they
+    do not, and explicit splits honoured."""
+    lib = N.lib()
+    t = N.Tune.of
+    assert lib.axon_gemm_resid3_workspace_bytes(16384, 512, 8192, None) == 0
+    # 8 row blocks of 1024 rows: 18 k splits of 15 k-blocks (16384 / 64 = 256 k-blocks)
+    want = -(-(18 * 1024 * 512 * 4) // 256) * 256 + 18 * 1024 * 4
+    assert lib.axon_gemm_resid3_workspace_bytes(1024, 512, 16384, None) == want
+    assert lib.axon_gemm_resid3_workspace_bytes(1024, 512, 16384, t({"split": 1})) == 0
+    assert lib.axon_gemm_resid3_workspace_bytes(1024, 512, 16384, t({"block_n": 100})) < 0  # rejected width
+    # attention: 64 query blocks at s = 8192 -> 2 key splits; 128 or more -> none
+    want = -(-(2 * 8192 * 128 * 4) // 256) * 256 + 2 * 8192 * 4
+    assert lib.axon_attention_fused_workspace_bytes(8192, 128, None) == want
+    assert lib.axon_attention_fused_workspace_bytes(32768, 128, None) == 0
+    assert lib.axon_attention_workspace_bytes(8192, 128, None) == want
+    # the two-GEMM form stages the [s, s] scores
+    assert lib.axon_attention_workspace_bytes(8192, 128, t({"variant": 1})) >= 8192 * 8192 * 2
+    assert lib.axon_attention_workspace_bytes(1024, 512, None) >= 1024 * 1024 * 2  # d = 512: two-GEMM form
+    # qkv_cte: the one-kernel default vs the row-pass variants (h + row scales)
+    assert lib.axon_qkv_cte_workspace_bytes(16384, 512, 8192, None) == 0
+    assert lib.axon_qkv_cte_workspace_bytes(578, 264, 1408, t({"variant": 1})) >= 578 * 1408 * 2 + 578 * 4
