@@ -1,9 +1,9 @@
 """Generate the golden parity fixtures from the reference's own spec refs.
 
-Run in a container where the Axon reference tree is mounted (default
-`/root/reference`, override with `AXON_REF_ROOT`):
+Run where the Axon reference tree is checked out, with `AXON_REF_ROOT`
+naming its root (the script falls back to the build container's checkout):
 
-    python tests/golden/make_golden.py
+    AXON_REF_ROOT=<reference checkout> python tests/golden/make_golden.py
 
 For each case it imports the reference's `kernels/<name>/refs.py` by path
 (those files need only numpy, torch and ml_dtypes), draws the seeded inputs
