@@ -231,3 +231,18 @@ def test_every_case_parses_and_matches_its_spec():
         assert len(c["sizes"]) == len(spec.dim_vars), case
         args = cli.build_parser().parse_args(cases.argv(case))
         assert args.sizes == c["sizes"]
+
+
+def test_every_case_resolves_and_binds_its_spec():
+    """Each named case splits back into its own kernel and case id (kernel
+    names share prefixes: softmax / softmax_mm, rmsnorm / rmsnorm_matmul),
+    names a spec package that loads, and gives one size per dim_var."""
+    from enzyme_b200 import cases
+
+    for name in cases.all_cases():
+        kernel, cid, c = cases.resolve(name)
+        assert f"{kernel}_{cid}" == name
+        spec = load_spec(kernel)
+        assert len(c["sizes"]) == len(spec.dim_vars), name
+        args = cases.argv(name)
+        assert args[0].endswith(f"kernels/{kernel}") and args[-1].endswith(f"{kernel}_{cid}.csv")
