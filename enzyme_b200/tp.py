@@ -6,9 +6,13 @@ Both follow the reference's sharding laws (src/axon/sharding.py):
   (columns) and W_down (rows). Sharding that class puts the first two GEMMs
   in S (each rank owns a column slice: no communication) and makes the down
   projection a contraction over a sharded class, hence Partial("+")
-  (sharding.py:380-384), which a terminal AllReduce resolves (:514-522). Here
-  the all-reduce is NCCL over NVLink/NVSwitch via torch.distributed, on fp32
-  partials so the sum adds no bf16 rounding.
+  (sharding.py:380-384), which a terminal AllReduce resolves (:514-522).
+  `FusedTPSwiGLU` (the path bench.py runs) resolves it without NCCL: the down
+  GEMM's epilogue scatters f16 partial rows to their owner ranks over NVLink
+  peer memory, owners sum them in fp32 and push the bf16 rows to every rank
+  (or store them once through an NVLink multicast address). `TPSwiGLU` keeps
+  the plain form -- an NCCL all-reduce of fp32 partials per slab -- for
+  comparison.
 * Adam. Every tensor is split along the same (flattened parameter) axis: the
   update is elementwise, so the plan is S everywhere with no combine step
   beyond a barrier (the reference's row-shard "P" plan).
@@ -16,7 +20,7 @@ Both follow the reference's sharding laws (src/axon/sharding.py):
 The per-rank compute is this library's CUDA kernels. `TPSwiGLU` splits the
 tokens into m-slabs and issues each slab's all-reduce asynchronously as soon
 as its partial is written, so the collective of slab i overlaps the GEMMs of
-slab i+1. The kernel calls are injected (`ops`), so the host logic -- shard
+slab i+1; its kernel calls are injected (`ops`), so that host logic -- shard
 ranges, slab schedule, collectives -- is testable on CPU ranks over gloo.
 """
 
