@@ -197,7 +197,13 @@ __global__ void __launch_bounds__(1024) cumsum_lookback(const Tin* __restrict__ 
         if ((zmask & need) && !timed_out) {
           if (++spins > kSpinLimit) {
             timed_out = true;
-            if (lane == 0) atomicExch(status, AXON_E_TIMEOUT);
+            // recorded in the workspace header and in the library's device
+            // status word: the allocation-free entry point's scratch is
+            // cleared by the next call, so only the latter survives for it
+            if (lane == 0) {
+              atomicExch(status, AXON_E_TIMEOUT);
+              atomicExch(&g_scan_error, AXON_E_TIMEOUT);
+            }
           } else {
             __nanosleep(spins < 64 ? 32 : 256);
           }
@@ -1098,6 +1104,9 @@ extern "C" int axon_cumsum_status(const void* workspace, void* stream) {
 // file-scope device array instead of a caller workspace. The array exists
 // once per device that loads this library and lives until the process exits.
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <mutex>
 
 namespace axon {
@@ -1109,22 +1118,51 @@ static __device__ __align__(256) unsigned char g_cumsum_scratch[kNoAllocScratchB
 constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mu;
 void* g_scratch_addr[kMaxDevices] = {};
+CUcontext g_scratch_ctx[kMaxDevices] = {};
+
+PFN_cuCtxGetCurrent_v4000 ctx_current_fn() {
+  static PFN_cuCtxGetCurrent_v4000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+  });
+  return fn;
+}
 
 // The device address of g_cumsum_scratch on the current device. In host code
 // the symbol is only a stand-in, so the address is looked up with
-// cudaGetSymbolAddress, once per device, with that device current.
+// cudaGetSymbolAddress, once per device, with that device current. The
+// device's context is recorded with it: a reset device gets a new context,
+// and the address is then looked up again instead of reusing a stale one.
 int scratch_address(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(AXON_E_CUDA, "axon_cumsum_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= kMaxDevices) return fail(AXON_E_UNSUPPORTED, "axon_cumsum_noalloc: device %d out of range", dev);
   std::lock_guard<std::mutex> lock(g_scratch_mu);
+  void* p = nullptr;
   if (g_scratch_addr[dev] == nullptr) {
-    void* p = nullptr;
+    // the first runtime call on this device makes its primary context current
     e = cudaGetSymbolAddress(&p, g_cumsum_scratch);
     if (e != cudaSuccess || p == nullptr)
       return fail(AXON_E_CUDA, "axon_cumsum_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+  }
+  CUcontext ctx = nullptr;
+  auto current = ctx_current_fn();
+  if (current == nullptr || current(&ctx) != CUDA_SUCCESS)
+    return fail(AXON_E_CUDA, "axon_cumsum_noalloc: cuCtxGetCurrent unavailable");
+  if (g_scratch_addr[dev] == nullptr || g_scratch_ctx[dev] != ctx) {
+    if (p == nullptr) {
+      e = cudaGetSymbolAddress(&p, g_cumsum_scratch);
+      if (e != cudaSuccess || p == nullptr)
+        return fail(AXON_E_CUDA, "axon_cumsum_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+    }
     g_scratch_addr[dev] = p;
+    g_scratch_ctx[dev] = ctx;
   }
   *out = g_scratch_addr[dev];
   return AXON_OK;

@@ -19,8 +19,11 @@
 //      it reads the output.
 //
 // Peer buffers are ordinary device allocations shared with CUDA IPC
-// (axon_ipc_handle / axon_ipc_open). No TMA, no multicast objects, no NCCL on
-// this path; loads and stores to peers are plain 16-byte accesses. Every wait
+// (axon_ipc_handle / axon_ipc_open). The all-gather pushes rows with plain
+// 16-byte peer stores or 1-D bulk copies (global <- shared) by default;
+// axon_tp_reduce_multicast instead stores each row once with multimem.st to an
+// NVLink multicast address (NVLS). No TMA tensor copy and no cluster-multicast
+// load is used anywhere on this path, and NCCL is not called. Every wait
 // gives up after about two seconds and records AXON_E_TIMEOUT, read and
 // cleared by axon_tp_status, so a rank that never arrives ends the step with
 // an error instead of a hung GPU.

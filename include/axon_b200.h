@@ -196,8 +196,11 @@ AXON_API int axon_cumsum_status(const void* workspace, void* stream);
  * so make that first call before any stream capture. Every call clears the
  * array on `stream` and then uses it: calls that overlap on the GPU (other
  * streams, other threads) race on the one array and must be serialised by
- * the caller. The look-back status word is not exposed; use axon_cumsum with
- * a workspace where AXON_E_TIMEOUT must be observable. */
+ * the caller. A look-back wait that gives up records AXON_E_TIMEOUT in the
+ * library's device status word, which axon_cumsum_status(NULL, stream) reads
+ * and clears; check it before trusting the output. The address lookup is
+ * repeated when the current device's context changes (after a
+ * cudaDeviceReset, for example). */
 AXON_API int axon_cumsum_noalloc(const void* x, void* y, int64_t m, int64_t n, int64_t ld_x,
                                  int64_t ld_y, int32_t in_dtype, int32_t out_dtype,
                                  const axon_tune_t* tune, void* stream);

@@ -75,7 +75,11 @@ def main() -> int:
     import ml_dtypes  # noqa: F401  (registers bfloat16 with numpy)
     import torch
 
-    root = Path(os.environ.get("AXON_REF_ROOT", "/root/reference"))
+    raw = os.environ.get("AXON_REF_ROOT")
+    if not raw:
+        print("set AXON_REF_ROOT to the root of the reference (Axon) source tree", file=sys.stderr)
+        return 2
+    root = Path(raw)
     if not (root / "kernels").is_dir():
         print(f"reference tree not found at {root}", file=sys.stderr)
         return 2

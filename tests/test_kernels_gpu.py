@@ -281,8 +281,9 @@ def test_rope_config_full_size(cuda_device):
     qd, kd = _t(q, cuda_device), _t(k, cuda_device)
     qo, ko = ops.rope_rotate_half(qd, kd, _t(c, cuda_device), _t(s, cuda_device))
     rows = np.arange(0, 4096, 37)
-    _close(_np(qo)[rows], f64.rope_rotate_half(q[rows], c[rows], s[rows]), 7.8125e-3, 2e-2, "rope q")
-    _close(_np(ko)[rows], f64.rope_rotate_half(k[rows], c[rows], s[rows]), 7.8125e-3, 2e-2, "rope k")
+    # the north star's bf16 bar (rtol = atol = 1e-2), not the eval cases' 2e-2
+    _close(_np(qo)[rows], f64.rope_rotate_half(q[rows], c[rows], s[rows]), 1e-2, 1e-2, "rope q")
+    _close(_np(ko)[rows], f64.rope_rotate_half(k[rows], c[rows], s[rows]), 1e-2, 1e-2, "rope k")
     # in place gives the same bits
     qo2, ko2 = ops.rope_rotate_half(qd, kd, _t(c, cuda_device), _t(s, cuda_device), q_out=qd, k_out=kd)
     assert torch.equal(qo2, qo) and torch.equal(ko2, ko)
@@ -447,6 +448,35 @@ def _adam_rel_err(got, want, inputs, beta1, beta2):
     return out
 
 
+def _adam_plain_err(got, want, inputs, beta1, beta2):
+    """The plain element-wise figure against float64, per output (p', m',
+    v'): the share of elements with |got - want| / |want| > 1e-5 and the
+    worst such ratio, for this kernel and for the reference's own fp32 CPU
+    path (the spec torch_ref) on the same inputs. Both miss 1e-5 on a small
+    share of elements where g + wd * p or p - update cancels."""
+    from oracle import cpu_torch
+
+    p, g, m, v, ss, ib, wd = (np.asarray(a, dtype=np.float64) for a in inputs)
+    f32 = [torch.from_numpy(np.ascontiguousarray(np.broadcast_to(a, p.shape) if a.ndim else a, dtype=np.float32))
+           for a in (p, g, m, v, ss, ib, wd)]
+    ref32 = cpu_torch.adam(*f32, beta1=beta1, beta2=beta2)
+    out = {}
+    for name, o, r, w in zip(("p", "m", "v"), got, ref32, want):
+        den = np.maximum(np.abs(w), 1e-30)
+        ours = np.abs(_np(o) - w) / den
+        theirs = np.abs(r.numpy().astype(np.float64) - w) / den
+        out[name] = {"share_over_1e-5": float((ours > 1e-5).mean()), "worst": float(ours.max()),
+                     "ref_share_over_1e-5": float((theirs > 1e-5).mean()), "ref_worst": float(theirs.max())}
+    return out
+
+
+def _assert_adam_plain(plain):
+    # no more elements above plain 1e-5 than twice the reference's own fp32
+    # path (plus a handful), on every output
+    for name, r in plain.items():
+        assert r["share_over_1e-5"] <= 2 * r["ref_share_over_1e-5"] + 1e-6, (name, plain)
+
+
 def test_adam_config_medium_and_inplace(cuda_device):
     spec = load_spec("fused_adam_cfg")
     ins = spec.make_inputs(p=1000, f=4096, rng=np.random.default_rng(SEED))
@@ -455,6 +485,7 @@ def test_adam_config_medium_and_inplace(cuda_device):
     out = ops.adam(p, gr, m, v, step_size=ss, inv_bc2_sqrt=ib, wd=wd, beta1=0.9, beta2=0.95)
     errs = _adam_rel_err(out, want, ins, 0.9, 0.95)
     assert max(errs) <= 1.0, errs
+    _assert_adam_plain(_adam_plain_err(out, want, ins, 0.9, 0.95))
     # in place with scalar hyper-parameters == out of place with per-row ones
     step, inv, wdv = (float(np.asarray(a)[0, 0]) for a in ins[4:])
     ops.adam(p, gr, m, v, step_size=step, inv_bc2_sqrt=inv, wd=wdv, beta1=0.9, beta2=0.95, out=(p, m, v))
@@ -479,8 +510,10 @@ def test_adam_full_size_sampled(cuda_device):
         z = np.zeros_like(p0)
         want = f64.adam(p0, g0, z, z, ss, ib, 0.1, beta1=0.9, beta2=0.95)
         got = (p[s:s + 1_000_000], m[s:s + 1_000_000], v[s:s + 1_000_000])
-        errs = _adam_rel_err(got, want, (p0, g0, z, z, np.float64(ss), np.float64(ib), np.float64(0.1)), 0.9, 0.95)
+        ins = (p0, g0, z, z, np.float64(ss), np.float64(ib), np.float64(0.1))
+        errs = _adam_rel_err(got, want, ins, 0.9, 0.95)
         assert max(errs) <= 1.0, (s, errs)
+        _assert_adam_plain(_adam_plain_err(got, want, ins, 0.9, 0.95))
     del p, g, m, v
     torch.cuda.empty_cache()
 

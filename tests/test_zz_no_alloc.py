@@ -6,9 +6,10 @@ cudaMalloc's device-wide synchronisation is not allowed). It uses a fixed
 static device array as its look-back scratch instead of a caller workspace.
 These tests check it against the workspace entry point `axon_cumsum` on the
 same inputs, twice in a row (the static scratch keeps the previous call's
-contents, so the second call proves it is cleared), and that shapes beyond
-the static capacity are refused on the host. This file is named to be
-collected last.
+contents, so the second call proves it is cleared), that the device status
+word read by `axon_cumsum_status(NULL, ...)` reports no look-back wait that
+gave up after each call, and that shapes beyond the static capacity are
+refused on the host. This file is named to be collected last.
 """
 
 from __future__ import annotations
@@ -51,6 +52,13 @@ def _cumsum_noalloc(x, y, tune):
                                        _code(y), tune, _stream())
 
 
+def _assert_no_timeout():
+    """The look-back kernel records a wait that gave up in the library's
+    device status word; reading it synchronises the stream and clears it."""
+    rc = N.lib().axon_cumsum_status(None, _stream())
+    assert rc == N.AXON_OK, N.last_error()
+
+
 @pytest.mark.parametrize("split", [0, 2048])
 def test_noalloc_matches_workspace_entry_point_twice(split, cuda_device):
     torch.cuda.set_device(cuda_device)
@@ -64,7 +72,7 @@ def test_noalloc_matches_workspace_entry_point_twice(split, cuda_device):
         got = torch.full_like(x, float("nan"))
         rc = _cumsum_noalloc(x, got, tune)
         assert rc == N.AXON_OK, N.last_error()
-        torch.cuda.synchronize()
+        _assert_no_timeout()
         np.testing.assert_allclose(got.cpu().numpy(), want.cpu().numpy(), rtol=1e-5, atol=1e-7)
 
 
@@ -75,7 +83,7 @@ def test_noalloc_bf16_in_fp32_out(cuda_device):
     _cumsum_with_workspace(x, want, None)
     got = torch.empty_like(want)
     assert _cumsum_noalloc(x, got, None) == N.AXON_OK, N.last_error()
-    torch.cuda.synchronize()
+    _assert_no_timeout()
     np.testing.assert_allclose(got.cpu().numpy(), want.cpu().numpy(), rtol=1e-5, atol=1e-5)
 
 
