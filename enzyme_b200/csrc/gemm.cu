@@ -2954,7 +2954,8 @@ extern "C" int axon_rmsnorm_matmul(const void* x, const void* w, void* y, void* 
                    AXON_EPI_ROWSCALE, tune, stream);
 }
 
-constexpr int kF16Act = 4;  // tune.precision value of the f16-activation mode
+constexpr int kF16Act = 4;        // tune.precision value of the f16-activation mode
+constexpr int kF16ActPrecast = 5;  // the same, with w3 passed as the caller's f16 copy
 constexpr int64_t kFusedMaxTiles = 320;  // see axon_silu_mlp
 
 static int silu_terms(const axon_tune_t* tune) {
@@ -2962,10 +2963,13 @@ static int silu_terms(const axon_tune_t* tune) {
   return p <= 0 ? 1 : p;
 }
 
-static bool silu_mode_ok(int terms) { return (terms >= 1 && terms <= 3) || terms == kF16Act; }
+static bool silu_f16(int terms) { return terms == kF16Act || terms == kF16ActPrecast; }
 
+static bool silu_mode_ok(int terms) { return (terms >= 1 && terms <= 3) || silu_f16(terms); }
+
+// precision 4 and 5 share one layout (the f16 copy of w3 goes unused at 5)
 static int64_t silu_ws_bytes(int64_t m, int64_t n, int64_t p, int terms) {
-  return terms == kF16Act ? m * n * 2 + n * p * 2 + (swiglu_counter_bytes(m) + 255) / 256 * 256 : m * n * 2 * terms;
+  return silu_f16(terms) ? m * n * 2 + n * p * 2 + (swiglu_counter_bytes(m) + 255) / 256 * 256 : m * n * 2 * terms;
 }
 
 extern "C" int64_t axon_silu_mlp_workspace_bytes(int64_t m, int64_t n, int64_t p, int32_t ab_dtype,
@@ -2973,7 +2977,7 @@ extern "C" int64_t axon_silu_mlp_workspace_bytes(int64_t m, int64_t n, int64_t p
   (void)ab_dtype;
   if (m < 0 || n < 0 || p < 0) return fail(AXON_E_SHAPE, "axon_silu_mlp_workspace_bytes: negative size");
   const int terms = silu_terms(tune);
-  if (!silu_mode_ok(terms)) return fail(AXON_E_ARG, "axon_silu_mlp: precision must be 1, 2, 3 or 4");
+  if (!silu_mode_ok(terms)) return fail(AXON_E_ARG, "axon_silu_mlp: precision must be 1, 2, 3, 4 or 5");
   return silu_ws_bytes(m, n, p, terms);
 }
 
@@ -2981,12 +2985,12 @@ extern "C" int axon_silu_mlp(const void* x, const void* w1, const void* w2, cons
                              void* workspace, int64_t workspace_bytes, int64_t m, int64_t n, int64_t k, int64_t p,
                              int32_t ab_dtype, int32_t c_dtype, const axon_tune_t* tune, void* stream) {
   const int terms = silu_terms(tune);
-  if (!silu_mode_ok(terms)) return fail(AXON_E_ARG, "axon_silu_mlp: precision must be 1, 2, 3 or 4");
+  if (!silu_mode_ok(terms)) return fail(AXON_E_ARG, "axon_silu_mlp: precision must be 1, 2, 3, 4 or 5");
   if (m < 0 || n < 0 || k < 0 || p < 0) return fail(AXON_E_SHAPE, "axon_silu_mlp: negative size");
   if (m == 0 || p == 0) return AXON_OK;
   if (terms > 1 && terms <= 3 && n % 64)
     return fail(AXON_E_SHAPE, "axon_silu_mlp: split precision needs n %% 64 == 0 (n=%lld)", (long long)n);
-  if (terms == kF16Act && (ab_dtype != AXON_BF16 || p % 8))
+  if (silu_f16(terms) && (ab_dtype != AXON_BF16 || p % 8))
     return fail(AXON_E_UNSUPPORTED, "axon_silu_mlp: the f16-activation mode takes bf16 operands and p %% 8 == 0");
   const int64_t need = silu_ws_bytes(m, n, p, terms);
   if (!workspace || workspace_bytes < need)
@@ -2996,14 +3000,20 @@ extern "C" int axon_silu_mlp(const void* x, const void* w1, const void* w2, cons
   up.block_n = t.block_n == 64 ? 0 : t.block_n;
   down.stages = 0;
   down.block_n = 0;
-  if (terms == kF16Act) {
+  if (silu_f16(terms)) {
     // The activation is written as f16 (8 more mantissa bits than bf16) and
-    // the down projection runs f16 x f16, on a per-call f16 copy of W_down:
-    // a tcgen05 f16-kind MMA takes both operands in one type.
+    // the down projection runs f16 x f16, on an f16 copy of W_down: a tcgen05
+    // f16-kind MMA takes both operands in one type. Precision 4 makes that
+    // copy in the workspace on every call; at precision 5 w3 already is the
+    // caller's f16 copy (made once, when the weights are loaded).
     __half* act = static_cast<__half*>(workspace);
     __half* w3h = reinterpret_cast<__half*>(static_cast<unsigned char*>(workspace) + m * n * 2);
     int* counters = reinterpret_cast<int*>(static_cast<unsigned char*>(workspace) + m * n * 2 + n * p * 2);
-    int rc = cast_impl(w3, w3h, n * p, AXON_BF16, AXON_F16, as_stream(stream));
+    int rc = AXON_OK;
+    if (terms == kF16ActPrecast)
+      w3h = static_cast<__half*>(const_cast<void*>(w3));
+    else
+      rc = cast_impl(w3, w3h, n * p, AXON_BF16, AXON_F16, as_stream(stream));
     if (rc) return rc;
     // variant 3: both GEMMs in one CTA-pair kernel; 1 / 2: two launches of
     // the one-CTA / CTA-pair GEMM; 0 (default): the fused kernel while the

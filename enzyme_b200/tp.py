@@ -347,8 +347,12 @@ class FusedTPSwiGLU:
         self.layout = PeerLayout(m, self.hidden, self.world, len(self.slabs), torch.empty(0, dtype=out_dtype).element_size())
         self.peers = PeerBuffers(self.layout, dev, group)
         self.y = self.peers.output(out_dtype)
-        self.w_down_h = torch.empty(w_down.shape, dtype=torch.float16, device=dev)
+        # the shard's W_down is fixed for the object's life: one f16 copy, made
+        # here (the down projection runs f16 x f16 on the f16 activation)
         from . import _native as N
+        from . import ops
+
+        self.w_down_h = ops.cast(w_down, torch.float16)
 
         # activation [m, n] f16 followed by the fused kernel's counters
         n = w_gate.shape[1]
@@ -378,6 +382,17 @@ class FusedTPSwiGLU:
                 raise ValueError("whole_step needs bf16 output, m % 256 == 0 and 1, 2, 4 or 8 ranks")
             self.done_per_epoch = int(N.lib().axon_tp_step_done_per_epoch(self.world, m, self.hidden))
 
+    def launches_per_step(self) -> int:
+        """Kernels this library launches per forward() (copy-engine transfers
+        not counted)."""
+        if self.whole_step:
+            return 2  # the step kernel, the wait on the done count
+        if len(self.slabs) == 1 and self.fused_kernel:
+            return 5  # fused GEMMs, signal, reduce + push, signal, wait
+        # per slab: gate/up GEMM, scattering down GEMM, signal, reduce, signal;
+        # then one wait per slab
+        return 6 * len(self.slabs)
+
     def close(self) -> None:
         torch.cuda.synchronize(self.w_gate.device)
         self.peers.close()
@@ -402,7 +417,6 @@ class FusedTPSwiGLU:
         ptrs = lambda vals: (ctypes.c_void_p * W)(*vals)  # noqa: E731
         tune = N.Tune.of(self.tune)
         out_code = {torch.bfloat16: N.AXON_BF16, torch.float16: N.AXON_F16, torch.float32: N.AXON_F32}[self.out_dtype]
-        ops.cast(self.w_down, torch.float16, out=self.w_down_h)
         y_ptrs = ptrs([b + lo.y_offset for b in self.peers.bases])
         mine = self.peers.bases[self.rank]
         if self.whole_step:

@@ -70,7 +70,8 @@ typedef struct axon_tune {
   int32_t split;        /* cumsum: elements per tile (variant 0) or CTAs per
                            row cluster (variant 1)                            */
   int32_t precision;    /* silu_mlp activation storage: 1 = one bf16 value,
-                           2 / 3 = split terms, 4 = f16 (see axon_silu_mlp)   */
+                           2 / 3 = split terms, 4 = f16, 5 = f16 with an f16
+                           W_down from the caller (see axon_silu_mlp)        */
   int32_t max_ctas;     /* GEMM: cap on the persistent grid (0 = one CTA per
                            SM); leaves SMs free for a concurrent collective   */
 } axon_tune_t;
@@ -491,8 +492,8 @@ AXON_API int axon_attention(const void* q, const void* k_t, const void* v, void*
                    int32_t c_dtype, const axon_tune_t* tune, void* stream);
 
 /* Bytes of scratch axon_silu_mlp needs: the [m, n] activation in ab_dtype
- * times tune->precision terms, or for precision 4 an f16 activation, an f16
- * copy of w3 ([n, p]) and the fused kernel's counters. */
+ * times tune->precision terms, or for precision 4 and 5 an f16 activation,
+ * room for an f16 copy of w3 ([n, p]) and the fused kernel's counters. */
 AXON_API int64_t axon_silu_mlp_workspace_bytes(int64_t m, int64_t n, int64_t p, int32_t ab_dtype,
                                                const axon_tune_t* tune);
 
@@ -508,11 +509,14 @@ AXON_API int64_t axon_silu_mlp_workspace_bytes(int64_t m, int64_t n, int64_t p, 
  *   4            f16 (ab_dtype bf16 only): the call converts w3 to an f16 copy
  *                in the workspace and runs the down projection f16 x f16
  *                (both MMA operands must share a type); 3 more mantissa bits
- *                than bf16 for ~3% extra traffic, finite only while |a| < 65504.
+ *                than bf16 for ~3% extra traffic, finite only while |a| < 65504;
+ *   5            as 4, with w3 passed as an f16 [n, p] matrix: the caller's
+ *                f16 copy of W_down, converted once when the weights are
+ *                loaded, so no call converts it again.
  * An fp32 reference at 1e-2 needs precision >= 2 (or 4) at the SwiGLU config
  * and 3 for N(0, 1) weights. In the column/row tensor-parallel form each rank
  * passes its shard (n = inter / G) and sums the fp32 partial outputs.
- * tune->variant at precision 4: 1 / 2 = two launches of the one-CTA / CTA-pair
+ * tune->variant at precision 4 and 5: 1 / 2 = two launches of the one-CTA / CTA-pair
  * GEMM, 3 = both GEMMs in one CTA-pair kernel (m >= 256), 0 (default) = 3
  * while the gate/up GEMM has fewer than 320 256 x 128 tiles, else 2. Other
  * precisions run two launches (variant as axon_gemm's). */

@@ -9,7 +9,9 @@ import torch
 
 
 def baseline_op(a):
-    return np.cumsum(a, axis=-1)
+    # the config's bar is rel 1e-5 against float64: a float32 running sum over
+    # 128256 columns is itself ~7e-5 off, so the reference evaluates in float64
+    return np.cumsum(np.asarray(a, dtype=np.float64), axis=-1)
 
 
 def torch_ref(x):

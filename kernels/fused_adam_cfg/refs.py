@@ -22,6 +22,9 @@ def hyper():
 
 
 def baseline_op(param, grad, exp_avg, exp_avg_sq, step_size, inv_bc2_sqrt, wd):
+    # evaluated in float64: the config's bar is rel 1e-5 against float64
+    param, grad, exp_avg, exp_avg_sq, step_size, inv_bc2_sqrt, wd = (
+        np.asarray(a, dtype=np.float64) for a in (param, grad, exp_avg, exp_avg_sq, step_size, inv_bc2_sqrt, wd))
     g = grad + wd * param
     m = BETA1 * exp_avg + (1.0 - BETA1) * g
     v = BETA2 * exp_avg_sq + (1.0 - BETA2) * (g * g)

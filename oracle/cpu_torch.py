@@ -65,3 +65,11 @@ def softmax_mm(x, w):
 def attention(q, k_t, v):
     e = torch.exp(q @ k_t)
     return (e / torch.sum(e, dim=1, keepdim=True)) @ v
+
+
+def matmul(x, w):
+    return x @ w
+
+
+def rmsnorm_matmul(x, w):
+    return rmsnorm_sum(x) @ w
