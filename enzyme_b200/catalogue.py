@@ -143,8 +143,11 @@ def constraints(spec_name: str, hw_variant: int, dims: dict, itemsize: int,
         out.append(_one(args[1]))
         out.append(_one(args[0]))
     elif spec_name in SCAN_SPECS and hw_variant == 1:
-        # N = CTAs per row cluster
-        out.append(TileConstraint(args[1], extent=8, tile_size=1, require_divisible=True, allowed=(1, 2, 4, 8)))
+        # N = CTAs per row cluster; each CTA stages its slice of the row (a
+        # multiple of 8 elements) in at most 200 KB of shared memory
+        n = dims["n"]
+        allowed = tuple(v for v in (1, 2, 4, 8) if (-(-n // v) + 7) // 8 * 8 * itemsize <= 200 * 1024)
+        out.append(TileConstraint(args[1], extent=8, tile_size=1, require_divisible=True, allowed=allowed or (0,)))
         out.append(_one(args[0]))
     elif spec_name in SCAN_SPECS:
         out.append(TileConstraint(args[1], extent=16384, tile_size=1024, require_divisible=True,

@@ -75,7 +75,7 @@ def test_cli_drop_in_leg_on_gpu(name, sizes, rtol, atol, case, must, tmp_path):
     # the reference's columns first, in order, then this backend's
     assert list(df.columns) == result_columns(spec)
     assert list(df.columns)[:len(_reference_columns(spec))] == _reference_columns(spec)
-    assert len(df) >= 2 and df["error"].isna().all(), df[["hw_variant", "error"]]
+    assert len(df) >= 2 and df["error"].isna().all(), df[["hw_variant", "tile_variant", "error"]].to_string()
     assert df["median_ms"].notna().all() and (df["median_ms"] > 0).all()
     assert (df["mode"] == "device").all() and (df["n_gpus"] == 1).all()
     correct = df["correct"].astype(str).str.lower() == "true"
@@ -95,7 +95,7 @@ def test_cli_drop_in_leg_on_gpu(name, sizes, rtol, atol, case, must, tmp_path):
 # one reference eval case (eval/sizes.json) per implemented spec family, run
 # the way `make <kernel>_<case>` runs it
 DRIVER_CASES = ["rmsnorm_h4096", "layernorm_llama70b", "softmax_sq1k", "rope_llama3_8b", "cumsum_nucleus",
-                "fused_adam_opt_1m", "matmul_sq1k", "rmsnorm_matmul_sq1k", "silu_mlp_sq1k", "qkv_cte_vision_l4",
+                "fused_adam_opt_1m", "matmul_sq1k", "rmsnorm_matmul_sq1k", "qkv_cte_vision_l4",
                 "softmax_mm_sq1k", "attention_nkilib_d128"]
 
 
@@ -115,3 +115,26 @@ def test_case_driver_on_gpu(case, tmp_path):
         assert (tmp_path / "out" / "winners" / f"{kernel}_{cid}_case.py").is_file()
         text = (tmp_path / "winners" / f"{kernel}_{cid}.py").read_text()
         assert "measured on   : NVIDIA B200" in text and "us median (on-device, correct" in text
+
+
+def test_case_driver_fails_loud_on_silu_mlp_sq1k(tmp_path):
+    """silu_mlp sq1k (eval/sizes.json: m = n = k = p = 1024, every input
+    N(0, 1)) is a bench-only case checked at Axon's permissive default
+    rtol = atol = 2e-2 (src/axon/cli.py:59-62). Its outputs have a standard
+    deviation of about 23000 and arise from sums of 1024 terms of about 700,
+    so a few outputs near zero carry an fp32 accumulation error of a few
+    hundredths: every variant, including the three-term (near-fp32)
+    activation, is verified wrong at the 0.02 absolute floor. Axon's winner
+    rule then fails the case loudly (src/axon/winner.py pick_winner: "Only
+    when every timed variant is verified incorrect does this fail loud");
+    the case driver must do the same, after benching and publishing every
+    key."""
+    kernel, cid = "silu_mlp", "sq1k"
+    r = subprocess.run([sys.executable, "-m", "enzyme_b200.cases", "run", f"{kernel}_{cid}", "--warmup", "3",
+                        "--bench", "10"], cwd=tmp_path, env=_env(), capture_output=True, text=True, timeout=900)
+    assert r.returncode != 0
+    assert "failed on-device correctness" in r.stdout + r.stderr, r.stdout[-3000:] + r.stderr[-3000:]
+    df = pd.read_csv(tmp_path / "out" / f"{kernel}_{cid}.csv")
+    assert len(df) >= 5 and df["error"].isna().all(), df[["hw_variant", "tile_variant", "error"]].to_string()
+    assert df["median_ms"].notna().all() and (df["median_ms"] > 0).all()
+    assert not (df["correct"].astype(str).str.lower() == "true").any()

@@ -223,3 +223,85 @@ def test_tp_flag_wait_times_out(cuda_device):
     N.check(N.lib().axon_tp_status(s))  # the record was cleared
     a = torch.randn(256, 256, device=cuda_device).bfloat16()
     assert torch.isfinite(ops.gemm(a, a, out_dtype=torch.float32)).all()
+
+
+CONFIG_ROW_STRIDE = 61
+
+
+def _config_tensors(dev):
+    """x [4096, 4096] and the full W_gate, W_up [4096, 14336], W_down [14336, 4096]
+    (bf16, N(0, 0.02) weights), drawn from one seeded generator on `dev`."""
+    m, h, inter = 4096, 4096, 14336
+    g = torch.Generator(device=dev).manual_seed(11)
+    x = torch.randn(m, h, device=dev, generator=g).bfloat16()
+    full = [(0.02 * torch.randn(*shape, device=dev, generator=g)).bfloat16()
+            for shape in ((h, inter), (h, inter), (inter, h))]
+    return x, full
+
+
+def _config_rank(rank, world, port, q):
+    """One rank of the fused path at the BASELINE SwiGLU config (m 4096,
+    hidden 4096, inter 14336): the same seeded full weights on every rank,
+    this rank's column/row shard, three steps; returns the sampled rows and a
+    checksum of the raw output bits."""
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from enzyme_b200 import ops, tp
+
+        dev = torch.device("cuda", rank)
+        m, h = 4096, 4096
+        x, full = _config_tensors(dev)
+        shards = tp.shard_swiglu(*full, rank, world)
+        f = tp.FusedTPSwiGLU(*shards, m=m, slabs=1)
+        try:
+            ys = [f.forward(x).clone() for _ in range(3)]
+            torch.cuda.synchronize()
+        finally:
+            f.close()
+        f.status()
+        ops.gemm_status()
+        repeat_equal = all(torch.equal(ys[0], y) for y in ys[1:])
+        words = ys[0].view(torch.int16).to(torch.int64)
+        checksum = (int(words.sum()), int((words * torch.arange(1, h + 1, device=dev)).sum()))
+        rows = torch.arange(0, m, CONFIG_ROW_STRIDE, device=dev)
+        q.put((rank, ys[0][rows].float().cpu().numpy(), repeat_equal, checksum))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_fused_tp_swiglu_config_shape_all_gpus():
+    """The fused tensor-parallel path at the BASELINE config on every GPU of
+    the box (the largest power of two up to 8): sampled rows against the
+    float64 oracle of the unsharded MLP at rtol = atol = 1e-2, bit-identical
+    outputs on every rank and over repeated steps."""
+    import torch.multiprocessing as mp
+
+    from oracle import f64
+
+    world = 1 << (min(torch.cuda.device_count(), 8).bit_length() - 1)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_config_rank, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted((q.get(timeout=600) for _ in range(world)), key=lambda t: t[0])
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs)
+    x, full = _config_tensors(torch.device("cuda", 0))  # the same draws as every rank's
+    rows = torch.arange(0, x.shape[0], CONFIG_ROW_STRIDE, device=x.device)
+    want = f64.silu_mlp(x[rows].float().cpu().numpy(), *(w.float().cpu().numpy() for w in full))
+    del x, full
+    for rank, y, repeat_equal, checksum in res:
+        assert repeat_equal, f"rank {rank}: repeated steps gave different bits"
+        assert checksum == res[0][3], f"rank {rank} holds a different output than rank 0"
+        np.testing.assert_allclose(y, want, rtol=1e-2, atol=1e-2)
