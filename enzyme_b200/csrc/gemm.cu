@@ -1641,7 +1641,8 @@ __global__ void __launch_bounds__(192, 1)
 
 constexpr int kSchedRing = 8;
 constexpr int kMlpLocal = 0, kMlpScatter = 1, kMlpStep = 2;
-constexpr int kStepColsPerTile = 1024;  // phase C: output columns per tile
+constexpr int kStepCommSmem = 160 * 1024;  // kMlpStep reduction CTAs: staging bytes at most
+constexpr int kStepCommCtas = 8;           // kMlpStep: default number of reduction CTAs
 
 struct MlpParams {
   void* c;                  // kMlpLocal: y [m, ldc]
@@ -1663,6 +1664,8 @@ struct MlpParams {
   void* y[kMaxPeers];       // each rank's output [m, n2] bf16
   int epoch;
   int group;                // row blocks per group of the tile order
+  int gemm_pairs;           // kMlpStep: clusters [0, gemm_pairs) run tiles, the rest reduce
+  int step_cols;            // kMlpStep: output columns per reduction unit (a multiple of 8)
 };
 
 __device__ __forceinline__ int ld_acquire_gpu_s32(const int* p) {
@@ -1741,10 +1744,8 @@ struct MlpTile {
 };
 
 struct MlpGrid {
-  int rb, ta_row, tb_row, tc_row, group;
+  int rb, ta_row, tb_row, group;
   __device__ int tiles() const { return rb * (ta_row + tb_row); }  // phases A and B: the ring's tiles
-  // phase C: units of 8 of this rank's rows x kStepColsPerTile columns, one warp each
-  __device__ int c_units(int world) const { return rb * tc_row * (32 / world); }
 };
 
 // Row groups of `group` 256-row blocks; the tile sequence is A0, A1, B0, A2,
@@ -1790,6 +1791,148 @@ __device__ __forceinline__ MlpTile mlp_tile(int t, const MlpGrid& g) {
   return x;  // not reached for t < tiles()
 }
 
+// Output columns per reduction unit of a whole tensor-parallel step: the
+// widest multiple of 8 (at most p) whose double-buffered staging -- world
+// f16 partial chunks and one bf16 output chunk per buffer -- fits
+// kStepCommSmem.
+__host__ __device__ __forceinline__ int step_cols(int world, int64_t p) {
+  int64_t ch = kStepCommSmem / (4 * (static_cast<int64_t>(world) + 1)) / 8 * 8;
+  if (ch > p) ch = p;
+  return static_cast<int>(ch);
+}
+
+// kMlpStep owner reduction, run by the reduction CTAs (clusters gemm_pairs
+// and up) while the other clusters run the GEMM tiles. Unit u of this rank
+// is (local row u / chunks, column chunk u % chunks); reduction CTA j takes
+// units j, j + C, ... (C = reduction CTAs) in order, i.e. row block by row
+// block as their partials complete. Per unit: thread 0 waits (bounded) until
+// every rank's partials of the unit's 256-row block have arrived
+// (arrive[rank][block], released by the phase-B epilogue warps of all
+// ranks), then fetches the world partial chunks from this rank's inbox with
+// 1-D bulk copies into one of two staging buffers, two units ahead; all 192
+// threads sum them in fp32 in rank order, round once to bf16 into a staging
+// output chunk, and thread 0 pushes that chunk to every rank's output with
+// 1-D bulk copies (global <- shared, no multicast). At the end the CTA waits
+// for its copies to complete, fences at system scope and adds its unit
+// count to every rank's done counter. Waits are bounded; a wait that gives
+// up records AXON_E_TIMEOUT in the device error word.
+__device__ void mlp_step_reduce(const MlpParams& p, uint8_t* smem, int cta, int ctas) {
+  const int W = p.world;
+  const int CH = p.step_cols;
+  const int chunks = (p.n2 + CH - 1) / CH;
+  const int rows_local = p.m / W;        // this rank's rows
+  const int rows_per_block = 256 / W;    // of them in each 256-row block
+  const int64_t slot = static_cast<int64_t>(rows_local) * p.n2;
+  const int tb_row = (p.n2 + 255) / 256;
+  const int target = p.epoch * 32 * tb_row;  // arrival count of a complete row block (wraps like the counts)
+  const int units = rows_local * chunks;
+  const int mine = units > cta ? (units - cta + ctas - 1) / ctas : 0;
+  __half* in = reinterpret_cast<__half*>(smem);                                  // [2][W][CH]
+  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(in + 2 * static_cast<int64_t>(W) * CH);  // [2][CH]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(out + 2 * CH);                      // 8-byte aligned: CH % 8 == 0
+  // this role's own flags: the staging buffers may cover the tile roles'
+  // shared-memory words
+  __shared__ int ok_s;
+  __shared__ int abort_s;
+  volatile int* abort_flag = &abort_s;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    ok_s = 1;
+    abort_s = 0;
+  }
+  __syncthreads();
+  int ready_block = -1;  // thread 0: the last row block whose arrival was seen
+  auto fetch = [&](int i) -> bool {  // thread 0: unit i of this CTA into buffer i & 1
+    const int u = cta + i * ctas;
+    const int lr = u / chunks, c = u - (u / chunks) * chunks;
+    const int blk = lr / rows_per_block;
+    if (blk > ready_block) {
+      if (!wait_count<true>(p.arrive[p.peer_rank] + blk, target, abort_flag)) return false;
+      ready_block = blk;
+      asm volatile("fence.proxy.async.global;" ::: "memory");  // peers' generic stores -> bulk-copy reads
+    }
+    const int col0 = c * CH;
+    const int cols = p.n2 - col0 < CH ? p.n2 - col0 : CH;
+    const uint32_t bytes = static_cast<uint32_t>(cols) * 2;
+    __half* dst = in + static_cast<int64_t>(i & 1) * W * CH;
+    mbar_expect_tx(&bar[i & 1], bytes * W);
+    for (int s = 0; s < W; ++s)
+      asm volatile(
+          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+              smem_u32(dst + s * CH)),
+          "l"(p.inbox + s * slot + static_cast<int64_t>(lr) * p.n2 + col0), "r"(bytes), "r"(smem_u32(&bar[i & 1]))
+          : "memory");
+    return true;
+  };
+  if (threadIdx.x == 0) {
+    bool ok = true;
+    for (int i = 0; i < 2 && i < mine && ok; ++i) ok = fetch(i);
+    if (!ok) ok_s = 0;
+  }
+  __syncthreads();
+  int done = 0;
+  for (int i = 0; i < mine && ok_s; ++i) {
+    const int u = cta + i * ctas;
+    const int lr = u / chunks, c = u - (u / chunks) * chunks;
+    const int col0 = c * CH;
+    const int cols = p.n2 - col0 < CH ? p.n2 - col0 : CH;
+    // one thread waits for the unit's partials (and for the copies of unit
+    // i - 2 to have read its output chunk); the barrier hands both on
+    if (threadIdx.x == 0) {
+      if (mbar_wait(&bar[i & 1], static_cast<uint32_t>((i >> 1) & 1), abort_flag))
+        asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+      else
+        ok_s = 0;
+    }
+    __syncthreads();
+    if (!ok_s) break;
+    const __half* src = in + static_cast<int64_t>(i & 1) * W * CH;
+    __nv_bfloat16* o = out + (i & 1) * CH;
+    for (int pk = threadIdx.x; pk < cols / 8; pk += blockDim.x) {
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int s = 0; s < W; ++s) {  // fixed rank order: the same sum on every run
+        Vec<__half> v;
+        v.u = *reinterpret_cast<const uint4*>(src + s * CH + pk * 8);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] += __half2float(v.e[e]);
+      }
+      Vec<__nv_bfloat16> r;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) r.e[e] = __float2bfloat16_rn(acc[e]);
+      *reinterpret_cast<uint4*>(o + pk * 8) = r.u;
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic smem accesses -> bulk copies
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const int64_t grow = (static_cast<int64_t>(lr >> 3) * W + p.peer_rank) * 8 + (lr & 7);
+      for (int d = 0; d < W; ++d)
+        asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(
+                         static_cast<__nv_bfloat16*>(p.y[d]) + grow * p.n2 + col0),
+                     "r"(smem_u32(o)), "r"(static_cast<uint32_t>(cols) * 2)
+                     : "memory");
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      if (i + 2 < mine && !fetch(i + 2)) ok_s = 0;
+    }
+    ++done;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // every push has landed
+    if (!*abort_flag && ok_s && done == mine && mine > 0) {
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+      __threadfence_system();
+      for (int d = 0; d < W; ++d)
+        asm volatile("red.relaxed.sys.global.add.s32 [%0], %1;" ::"l"(p.done[d]), "r"(mine) : "memory");
+    } else if (done < mine) {
+      // a wait gave up: fetches issued ahead may still be landing in this
+      // CTA's shared memory (failure path only)
+      for (int k = 0; k < 1000; ++k) __nanosleep(1000);
+    }
+  }
+}
+
 template <typename TC, int MODE>
 __global__ void __launch_bounds__(192, 1)
     swiglu_fused_pair(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmWg,
@@ -1822,8 +1965,9 @@ __global__ void __launch_bounds__(192, 1)
   grid.rb = (p.m + 2 * BM - 1) / (2 * BM);
   grid.ta_row = (p.n1 + BH - 1) / BH;
   grid.tb_row = (p.n2 + BN - 1) / BN;
-  grid.tc_row = MODE == kMlpStep ? (p.n2 + kStepColsPerTile - 1) / kStepColsPerTile : 0;
   grid.group = p.group;
+  // kMlpStep: clusters from gemm_pairs on run the owner reduction, not tiles
+  const bool reducer = MODE == kMlpStep && static_cast<int>(blockIdx.x >> 1) >= p.gemm_pairs;
   const int tiles = grid.tiles();
   const int kb_a = (p.k1 + BK - 1) / BK, kb_b = (p.n1 + BK - 1) / BK;
   int* counter = p.ready + grid.rb;
@@ -1846,7 +1990,7 @@ __global__ void __launch_bounds__(192, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
-  if (warp == 1) {
+  if (warp == 1 && !reducer) {
     asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(TMEM_COLS)
                  : "memory");
@@ -1855,6 +1999,15 @@ __global__ void __launch_bounds__(192, 1)
   }
   __syncthreads();
   cluster_barrier();
+  if constexpr (MODE == kMlpStep) {
+    if (reducer) {  // both CTAs of the cluster: no tiles, no tensor memory
+      mlp_step_reduce(p, smem, static_cast<int>(blockIdx.x) - 2 * p.gemm_pairs,
+                      static_cast<int>(gridDim.x) - 2 * p.gemm_pairs);
+      __syncthreads();
+      cluster_barrier();
+      return;
+    }
+  }
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -1971,89 +2124,6 @@ __global__ void __launch_bounds__(192, 1)
     // ---------------- epilogue (both CTAs, their own 128 rows) ----------------
     const int q = warp & 3;
     int mm = 0;
-    // Phase C (kMlpStep) in units of 8 of this rank's rows x
-    // kStepColsPerTile columns, one warp each, claimed from a counter: sum
-    // the world partials in fp32 in rank order, round once to bf16, store to
-    // every rank's output, count done on every rank. Between its GEMM tiles a
-    // warp takes one unit whose rows have all arrived (no waiting); after the
-    // last tile it takes units until none is left.
-    const int W = p.world > 0 ? p.world : 1;
-    const int upb = 32 / W;                                 // units per row block and column chunk
-    const int c_units = grid.c_units(W);
-    const int c_target = p.epoch * 32 * grid.tb_row;        // arrival count of a complete row block
-    int* c_counter = p.ready + grid.rb + 1;
-    auto c_claim = [&](bool block) -> int {                 // unit, -1 none ready now, -2 none left
-      int u = -2;
-      if (lane == 0) {
-        if (block) {
-          u = *abort_flag ? c_units : atomicAdd(c_counter, 1);
-          if (u >= c_units || !wait_count<true>(p.arrive[p.peer_rank] + u / (grid.tc_row * upb), c_target,
-                                                abort_flag))
-            u = -2;
-        } else {
-          for (int tries = 0; tries < 4; ++tries) {
-            const int v = ld_acquire_gpu_s32(c_counter);
-            if (v >= c_units) break;
-            u = -1;
-            if (ld_acquire_sys_s32(p.arrive[p.peer_rank] + v / (grid.tc_row * upb)) - c_target < 0) break;
-            if (atomicCAS(c_counter, v, v + 1) == v) {
-              u = v;
-              break;
-            }
-          }
-        }
-      }
-      return __shfl_sync(0xffffffffu, u, 0);
-    };
-    auto c_work = [&](int u) {
-      const int r = u / (grid.tc_row * upb);
-      const int rem = u - r * grid.tc_row * upb;
-      const int c = rem / upb, sub = rem - (rem / upb) * upb;
-      const int64_t lr0 = static_cast<int64_t>(r) * (2 * BM / W) + sub * 8;
-      const int col0 = c * kStepColsPerTile;
-      const int ncols = p.n2 - col0 < kStepColsPerTile ? p.n2 - col0 : kStepColsPerTile;
-      const int pkr = ncols / 8;  // 16-byte packets per row
-      const int total = 8 * pkr;
-      const int64_t slot = static_cast<int64_t>(p.rows_per_owner) * p.n2;
-      // two packets per lane per pass, every source's load issued before any sum
-      for (int idx0 = lane; idx0 < total; idx0 += 64) {
-        Vec<__half> v[2][kMaxPeers];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int idx = idx0 + h * 32;
-          const int64_t lr = lr0 + idx / pkr;
-          const int col = col0 + (idx % pkr) * 8;
-#pragma unroll
-          for (int s = 0; s < kMaxPeers; ++s)  // written by other GPUs: loads that skip cached copies
-            if (s < W && idx < total)
-              v[h][s].u = __ldcv(reinterpret_cast<const uint4*>(p.inbox + s * slot + lr * p.n2 + col));
-        }
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int idx = idx0 + h * 32;
-          if (idx >= total) break;
-          const int64_t lr = lr0 + idx / pkr;
-          const int col = col0 + (idx % pkr) * 8;
-          float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-          for (int s = 0; s < kMaxPeers; ++s)  // fixed rank order
-            if (s < W)
-#pragma unroll
-              for (int e = 0; e < 8; ++e) acc[e] += __half2float(v[h][s].e[e]);
-          Vec<__nv_bfloat16> o;
-#pragma unroll
-          for (int e = 0; e < 8; ++e) o.e[e] = __float2bfloat16_rn(acc[e]);
-          const int64_t grow = ((lr >> 3) * W + p.peer_rank) * 8 + (lr & 7);
-          for (int d = 0; d < W; ++d) st_vec(static_cast<__nv_bfloat16*>(p.y[d]) + grow * p.n2 + col, o);
-        }
-      }
-      __threadfence_system();
-      __syncwarp();
-      if (lane < W) red_release_sys_add(p.done[lane], 1);
-    };
-    (void)c_claim;
-    (void)c_work;
-    (void)c_target;
     for (int i = 0;; ++i) {
       const int t = next_tile(i, false);  // every lane reads the slot ...
       __syncwarp();                       // ... before one arrival frees it for the whole warp
@@ -2129,19 +2199,6 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_u32(smem_u32(&tempty[buf]), 0), 1);
-      if constexpr (MODE == kMlpStep) {
-        const int u = c_claim(false);
-        if (u >= 0) c_work(u);
-      }
-    }
-    if constexpr (MODE == kMlpStep) {
-      // ---- phase C, the rest: claim units until none is left, waiting
-      // (bounded) for each unit's rows to arrive from every rank
-      for (;;) {
-        const int u = c_claim(true);
-        if (u < 0) break;
-        c_work(u);
-      }
     }
   }
 
@@ -2298,8 +2355,11 @@ template <typename TC, int MODE>
 int launch_swiglu_fused(const CUtensorMap& mx, const CUtensorMap& mg, const CUtensorMap& mu, const CUtensorMap& ma,
                         const CUtensorMap& md, const MlpParams& mp, cudaStream_t s) {
   constexpr int STAGE = A_BYTES + 128 * BK * 2;
-  const size_t smem =
-      static_cast<size_t>(mp.stages) * STAGE + 1024 + 512 + (MODE != kMlpLocal ? kPeerStageBytes : 0);
+  size_t smem = static_cast<size_t>(mp.stages) * STAGE + 1024 + 512 + (MODE != kMlpLocal ? kPeerStageBytes : 0);
+  if (MODE == kMlpStep) {  // the reduction CTAs stage in the same dynamic shared memory
+    const size_t comm = 1024 + 4 * (static_cast<size_t>(mp.world) + 1) * mp.step_cols + 16;
+    if (comm > smem) smem = comm;
+  }
   auto kern = swiglu_fused_pair<TC, MODE>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return fail(AXON_E_LAUNCH, "axon_silu_mlp: smem attribute: %s", cudaGetErrorString(e));
@@ -2328,12 +2388,21 @@ int launch_swiglu_fused(const CUtensorMap& mx, const CUtensorMap& mg, const CUte
   const int64_t tiles = rb * ((mp.n1 + 127) / 128 + (mp.n2 + 255) / 256);
   int64_t pairs = pairs_cap;
   if (mp.max_ctas > 0 && mp.max_ctas / 2 < pairs) pairs = mp.max_ctas / 2 > 0 ? mp.max_ctas / 2 : 1;
+  MlpParams lp = mp;
+  int64_t extra = 0;  // kMlpStep: reduction clusters beside the GEMM clusters
+  if (MODE == kMlpStep) {
+    extra = (lp.gemm_pairs + 1) / 2;  // gemm_pairs carries the requested reduction CTAs here
+    if (extra < 1) extra = 1;
+    if (pairs - extra < 1) return fail(AXON_E_ARG, "axon_tp_mlp_step: no CTA pairs left for the GEMM tiles");
+    pairs -= extra;
+  }
   if (tiles < pairs) pairs = tiles;
+  if (MODE == kMlpStep) lp.gemm_pairs = static_cast<int>(pairs);
   // row-block counters and the tile counter start at zero every call
   e = cudaMemsetAsync(mp.ready, 0, static_cast<size_t>(rb + 2) * sizeof(int), s);
   if (e != cudaSuccess) return fail(AXON_E_CUDA, "axon_silu_mlp: counter reset: %s", cudaGetErrorString(e));
-  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
-  e = cudaLaunchKernelEx(&cfg, kern, mx, mg, mu, ma, md, mp);
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * (pairs + extra)), 1, 1);
+  e = cudaLaunchKernelEx(&cfg, kern, mx, mg, mu, ma, md, lp);
   if (e != cudaSuccess) return fail(AXON_E_LAUNCH, "axon_silu_mlp: %s", cudaGetErrorString(e));
   return launch_status("axon_silu_mlp");
 }
@@ -2394,13 +2463,18 @@ int swiglu_fused_impl(const void* x, const void* w1, const void* w2, const void*
     }
     mp.inbox = static_cast<const __half*>(step->inbox);
     mp.epoch = step->epoch;
+    // the reduction CTAs requested (tune.split, default kStepCommCtas; the
+    // launch turns this into clusters) and the columns of one unit
+    mp.gemm_pairs = t.split > 0 ? t.split : kStepCommCtas;
+    mp.step_cols = step_cols(world, n2);
   }
   mp.act = act;
   mp.ready = counters;
   // tile order: two groups for one GPU (the weights are read twice), groups
   // of four row blocks for a tensor-parallel step (more overlap of the down
-  // projection's traffic with gate/up tiles; the shard's weights are small)
-  mp.group = step != nullptr ? 4 : 8;
+  // projection's traffic with gate/up tiles; the shard's weights are small);
+  // tune.rows_per_cta overrides the group size of a step
+  mp.group = step != nullptr ? (t.rows_per_cta > 0 ? t.rows_per_cta : 4) : 8;
   mp.m = static_cast<int>(m);
   mp.n1 = static_cast<int>(n1);
   mp.k1 = static_cast<int>(k1);
@@ -2899,9 +2973,10 @@ extern "C" int axon_tp_mlp_partial(const void* x, const void* w_gate, const void
 
 extern "C" int64_t axon_tp_step_done_per_epoch(int32_t world, int64_t m, int64_t p) {
   if (world < 1 || m < 0 || p < 0) return fail(AXON_E_ARG, "axon_tp_step_done_per_epoch: bad argument");
-  // every phase-C unit (8 rows of an owner x kStepColsPerTile columns) counts
-  // once on every rank: world owners x (m / 256 row blocks x chunks x 32 / world)
-  return static_cast<int64_t>(32) * ((m + 255) / 256) * ((p + kStepColsPerTile - 1) / kStepColsPerTile);
+  // every reduction unit (one owned row x one column chunk) counts once on
+  // every rank: world owners x m / world rows x chunks
+  const int ch = step_cols(world, p);
+  return ch > 0 ? m * ((p + ch - 1) / ch) : 0;
 }
 
 extern "C" int axon_tp_mlp_step(const void* x, const void* w_gate, const void* w_up, const void* w_down_h,
