@@ -156,6 +156,9 @@ SIGNATURES: dict[str, tuple] = {
     "axon_tp_mlp_step": (
         _I32, [_P, _P, _P, _P, _P, _I64, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I64, _I64, _I64, _I64, _TUNE, _P]
     ),
+    "axon_tp_mlp_step_multicast": (
+        _I32, [_P, _P, _P, _P, _P, _I64, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I64, _I64, _I64, _I64, _TUNE, _P]
+    ),
     "axon_tp_wait_count": (_I32, [_P, _I32, _P]),
     "axon_tp_signal": (_I32, [_P, _I32, _I32, _I32, _P]),
     "axon_tp_wait": (_I32, [_P, _I32, _I32, _P]),

@@ -1509,7 +1509,7 @@ __global__ void __launch_bounds__(192, 1)
     tc_commit_to(smem_u32(drain));
     volatile int never = 0;
     mbar_wait(drain, 0, &never);
-  } else if (warp >= 2) {
+  } else if (warp >= 2 && warp < 6) {
     // ---------------- epilogue (both CTAs, their own 128 rows) ----------------
     const int q = warp & 3;
     int local = 0;
@@ -1621,14 +1621,29 @@ __global__ void __launch_bounds__(192, 1)
 // tiles never wait, so every wait ends without assuming co-residency.
 //
 // Modes: kMlpLocal writes y; kMlpScatter writes each f16 partial row of y to
-// its owner rank's inbox (axon_tp_mlp_partial); kMlpStep (axon_tp_mlp_step)
-// is a whole tensor-parallel step: rows are owned in 8-row granules dealt to
-// the ranks in turn, each phase-B epilogue warp releases its rows' arrival
-// counts into the owners' counters (system scope, over NVLink), and phase-C
-// tiles -- claimed after every phase-B tile -- wait for all ranks' partials of
-// a row block of this rank's rows, sum them in fp32 in rank order, round once
-// to bf16 and store them into every rank's output, then count themselves done
-// on every rank. A phase-C wait depends only on other ranks' phase-B tiles,
+// its owner rank's inbox (axon_tp_mlp_partial). kMlpStep (axon_tp_mlp_step)
+// and kMlpStepMC (axon_tp_mlp_step_multicast) run a whole tensor-parallel
+// step: rows are owned in 8-row granules dealt to the ranks in turn, and two
+// reduction warps per CTA (warps 6 and 7, beside the tile roles) claim units
+// of this rank's rows -- one row x kStepCols columns, in row-block order --
+// wait (bounded) until every rank's partials of the unit's 256-row block have
+// arrived, and resolve the all-reduce for them while the GEMM tiles go on:
+//   kMlpStep    each phase-B epilogue warp writes its f16 partial rows into
+//               the owners' inboxes over NVLink and releases them into the
+//               owners' arrival counts; a reduction warp sums the world
+//               inbox copies in fp32 in rank order, rounds once to bf16 and
+//               stores the row into every rank's output;
+//   kMlpStepMC  each phase-B epilogue warp writes its f16 partial rows into
+//               this rank's own partial buffer (bound to an NVLink multicast
+//               object) and releases them into every rank's arrival counts;
+//               a reduction warp reads each 16-byte packet of an owned row
+//               once through the multicast address with multimem.ld_reduce
+//               (the NVSwitch adds the world copies, accumulating in fp32),
+//               rounds to bf16 and stores it once with multimem.st to the
+//               output's multicast address, which the switch writes into
+//               every rank's output.
+// At the end each reduction warp adds its unit count to every rank's done
+// count. A reduction wait depends only on phase-B tiles (of every rank),
 // which depend only on their own phase A: no cycle across GPUs. Arrival and
 // done counts accumulate over steps (epoch * per-step count), so nothing is
 // reset between steps.
@@ -1640,9 +1655,11 @@ __global__ void __launch_bounds__(192, 1)
 // CTAs) frees a slot by arriving on the leader's slot barrier.
 
 constexpr int kSchedRing = 8;
-constexpr int kMlpLocal = 0, kMlpScatter = 1, kMlpStep = 2;
-constexpr int kStepCommSmem = 160 * 1024;  // kMlpStep reduction CTAs: staging bytes at most
-constexpr int kStepCommCtas = 8;           // kMlpStep: default number of reduction CTAs
+constexpr int kMlpLocal = 0, kMlpScatter = 1, kMlpStep = 2, kMlpStepMC = 3;
+constexpr int kStepCols = 1024;      // reduction unit: one owned row x this many columns
+constexpr int kStepWarps = 2;        // reduction warps per CTA (kMlpStep, kMlpStepMC)
+
+__host__ __device__ constexpr int mlp_threads(int mode) { return mode >= kMlpStep ? 192 + 32 * kStepWarps : 192; }
 
 struct MlpParams {
   void* c;                  // kMlpLocal: y [m, ldc]
@@ -1664,8 +1681,10 @@ struct MlpParams {
   void* y[kMaxPeers];       // each rank's output [m, n2] bf16
   int epoch;
   int group;                // row blocks per group of the tile order
-  int gemm_pairs;           // kMlpStep: clusters [0, gemm_pairs) run tiles, the rest reduce
-  int step_cols;            // kMlpStep: output columns per reduction unit (a multiple of 8)
+  // kMlpStepMC
+  __half* part;             // this rank's partial of y [m, n2] f16 (bound to a multicast object)
+  const __half* part_mc;    // the partials' multicast address
+  __nv_bfloat16* y_mc;      // the outputs' multicast address
 };
 
 __device__ __forceinline__ int ld_acquire_gpu_s32(const int* p) {
@@ -1791,150 +1810,129 @@ __device__ __forceinline__ MlpTile mlp_tile(int t, const MlpGrid& g) {
   return x;  // not reached for t < tiles()
 }
 
-// Output columns per reduction unit of a whole tensor-parallel step: the
-// widest multiple of 8 (at most p) whose double-buffered staging -- world
-// f16 partial chunks and one bf16 output chunk per buffer -- fits
-// kStepCommSmem.
-__host__ __device__ __forceinline__ int step_cols(int world, int64_t p) {
-  int64_t ch = kStepCommSmem / (4 * (static_cast<int64_t>(world) + 1)) / 8 * 8;
-  if (ch > p) ch = p;
-  return static_cast<int>(ch);
+// 16 bytes through a multicast address: the NVSwitch reads the packet from
+// every GPU bound to the object and returns the sum (f16 pairs added in
+// fp32, rounded once to f16).
+__device__ __forceinline__ uint4 multimem_ld_add_f16x8(const __half* mc) {
+  uint4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.f16x2 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(mc)
+               : "memory");
+  return v;
 }
 
-// kMlpStep owner reduction, run by the reduction CTAs (clusters gemm_pairs
-// and up) while the other clusters run the GEMM tiles. Unit u of this rank
-// is (local row u / chunks, column chunk u % chunks); reduction CTA j takes
-// units j, j + C, ... (C = reduction CTAs) in order, i.e. row block by row
-// block as their partials complete. Per unit: thread 0 waits (bounded) until
-// every rank's partials of the unit's 256-row block have arrived
-// (arrive[rank][block], released by the phase-B epilogue warps of all
-// ranks), then fetches the world partial chunks from this rank's inbox with
-// 1-D bulk copies into one of two staging buffers, two units ahead; all 192
-// threads sum them in fp32 in rank order, round once to bf16 into a staging
-// output chunk, and thread 0 pushes that chunk to every rank's output with
-// 1-D bulk copies (global <- shared, no multicast). At the end the CTA waits
-// for its copies to complete, fences at system scope and adds its unit
-// count to every rank's done counter. Waits are bounded; a wait that gives
-// up records AXON_E_TIMEOUT in the device error word.
-__device__ void mlp_step_reduce(const MlpParams& p, uint8_t* smem, int cta, int ctas) {
+// 16 bytes stored once to a multicast address; the switch writes them into
+// every GPU bound to the object (bits only: the .f32 form is the 16-byte
+// store).
+__device__ __forceinline__ void multimem_st_b128(void* mc, uint4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+// The reduction warps of a whole tensor-parallel step (kMlpStep, kMlpStepMC;
+// see above). Units are claimed from counters[rb + 1] in order, so the
+// row blocks a warp waits for only grow; a wait that gives up aborts the CTA
+// and records AXON_E_TIMEOUT.
+template <int MODE>
+__device__ void mlp_step_reduce_warp(const MlpParams& p, int rb, int lane, volatile int* abort_flag) {
   const int W = p.world;
-  const int CH = p.step_cols;
-  const int chunks = (p.n2 + CH - 1) / CH;
-  const int rows_local = p.m / W;        // this rank's rows
-  const int rows_per_block = 256 / W;    // of them in each 256-row block
-  const int64_t slot = static_cast<int64_t>(rows_local) * p.n2;
-  const int tb_row = (p.n2 + 255) / 256;
-  const int target = p.epoch * 32 * tb_row;  // arrival count of a complete row block (wraps like the counts)
+  const int rows_local = p.m / W;
+  const int rows_per_block = 256 / W;
+  const int chunks = (p.n2 + kStepCols - 1) / kStepCols;
   const int units = rows_local * chunks;
-  const int mine = units > cta ? (units - cta + ctas - 1) / ctas : 0;
-  __half* in = reinterpret_cast<__half*>(smem);                                  // [2][W][CH]
-  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(in + 2 * static_cast<int64_t>(W) * CH);  // [2][CH]
-  uint64_t* bar = reinterpret_cast<uint64_t*>(out + 2 * CH);                      // 8-byte aligned: CH % 8 == 0
-  // this role's own flags: the staging buffers may cover the tile roles'
-  // shared-memory words
-  __shared__ int ok_s;
-  __shared__ int abort_s;
-  volatile int* abort_flag = &abort_s;
-  if (threadIdx.x == 0) {
-    mbar_init(&bar[0], 1);
-    mbar_init(&bar[1], 1);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    ok_s = 1;
-    abort_s = 0;
-  }
-  __syncthreads();
-  int ready_block = -1;  // thread 0: the last row block whose arrival was seen
-  auto fetch = [&](int i) -> bool {  // thread 0: unit i of this CTA into buffer i & 1
-    const int u = cta + i * ctas;
+  const int tb_row = (p.n2 + 255) / 256;
+  // arrival count of a complete row block: kMlpStep counts granules into the
+  // owner (32 per tile, over the world ranks' tiles); kMlpStepMC counts every
+  // epilogue warp of every rank's tiles into every rank
+  const int per_block = MODE == kMlpStepMC ? W * tb_row * 8 : 32 * tb_row;
+  const int target = p.epoch * per_block;
+  const int64_t slot = static_cast<int64_t>(rows_local) * p.n2;
+  int* ctr = p.ready + rb + 1;
+  int seen = -1, mine = 0;
+  bool ok = true;
+  for (;;) {
+    int u = 0;
+    if (lane == 0) u = *abort_flag ? units : atomicAdd(ctr, 1);
+    u = __shfl_sync(0xffffffffu, u, 0);
+    if (u >= units) break;
     const int lr = u / chunks, c = u - (u / chunks) * chunks;
     const int blk = lr / rows_per_block;
-    if (blk > ready_block) {
-      if (!wait_count<true>(p.arrive[p.peer_rank] + blk, target, abort_flag)) return false;
-      ready_block = blk;
-      asm volatile("fence.proxy.async.global;" ::: "memory");  // peers' generic stores -> bulk-copy reads
-    }
-    const int col0 = c * CH;
-    const int cols = p.n2 - col0 < CH ? p.n2 - col0 : CH;
-    const uint32_t bytes = static_cast<uint32_t>(cols) * 2;
-    __half* dst = in + static_cast<int64_t>(i & 1) * W * CH;
-    mbar_expect_tx(&bar[i & 1], bytes * W);
-    for (int s = 0; s < W; ++s)
-      asm volatile(
-          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-              smem_u32(dst + s * CH)),
-          "l"(p.inbox + s * slot + static_cast<int64_t>(lr) * p.n2 + col0), "r"(bytes), "r"(smem_u32(&bar[i & 1]))
-          : "memory");
-    return true;
-  };
-  if (threadIdx.x == 0) {
-    bool ok = true;
-    for (int i = 0; i < 2 && i < mine && ok; ++i) ok = fetch(i);
-    if (!ok) ok_s = 0;
-  }
-  __syncthreads();
-  int done = 0;
-  for (int i = 0; i < mine && ok_s; ++i) {
-    const int u = cta + i * ctas;
-    const int lr = u / chunks, c = u - (u / chunks) * chunks;
-    const int col0 = c * CH;
-    const int cols = p.n2 - col0 < CH ? p.n2 - col0 : CH;
-    // one thread waits for the unit's partials (and for the copies of unit
-    // i - 2 to have read its output chunk); the barrier hands both on
-    if (threadIdx.x == 0) {
-      if (mbar_wait(&bar[i & 1], static_cast<uint32_t>((i >> 1) & 1), abort_flag))
-        asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-      else
-        ok_s = 0;
-    }
-    __syncthreads();
-    if (!ok_s) break;
-    const __half* src = in + static_cast<int64_t>(i & 1) * W * CH;
-    __nv_bfloat16* o = out + (i & 1) * CH;
-    for (int pk = threadIdx.x; pk < cols / 8; pk += blockDim.x) {
-      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (int s = 0; s < W; ++s) {  // fixed rank order: the same sum on every run
-        Vec<__half> v;
-        v.u = *reinterpret_cast<const uint4*>(src + s * CH + pk * 8);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[e] += __half2float(v.e[e]);
+    if (blk > seen) {
+      int got = 1;
+      if (lane == 0) got = wait_count<true>(p.arrive[p.peer_rank] + blk, target, abort_flag) ? 1 : 0;
+      got = __shfl_sync(0xffffffffu, got, 0);
+      if (!got) {
+        ok = false;
+        break;
       }
-      Vec<__nv_bfloat16> r;
+      seen = blk;
+      if constexpr (MODE == kMlpStepMC) asm volatile("fence.proxy.alias;" ::: "memory");
+    }
+    const int col0 = c * kStepCols;
+    const int packets = (p.n2 - col0 < kStepCols ? p.n2 - col0 : kStepCols) / 8;
+    const int64_t grow = (static_cast<int64_t>(lr >> 3) * W + p.peer_rank) * 8 + (lr & 7);
+    if constexpr (MODE == kMlpStepMC) {
+      // four packets per lane in flight, each the world-sum of one 16-byte piece
+      for (int pk0 = lane; pk0 < packets; pk0 += 128) {
+        uint4 v[4];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) r.e[e] = __float2bfloat16_rn(acc[e]);
-      *reinterpret_cast<uint4*>(o + pk * 8) = r.u;
+        for (int h = 0; h < 4; ++h)
+          if (pk0 + 32 * h < packets) v[h] = multimem_ld_add_f16x8(p.part_mc + grow * p.n2 + col0 + (pk0 + 32 * h) * 8);
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          if (pk0 + 32 * h >= packets) break;
+          const __half* hv = reinterpret_cast<const __half*>(&v[h]);
+          Vec<__nv_bfloat16> o;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) o.e[e] = __float2bfloat16_rn(__half2float(hv[e]));
+          multimem_st_b128(p.y_mc + grow * p.n2 + col0 + (pk0 + 32 * h) * 8, o.u);
+        }
+      }
+    } else {
+      const int64_t lrow = static_cast<int64_t>(lr) * p.n2 + col0;
+      // two packets per lane in flight, every rank's copy loaded before any sum
+      for (int pk0 = lane; pk0 < packets; pk0 += 64) {
+        Vec<__half> v[2][kMaxPeers];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int pk = pk0 + 32 * h;
+#pragma unroll
+          for (int s2 = 0; s2 < kMaxPeers; ++s2)  // written by other GPUs: loads that skip cached copies
+            if (s2 < W && pk < packets)
+              v[h][s2].u = __ldcv(reinterpret_cast<const uint4*>(p.inbox + s2 * slot + lrow + pk * 8));
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int pk = pk0 + 32 * h;
+          if (pk >= packets) break;
+          float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int s2 = 0; s2 < kMaxPeers; ++s2)  // fixed rank order: the same sum on every run
+            if (s2 < W)
+#pragma unroll
+              for (int e = 0; e < 8; ++e) acc[e] += __half2float(v[h][s2].e[e]);
+          Vec<__nv_bfloat16> o;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) o.e[e] = __float2bfloat16_rn(acc[e]);
+          for (int d = 0; d < W; ++d)
+            st_vec(static_cast<__nv_bfloat16*>(p.y[d]) + grow * p.n2 + col0 + pk * 8, o);
+        }
+      }
     }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic smem accesses -> bulk copies
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      const int64_t grow = (static_cast<int64_t>(lr >> 3) * W + p.peer_rank) * 8 + (lr & 7);
-      for (int d = 0; d < W; ++d)
-        asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(
-                         static_cast<__nv_bfloat16*>(p.y[d]) + grow * p.n2 + col0),
-                     "r"(smem_u32(o)), "r"(static_cast<uint32_t>(cols) * 2)
-                     : "memory");
-      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-      if (i + 2 < mine && !fetch(i + 2)) ok_s = 0;
-    }
-    ++done;
-    __syncthreads();
+    ++mine;
   }
-  if (threadIdx.x == 0) {
-    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // every push has landed
-    if (!*abort_flag && ok_s && done == mine && mine > 0) {
-      asm volatile("fence.proxy.async.global;" ::: "memory");
-      __threadfence_system();
-      for (int d = 0; d < W; ++d)
-        asm volatile("red.relaxed.sys.global.add.s32 [%0], %1;" ::"l"(p.done[d]), "r"(mine) : "memory");
-    } else if (done < mine) {
-      // a wait gave up: fetches issued ahead may still be landing in this
-      // CTA's shared memory (failure path only)
-      for (int k = 0; k < 1000; ++k) __nanosleep(1000);
-    }
-  }
+  // publish this warp's rows: every store before the done counts (system scope)
+  if constexpr (MODE == kMlpStepMC) asm volatile("fence.proxy.alias;" ::: "memory");
+  __threadfence_system();
+  __syncwarp();
+  if (ok && mine > 0 && lane < W && !*abort_flag)
+    asm volatile("red.relaxed.sys.global.add.s32 [%0], %1;" ::"l"(p.done[lane]), "r"(mine) : "memory");
 }
 
 template <typename TC, int MODE>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(mlp_threads(MODE), 1)
     swiglu_fused_pair(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmWg,
                       const __grid_constant__ CUtensorMap tmWu, const __grid_constant__ CUtensorMap tmAct,
                       const __grid_constant__ CUtensorMap tmWd, MlpParams p) {
@@ -1966,8 +1964,6 @@ __global__ void __launch_bounds__(192, 1)
   grid.ta_row = (p.n1 + BH - 1) / BH;
   grid.tb_row = (p.n2 + BN - 1) / BN;
   grid.group = p.group;
-  // kMlpStep: clusters from gemm_pairs on run the owner reduction, not tiles
-  const bool reducer = MODE == kMlpStep && static_cast<int>(blockIdx.x >> 1) >= p.gemm_pairs;
   const int tiles = grid.tiles();
   const int kb_a = (p.k1 + BK - 1) / BK, kb_b = (p.n1 + BK - 1) / BK;
   int* counter = p.ready + grid.rb;
@@ -1990,7 +1986,7 @@ __global__ void __launch_bounds__(192, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
-  if (warp == 1 && !reducer) {
+  if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(TMEM_COLS)
                  : "memory");
@@ -1999,15 +1995,6 @@ __global__ void __launch_bounds__(192, 1)
   }
   __syncthreads();
   cluster_barrier();
-  if constexpr (MODE == kMlpStep) {
-    if (reducer) {  // both CTAs of the cluster: no tiles, no tensor memory
-      mlp_step_reduce(p, smem, static_cast<int>(blockIdx.x) - 2 * p.gemm_pairs,
-                      static_cast<int>(gridDim.x) - 2 * p.gemm_pairs);
-      __syncthreads();
-      cluster_barrier();
-      return;
-    }
-  }
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -2161,6 +2148,23 @@ __global__ void __launch_bounds__(192, 1)
           __threadfence();
           atomicAdd(p.ready + x.r, 1);
         }
+      } else if constexpr (MODE == kMlpStepMC) {
+        // this rank's partial rows into its own (multicast-bound) buffer, then
+        // released into every rank's arrival count of the row block
+        __half* prow = p.part + (row_ok ? row : 0) * static_cast<int64_t>(p.n2);
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          __syncwarp();
+          tmem_ld32(tbase + c * 32, v);
+          tmem_wait_ld();
+          const int64_t col = static_cast<int64_t>(x.c) * BN + c * 32;
+          if (row_ok && col < p.n2) store32<__half>(prow + col, v, col, p.n2);
+        }
+        asm volatile("fence.proxy.alias;" ::: "memory");  // unicast stores -> the switch's multicast reads
+        __threadfence_system();
+        __syncwarp();
+        if (lane < p.world) red_release_sys_add(p.arrive[lane] + x.r, 1);
       } else if constexpr (MODE != kMlpLocal) {
         __half* stg = reinterpret_cast<__half*>(smem + S * STAGE + 512) + q * 32 * kPeerStageHalves;
         GemmParams gp{};
@@ -2200,6 +2204,9 @@ __global__ void __launch_bounds__(192, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_u32(smem_u32(&tempty[buf]), 0), 1);
     }
+  } else if (warp >= 6) {
+    // ---------------- reduction warps (kMlpStep, kMlpStepMC) ----------------
+    if constexpr (MODE >= kMlpStep) mlp_step_reduce_warp<MODE>(p, grid.rb, lane, abort_flag);
   }
 
   __syncthreads();
@@ -2355,11 +2362,8 @@ template <typename TC, int MODE>
 int launch_swiglu_fused(const CUtensorMap& mx, const CUtensorMap& mg, const CUtensorMap& mu, const CUtensorMap& ma,
                         const CUtensorMap& md, const MlpParams& mp, cudaStream_t s) {
   constexpr int STAGE = A_BYTES + 128 * BK * 2;
-  size_t smem = static_cast<size_t>(mp.stages) * STAGE + 1024 + 512 + (MODE != kMlpLocal ? kPeerStageBytes : 0);
-  if (MODE == kMlpStep) {  // the reduction CTAs stage in the same dynamic shared memory
-    const size_t comm = 1024 + 4 * (static_cast<size_t>(mp.world) + 1) * mp.step_cols + 16;
-    if (comm > smem) smem = comm;
-  }
+  const size_t smem =
+      static_cast<size_t>(mp.stages) * STAGE + 1024 + 512 + (MODE != kMlpLocal ? kPeerStageBytes : 0);
   auto kern = swiglu_fused_pair<TC, MODE>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return fail(AXON_E_LAUNCH, "axon_silu_mlp: smem attribute: %s", cudaGetErrorString(e));
@@ -2369,7 +2373,7 @@ int launch_swiglu_fused(const CUtensorMap& mx, const CUtensorMap& mg, const CUte
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg.blockDim = dim3(192, 1, 1);
+  cfg.blockDim = dim3(mlp_threads(MODE), 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cfg.attrs = attr;
@@ -2388,21 +2392,12 @@ int launch_swiglu_fused(const CUtensorMap& mx, const CUtensorMap& mg, const CUte
   const int64_t tiles = rb * ((mp.n1 + 127) / 128 + (mp.n2 + 255) / 256);
   int64_t pairs = pairs_cap;
   if (mp.max_ctas > 0 && mp.max_ctas / 2 < pairs) pairs = mp.max_ctas / 2 > 0 ? mp.max_ctas / 2 : 1;
-  MlpParams lp = mp;
-  int64_t extra = 0;  // kMlpStep: reduction clusters beside the GEMM clusters
-  if (MODE == kMlpStep) {
-    extra = (lp.gemm_pairs + 1) / 2;  // gemm_pairs carries the requested reduction CTAs here
-    if (extra < 1) extra = 1;
-    if (pairs - extra < 1) return fail(AXON_E_ARG, "axon_tp_mlp_step: no CTA pairs left for the GEMM tiles");
-    pairs -= extra;
-  }
   if (tiles < pairs) pairs = tiles;
-  if (MODE == kMlpStep) lp.gemm_pairs = static_cast<int>(pairs);
   // row-block counters and the tile counter start at zero every call
   e = cudaMemsetAsync(mp.ready, 0, static_cast<size_t>(rb + 2) * sizeof(int), s);
   if (e != cudaSuccess) return fail(AXON_E_CUDA, "axon_silu_mlp: counter reset: %s", cudaGetErrorString(e));
-  cfg.gridDim = dim3(static_cast<unsigned>(2 * (pairs + extra)), 1, 1);
-  e = cudaLaunchKernelEx(&cfg, kern, mx, mg, mu, ma, md, lp);
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
+  e = cudaLaunchKernelEx(&cfg, kern, mx, mg, mu, ma, md, mp);
   if (e != cudaSuccess) return fail(AXON_E_LAUNCH, "axon_silu_mlp: %s", cudaGetErrorString(e));
   return launch_status("axon_silu_mlp");
 }
@@ -2419,9 +2414,12 @@ int64_t swiglu_counter_bytes(int64_t m) { return ((m + 255) / 256 + 2) * 4; }
 struct StepArgs {
   int32_t* const* arrive;
   int32_t* const* done;
-  const void* inbox;
-  void* const* ys;
+  const void* inbox;  // kMlpStep
+  void* const* ys;    // kMlpStep
   int epoch;
+  void* part;         // kMlpStepMC: this rank's partial buffer, its multicast address and the output's
+  const void* part_mc;
+  void* y_mc;
 };
 
 int swiglu_fused_impl(const void* x, const void* w1, const void* w2, const void* w3h, __half* act, int* counters,
@@ -2434,7 +2432,7 @@ int swiglu_fused_impl(const void* x, const void* w1, const void* w2, const void*
   if (!aligned16(x) || !aligned16(w1) || !aligned16(w2) || !aligned16(w3h) || !aligned16(act) ||
       (c != nullptr && !aligned16(c)))
     return fail(AXON_E_ALIGN, "axon_silu_mlp: operands must be 16-byte aligned");
-  const int extra = peers != nullptr ? kPeerStageBytes : 0;
+  const int extra = peers != nullptr || step != nullptr ? kPeerStageBytes : 0;
   const int smax = (232448 - 1024 - 512 - extra) / (A_BYTES + 128 * BK * 2) > 8
                        ? 8
                        : (232448 - 1024 - 512 - extra) / (A_BYTES + 128 * BK * 2);
@@ -2449,8 +2447,9 @@ int swiglu_fused_impl(const void* x, const void* w1, const void* w2, const void*
   if (rc) return rc;
   MlpParams mp{};
   mp.c = c;
-  if (peers != nullptr) {
-    for (int i = 0; i < world; ++i) mp.peers[i] = peers[i];
+  if (peers != nullptr || step != nullptr) {
+    if (peers != nullptr)
+      for (int i = 0; i < world; ++i) mp.peers[i] = peers[i];
     mp.peer_rank = peer_rank;
     mp.rows_per_owner = static_cast<int>(rows_per_owner);
     mp.world = world;
@@ -2459,14 +2458,13 @@ int swiglu_fused_impl(const void* x, const void* w1, const void* w2, const void*
     for (int i = 0; i < world; ++i) {
       mp.arrive[i] = step->arrive[i];
       mp.done[i] = step->done[i];
-      mp.y[i] = step->ys[i];
+      if (step->ys) mp.y[i] = step->ys[i];
     }
     mp.inbox = static_cast<const __half*>(step->inbox);
     mp.epoch = step->epoch;
-    // the reduction CTAs requested (tune.split, default kStepCommCtas; the
-    // launch turns this into clusters) and the columns of one unit
-    mp.gemm_pairs = t.split > 0 ? t.split : kStepCommCtas;
-    mp.step_cols = step_cols(world, n2);
+    mp.part = static_cast<__half*>(step->part);
+    mp.part_mc = static_cast<const __half*>(step->part_mc);
+    mp.y_mc = static_cast<__nv_bfloat16*>(step->y_mc);
   }
   mp.act = act;
   mp.ready = counters;
@@ -2487,6 +2485,8 @@ int swiglu_fused_impl(const void* x, const void* w1, const void* w2, const void*
   mp.idesc_a = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | shape;
   mp.idesc_b = (1u << 4) | (1u << 16) | shape;
   cudaStream_t s = as_stream(stream);
+  if (step != nullptr && step->part != nullptr)
+    return launch_swiglu_fused<__half, kMlpStepMC>(mx, mg, mu, ma, md, mp, s);
   if (step != nullptr) return launch_swiglu_fused<__half, kMlpStep>(mx, mg, mu, ma, md, mp, s);
   if (peers != nullptr) return launch_swiglu_fused<__half, kMlpScatter>(mx, mg, mu, ma, md, mp, s);
   switch (c_dtype) {
@@ -2973,10 +2973,9 @@ extern "C" int axon_tp_mlp_partial(const void* x, const void* w_gate, const void
 
 extern "C" int64_t axon_tp_step_done_per_epoch(int32_t world, int64_t m, int64_t p) {
   if (world < 1 || m < 0 || p < 0) return fail(AXON_E_ARG, "axon_tp_step_done_per_epoch: bad argument");
-  // every reduction unit (one owned row x one column chunk) counts once on
-  // every rank: world owners x m / world rows x chunks
-  const int ch = step_cols(world, p);
-  return ch > 0 ? m * ((p + ch - 1) / ch) : 0;
+  // every reduction unit (one owned row x kStepCols columns) counts once on
+  // every rank: world owners x m / world rows x column chunks
+  return m * ((p + kStepCols - 1) / kStepCols);
 }
 
 extern "C" int axon_tp_mlp_step(const void* x, const void* w_gate, const void* w_up, const void* w_down_h,
@@ -2999,9 +2998,35 @@ extern "C" int axon_tp_mlp_step(const void* x, const void* w_gate, const void* w
   if (!aligned16(inbox)) return fail(AXON_E_ALIGN, "axon_tp_mlp_step: inbox unaligned");
   __half* act = static_cast<__half*>(workspace);
   int* counters = reinterpret_cast<int*>(static_cast<unsigned char*>(workspace) + m * n * 2);
-  StepArgs sa{arrive, done, inbox, ys, epoch};
+  StepArgs sa{arrive, done, inbox, ys, epoch, nullptr, nullptr, nullptr};
   return swiglu_fused_impl(x, w_gate, w_up, w_down_h, act, counters, nullptr, p, AXON_F16, m, n, k, p,
                            tune_or_default(tune), stream, inboxes, world, rank, m / world, &sa);
+}
+
+extern "C" int axon_tp_mlp_step_multicast(const void* x, const void* w_gate, const void* w_up,
+                                          const void* w_down_h, void* workspace, int64_t workspace_bytes, void* part,
+                                          const void* part_mc, void* y_mc, int32_t* const* arrive,
+                                          int32_t* const* done, int32_t world, int32_t rank, int32_t epoch, int64_t m,
+                                          int64_t n, int64_t k, int64_t p, const axon_tune_t* tune, void* stream) {
+  if (world < 1 || world > kMaxPeers || (world & (world - 1)) || rank < 0 || rank >= world)
+    return fail(AXON_E_ARG, "axon_tp_mlp_step_multicast: world must be 1, 2, 4 or 8 and 0 <= rank < world");
+  if (m <= 0 || n <= 0 || k <= 0 || p <= 0)
+    return fail(AXON_E_SHAPE, "axon_tp_mlp_step_multicast: sizes must be positive");
+  if (m % 256) return fail(AXON_E_SHAPE, "axon_tp_mlp_step_multicast: m (%lld) must be a multiple of 256", (long long)m);
+  if (!x || !w_gate || !w_up || !w_down_h || !part || !part_mc || !y_mc || !arrive || !done)
+    return fail(AXON_E_ARG, "axon_tp_mlp_step_multicast: NULL argument");
+  if (!aligned16(part) || !aligned16(part_mc) || !aligned16(y_mc))
+    return fail(AXON_E_ALIGN, "axon_tp_mlp_step_multicast: partial and output buffers must be 16-byte aligned");
+  const int64_t need = m * n * 2 + swiglu_counter_bytes(m);
+  if (!workspace || workspace_bytes < need)
+    return fail(AXON_E_ARG, "axon_tp_mlp_step_multicast: workspace of %lld bytes needed", (long long)need);
+  for (int i = 0; i < world; ++i)
+    if (!arrive[i] || !done[i]) return fail(AXON_E_ARG, "axon_tp_mlp_step_multicast: counters of rank %d NULL", i);
+  __half* act = static_cast<__half*>(workspace);
+  int* counters = reinterpret_cast<int*>(static_cast<unsigned char*>(workspace) + m * n * 2);
+  StepArgs sa{arrive, done, nullptr, nullptr, epoch, part, part_mc, y_mc};
+  return swiglu_fused_impl(x, w_gate, w_up, w_down_h, act, counters, nullptr, p, AXON_F16, m, n, k, p,
+                           tune_or_default(tune), stream, nullptr, world, rank, m / world, &sa);
 }
 
 extern "C" int axon_gemm_status(void* stream) {

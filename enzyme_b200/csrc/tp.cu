@@ -91,7 +91,10 @@ __global__ void tp_wait_kernel(const int* flags, int world, int epoch) {
 }
 
 __global__ void tp_wait_count_kernel(const int* counter, int target) {
-  if (threadIdx.x == 0 && !wait_flags(counter, 1, target)) atomicExch(&g_tp_error, AXON_E_TIMEOUT);
+  if (threadIdx.x != 0) return;
+  if (!wait_flags(counter, 1, target)) atomicExch(&g_tp_error, AXON_E_TIMEOUT);
+  // outputs may have arrived through a multicast alias of this rank's buffer
+  asm volatile("fence.proxy.alias;" ::: "memory");
 }
 
 template <typename Tout>

@@ -317,9 +317,21 @@ class FusedTPSwiGLU:
 
     whole_step=True runs the step as one kernel (axon_tp_mlp_step): rows are
     owned in 8-row granules dealt to the ranks in turn, so every owner's rows
-    complete while the down projection is still running, and the reduction
-    and all-gather push run as the kernel's last tiles; one wait for the done
-    count ends the step.
+    complete while the down projection is still running; two reduction warps
+    in every CTA, beside the GEMM roles, reduce and push this rank's rows of
+    each 256-row block as soon as every rank's partials of that block have
+    arrived, overlapped with the GEMM tiles that follow; one wait for the
+    done count ends the step. tune["rows_per_cta"] sets the row blocks per
+    group of the kernel's tile order (default 4).
+
+    whole_step=True with multicast_gather=True runs the same kernel with the
+    all-reduce done by the NVLink switch (axon_tp_mlp_step_multicast): the
+    partials stay in each rank's own buffer, the reduction warps read every
+    owned packet once through the partials' multicast address with
+    multimem.ld_reduce and store the bf16 sum once, with multimem.st, to the
+    output's multicast address. Each byte crosses NVLink once each way
+    instead of twice. Needs GPUs behind an NVSwitch with multicast
+    (multicast_supported).
 
     multicast_gather=True puts the output in symmetric memory bound to an
     NVLink multicast object and has each owner store its summed rows once, to
@@ -371,10 +383,15 @@ class FusedTPSwiGLU:
         # all-gather through one multicast store per output packet
         self.multicast_gather = bool(multicast_gather)
         self._y_mc, self._symm = 0, None
+        self._part, self._part_mc, self._part_symm = None, 0, None
         if self.multicast_gather:
-            if copy_engine_gather or whole_step:
-                raise ValueError("multicast_gather replaces the copy-engine and whole-step all-gathers")
+            if copy_engine_gather:
+                raise ValueError("multicast_gather replaces the copy-engine all-gather")
             self.y, self._y_mc, self._symm = multicast_output(m, self.hidden, out_dtype, dev, group)
+            if whole_step:
+                # each rank's f16 partial of y, bound to its own multicast object
+                self._part, self._part_mc, self._part_symm = multicast_output(m, self.hidden, torch.float16, dev,
+                                                                              group)
         # one kernel per step (axon_tp_mlp_step): both GEMMs and the reduction
         self.whole_step = bool(whole_step)
         if self.whole_step:
@@ -397,10 +414,11 @@ class FusedTPSwiGLU:
         torch.cuda.synchronize(self.w_gate.device)
         self.peers.close()
         if self._symm is not None:
-            # every rank done with the multicast output before any unmaps it
+            # every rank done with the multicast buffers before any unmaps them
             if self.world > 1:
                 dist.barrier(group=self.group)
             self.y, self._symm, self._y_mc = None, None, 0
+            self._part, self._part_symm, self._part_mc = None, None, 0
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         import ctypes
@@ -419,6 +437,17 @@ class FusedTPSwiGLU:
         out_code = {torch.bfloat16: N.AXON_BF16, torch.float16: N.AXON_F16, torch.float32: N.AXON_F32}[self.out_dtype]
         y_ptrs = ptrs([b + lo.y_offset for b in self.peers.bases])
         mine = self.peers.bases[self.rank]
+        if self.whole_step and self._part is not None:
+            bases = self.peers.bases
+            N.check(lib.axon_tp_mlp_step_multicast(
+                x.data_ptr(), self.w_gate.data_ptr(), self.w_up.data_ptr(), self.w_down_h.data_ptr(),
+                self.ws.data_ptr(), self.ws.numel(), self._part.data_ptr(), ctypes.c_void_p(self._part_mc),
+                ctypes.c_void_p(self._y_mc), ptrs([b + lo.counts_offset for b in bases]),
+                ptrs([b + lo.done_count_offset for b in bases]), W, self.rank, e, self.m, self.act.shape[1],
+                x.shape[1], self.hidden, tune, main.cuda_stream))
+            target = (e * self.done_per_epoch + 2 ** 31) % 2 ** 32 - 2 ** 31  # int32 wrap, as the counters
+            N.check(lib.axon_tp_wait_count(mine + lo.done_count_offset, target, main.cuda_stream))
+            return self.y
         if self.whole_step:
             bases = self.peers.bases
             N.check(lib.axon_tp_mlp_step(

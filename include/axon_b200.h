@@ -312,16 +312,20 @@ AXON_API int axon_tp_mlp_partial(const void* x, const void* w_gate, const void* 
 /* One whole tensor-parallel SwiGLU step of rank `rank` in one kernel (world
  * 1, 2, 4 or 8; m a multiple of 256): the two GEMMs as axon_tp_mlp_partial,
  * with output rows owned in 8-row granules dealt to the ranks in turn (row r
- * belongs to rank (r / 8) % world), each phase-B warp releasing its rows into
- * the owners' arrival counts arrive[o][r / 256] (system scope), and then the
- * owner-side reduction inside the same kernel: for each 256-row block, once
- * all ranks' partials of this rank's rows have arrived, they are summed in
- * fp32 in rank order, rounded once to bf16 and stored to every rank's output
- * ys[d] [m, p] bf16, and done[d] is incremented on every rank. Counts
- * accumulate: step `epoch` (1, 2, ...) is complete on a rank when its done
- * count reaches epoch * axon_tp_step_done_per_epoch(world, m, p)
- * (axon_tp_wait_count). inbox = this rank's inbox, inboxes[o] = rank o's,
- * each [world][m / world][p] f16; workspace as axon_tp_mlp_partial's. */
+ * belongs to rank (r / 8) % world), each phase-B warp writing its f16 partial
+ * rows into the owners' inboxes and releasing them into the owners' arrival
+ * counts arrive[o][r / 256] (system scope). Two reduction warps in every CTA,
+ * beside the GEMM roles, resolve the all-reduce while the tiles go on: for
+ * each of this rank's rows (1024-column units, in row-block order), once all
+ * ranks' partials of its 256-row block have arrived, the world copies are
+ * summed in fp32 in rank order, rounded once to bf16 and stored to every
+ * rank's output ys[d] [m, p] bf16; at the end each warp adds its unit count
+ * to done[d] on every rank. Counts accumulate: step `epoch` (1, 2, ...) is
+ * complete on a rank when its done count reaches
+ * epoch * axon_tp_step_done_per_epoch(world, m, p) (axon_tp_wait_count).
+ * inbox = this rank's inbox, inboxes[o] = rank o's, each [world][m / world][p]
+ * f16; workspace as axon_tp_mlp_partial's. tune->rows_per_cta sets the row
+ * blocks per group of the tile order (default 4). */
 AXON_API int64_t axon_tp_step_done_per_epoch(int32_t world, int64_t m, int64_t p);
 AXON_API int axon_tp_mlp_step(const void* x, const void* w_gate, const void* w_up,
                      const void* w_down_h, void* workspace, int64_t workspace_bytes,
@@ -330,8 +334,31 @@ AXON_API int axon_tp_mlp_step(const void* x, const void* w_gate, const void* w_u
                      int32_t epoch, int64_t m, int64_t n, int64_t k, int64_t p,
                      const axon_tune_t* tune, void* stream);
 
+/* The same step with the all-reduce done by the NVLink switch (NVLS): each
+ * rank's phase-B warps write its f16 partial of y into its own buffer `part`
+ * [m, p] (every rank's `part` bound to one NVLink multicast object whose
+ * address is part_mc) and release the rows into every rank's arrival counts
+ * arrive[d][r / 256]; the reduction warps read each 16-byte packet of this
+ * rank's rows once through part_mc with multimem.ld_reduce (the switch adds
+ * the world f16 copies, accumulating in fp32, and returns the f16 sum), round
+ * it to bf16 and store it once with multimem.st to y_mc, the multicast
+ * address of the [m, p] bf16 outputs, which the switch writes into every
+ * rank's output. Each partial crosses NVLink once (to the switch) and each
+ * output packet leaves its owner once. Counts and completion as
+ * axon_tp_mlp_step (the same done count per epoch). The result may differ
+ * from axon_tp_mlp_step's in the last bit (the switch's f16 rounding of the
+ * sum before bf16); every rank holds the same bits. */
+AXON_API int axon_tp_mlp_step_multicast(const void* x, const void* w_gate, const void* w_up,
+                               const void* w_down_h, void* workspace, int64_t workspace_bytes,
+                               void* part, const void* part_mc, void* y_mc,
+                               int32_t* const* arrive, int32_t* const* done, int32_t world,
+                               int32_t rank, int32_t epoch, int64_t m, int64_t n, int64_t k,
+                               int64_t p, const axon_tune_t* tune, void* stream);
+
 /* Bounded wait (~2 s) on `stream` until *counter >= target (wrap-safe); a
- * wait that gives up records AXON_E_TIMEOUT for axon_tp_status. */
+ * wait that gives up records AXON_E_TIMEOUT for axon_tp_status. A later
+ * read of an output written through a multicast address is ordered after
+ * the wait. */
 AXON_API int axon_tp_wait_count(const int32_t* counter, int32_t target, void* stream);
 
 /* After the work already on `stream`: a system-scope fence, then

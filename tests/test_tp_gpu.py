@@ -11,6 +11,12 @@
   store per packet through the NVLink switch); checked against the oracle,
   across ranks and over repeated steps (epoch flags), and on one rank
   without a process group.
+* The whole step in one kernel, its reduction warps resolving the
+  all-reduce beside the GEMM tiles, through the owners' inboxes or through
+  the NVLink switch (multimem.ld_reduce of the partials, multimem.st of the
+  sums).
+* The BASELINE SwiGLU config on every GPU of the box (the largest power of
+  two up to 8), default path and whole step.
 * A flag wait that nobody satisfies gives up with AXON_E_TIMEOUT and the
   context stays usable.
 NVLS is off (NCCL_NVLS_ENABLE=0) and the process group has a short timeout.
@@ -136,6 +142,7 @@ def _fused_rank(rank, world, port, q, whole_step=False, ce=False, mc=False):
         if mc and not tp.multicast_supported(dev):
             q.put((rank, None, None))  # every rank sees the same GPUs, so all skip
             return
+        # whole_step + mc: the all-reduce by the switch (multimem.ld_reduce / multimem.st)
         f = tp.FusedTPSwiGLU(*shards, m=1024, slabs=2, tune={"max_ctas": 132}, whole_step=whole_step,
                              copy_engine_gather=ce, multicast_gather=mc)
         try:
@@ -147,7 +154,7 @@ def _fused_rank(rank, world, port, q, whole_step=False, ce=False, mc=False):
         f.status()
         ops.gemm_status()
         same = bool(torch.equal(y1, y2))
-        if mc:  # the multicast all-gather carries the bits of the bulk-copy push
+        if mc and not whole_step:  # the multicast all-gather carries the bits of the bulk-copy push
             plain = tp.FusedTPSwiGLU(*shards, m=1024, slabs=2, tune={"max_ctas": 132})
             same = same and bool(torch.equal(y1, plain.forward(xd)))
             plain.close()
@@ -158,7 +165,7 @@ def _fused_rank(rank, world, port, q, whole_step=False, ce=False, mc=False):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 @pytest.mark.parametrize("whole_step,ce,mc", [(False, False, False), (True, False, False), (False, True, False),
-                                              (False, False, True)])
+                                              (False, False, True), (True, False, True)])
 def test_fused_tp_swiglu_two_gpus(whole_step, ce, mc):
     import torch.multiprocessing as mp
 
@@ -239,7 +246,7 @@ def _config_tensors(dev):
     return x, full
 
 
-def _config_rank(rank, world, port, q):
+def _config_rank(rank, world, port, q, whole_step=False, mc=False):
     """One rank of the fused path at the BASELINE SwiGLU config (m 4096,
     hidden 4096, inter 14336): the same seeded full weights on every rank,
     this rank's column/row shard, three steps; returns the sampled rows and a
@@ -259,7 +266,10 @@ def _config_rank(rank, world, port, q):
         m, h = 4096, 4096
         x, full = _config_tensors(dev)
         shards = tp.shard_swiglu(*full, rank, world)
-        f = tp.FusedTPSwiGLU(*shards, m=m, slabs=1)
+        if mc and not tp.multicast_supported(dev):
+            q.put((rank, None, True, None))  # every rank sees the same GPUs, so all skip
+            return
+        f = tp.FusedTPSwiGLU(*shards, m=m, slabs=1, whole_step=whole_step, multicast_gather=mc)
         try:
             ys = [f.forward(x).clone() for _ in range(3)]
             torch.cuda.synchronize()
@@ -277,7 +287,8 @@ def _config_rank(rank, world, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_fused_tp_swiglu_config_shape_all_gpus():
+@pytest.mark.parametrize("whole_step,mc", [(False, False), (True, False), (True, True)])
+def test_fused_tp_swiglu_config_shape_all_gpus(whole_step, mc):
     """The fused tensor-parallel path at the BASELINE config on every GPU of
     the box (the largest power of two up to 8): sampled rows against the
     float64 oracle of the unsharded MLP at rtol = atol = 1e-2, bit-identical
@@ -290,13 +301,15 @@ def test_fused_tp_swiglu_config_shape_all_gpus():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_config_rank, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_config_rank, args=(r, world, port, q, whole_step, mc)) for r in range(world)]
     for p in procs:
         p.start()
     res = sorted((q.get(timeout=600) for _ in range(world)), key=lambda t: t[0])
     for p in procs:
         p.join(timeout=120)
     assert all(p.exitcode == 0 for p in procs)
+    if any(y is None for _, y, _, _ in res):
+        pytest.skip("no NVLink multicast on these GPUs")
     x, full = _config_tensors(torch.device("cuda", 0))  # the same draws as every rank's
     rows = torch.arange(0, x.shape[0], CONFIG_ROW_STRIDE, device=x.device)
     want = f64.silu_mlp(x[rows].float().cpu().numpy(), *(w.float().cpu().numpy() for w in full))
