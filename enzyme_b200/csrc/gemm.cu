@@ -1509,7 +1509,7 @@ __global__ void __launch_bounds__(192, 1)
     tc_commit_to(smem_u32(drain));
     volatile int never = 0;
     mbar_wait(drain, 0, &never);
-  } else if (warp >= 2 && warp < 6) {
+  } else if (warp >= 2) {
     // ---------------- epilogue (both CTAs, their own 128 rows) ----------------
     const int q = warp & 3;
     int local = 0;
@@ -2107,7 +2107,7 @@ __global__ void __launch_bounds__(mlp_threads(MODE), 1)
     tc_commit_to(smem_u32(drain));
     volatile int never = 0;
     mbar_wait(drain, 0, &never);
-  } else if (warp >= 2) {
+  } else if (warp >= 2 && warp < 6) {
     // ---------------- epilogue (both CTAs, their own 128 rows) ----------------
     const int q = warp & 3;
     int mm = 0;
