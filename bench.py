@@ -121,6 +121,10 @@ class SwiGLU(Workload):
     SLABS = 1
     TP_TUNE = None
     REDUCE_CTAS = 32
+    # "auto": the whole step in one kernel with the all-reduce done by the
+    # NVLink switch where the GPUs support multicast, else the separate
+    # GEMM / reduce launches; "whole" and "slabs" force one of the two
+    TP_MODE = os.environ.get("AXON_BENCH_TP_MODE", "auto")
 
     def __init__(self, dev, rank, world):
         super().__init__(dev, rank, world)
@@ -147,10 +151,17 @@ class SwiGLU(Workload):
             # column/row tensor parallel: W_gate/W_up column shard, W_down row
             # shard; the down GEMM scatters f16 partial rows to their owner
             # ranks over NVLink, owners reduce and push bf16 rows to every rank
-            from enzyme_b200.tp import FusedTPSwiGLU
+            from enzyme_b200.tp import FusedTPSwiGLU, multicast_supported
 
+            mode = self.TP_MODE
+            if mode == "auto":
+                ok = torch.tensor([1 if multicast_supported(dev) else 0], device=dev)
+                dist.all_reduce(ok, op=dist.ReduceOp.MIN)  # every rank takes the same path
+                mode = "nvls" if ok.item() else "slabs"
+            self.tp_mode = mode
             self.tp = FusedTPSwiGLU(self.w1, self.w2, self.w3, m=m, slabs=self.SLABS, tune=self.TP_TUNE,
-                                    reduce_ctas=self.REDUCE_CTAS)
+                                    reduce_ctas=self.REDUCE_CTAS, whole_step=mode in ("nvls", "whole"),
+                                    multicast_gather=mode == "nvls")
             self.y = self.tp.y
             self.use_graph = False  # each step carries a new epoch for the peer flags
             self.launches_per_step = self.tp.launches_per_step()
@@ -255,8 +266,12 @@ class SwiGLU(Workload):
             f"{rows} of 4096 tokens (fp32 torch, same weights shape)"
 
     def config(self):
-        par = "tp1" if self.world == 1 else (f"tp{self.world} (reduce-scatter in the down GEMM over NVLink, "
-                                             f"owner reduce + all-gather push)")
+        how = {"nvls": "one kernel per step: GEMM tiles beside reduction warps, all-reduce by the NVLink switch "
+                       "(multimem.ld_reduce + multimem.st)",
+               "whole": "one kernel per step: GEMM tiles beside reduction warps, reduce-scatter into owners' "
+                        "inboxes, all-gather by peer stores",
+               "slabs": "reduce-scatter in the down GEMM over NVLink, owner reduce + all-gather push"}
+        par = "tp1" if self.world == 1 else f"tp{self.world} ({how[self.tp_mode]})"
         ws = (self.M * self.H * 2 * 2 + 3 * self.H * self.shard * 2 + self.M * self.shard * 2) / 2**20
         return {"workload": "silu_mlp_swiglu: m 4096, h 4096, inter 14336, bf16, W ~ N(0, 0.02), f16 act",
                 "parallelism": par, "l2": f"x over 2 buffers; {ws:.0f} MiB touched per GPU per step > L2"}

@@ -928,8 +928,8 @@ __global__ void __launch_bounds__(256) resid3_reduce_kernel(const float* __restr
 //              softmax;
 //   warps 2-17 softmax: four warps per TMEM lane quarter, each on 32 of the
 //              block's 128 keys (thread = query row = TMEM lane): tcgen05.ld
-//              the 32 scores, e = exp(s) rounded to bf16 (keys past s are 0),
-//              l += e as stored, and e written into a 128-byte-swizzled P
+//              the 32 scores, e = exp(s) (keys past s are 0), l += e in
+//              fp32, and e rounded to bf16 into a 128-byte-swizzled P
 //              slab (the A operand of the second product; two slabs); after
 //              the last block the four partial row sums meet in shared
 //              memory and the key-quarter-0 warps add them in a fixed order
@@ -937,21 +937,46 @@ __global__ void __launch_bounds__(256) resid3_reduce_kernel(const float* __restr
 //              fp32 partial O and l.
 // Scores never reach global memory. Split keys are combined by
 // attn_reduce_kernel in a fixed order. Every wait is bounded.
-// Two floats rounded to the operand type by one packed conversion
-// (cvt.rn.bf16x2.f32 / cvt.rn.f16x2.f32); `sum` gains the rounded values.
+// exp of a pair of scores as 2^(x log2 e): one packed f32x2 multiply by
+// log2 e and the ISA's ex2.approx (flush-to-zero: the scores' exponentials
+// are never subnormal; keys past s come in as -inf and give +0).
+__device__ __forceinline__ float2 exp_pair(float a, float b) {
+  constexpr float kLog2e = 1.4426950408889634f;
+  uint64_t x, y;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(a), "f"(b));
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(y) : "l"(x), "l"(static_cast<uint64_t>(__float_as_uint(kLog2e)) << 32 |
+                                                          __float_as_uint(kLog2e)));
+  float ya, yb, ea, eb;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(ya), "=f"(yb) : "l"(y));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(ea) : "f"(ya));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(eb) : "f"(yb));
+  return make_float2(ea, eb);
+}
+
+// Two floats rounded to the operand type by one packed conversion, the
+// first in the low half.
 template <typename T>
-__device__ __forceinline__ uint32_t pack2(float a, float b, float& sum);
+__device__ __forceinline__ uint32_t cvt_pack2(float lo, float hi);
 template <>
-__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b, float& sum) {
-  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-  sum += __low2float(h) + __high2float(h);
-  return *reinterpret_cast<const uint32_t*>(&h);
+__device__ __forceinline__ uint32_t cvt_pack2<__nv_bfloat16>(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
 }
 template <>
-__device__ __forceinline__ uint32_t pack2<__half>(float a, float b, float& sum) {
-  const __half2 h = __floats2half2_rn(a, b);
-  sum += __low2float(h) + __high2float(h);
-  return *reinterpret_cast<const uint32_t*>(&h);
+__device__ __forceinline__ uint32_t cvt_pack2<__half>(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+
+// sum += (a, b), two lanes of fp32 in one packed add
+__device__ __forceinline__ void add_pair(float2& sum, float2 v) {
+  uint64_t x, y, z;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(sum.x), "f"(sum.y));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(y) : "f"(v.x), "f"(v.y));
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(z) : "l"(x), "l"(y));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(sum.x), "=f"(sum.y) : "l"(z));
 }
 
 constexpr int kAttnSoftmaxWarps = 16;
@@ -1204,14 +1229,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             if (key0 + kk >= p.s) v[kk] = -INFINITY;
         }
         uint4 pk[4];
+        float2 lsum = make_float2(0.f, 0.f);  // this block's exponentials, in fp32 before rounding
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
           uint32_t w[4];
 #pragma unroll
-          for (int e = 0; e < 8; e += 2)  // two exponentials rounded by one packed conversion
-            w[e / 2] = pack2<TA>(__expf(v[t * 8 + e]), __expf(v[t * 8 + e + 1]), l);
+          for (int e = 0; e < 8; e += 2) {  // two exponentials, one packed multiply, add and conversion
+            const float2 ex = exp_pair(v[t * 8 + e], v[t * 8 + e + 1]);
+            add_pair(lsum, ex);
+            w[e / 2] = cvt_pack2<TA>(ex.x, ex.y);
+          }
           pk[t] = make_uint4(w[0], w[1], w[2], w[3]);
         }
+        l += lsum.x + lsum.y;
         uint8_t* line = sp + pb * P_BYTES + (kq >> 1) * A_BYTES + row * 128;
         const int cb = (kq & 1) * 4;
 #pragma unroll
