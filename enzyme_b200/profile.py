@@ -72,6 +72,15 @@ def case_cumsum_balanced(gen):
     return lambda: ops.cumsum(x, out=y, workspace=ws, tune=tune)
 
 
+def case_cumsum_rowpair(gen):
+    """cumsum_rowpair: the nucleus config by a CTA pair per row (variant 4)."""
+    from . import ops
+
+    x = _cumsum_rows(gen)
+    y = torch.empty_like(x)
+    return lambda: ops.cumsum(x, out=y, tune={"variant": 4})
+
+
 def case_rope_split(gen):
     """rope_split_vec: the rope spec's layout, four [64, 2 Mi] bf16 inputs."""
     from . import ops
@@ -149,8 +158,8 @@ def case_tp_slabs(gen):
 
 def case_tp_step(gen):
     """swiglu_fused_pair<__half, 2>: the whole tensor-parallel step in one
-    kernel on one rank (world 1, inter 3584), GEMM tiles and the owner
-    reduction CTAs."""
+    kernel on one rank (world 1, inter 3584): GEMM tiles beside the
+    reduction warps."""
     from .tp import FusedTPSwiGLU
 
     x, w1, w2, w3 = _tp_shard(gen, 3584)
@@ -163,6 +172,7 @@ CASES = {
     "cast": (case_cast, "cast_vec"),
     "cumsum_lookback": (case_cumsum_lookback, "cumsum_lookback"),
     "cumsum_balanced": (case_cumsum_balanced, "cumsum_balanced"),
+    "cumsum_rowpair": (case_cumsum_rowpair, "cumsum_rowpair"),
     "rope_split": (case_rope_split, "rope_split_vec"),
     "softmax_mm": (case_softmax_mm, "row_prologue_kernel"),
     "qkv_split": (case_qkv_split, "resid3_reduce_kernel"),
