@@ -16,8 +16,8 @@ Tile knob meaning (the CUDA counterpart of TILES_IN_BLOCK_*):
                         (row_bulk_warp: v warps per CTA, one row each);
                         TILES_IN_BLOCK_M must be 1 (rows per CTA are derived).
   cumsum                TILES_IN_BLOCK_N = v -> 1024*v elements per scan tile
-                        (cluster_dsmem: v CTAs per row; row_stream,
-                        balanced_ranges and row_pair: v = 1).
+                        (cluster_dsmem: v CTAs per row; row_stream and
+                        balanced_ranges: v = 1).
   GEMM specs            (matmul, rmsnorm_matmul, qkv_cte, softmax_mm)
                         TILES_IN_BLOCK_M must be 1 (128-row tcgen05 tiles per CTA),
                         TILES_IN_BLOCK_N = v -> BLOCK_N = 64*v,
@@ -75,7 +75,7 @@ def variants(spec_name: str) -> list[Variant]:
         return [Variant(0, "token_blocked"), Variant(1, "flat_vec16")]
     if spec_name in SCAN_SPECS:
         return [Variant(0, "decoupled_lookback"), Variant(1, "cluster_dsmem"), Variant(2, "row_stream"),
-                Variant(3, "balanced_ranges"), Variant(4, "row_pair")]
+                Variant(3, "balanced_ranges")]
     if spec_name in ADAM_SPECS:
         return [Variant(0, "grid_stride_vec")]
     if spec_name in GEMM_SPECS:
@@ -138,9 +138,8 @@ def constraints(spec_name: str, hw_variant: int, dims: dict, itemsize: int,
     elif spec_name in ROPE_SPECS or spec_name in ADAM_SPECS:
         out.append(TileConstraint(args[1], extent=256, tile_size=32, require_divisible=True, allowed=(1, 2, 4, 8)))
         out.append(_one(args[0]))
-    elif spec_name in SCAN_SPECS and hw_variant in (2, 3, 4):
-        # one CTA per row (2), per SM (3) or a CTA pair per row (4), no tile
-        # knob: N must be 1
+    elif spec_name in SCAN_SPECS and hw_variant in (2, 3):
+        # one CTA per row (2) or per SM (3), no tile knob: N must be 1
         out.append(_one(args[1]))
         out.append(_one(args[0]))
     elif spec_name in SCAN_SPECS and hw_variant == 1:
@@ -191,7 +190,7 @@ def tune_for(spec_name: str, hw_variant: int, tiles: dict[str, int]) -> dict | l
     if spec_name in ROPE_SPECS or spec_name in ADAM_SPECS:
         return {"variant": hw_variant, "threads": 32 * t["N"]}
     if spec_name in SCAN_SPECS:
-        if hw_variant in (2, 3, 4):
+        if hw_variant in (2, 3):
             return {"variant": hw_variant}
         return {"variant": hw_variant, "split": t["N"] if hw_variant == 1 else 1024 * t["N"]}
     if spec_name in GEMM_SPECS:

@@ -78,8 +78,7 @@ static const char* kVariants[][2] = {
      "{\"op\":\"cumsum\",\"variants\":[{\"id\":0,\"name\":\"decoupled_lookback\",\"knobs\":{\"split\":[0,2048,4096,8192,16384]}},"
      "{\"id\":1,\"name\":\"cluster_dsmem\",\"knobs\":{\"split\":[0,1,2,4,8]}},"
      "{\"id\":2,\"name\":\"row_stream\",\"knobs\":{\"stages\":[0,2,3,4],\"block_k\":[0,16,24,32,48],\"split\":[0,1,2]}},"
-     "{\"id\":3,\"name\":\"balanced_ranges\",\"knobs\":{\"stages\":[0,2,3,4,6],\"block_k\":[0,16,32],\"max_ctas\":[0]}},"
-     "{\"id\":4,\"name\":\"row_pair\",\"knobs\":{\"stages\":[0,2,3]}}]}"},
+     "{\"id\":3,\"name\":\"balanced_ranges\",\"knobs\":{\"stages\":[0,2,3,4,6],\"block_k\":[0,16,32],\"max_ctas\":[0]}}]}"},
     {"adam",
      "{\"op\":\"adam\",\"variants\":[{\"id\":0,\"name\":\"grid_stride_vec\",\"knobs\":{\"threads\":[0,128,256,512]}}]}"},
     {"gemm",

@@ -622,230 +622,6 @@ int launch_rowstream(const void* x, void* y, int64_t m, int64_t n, int64_t ld_x,
   return launch_status("axon_cumsum");
 }
 
-// ---- variant 4: a row per CTA pair, chunks dealt alternately -----------------------
-//
-// A row's streaming rate in variant 2 is one CTA's: with 256 rows on 148 SMs
-// it, not HBM, sets the time. Here a cluster of two CTAs shares a row: CTA r
-// (r = 0, 1) streams chunks r, r + 2, r + 4, ... through its own ring of bulk
-// copies, exactly as variant 2 streams its row. A chunk's outputs need the
-// row's running sum up to the chunk, which the other CTA finishes: once a
-// CTA has its chunk's total it takes the carry of the previous chunk from the
-// peer (a float64 the peer stored into this CTA's shared memory, announced by
-// a remote mbarrier arrival; bounded wait), sends carry + total on to the peer
-// for the next chunk, and only then writes its outputs, so the two CTAs'
-// loads, scans and stores overlap and only the carry hand-off is serial.
-// Four 256-thread CTAs share an SM, so the 512 CTAs of the nucleus config
-// all run at once. Numerics are variant 2's: a float64 running sum across
-// chunks, a chunk-local fp32 prefix.
-constexpr int kPairThreads = 256;
-constexpr int kPairStages = 3;   // default ring: 3 x 16 KB per CTA
-constexpr int kPairChunkKB = 16;
-
-template <typename Tin, typename Tout>
-__global__ void __launch_bounds__(kPairThreads, 4) cumsum_rowpair(const Tin* __restrict__ x, Tout* __restrict__ y,
-                                                                  int64_t n, int64_t ld_x, int64_t ld_y, bool vec_out,
-                                                                  int stages) {
-  constexpr int NW = kPairThreads / 32;
-  constexpr int E = Vec<Tin>::E;
-  constexpr int64_t kChunk = kPairChunkKB * 1024 / static_cast<int64_t>(sizeof(Tin));
-  constexpr int64_t PPW = kChunk / E / NW;  // packets per warp per chunk
-  static_assert(PPW % 32 == 0, "whole segments per warp");
-  constexpr int NSEG = static_cast<int>(PPW / 32);
-  constexpr int64_t kStageBytes = kPairChunkKB * 1024;
-  extern __shared__ __align__(128) unsigned char dyn_smem[];
-  __shared__ __align__(8) uint64_t full[kRowMaxStages];
-  __shared__ __align__(8) uint64_t carry_bar;  // the peer's carry for this CTA's next chunk has landed
-  __shared__ double carry_in;                  // ... written here by the peer
-  __shared__ double s_cin[2];                  // this chunk's incoming carry, for every warp
-  __shared__ float s_warp[2][NW];
-  __shared__ int s_abort;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  const int64_t row = blockIdx.x >> 1;
-  const Tin* src = x + row * ld_x;
-  Tout* dst = y + row * ld_y;
-  const int64_t nchunks = (n + kChunk - 1) / kChunk;
-  const int64_t mine = nchunks > r ? (nchunks - r + 1) / 2 : 0;  // chunks r, r + 2, ...
-
-  auto chunk_len = [&](int64_t c) { return n - c * kChunk < kChunk ? n - c * kChunk : kChunk; };
-  auto issue = [&](int64_t i) {  // this CTA's i-th chunk into stage i % stages
-    const int64_t c = r + 2 * i;
-    const int st = static_cast<int>(i % stages);
-    const uint32_t bytes = static_cast<uint32_t>(chunk_len(c) * static_cast<int64_t>(sizeof(Tin)) / 16 * 16);
-    if (bytes == 0) {
-      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sm100::smem_addr(&full[st])) : "memory");
-      return;
-    }
-    sm100::mbar_expect_tx(&full[st], bytes);
-    sm100::bulk_g2s(dyn_smem + st * kStageBytes, src + c * kChunk, bytes, &full[st]);
-  };
-
-  if (tid == 0) {
-    for (int st = 0; st < stages; ++st) sm100::mbar_init(&full[st], 1);
-    sm100::mbar_init(&carry_bar, 1);
-    s_abort = 0;
-    sm100::mbar_init_fence();
-  }
-  __syncthreads();
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-  pdl_wait();
-  pdl_trigger();
-  if (tid == 0)
-    for (int64_t i = 0; i < mine && i < stages; ++i) issue(i);
-  const uint32_t peer_carry = static_cast<uint32_t>(__cvta_generic_to_shared(&carry_in));
-  const uint32_t peer_bar = static_cast<uint32_t>(__cvta_generic_to_shared(&carry_bar));
-  uint32_t peer_carry_addr, peer_bar_addr;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(peer_carry_addr) : "r"(peer_carry), "r"(r ^ 1u));
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(peer_bar_addr) : "r"(peer_bar), "r"(r ^ 1u));
-
-  for (int64_t i = 0; i < mine; ++i) {
-    const int64_t c = r + 2 * i;
-    const int st = static_cast<int>(i % stages);
-    const int b = static_cast<int>(i & 1);
-    const int64_t len = chunk_len(c);
-    const int64_t bulk_elems = len * static_cast<int64_t>(sizeof(Tin)) / 16 * 16 / static_cast<int64_t>(sizeof(Tin));
-    const Tin* buf = reinterpret_cast<const Tin*>(dyn_smem + st * kStageBytes);
-    const Tin* gsrc = src + c * kChunk;
-    if (!s_abort && !sm100::mbar_wait_bounded(&full[st], static_cast<uint32_t>((i / stages) & 1), kBulkWaitNs)) {
-      s_abort = 1;
-      atomicExch(&g_scan_error, AXON_E_TIMEOUT);
-    }
-    const bool full_chunk = len == kChunk;
-    const int wbase = warp * static_cast<int>(PPW) + lane;
-    Vec<Tin> raw[NSEG];
-    float wsum = 0.f;
-#pragma unroll
-    for (int q = 0; q < NSEG; ++q) {
-      const int e0 = (wbase + q * 32) * E;
-      if (full_chunk || e0 + E <= bulk_elems) {
-        raw[q] = *reinterpret_cast<const Vec<Tin>*>(buf + e0);
-      } else {
-#pragma unroll
-        for (int e = 0; e < E; ++e) {
-          const int64_t j = e0 + e;
-          raw[q].e[e] = j < bulk_elems ? buf[j] : j < len ? gsrc[j] : from_f<Tin>(0.f);
-        }
-      }
-#pragma unroll
-      for (int e = 0; e < E; ++e) wsum += to_f(raw[q].e[e]);
-    }
-    wsum = warp_sum(wsum);
-    if (lane == 0) s_warp[b][warp] = wsum;
-    // the carry into this chunk: nothing for the row's first chunk, else
-    // the peer's running sum through the previous chunk (bounded wait)
-    if (tid == 0) {
-      double cin = 0.0;
-      if (c > 0) {
-        const uint32_t parity = static_cast<uint32_t>((r == 0 ? i - 1 : i) & 1);
-        if (!s_abort && !sm100::mbar_wait_bounded(&carry_bar, parity, kBulkWaitNs)) {
-          s_abort = 1;
-          atomicExch(&g_scan_error, AXON_E_TIMEOUT);
-        }
-        asm volatile("fence.acq_rel.cluster;" ::: "memory");
-        cin = *reinterpret_cast<volatile double*>(&carry_in);
-      }
-      s_cin[b] = cin;
-    }
-    __syncthreads();
-    if (tid == 0 && i + stages < mine) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      issue(i + stages);
-    }
-    float wi = lane < NW ? s_warp[b][lane] : 0.f;
-#pragma unroll
-    for (int o = 1; o < NW; o <<= 1) {
-      const float up = __shfl_up_sync(0xffffffffu, wi, o);
-      if (lane >= o) wi += up;
-    }
-    const float chunk_total = __shfl_sync(0xffffffffu, wi, NW - 1);
-    const float warp_excl = __shfl_sync(0xffffffffu, wi, warp > 0 ? warp - 1 : 0);
-    const double carry = s_cin[b];
-    // hand the running sum through this chunk on to the peer's next chunk
-    if (tid == 0 && c + 1 < nchunks) {
-      const double out = carry + static_cast<double>(chunk_total);
-      asm volatile("st.shared::cluster.f64 [%0], %1;" ::"r"(peer_carry_addr), "d"(out) : "memory");
-      asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(peer_bar_addr) : "memory");
-    }
-    const float carry_f = static_cast<float>(carry);
-    float seg_carry = warp > 0 ? warp_excl : 0.f;
-    Tout* cdst = dst + c * kChunk;
-#pragma unroll
-    for (int j = 0; j < NSEG; ++j) {
-      const int e0 = (wbase + j * 32) * E;
-      float v[E];
-#pragma unroll
-      for (int q = 0; q < E; ++q) v[q] = to_f(raw[j].e[q]);
-#pragma unroll
-      for (int q = 1; q < E; ++q) v[q] += v[q - 1];
-      const float own = v[E - 1];
-      float incl = own;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float up = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += up;
-      }
-      const float base = seg_carry + (incl - own);
-#pragma unroll
-      for (int q = 0; q < E; ++q) v[q] = carry_f + (base + v[q]);
-      if (full_chunk) store_packet<Tout, E>(cdst + e0, v, E, vec_out);
-      else if (e0 < len) store_packet<Tout, E>(cdst + e0, v, len - e0, vec_out);
-      seg_carry += __shfl_sync(0xffffffffu, incl, 31);
-    }
-  }
-  // copies may still be landing only if a wait gave up: let them finish
-  // before the CTA's shared memory is released (failure path only)
-  if (tid == 0 && s_abort)
-    for (int k = 0; k < 2000; ++k) __nanosleep(1000);
-  // neither CTA leaves while its peer may still store into its shared memory
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-template <typename Tin, typename Tout>
-int launch_rowpair(const void* x, void* y, int64_t m, int64_t n, int64_t ld_x, int64_t ld_y, const axon_tune_t& t,
-                   cudaStream_t s) {
-  if (!aligned16(x) || (m > 1 && (ld_x * sizeof(Tin)) % 16))
-    return fail(AXON_E_UNSUPPORTED, "axon_cumsum: variant 4 needs 16-byte aligned input rows");
-  if (m > 0x3fffffffLL) return fail(AXON_E_SHAPE, "axon_cumsum: too many rows (%lld)", (long long)m);
-  const int stages = t.stages ? t.stages : kPairStages;
-  if (stages < 2 || stages > 3) return fail(AXON_E_ARG, "axon_cumsum: variant 4 stages must be 2 or 3");
-  if (t.threads != 0 && t.threads != kPairThreads)
-    return fail(AXON_E_ARG, "axon_cumsum: variant 4 runs %d threads", kPairThreads);
-  const bool vec_out = aligned16(y) && (ld_y * sizeof(Tout)) % 16 == 0;
-  const size_t smem = static_cast<size_t>(stages) * kPairChunkKB * 1024;
-  auto kern = cumsum_rowpair<Tin, Tout>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  if (e != cudaSuccess) return fail(AXON_E_LAUNCH, "axon_cumsum: smem attribute: %s", cudaGetErrorString(e));
-  cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
-  cfg.gridDim = dim3(static_cast<unsigned>(2 * m), 1, 1);
-  cfg.blockDim = dim3(kPairThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 2 : 1;
-  e = cudaLaunchKernelEx(&cfg, kern, static_cast<const Tin*>(x), static_cast<Tout*>(y), n, ld_x, ld_y, vec_out,
-                         stages);
-  if (e != cudaSuccess) return fail(AXON_E_LAUNCH, "axon_cumsum: row-pair launch failed: %s", cudaGetErrorString(e));
-  return launch_status("axon_cumsum");
-}
-
-template <typename Tin>
-int dispatch_rowpair(int32_t out_dtype, const void* x, void* y, int64_t m, int64_t n, int64_t ld_x, int64_t ld_y,
-                     const axon_tune_t& t, cudaStream_t s) {
-  switch (out_dtype) {
-    case AXON_F32: return launch_rowpair<Tin, float>(x, y, m, n, ld_x, ld_y, t, s);
-    case AXON_BF16: return launch_rowpair<Tin, __nv_bfloat16>(x, y, m, n, ld_x, ld_y, t, s);
-    default: return fail(AXON_E_UNSUPPORTED, "axon_cumsum: unsupported output dtype %d", out_dtype);
-  }
-}
-
 // ---- variant 3: balanced chunk ranges --------------------------------------------
 //
 // One CTA per row loads the SMs unevenly whenever the row count is not a
@@ -1204,7 +980,7 @@ using namespace axon;
 extern "C" int64_t axon_cumsum_workspace_bytes(int64_t m, int64_t n, const axon_tune_t* tune) {
   axon_tune_t t = tune_or_default(tune);
   if (m < 0 || n < 0) return fail(AXON_E_SHAPE, "axon_cumsum_workspace_bytes: negative size");
-  if (t.variant == 1 || t.variant == 2 || t.variant == 4) return 0;
+  if (t.variant == 1 || t.variant == 2) return 0;
   const int64_t balanced = kBalSlotOffset + static_cast<int64_t>(sizeof(ScanSlot)) * kBalMaxSlots;
   if (t.variant == 3) return balanced;
   // variant 0 may run variant 3 (short aligned rows): room for either
@@ -1251,15 +1027,6 @@ extern "C" int axon_cumsum(const void* x, void* y, int64_t m, int64_t n, int64_t
       case AXON_BF16:
         return dispatch_balanced<__nv_bfloat16>(out_dtype, x, y, m, n, ld_x, ld_y, t, workspace, workspace_bytes,
                                                 s);
-      default: return fail(AXON_E_UNSUPPORTED, "axon_cumsum: unsupported input dtype %d", in_dtype);
-    }
-  }
-  if (t.variant == 4) {
-    if (m == 0 || n == 0) return AXON_OK;
-    cudaStream_t s = as_stream(stream);
-    switch (in_dtype) {
-      case AXON_F32: return dispatch_rowpair<float>(out_dtype, x, y, m, n, ld_x, ld_y, t, s);
-      case AXON_BF16: return dispatch_rowpair<__nv_bfloat16>(out_dtype, x, y, m, n, ld_x, ld_y, t, s);
       default: return fail(AXON_E_UNSUPPORTED, "axon_cumsum: unsupported input dtype %d", in_dtype);
     }
   }

@@ -72,15 +72,6 @@ def case_cumsum_balanced(gen):
     return lambda: ops.cumsum(x, out=y, workspace=ws, tune=tune)
 
 
-def case_cumsum_rowpair(gen):
-    """cumsum_rowpair: the nucleus config by a CTA pair per row (variant 4)."""
-    from . import ops
-
-    x = _cumsum_rows(gen)
-    y = torch.empty_like(x)
-    return lambda: ops.cumsum(x, out=y, tune={"variant": 4})
-
-
 def case_rope_split(gen):
     """rope_split_vec: the rope spec's layout, four [64, 2 Mi] bf16 inputs."""
     from . import ops
@@ -172,7 +163,6 @@ CASES = {
     "cast": (case_cast, "cast_vec"),
     "cumsum_lookback": (case_cumsum_lookback, "cumsum_lookback"),
     "cumsum_balanced": (case_cumsum_balanced, "cumsum_balanced"),
-    "cumsum_rowpair": (case_cumsum_rowpair, "cumsum_rowpair"),
     "rope_split": (case_rope_split, "rope_split_vec"),
     "softmax_mm": (case_softmax_mm, "row_prologue_kernel"),
     "qkv_split": (case_qkv_split, "resid3_reduce_kernel"),

@@ -71,20 +71,24 @@ def device_id() -> str:
 
         if torch.cuda.is_available():
             p = torch.cuda.get_device_properties(0)
-            return (f"{p.name} (sm_{p.major}{p.minor}0a build, {p.multi_processor_count} SMs, "
-                    f"{p.total_memory // 2**30} GiB), CUDA {torch.version.cuda}")
+            return (f"{p.name} (compute capability {p.major}.{p.minor}, {p.multi_processor_count} SMs, "
+                    f"{p.total_memory // 2**30} GiB), torch CUDA {torch.version.cuda}")
     except Exception:
         pass
     return "unknown device"
 
 
 def source_commit(repo: Path) -> str:
+    """The source commit: git's HEAD, else AXON_SOURCE_COMMIT (a checkout
+    copied without its history, e.g. to a GPU host), else "unknown"."""
+    import os
+
     try:
         out = subprocess.run(["git", "rev-parse", "--short", "HEAD"], capture_output=True, text=True, cwd=repo,
                              timeout=10).stdout.strip()
-        return out or "unknown"
     except Exception:
-        return "unknown"
+        out = ""
+    return out or os.environ.get("AXON_SOURCE_COMMIT", "") or "unknown"
 
 
 def _correct(v) -> bool:

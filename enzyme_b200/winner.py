@@ -9,6 +9,8 @@ unverified, not wrong. The export copies the winning variant module to
 
 from __future__ import annotations
 
+import os
+
 import shutil
 from dataclasses import dataclass
 from pathlib import Path
@@ -98,9 +100,11 @@ def provenance(spec: KernelSpec, winner: WinnerRow, case_id: str) -> str:
         pass
     try:
         commit = subprocess.run(["git", "rev-parse", "--short", "HEAD"], capture_output=True, text=True,
-                                cwd=Path(__file__).resolve().parent, timeout=10).stdout.strip() or "unknown"
+                                cwd=Path(__file__).resolve().parent, timeout=10).stdout.strip()
     except Exception:
-        commit = "unknown"
+        commit = ""
+    # a checkout copied without its history (e.g. to a GPU host) names it here
+    commit = commit or os.environ.get("AXON_SOURCE_COMMIT", "") or "unknown"
     rec = {"spec": spec.name, "case": case_id, "device": device, "commit": commit,
            "sizes": dict(zip(spec.dim_vars, winner.sizes)),
            "tiles": dict(zip(spec.tile_args, winner.tile_values)), "hw_variant": winner.hw_variant,

@@ -173,12 +173,8 @@ AXON_API int64_t axon_cumsum_workspace_bytes(int64_t m, int64_t n, const axon_tu
  * first use and every completed call leaves it so; after AXON_E_TIMEOUT zero
  * it again. tune->stages (default 4) x tune->block_k (16 or 32 KB, default
  * 32) is the ring per CTA; 16-byte aligned input rows.
- * Variant 4: a cluster of two 256-thread CTAs per row; CTA r streams chunks
- * r, r + 2, ... (16 KB, tune->stages 2 or 3, default 3) and the float64
- * running sum passes between the two through distributed shared memory, so
- * a row streams at two CTAs' rate; no workspace, 16-byte aligned input rows.
- * Variants 1 to 4 record a bulk-copy or carry wait that gave up in a device
- * word: axon_cumsum_status(NULL, ...). */
+ * Variants 1, 2 and 3 record a bulk-copy or carry wait that gave up in a
+ * device word: axon_cumsum_status(NULL, ...). */
 AXON_API int axon_cumsum(const void* x, void* y, int64_t m, int64_t n, int64_t ld_x,
                 int64_t ld_y, int32_t in_dtype, int32_t out_dtype, void* workspace,
                 int64_t workspace_bytes, const axon_tune_t* tune, void* stream);
