@@ -78,3 +78,24 @@ def test_reference_style_spec_package_loads(tmp_path):
     install_axon_alias()
     spec = load_path(pkg)
     assert spec.name == "double"
+
+
+def test_cluster_scan_keys_fit_shared_memory():
+    """cumsum variant 1 stages a row slice of a multiple of 8 elements per CTA
+    in at most 200 KB: the nucleus rows (128256 fp32) need 4 or 8 CTAs."""
+    from enzyme_b200 import catalogue
+
+    cons = catalogue.constraints("cumsum_nucleus_sorted", 1, {"m": 256, "n": 128256}, 4,
+                                 ("TILES_IN_BLOCK_M", "TILES_IN_BLOCK_N"))
+    assert cons[0].allowed == (4, 8)
+    cons = catalogue.constraints("cumsum", 1, {"m": 8, "n": 1000}, 4, ("TILES_IN_BLOCK_M", "TILES_IN_BLOCK_N"))
+    assert cons[0].allowed == (1, 2, 4, 8)
+
+
+def test_profile_cases_list_without_a_gpu(capsys):
+    from enzyme_b200 import profile
+
+    assert profile.main(["--list"]) == 0
+    out = capsys.readouterr().out
+    for name in profile.CASES:
+        assert name in out

@@ -83,3 +83,14 @@ def test_decide_write_unmeasured_artifact_is_superseded(tmp_path):
     assert decide_write(p, 5.0, False) is None  # absent
     p.write_text('"""hand written"""\n')
     assert decide_write(p, 50.0, False) is None  # no measurement recorded
+
+
+def test_source_commit_off_git_comes_from_the_environment(tmp_path, monkeypatch):
+    """A checkout copied without its history (as to a GPU host) records the
+    commit it was copied from, when the caller names it."""
+    from enzyme_b200 import specialize
+
+    monkeypatch.setenv("AXON_SOURCE_COMMIT", "abc1234")
+    assert specialize.source_commit(tmp_path) == "abc1234"
+    monkeypatch.delenv("AXON_SOURCE_COMMIT")
+    assert specialize.source_commit(tmp_path) == "unknown"
