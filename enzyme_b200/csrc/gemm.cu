@@ -984,31 +984,13 @@ constexpr int kAttnThreads = (2 + kAttnSoftmaxWarps) * 32;
 constexpr int kAttnSoftmaxThreads = kAttnSoftmaxWarps * 32;
 
 struct AttnParams {
-  void* y;        // [s, D] output (splits == 1, bal == 0)
-  float* part;    // [splits][s][D] partial O (splits > 1), or [2 * bal][128][D] (bal > 0)
-  float* lpart;   // [splits][s] partial row sums, or [2 * bal][128]
+  void* y;        // [s, D] output (splits == 1)
+  float* part;    // [splits][s][D] partial O (splits > 1)
+  float* lpart;   // [splits][s] partial row sums
   int s;
   int splits, kblk_per_split;  // key blocks (128 keys) per split
-  int bal;        // > 0: balanced key ranges over exactly this many CTAs (see attn_bal_range)
   uint32_t idesc_s, idesc_o;
 };
-
-// Balanced key ranges: the nq x nkb (query block, key block) pairs in
-// query-major order are cut into `ctas` equal contiguous ranges, one per CTA,
-// so every CTA computes the same number of blocks whatever the query block
-// count (with two key splits, 64 query blocks would leave 20 of 148 SMs idle).
-// CTA c's range [c W / ctas, (c + 1) W / ctas) spans at most two query blocks
-// when W / ctas <= nkb; its k-th piece (k = 0, 1) is unit c + k * ctas, whose
-// partial O and row sums go to slot c + k * ctas.
-__host__ __device__ __forceinline__ int64_t attn_bal_start(int64_t c, int64_t w, int64_t ctas) { return c * w / ctas; }
-
-// Pieces of CTA c's range (0, 1 or 2).
-__host__ __device__ __forceinline__ int attn_bal_pieces(int64_t c, int64_t nq, int64_t nkb, int64_t ctas) {
-  const int64_t w = nq * nkb;
-  const int64_t g0 = attn_bal_start(c, w, ctas), g1 = attn_bal_start(c + 1, w, ctas);
-  if (g1 <= g0) return 0;
-  return static_cast<int>((g1 - 1) / nkb - g0 / nkb + 1);
-}
 
 template <int D, typename TA, typename TC>
 __global__ void __launch_bounds__(kAttnThreads, 1)
@@ -1052,19 +1034,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nq = (p.s + 127) / 128;
   const int nkb = (p.s + 127) / 128;
-  // balanced ranges: this CTA's units are blockIdx.x + k * bal, k < its pieces
-  const int units = p.bal > 0 ? attn_bal_pieces(blockIdx.x, nq, nkb, p.bal) * p.bal : nq * p.splits;
+  const int units = nq * p.splits;
   auto unit_range = [&](int u, int& qb, int& j0, int& j1) {
-    if (p.bal > 0) {
-      const int64_t w = static_cast<int64_t>(nq) * nkb;
-      const int64_t c = u % p.bal, k = u / p.bal;
-      const int64_t g0 = attn_bal_start(c, w, p.bal), g1 = attn_bal_start(c + 1, w, p.bal);
-      qb = static_cast<int>(g0 / nkb + k);
-      const int64_t q0 = static_cast<int64_t>(qb) * nkb;
-      j0 = static_cast<int>((g0 > q0 ? g0 : q0) - q0);
-      j1 = static_cast<int>((g1 < q0 + nkb ? g1 : q0 + nkb) - q0);
-      return;
-    }
     qb = u / p.splits;
     j0 = (u % p.splits) * p.kblk_per_split;
     j1 = j0 + p.kblk_per_split < nkb ? j0 + p.kblk_per_split : nkb;
@@ -1303,8 +1274,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const int64_t grow = static_cast<int64_t>(qb) * 128 + row;
       const bool row_ok = grow < p.s;
       const int split = u % p.splits;
-      // partial rows: [split][s] with key splits, [unit][128] with balanced ranges
-      const int64_t prow = p.bal > 0 ? static_cast<int64_t>(u) * 128 + row : static_cast<int64_t>(split) * p.s + grow;
       const float inv_l = 1.0f / l;
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
@@ -1313,15 +1282,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tmem_ld32(t_o + lane_off + c * 32, v);
         tmem_wait_ld();
         if (!row_ok) continue;
-        if (p.splits == 1 && p.bal == 0) {
+        if (p.splits == 1) {
 #pragma unroll
           for (int e = 0; e < 32; ++e) v[e] *= inv_l;
           store32<TC>(static_cast<TC*>(p.y) + grow * D + c * 32, v, c * 32, D);
         } else {
-          store32<float>(p.part + prow * D + c * 32, v, c * 32, D);
+          store32<float>(p.part + (static_cast<int64_t>(split) * p.s + grow) * D + c * 32, v, c * 32, D);
         }
       }
-      if ((p.splits > 1 || p.bal > 0) && row_ok) p.lpart[prow] = l;
+      if (p.splits > 1 && row_ok) p.lpart[static_cast<int64_t>(split) * p.s + grow] = l;
       tc_fence_before();
       mbar_arrive(oempty);
     }
@@ -1376,47 +1345,6 @@ __global__ void __launch_bounds__(256) attn_reduce_kernel(const float* __restric
   dst[1] = from_f<TC>(acc.y * r);
   dst[2] = from_f<TC>(acc.z * r);
   dst[3] = from_f<TC>(acc.w * r);
-}
-
-// Balanced ranges of attn_fused: row i of query block t gathers the pieces
-// of the CTAs whose ranges cover block t, in key order (CTA order), and
-// divides the summed O by the summed row sums. Four outputs per thread.
-template <typename TC>
-__global__ void __launch_bounds__(256) attn_reduce_bal_kernel(const float* __restrict__ part,
-                                                              const float* __restrict__ lpart, TC* __restrict__ y,
-                                                              int64_t s, int64_t d, int64_t nkb, int64_t ctas) {
-  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  pdl_wait();
-  pdl_trigger();
-  const int64_t per_row = d / 4;
-  if (idx >= s * per_row) return;
-  const int64_t i = idx / per_row, j = (idx - i * per_row) * 4;
-  const int64_t t = i / 128, r = i - t * 128;
-  const int64_t nq = (s + 127) / 128, w = nq * nkb;
-  const int64_t lo = t * nkb, hi = lo + nkb;
-  // the CTA whose range holds block pair lo
-  int64_t c = lo * ctas / w;
-  while (c > 0 && attn_bal_start(c, w, ctas) > lo) --c;
-  while (c + 1 < ctas && attn_bal_start(c + 1, w, ctas) <= lo) ++c;
-  float l = 0.f;
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (; c < ctas && attn_bal_start(c, w, ctas) < hi; ++c) {
-    if (attn_bal_start(c + 1, w, ctas) <= attn_bal_start(c, w, ctas)) continue;  // an empty range
-    const int64_t k = attn_bal_start(c, w, ctas) < lo ? 1 : 0;  // the second piece of a range begun earlier
-    const int64_t row = (c + k * ctas) * 128 + r;
-    l += lpart[row];
-    const float4 v = *reinterpret_cast<const float4*>(part + row * d + j);
-    acc.x += v.x;
-    acc.y += v.y;
-    acc.z += v.z;
-    acc.w += v.w;
-  }
-  const float rl = 1.0f / l;
-  TC* dst = y + i * d + j;
-  dst[0] = from_f<TC>(acc.x * rl);
-  dst[1] = from_f<TC>(acc.y * rl);
-  dst[2] = from_f<TC>(acc.z * rl);
-  dst[3] = from_f<TC>(acc.w * rl);
 }
 
 // ---- variant 2: CTA pairs (tcgen05 cta_group::2) ------------------------------------
@@ -2903,26 +2831,13 @@ namespace {
 
 struct AttnPlan {
   int splits, kblk_per_split;
-  int bal;  // > 0: balanced key ranges over this many CTAs
   int64_t ws_bytes;
 };
 
-// Work split: while the 128-row query blocks leave SMs idle, balanced key
-// ranges, one per CTA on every SM (unless tune.split asks for equal key
-// splits of the query blocks: at least two key blocks a split).
+// Key splits: while the 128-row query blocks leave SMs idle, at least two
+// key blocks a split.
 AttnPlan attn_plan(int64_t s, int64_t d, const axon_tune_t& t) {
   const int64_t nb = (s + 127) / 128;
-  int64_t ctas = sm_count();
-  if (t.max_ctas > 0 && t.max_ctas < ctas) ctas = t.max_ctas;
-  if (t.split == 0 && nb < ctas && nb * nb >= ctas) {
-    // ranges of at most nb pairs, so each spans at most two query blocks
-    AttnPlan pl;
-    pl.splits = 1;
-    pl.kblk_per_split = static_cast<int>(nb);
-    pl.bal = static_cast<int>(ctas);
-    pl.ws_bytes = (2 * ctas * 128 * d * 4 + 255) / 256 * 256 + 2 * ctas * 128 * 4;
-    return pl;
-  }
   int64_t splits = t.split;
   if (splits <= 0) {
     splits = nb >= sm_count() ? 1 : sm_count() / nb;
@@ -2935,7 +2850,6 @@ AttnPlan attn_plan(int64_t s, int64_t d, const axon_tune_t& t) {
   AttnPlan pl;
   pl.splits = static_cast<int>(splits);
   pl.kblk_per_split = static_cast<int>(per);
-  pl.bal = 0;
   pl.ws_bytes = splits > 1 ? (splits * s * d * 4 + 255) / 256 * 256 + splits * s * 4 : 0;
   return pl;
 }
@@ -2950,18 +2864,11 @@ int launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap&
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return fail(AXON_E_LAUNCH, "axon_attention: smem attribute: %s", cudaGetErrorString(e));
   const int64_t units = static_cast<int64_t>((ap.s + 127) / 128) * ap.splits;
-  const int grid = ap.bal > 0 ? ap.bal : static_cast<int>(balanced_grid(units, cap));
+  const int grid = static_cast<int>(balanced_grid(units, cap));
   kern<<<grid, kAttnThreads, smem, st>>>(mq, mk, mv, ap);
   int rc = launch_status("axon_attention");
-  if (rc || (ap.splits == 1 && ap.bal == 0)) return rc;
+  if (rc || ap.splits == 1) return rc;
   const int64_t packets = static_cast<int64_t>(ap.s) * (D / 4);
-  if (ap.bal > 0) {
-    launch_k(attn_reduce_bal_kernel<TC>, dim3(static_cast<unsigned>((packets + 255) / 256)), dim3(256), 0, st,
-             static_cast<const float*>(ap.part), static_cast<const float*>(ap.lpart), static_cast<TC*>(ap.y),
-             static_cast<int64_t>(ap.s), static_cast<int64_t>(D), static_cast<int64_t>((ap.s + 127) / 128),
-             static_cast<int64_t>(ap.bal));
-    return launch_status("axon_attention");
-  }
   launch_k(attn_reduce_kernel<TC>, dim3(static_cast<unsigned>((packets + 255) / 256)), dim3(256), 0, st,
            static_cast<const float*>(ap.part), static_cast<const float*>(ap.lpart), static_cast<TC*>(ap.y),
            static_cast<int64_t>(ap.s), static_cast<int64_t>(D), ap.splits);
@@ -3004,8 +2911,8 @@ extern "C" int axon_attention_fused(const void* q, const void* k_t, const void* 
   if (t.split < 0 || t.max_ctas < 0) return fail(AXON_E_ARG, "axon_attention_fused: negative tune field");
   const AttnPlan pl = attn_plan(s, d, t);
   if (pl.ws_bytes > 0 && (!workspace || workspace_bytes < pl.ws_bytes || !aligned16(workspace)))
-    return fail(AXON_E_ARG, "axon_attention_fused: the split keys need a 16-byte aligned workspace of %lld bytes",
-                (long long)pl.ws_bytes);
+    return fail(AXON_E_ARG, "axon_attention_fused: %d key splits need a 16-byte aligned workspace of %lld bytes",
+                pl.splits, (long long)pl.ws_bytes);
   CUtensorMap mq, mk, mv;
   int rc = make_map(&mq, q, ab_dtype, d, s, d, 64, 128, "q");  // [s, d]: 128 rows x 64 of the head dim
   if (!rc) rc = make_map(&mk, k_t, ab_dtype, s, d, s, 64, 64, "k_t");  // [d, s]: 64 keys x 64 of the head dim
@@ -3017,15 +2924,10 @@ extern "C" int axon_attention_fused(const void* q, const void* k_t, const void* 
     ap.part = static_cast<float*>(workspace);
     ap.lpart = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) +
                                         (static_cast<int64_t>(pl.splits) * s * d * 4 + 255) / 256 * 256);
-  } else if (pl.bal > 0) {
-    ap.part = static_cast<float*>(workspace);
-    ap.lpart = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) +
-                                        (2 * static_cast<int64_t>(pl.bal) * 128 * d * 4 + 255) / 256 * 256);
   }
   ap.s = static_cast<int>(s);
   ap.splits = pl.splits;
   ap.kblk_per_split = pl.kblk_per_split;
-  ap.bal = pl.bal;
   const uint32_t fmt = ab_dtype == AXON_BF16 ? 1u : 0u;
   const uint32_t base = (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 16) | ((128u >> 4) << 24);
   ap.idesc_s = base | ((128u >> 3) << 17);

@@ -496,13 +496,10 @@ AXON_API int axon_softmax_mm(const void* x, const void* w, void* y, void* worksp
  * S = q @ k_t_j per 128-key block into tensor memory, P = exp(S) (bf16, keys
  * past s zero) written by four softmax warps into a swizzled shared-memory
  * slab with the row sums kept in registers, O += P @ v_j in tensor memory,
- * y = O / l; scores never reach global memory. While the query blocks leave
- * SMs idle, the work is split over CTAs, the fp32 partial O and row sums
- * added in key order by a second pass: by default the (query block, key
- * block) pairs are cut into one equal contiguous range per CTA on every SM
- * (max_ctas caps the CTAs), or, with tune->split > 0, each query block's
- * keys into that many equal splits. workspace:
- * axon_attention_fused_workspace_bytes (0 when nothing is split). */
+ * y = O / l; scores never reach global memory. Key blocks are split over
+ * CTAs while the query blocks leave SMs idle (tune->split: splits, 0 = auto;
+ * max_ctas caps the grid), the fp32 partials added in order by a second
+ * pass. workspace: axon_attention_fused_workspace_bytes (0 without splits). */
 AXON_API int64_t axon_attention_fused_workspace_bytes(int64_t s, int64_t d, const axon_tune_t* tune);
 AXON_API int axon_attention_fused(const void* q, const void* k_t, const void* v, void* y, void* workspace,
                          int64_t workspace_bytes, int64_t s, int64_t d, int32_t ab_dtype,

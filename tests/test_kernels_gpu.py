@@ -154,11 +154,9 @@ def test_softmax_mm(dims, cuda_device):
     _close(y, f64.softmax_mm(*ins), 1e-2, 1e-2, f"softmax_mm {dims}")
 
 
-# the one-kernel default (d 64 / 128; balanced key ranges, equal, single and
-# explicit key splits, a capped grid, ragged s), then the two-GEMM form
-# (variant 1; d = 512 always)
+# the one-kernel default (d 64 / 128; auto, single and explicit key splits,
+# a capped grid, ragged s), then the two-GEMM form (variant 1; d = 512 always)
 @pytest.mark.parametrize("s,d,tune", [(1024, 128, None), (1000, 128, None), (2048, 64, None), (8192, 128, None),
-                                      (3000, 128, None), (4000, 64, {"max_ctas": 100}),
                                       (2048, 128, {"split": 1}), (1000, 128, {"split": 3}),
                                       (4096, 128, {"max_ctas": 5}), (136, 64, None),
                                       (1024, 128, {"variant": 1}), (1000, 128, {"variant": 1}),
