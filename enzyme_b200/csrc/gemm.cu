@@ -1758,6 +1758,37 @@ __device__ __forceinline__ bool wait_count(const int* ctr, int target, volatile 
   }
 }
 
+// Bounded wait for the reduction warps, whose counters other GPUs raise
+// late in the kernel: relaxed system-scope polls with a growing sleep (up to
+// 2 us) so the waiting warps take next to no issue slots or memory
+// bandwidth from the tile roles on the same SM, and one acquire fence once
+// the count is reached.
+__device__ __forceinline__ bool wait_count_idle(const int* ctr, int target, volatile int* abort_flag) {
+  auto ld = [&]() {
+    int v;
+    asm volatile("ld.relaxed.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+    return v;
+  };
+  const uint64_t t0 = globaltimer();
+  uint32_t nap = 64;
+  for (uint32_t i = 0;; ++i) {
+    if (ld() - target >= 0) {
+      asm volatile("fence.acq_rel.sys;" ::: "memory");
+      return true;
+    }
+    if ((i & 7) == 7) {
+      if (*abort_flag) return false;
+      if (globaltimer() - t0 > kTimeoutNs) {
+        *abort_flag = 1;
+        atomicExch(&g_gemm_error, AXON_E_TIMEOUT);
+        return false;
+      }
+    }
+    __nanosleep(nap);
+    if (nap < 2048) nap <<= 1;
+  }
+}
+
 // mbar_wait with cluster-scope acquire: for barriers a thread of the other
 // CTA of the pair arrives on after writing this CTA's shared memory.
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
@@ -1891,7 +1922,7 @@ __device__ void mlp_step_reduce_warp(const MlpParams& p, int rb, int lane, volat
     const int blk = lr / rows_per_block;
     if (blk > seen) {
       int got = 1;
-      if (lane == 0) got = wait_count<true>(p.arrive[p.peer_rank] + blk, target, abort_flag) ? 1 : 0;
+      if (lane == 0) got = wait_count_idle(p.arrive[p.peer_rank] + blk, target, abort_flag) ? 1 : 0;
       got = __shfl_sync(0xffffffffu, got, 0);
       if (!got) {
         ok = false;
