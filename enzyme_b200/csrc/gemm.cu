@@ -916,12 +916,14 @@ __global__ void __launch_bounds__(256) resid3_reduce_kernel(const float* __restr
 //
 // The spec's softmax has no max shift, so no running maximum and no
 // rescaling are needed: P = exp(S) feeds the second product directly and the
-// row sums add up. One CTA (576 threads) owns 128 query rows and a range of
+// row sums add up. One CTA (608 threads) owns 128 query rows and a range of
 // 128-key blocks:
 //   warp 0     TMA: the Q tile once per unit, then per key block the k_t slab
-//              [D, 128 keys] and the v slab [128 keys, D] (both consumed as
-//              MN-major B operands, as the GEMM consumes weights), two stages
-//              each, a k_t stage freed as soon as its scores are computed;
+//              [D, 128 keys] (consumed as an MN-major B operand, as the GEMM
+//              consumes weights), two stages, a stage refilled as soon as
+//              its scores are computed;
+//   warp 18    TMA: per key block the v slab [128 keys, D], two stages, each
+//              refilled once its second product has read it;
 //   warp 1     TMEM + MMA: S_j = Q @ k_t_j (M 128, N 128, K D) into one of two
 //              TMEM score buffers, then O += P_{j-1} @ v_{j-1} (N = D) into the
 //              TMEM output, so the next block's scores overlap this block's
@@ -980,7 +982,7 @@ __device__ __forceinline__ void add_pair(float2& sum, float2 v) {
 }
 
 constexpr int kAttnSoftmaxWarps = 16;
-constexpr int kAttnThreads = (2 + kAttnSoftmaxWarps) * 32;
+constexpr int kAttnThreads = (3 + kAttnSoftmaxWarps) * 32;  // + the v producer warp, last
 constexpr int kAttnSoftmaxThreads = kAttnSoftmaxWarps * 32;
 
 struct AttnParams {
@@ -1103,6 +1105,26 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           for (int c = 0; c < 2; ++c)
             tma_load_2d(&tmK, &kfull[stage], st + (a * 2 + c) * B_CHUNK, j * 128 + c * 64, a * 64);
         issued[stage] += 1;
+        if (++stage == 2) {
+          stage = 0;
+          ph ^= 1u;
+        }
+      }
+      if (!ok) break;
+    }
+  } else if (warp == 2 + kAttnSoftmaxWarps && lane == 0) {
+    // ---------------- TMA producer of v ----------------
+    // Its own thread, so a k_t slab is refilled as soon as its scores are
+    // computed instead of queueing behind the v slab of the block before,
+    // which waits for that block's softmax and second product.
+    int stage = 0;
+    uint32_t ph = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+      int qb, j0, j1;
+      unit_range(u, qb, j0, j1);
+      bool ok = true;
+      for (int j = j0; j < j1; ++j) {
+        uint8_t* st = skv + stage * KV_STAGE;
         if (!mbar_wait(&vempty[stage], ph ^ 1u, abort_flag)) {
           ok = false;
           break;
@@ -1195,7 +1217,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (!ok) break;
       tc_commit(ofull);
     }
-  } else if (warp >= 2) {
+  } else if (warp >= 2 && warp < 2 + kAttnSoftmaxWarps) {
     // ---------------- softmax and output ----------------
     const int q = warp & 3;             // TMEM lane quarter this warp may access
     const int kq = (warp - 2) >> 2;     // its quarter of the block's keys / O's columns
