@@ -101,6 +101,30 @@ class Workload:
     def job_work(self) -> float:  # whole-job work per step (all ranks)
         return self.per_step_work() * self.world
 
+    # End to end through the public call for workloads whose step reads
+    # `e2e_inputs()` and writes `e2e_output()` (single set): the inputs come
+    # from pinned host memory and the output goes back to it inside the
+    # timed loop. Workloads with rotating sets define their own.
+    def e2e_inputs(self):
+        raise NotImplementedError
+
+    def e2e_output(self):
+        raise NotImplementedError
+
+    def e2e_setup(self):
+        ins = self.e2e_inputs()
+        self.h = [t.cpu().pin_memory() for t in ins]
+        out = self.e2e_output()
+        self.ho = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+        self.h2d = sum(t.numel() * t.element_size() for t in self.h)
+        self.d2h = self.ho.numel() * self.ho.element_size()
+
+    def e2e_step(self, i):
+        for d, h in zip(self.e2e_inputs(), self.h):
+            d.copy_(h, non_blocking=True)
+        self.launch(0)
+        self.ho.copy_(self.e2e_output(), non_blocking=True)
+
     def _randn(self, *shape, dtype=torch.bfloat16, scale=1.0):
         t = torch.randn(*shape, device=self.dev, generator=self.gen)
         if scale != 1.0:
@@ -643,6 +667,12 @@ class QkvCte(Workload):
     def launch(self, i):
         ops.qkv_cte(*self.ins, self.w, out=self.y, workspace=self.ws)
 
+    def e2e_inputs(self):
+        return [*self.ins, self.w]
+
+    def e2e_output(self):
+        return self.y
+
     def cpu_step(self):
         from oracle import cpu_torch
 
@@ -685,6 +715,12 @@ class SoftmaxMM(Workload):
         x, w, y, ws = self.sets[i % self.nsets]
         ops.softmax_mm(x, w, out=y, workspace=ws)
 
+    def e2e_inputs(self):
+        return list(self.sets[0][:2])
+
+    def e2e_output(self):
+        return self.sets[0][2]
+
     def cpu_step(self):
         from oracle import cpu_torch
 
@@ -723,6 +759,12 @@ class Attention(Workload):
 
     def launch(self, i):
         ops.attention(self.q, self.kt, self.v, out=self.y, workspace=self.ws)
+
+    def e2e_inputs(self):
+        return [self.q, self.kt, self.v]
+
+    def e2e_output(self):
+        return self.y
 
     def cpu_step(self):
         from oracle import cpu_torch

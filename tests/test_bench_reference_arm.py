@@ -74,3 +74,17 @@ def test_reference_line(name):
     for key in ("metric", "unit", "cpu_baseline", "e2e", "higher_is_better", "config"):
         assert key in line
     assert line["e2e"]["h2d_bytes_per_step"] == 0
+
+
+def test_every_workload_has_an_end_to_end_path():
+    """`python bench.py --workload NAME` reports `e2e` for any workload: each
+    class either defines its own end-to-end step or names the inputs and the
+    output the generic one copies."""
+    import bench
+
+    for name, make in bench.WORKLOADS.items():
+        cls = getattr(make, "cls", make)
+        own = "e2e_setup" in vars(cls) or any("e2e_setup" in vars(b) for b in cls.__mro__[1:-1]
+                                              if b is not bench.Workload)
+        generic = "e2e_inputs" in vars(cls) and "e2e_output" in vars(cls)
+        assert own or generic, name
