@@ -1052,8 +1052,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(&vfull[b], 1);
       mbar_init(&vempty[b], 1);
       mbar_init(&sfull[b], 1);
-      mbar_init(&sempty[b], kAttnSoftmaxThreads);
-      mbar_init(&pfull[b], kAttnSoftmaxThreads);
+      mbar_init(&sempty[b], kAttnSoftmaxWarps);  // one arrival per softmax warp
+      mbar_init(&pfull[b], kAttnSoftmaxWarps);
       mbar_init(&pempty[b], 1);
     }
     for (int i = 0; i < 4; ++i) issued[i] = consumed[i] = 0;
@@ -1243,7 +1243,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tmem_ld32(t_s0 + sb * 128 + lane_off + kq * 32, v);
         tmem_wait_ld();
         tc_fence_before();
-        mbar_arrive(&sempty[sb]);
+        __syncwarp();  // every lane's scores are in registers: one arrival for the warp
+        if (lane == 0) mbar_arrive(&sempty[sb]);
         const int key0 = j * 128 + kq * 32;
         if (key0 + 32 > p.s) {  // the ragged last block: keys past s weigh nothing
 #pragma unroll
@@ -1269,7 +1270,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
         for (int t = 0; t < 4; ++t) *reinterpret_cast<uint4*>(line + (((cb + t) ^ (row & 7)) * 16)) = pk[t];
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P -> the tensor cores' reads
-        mbar_arrive(&pfull[pb]);
+        __syncwarp();  // the warp's P lines are written: one arrival for the warp
+        if (lane == 0) mbar_arrive(&pfull[pb]);
         if (++sb == 2) {
           sb = 0;
           sph ^= 1u;
