@@ -1042,11 +1042,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     j0 = (u % p.splits) * p.kblk_per_split;
     j1 = j0 + p.kblk_per_split < nkb ? j0 + p.kblk_per_split : nkb;
   };
-  // The i-th key block a unit visits: its range rotated by the unit index,
-  // so the CTAs running at once read different k_t / v slabs instead of all
-  // asking L2 for the same lines at the same time. Every role walks the same
-  // order; the order is fixed per unit, so results are deterministic.
-  auto key_block = [&](int u, int j0, int j1, int i) { return j0 + (i + u) % (j1 - j0); };
 
   if (threadIdx.x == 0) {
     mbar_init(qfull, 1);
@@ -1097,8 +1092,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       for (int a = 0; a < KA; ++a) tma_load_2d(&tmQ, qfull, sq + a * A_BYTES, a * 64, qb * 128);
       *q_issued += 1;
       bool ok = true;
-      for (int i = 0; i < j1 - j0; ++i) {
-        const int j = key_block(u, j0, j1, i);
+      for (int j = j0; j < j1; ++j) {
         uint8_t* st = skv + stage * KV_STAGE;
         if (!mbar_wait(&kempty[stage], ph ^ 1u, abort_flag)) {
           ok = false;
@@ -1129,8 +1123,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       int qb, j0, j1;
       unit_range(u, qb, j0, j1);
       bool ok = true;
-      for (int i = 0; i < j1 - j0; ++i) {
-        const int j = key_block(u, j0, j1, i);
+      for (int j = j0; j < j1; ++j) {
         uint8_t* st = skv + stage * KV_STAGE;
         if (!mbar_wait(&vempty[stage], ph ^ 1u, abort_flag)) {
           ok = false;
@@ -1189,7 +1182,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (!mbar_wait(qfull, uq & 1, abort_flag)) break;
       int prev = -1;
       uint32_t prev_ph = 0;
-      for (int i = 0; i < j1 - j0 && ok; ++i) {
+      for (int j = j0; j < j1 && ok; ++j) {
         if (!mbar_wait(&kfull[stage], ph, abort_flag) || !mbar_wait(&sempty[sb], sph ^ 1u, abort_flag)) {
           ok = false;
           break;
@@ -1206,12 +1199,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tc_commit(&sfull[sb]);
         tc_commit(&kempty[stage]);            // this k_t slab is read
         consumed[stage] += 1;
-        if (i == j1 - j0 - 1) tc_commit(qempty);  // the unit's last read of Q
+        if (j == j1 - 1) tc_commit(qempty);  // the unit's last read of Q
         if (++sb == 2) {
           sb = 0;
           sph ^= 1u;
         }
-        if (prev >= 0) mma2(prev, prev_ph, i == 1);
+        if (prev >= 0) mma2(prev, prev_ph, j == j0 + 1);
         prev = stage;
         prev_ph = ph;
         if (++stage == 2) {
@@ -1238,8 +1231,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       unit_range(u, qb, j0, j1);
       float l = 0.f;
       bool ok = true;
-      for (int i = 0; i < j1 - j0; ++i) {
-        const int j = key_block(u, j0, j1, i);
+      for (int j = j0; j < j1; ++j) {
         if (!mbar_wait_backoff(&sfull[sb], sph, abort_flag) ||
             !mbar_wait_backoff(&pempty[pb], pph ^ 1u, abort_flag)) {
           ok = false;

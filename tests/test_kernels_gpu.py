@@ -161,7 +161,7 @@ def test_softmax_mm(dims, cuda_device):
                                       (4096, 128, {"max_ctas": 5}), (136, 64, None),
                                       # the CTA-pair kernel: even and odd query-block counts, ragged s, splits
                                       (8192, 128, {"block_m": 256}), (1000, 128, {"block_m": 256}),
-                                      (1096, 128, {"block_m": 256}), (2048, 128, {"block_m": 256, "split": 1}),
+                                      (1100, 128, {"block_m": 256}), (2048, 128, {"block_m": 256, "split": 1}),
                                       (4096, 128, {"block_m": 256, "split": 3}),
                                       (1024, 128, {"variant": 1}), (1000, 128, {"variant": 1}),
                                       (2048, 128, {"variant": 1, "block_n": 128}),
