@@ -1659,369 +1659,6 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
-// ---- attention_nkilib on CTA pairs (tcgen05 cta_group::2), head dim 128 ----------
-//
-// The one-CTA kernel streams every key block's k_t and v slabs (64 KB) per
-// 128 query rows, and at 128 CTAs that stream from L2 sets the pace: a slab
-// arrives ~3 us after it is requested and a block takes ~1.7 us against
-// ~0.5 us of tensor work. Here a cluster of two CTAs owns 256 query rows
-// (CTA r: rows 128 r .. 128 r + 127 of the pair's pair of query blocks) and
-// every product is one tcgen05.mma.cta_group::2 (M = 256) issued by the
-// leader: for S = Q k_t_j each CTA stages its own Q and half of the k_t slab
-// (64 keys), for O += P v_j its own P and half of the v slab (64 of the
-// head dim), so each SM streams half the bytes per FLOP of the one-CTA
-// kernel. Each CTA's TMEM receives its own 128 rows of S and O, so the
-// softmax and the output are the one-CTA kernel's. Both CTAs' loads
-// complete on the leader's barriers, which the leader's producers arm with
-// both CTAs' bytes; the leader's MMA thread commits to the barriers of both
-// CTAs; softmax and output warps release score buffers, P slabs and O by
-// arriving on the leader's barriers. Every wait is bounded; a cluster
-// barrier precedes exit.
-constexpr int kAttnPairKStages = 3;
-constexpr int kAttnPairVStages = 3;
-
-template <typename TA, typename TC>
-__global__ void __launch_bounds__(kAttnThreads, 1)
-    attn_fused_pair(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                    const __grid_constant__ CUtensorMap tmV, AttnParams p) {
-  constexpr int D = 128, KA = 2;
-  constexpr int Q_BYTES = KA * A_BYTES;   // this CTA's 128 query rows x D
-  constexpr int KH_BYTES = KA * B_CHUNK;  // its half of a k_t slab: 64 keys per k-atom
-  constexpr int VH_BYTES = 2 * B_CHUNK;   // its half of a v slab: 64 of D per 64-key half
-  constexpr int KS = kAttnPairKStages, VS = kAttnPairVStages;
-  constexpr int P_BYTES = 2 * A_BYTES;    // [128, 128 keys] as two k-atoms
-  constexpr uint32_t TMEM_COLS = 512;     // S0 | S1 | O
-
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sq = smem;
-  uint8_t* sk = sq + Q_BYTES;
-  uint8_t* sv = sk + KS * KH_BYTES;
-  uint8_t* sp = sv + VS * VH_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sp + 2 * P_BYTES);
-  uint64_t* qfull = bars;
-  uint64_t* qempty = bars + 1;
-  uint64_t* kfull = bars + 2;            // [KS]
-  uint64_t* kempty = kfull + KS;         // [KS]
-  uint64_t* vfull = kempty + KS;         // [VS]
-  uint64_t* vempty = vfull + VS;         // [VS]
-  uint64_t* sfull = vempty + VS;         // [2] TMEM score buffers
-  uint64_t* sempty = sfull + 2;          // [2]
-  uint64_t* pfull = sempty + 2;          // [2] P slabs
-  uint64_t* pempty = pfull + 2;          // [2]
-  uint64_t* ofull = pempty + 2;
-  uint64_t* oempty = ofull + 1;
-  uint64_t* lbar = oempty + 1;           // a unit's partial row sums are in place
-  uint64_t* lfree = lbar + 1;            // ... and have been read
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 40);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* lred = reinterpret_cast<float*>(bars + 48);  // [key quarters 1..3][128 rows]
-
-  uint32_t rank;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
-  const bool leader = rank == 0;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nq = (p.s + 127) / 128;
-  const int nkb = (p.s + 127) / 128;
-  const int nqp = (nq + 1) / 2;  // pairs of query blocks
-  const int units = nqp * p.splits;
-  const int pair = static_cast<int>(blockIdx.x >> 1), npairs = static_cast<int>(gridDim.x >> 1);
-  auto unit_range = [&](int u, int& qb, int& j0, int& j1) {  // qb: this CTA's query block
-    qb = 2 * (u / p.splits) + static_cast<int>(rank);
-    j0 = (u % p.splits) * p.kblk_per_split;
-    j1 = j0 + p.kblk_per_split < nkb ? j0 + p.kblk_per_split : nkb;
-  };
-  auto on_leader = [](const void* bar) { return mapa_u32(smem_u32(bar), 0); };
-  auto on_peer = [](const void* bar) { return mapa_u32(smem_u32(bar), 1); };
-
-  if (threadIdx.x == 0) {
-    mbar_init(qfull, 1);
-    mbar_init(qempty, 1);
-    for (int b = 0; b < KS; ++b) {
-      mbar_init(&kfull[b], 1);
-      mbar_init(&kempty[b], 1);
-    }
-    for (int b = 0; b < VS; ++b) {
-      mbar_init(&vfull[b], 1);
-      mbar_init(&vempty[b], 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&sfull[b], 1);
-      mbar_init(&sempty[b], 2 * kAttnSoftmaxWarps);  // one arrival per softmax warp of either CTA
-      mbar_init(&pfull[b], 2 * kAttnSoftmaxWarps);
-      mbar_init(&pempty[b], 1);
-    }
-    mbar_init(ofull, 1);
-    mbar_init(oempty, 8);  // the four output warps of either CTA
-    mbar_init(lbar, kAttnSoftmaxThreads);
-    mbar_init(lfree, 128);
-    *abort_flag = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-  }
-  if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(TMEM_COLS)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-    tc_fence_before();
-  }
-  __syncthreads();
-  cluster_barrier();  // both CTAs' barriers exist before either is addressed remotely
-  tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-  const uint32_t t_s0 = tmem_base, t_o = tmem_base + 256;
-
-  if (warp == 0 && lane == 0) {
-    // ---------------- TMA: Q and this CTA's half of each k_t slab ----------------
-    int ks = 0;
-    uint32_t kph = 0;
-    int uq = 0;
-    for (int u = pair; u < units; u += npairs, ++uq) {
-      int qb, j0, j1;
-      unit_range(u, qb, j0, j1);
-      if (!mbar_wait(qempty, (uq & 1) ^ 1u, abort_flag)) break;
-      if (leader) mbar_expect_tx(qfull, 2 * Q_BYTES);
-#pragma unroll
-      for (int a = 0; a < KA; ++a) tma_load_2d_pair(&tmQ, on_leader(qfull), sq + a * A_BYTES, a * 64, qb * 128);
-      bool ok = true;
-      for (int j = j0; j < j1; ++j) {
-        if (!mbar_wait(&kempty[ks], kph ^ 1u, abort_flag)) {
-          ok = false;
-          break;
-        }
-        if (leader) mbar_expect_tx(&kfull[ks], 2 * KH_BYTES);
-#pragma unroll
-        for (int a = 0; a < KA; ++a)
-          tma_load_2d_pair(&tmK, on_leader(&kfull[ks]), sk + ks * KH_BYTES + a * B_CHUNK,
-                           j * 128 + static_cast<int>(rank) * 64, a * 64);
-        if (++ks == KS) {
-          ks = 0;
-          kph ^= 1u;
-        }
-      }
-      if (!ok) break;
-    }
-  } else if (warp == 2 + kAttnSoftmaxWarps && lane == 0) {
-    // ---------------- TMA: this CTA's half of each v slab ----------------
-    int vs = 0;
-    uint32_t vph = 0;
-    for (int u = pair; u < units; u += npairs) {
-      int qb, j0, j1;
-      unit_range(u, qb, j0, j1);
-      bool ok = true;
-      for (int j = j0; j < j1; ++j) {
-        if (!mbar_wait(&vempty[vs], vph ^ 1u, abort_flag)) {
-          ok = false;
-          break;
-        }
-        if (leader) mbar_expect_tx(&vfull[vs], 2 * VH_BYTES);
-#pragma unroll
-        for (int kb = 0; kb < 2; ++kb)
-          tma_load_2d_pair(&tmV, on_leader(&vfull[vs]), sv + vs * VH_BYTES + kb * B_CHUNK,
-                           static_cast<int>(rank) * 64, j * 128 + kb * 64);
-        if (++vs == VS) {
-          vs = 0;
-          vph ^= 1u;
-        }
-      }
-      if (!ok) break;
-    }
-  } else if (warp == 1 && lane == 0 && leader) {
-    // ---------------- MMA issuer (leader only) ----------------
-    int ks = 0, vs = 0, sb = 0, pb = 0;
-    uint32_t kph = 0, vph = 0, sph = 0, pph = 0;
-    int uq = 0;
-    bool ok = true;
-    auto commit_both = [&](uint64_t* bar) {
-      tc_commit_to(smem_u32(bar));
-      tc_commit_to(on_peer(bar));
-    };
-    // O += P @ v for the next block in order
-    auto mma2 = [&](bool first) {
-      if (!mbar_wait(&pfull[pb], pph, abort_flag) || !mbar_wait(&vfull[vs], vph, abort_flag)) {
-        ok = false;
-        return;
-      }
-      if (first && !mbar_wait(oempty, (uq & 1) ^ 1u, abort_flag)) {
-        ok = false;
-        return;
-      }
-      tc_fence_after();
-      const uint32_t pa = smem_u32(sp + pb * P_BYTES);
-      const uint32_t vb = smem_u32(sv + vs * VH_BYTES);
-#pragma unroll
-      for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          tc_mma_pair(t_o, sdesc(pa + kb * A_BYTES + k * 32, 16, 1024), sdesc(vb + kb * B_CHUNK + k * 2048, B_CHUNK, 1024),
-                      p.idesc_o, (first && kb == 0 && k == 0) ? 0u : 1u);
-      commit_both(&pempty[pb]);
-      commit_both(&vempty[vs]);
-      if (++pb == 2) {
-        pb = 0;
-        pph ^= 1u;
-      }
-      if (++vs == VS) {
-        vs = 0;
-        vph ^= 1u;
-      }
-    };
-    for (int u = pair; u < units && ok; u += npairs, ++uq) {
-      int qb, j0, j1;
-      unit_range(u, qb, j0, j1);
-      if (!mbar_wait(qfull, uq & 1, abort_flag)) break;
-      bool pending = false;
-      for (int j = j0; j < j1 && ok; ++j) {
-        if (!mbar_wait(&kfull[ks], kph, abort_flag) || !mbar_wait(&sempty[sb], sph ^ 1u, abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t qa = smem_u32(sq);
-        const uint32_t kt = smem_u32(sk + ks * KH_BYTES);
-#pragma unroll
-        for (int a = 0; a < KA; ++a)
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            tc_mma_pair(t_s0 + sb * 128, sdesc(qa + a * A_BYTES + k * 32, 16, 1024),
-                        sdesc(kt + a * B_CHUNK + k * 2048, B_CHUNK, 1024), p.idesc_s, (a | k) != 0 ? 1u : 0u);
-        commit_both(&sfull[sb]);
-        commit_both(&kempty[ks]);             // this k_t stage is read
-        if (j == j1 - 1) commit_both(qempty);  // the unit's last read of Q
-        if (++sb == 2) {
-          sb = 0;
-          sph ^= 1u;
-        }
-        if (++ks == KS) {
-          ks = 0;
-          kph ^= 1u;
-        }
-        if (pending) mma2(j == j0 + 1);
-        pending = true;
-      }
-      if (!ok) break;
-      if (pending) mma2(j1 - j0 == 1);
-      if (!ok) break;
-      commit_both(ofull);
-    }
-  } else if (warp >= 2 && warp < 2 + kAttnSoftmaxWarps) {
-    // ---------------- softmax and output (both CTAs, their own 128 rows) ----------------
-    const int q = warp & 3;             // TMEM lane quarter this warp may access
-    const int kq = (warp - 2) >> 2;     // its quarter of the block's keys / O's columns
-    const int row = q * 32 + lane;
-    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
-    int sb = 0, pb = 0;
-    uint32_t sph = 0, pph = 0;
-    int uq = 0;
-    for (int u = pair; u < units; u += npairs, ++uq) {
-      int qb, j0, j1;
-      unit_range(u, qb, j0, j1);
-      float l = 0.f;
-      bool ok = true;
-      for (int j = j0; j < j1; ++j) {
-        if (!mbar_wait_backoff(&sfull[sb], sph, abort_flag) ||
-            !mbar_wait_backoff(&pempty[pb], pph ^ 1u, abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        float v[32];
-        __syncwarp();
-        tmem_ld32(t_s0 + sb * 128 + lane_off + kq * 32, v);
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();  // every lane's scores are in registers: one arrival for the warp
-        if (lane == 0) mbar_arrive_cluster(on_leader(&sempty[sb]), 1);
-        const int key0 = j * 128 + kq * 32;
-        if (key0 + 32 > p.s) {  // the ragged last block: keys past s weigh nothing
-#pragma unroll
-          for (int kk = 0; kk < 32; ++kk)
-            if (key0 + kk >= p.s) v[kk] = -INFINITY;
-        }
-        uint4 pk[4];
-        float2 lsum = make_float2(0.f, 0.f);
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          uint32_t w[4];
-#pragma unroll
-          for (int e = 0; e < 8; e += 2) {
-            const float2 ex = exp_pair(v[t * 8 + e], v[t * 8 + e + 1]);
-            add_pair(lsum, ex);
-            w[e / 2] = cvt_pack2<TA>(ex.x, ex.y);
-          }
-          pk[t] = make_uint4(w[0], w[1], w[2], w[3]);
-        }
-        l += lsum.x + lsum.y;
-        uint8_t* line = sp + pb * P_BYTES + (kq >> 1) * A_BYTES + row * 128;
-        const int cb = (kq & 1) * 4;
-#pragma unroll
-        for (int t = 0; t < 4; ++t) *reinterpret_cast<uint4*>(line + (((cb + t) ^ (row & 7)) * 16)) = pk[t];
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P -> the tensor cores' reads
-        __syncwarp();  // the warp's P lines are written: one arrival for the warp
-        if (lane == 0) mbar_arrive_cluster(on_leader(&pfull[pb]), 1);
-        if (++sb == 2) {
-          sb = 0;
-          sph ^= 1u;
-        }
-        if (++pb == 2) {
-          pb = 0;
-          pph ^= 1u;
-        }
-      }
-      if (!ok) break;
-      // the row's four partial sums meet in shared memory; the key-quarter 0
-      // warps add them in key order and write the output
-      if (kq != 0) {
-        if (!mbar_wait(lfree, (uq & 1) ^ 1u, abort_flag)) break;  // the last unit's sums were read
-        lred[(kq - 1) * 128 + row] = l;
-      }
-      mbar_arrive(lbar);
-      if (kq != 0) continue;
-      if (!mbar_wait_backoff(lbar, uq & 1, abort_flag)) break;
-      l = ((l + lred[row]) + lred[128 + row]) + lred[256 + row];
-      mbar_arrive(lfree);
-      if (!mbar_wait_backoff(ofull, uq & 1, abort_flag)) break;
-      tc_fence_after();
-      const int64_t grow = static_cast<int64_t>(qb) * 128 + row;
-      const bool row_ok = grow < p.s;
-      const int split = u % p.splits;
-      const float inv_l = 1.0f / l;
-#pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        float v[32];
-        __syncwarp();
-        tmem_ld32(t_o + lane_off + c * 32, v);
-        tmem_wait_ld();
-        if (!row_ok) continue;
-        if (p.splits == 1) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) v[e] *= inv_l;
-          store32<TC>(static_cast<TC*>(p.y) + grow * D + c * 32, v, c * 32, D);
-        } else {
-          store32<float>(p.part + (static_cast<int64_t>(split) * p.s + grow) * D + c * 32, v, c * 32, D);
-        }
-      }
-      if (p.splits > 1 && row_ok) p.lpart[static_cast<int64_t>(split) * p.s + grow] = l;
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(on_leader(oempty), 1);
-    }
-  }
-
-  __syncthreads();
-  if (threadIdx.x == 0 && *abort_flag) {
-    // copies issued by this CTA may still be landing (failure path only)
-    for (int k = 0; k < 1000; ++k) __nanosleep(1000);
-  }
-  cluster_barrier();  // neither CTA leaves while the other may still address it
-  if (warp == 1) {
-    tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
-                 : "memory");
-  }
-}
-
 // ---- fused SwiGLU: both GEMMs (and, for tensor parallelism, the reduction) in one kernel
 //
 // y = (silu(x @ W_gate) * (x @ W_up)) @ W_down with the f16 activation of
@@ -3249,20 +2886,16 @@ namespace {
 
 struct AttnPlan {
   int splits, kblk_per_split;
-  bool pair;  // the CTA-pair kernel (head dim 128; tune.block_m 128 asks for the one-CTA kernel)
   int64_t ws_bytes;
 };
 
-// Key splits: while the query blocks (in pairs, for the CTA-pair kernel)
-// leave SMs idle, at least two key blocks a split.
+// Key splits: while the 128-row query blocks leave SMs idle, at least two
+// key blocks a split.
 AttnPlan attn_plan(int64_t s, int64_t d, const axon_tune_t& t) {
   const int64_t nb = (s + 127) / 128;
-  const bool pair = d == 128 && t.block_m == 256;
-  const int64_t workers = pair ? sm_count() / 2 : sm_count();
-  const int64_t rows = pair ? (nb + 1) / 2 : nb;
   int64_t splits = t.split;
   if (splits <= 0) {
-    splits = rows >= workers ? 1 : workers / rows;
+    splits = nb >= sm_count() ? 1 : sm_count() / nb;
     if (splits > nb / 2) splits = nb / 2;
     if (splits < 1) splits = 1;
   }
@@ -3272,7 +2905,6 @@ AttnPlan attn_plan(int64_t s, int64_t d, const axon_tune_t& t) {
   AttnPlan pl;
   pl.splits = static_cast<int>(splits);
   pl.kblk_per_split = static_cast<int>(per);
-  pl.pair = pair;
   pl.ws_bytes = splits > 1 ? (splits * s * d * 4 + 255) / 256 * 256 + splits * s * 4 : 0;
   return pl;
 }
@@ -3296,61 +2928,6 @@ int launch_attn(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap&
            static_cast<const float*>(ap.part), static_cast<const float*>(ap.lpart), static_cast<TC*>(ap.y),
            static_cast<int64_t>(ap.s), static_cast<int64_t>(D), ap.splits);
   return launch_status("axon_attention");
-}
-
-// The CTA-pair kernel: clusters of two CTAs, each pair on two query blocks
-// and a key split; the grid is capped at the pairs the GPU holds at once.
-template <typename TA, typename TC>
-int launch_attn_pair(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const AttnParams& ap,
-                     cudaStream_t st) {
-  constexpr size_t smem = static_cast<size_t>(2) * A_BYTES + kAttnPairKStages * 2 * B_CHUNK +
-                          kAttnPairVStages * 2 * B_CHUNK + 2 * 2 * A_BYTES + 48 * 8 + 3 * 128 * 4 + 1024;
-  auto kern = attn_fused_pair<TA, TC>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  if (e != cudaSuccess) return fail(AXON_E_LAUNCH, "axon_attention: smem attribute: %s", cudaGetErrorString(e));
-  cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.blockDim = dim3(kAttnThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  static int pairs_cap = 0;
-  if (pairs_cap == 0) {
-    cfg.gridDim = dim3(2, 1, 1);
-    int clusters = 0;
-    e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
-    if (e != cudaSuccess || clusters <= 0)
-      return fail(AXON_E_LAUNCH, "axon_attention: no room for a CTA pair (%s)", cudaGetErrorString(e));
-    pairs_cap = clusters;
-  }
-  const int64_t units = static_cast<int64_t>(((ap.s + 127) / 128 + 1) / 2) * ap.splits;
-  const int64_t pairs = units < pairs_cap ? units : pairs_cap;
-  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
-  e = cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, ap);
-  if (e != cudaSuccess) return fail(AXON_E_LAUNCH, "axon_attention: pair launch: %s", cudaGetErrorString(e));
-  int rc = launch_status("axon_attention");
-  if (rc || ap.splits == 1) return rc;
-  const int64_t packets = static_cast<int64_t>(ap.s) * (128 / 4);
-  launch_k(attn_reduce_kernel<TC>, dim3(static_cast<unsigned>((packets + 255) / 256)), dim3(256), 0, st,
-           static_cast<const float*>(ap.part), static_cast<const float*>(ap.lpart), static_cast<TC*>(ap.y),
-           static_cast<int64_t>(ap.s), static_cast<int64_t>(128), ap.splits);
-  return launch_status("axon_attention");
-}
-
-template <typename TA>
-int dispatch_attn_pair(int32_t c_dtype, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
-                       const AttnParams& ap, cudaStream_t st) {
-  switch (c_dtype) {
-    case AXON_BF16: return launch_attn_pair<TA, __nv_bfloat16>(mq, mk, mv, ap, st);
-    case AXON_F16: return launch_attn_pair<TA, __half>(mq, mk, mv, ap, st);
-    case AXON_F32: return launch_attn_pair<TA, float>(mq, mk, mv, ap, st);
-    default: return fail(AXON_E_UNSUPPORTED, "axon_attention: unsupported output dtype %d", c_dtype);
-  }
 }
 
 template <int D, typename TA>
@@ -3413,13 +2990,6 @@ extern "C" int axon_attention_fused(const void* q, const void* k_t, const void* 
   int64_t cap = sm_count();
   if (t.max_ctas > 0 && t.max_ctas < cap) cap = t.max_ctas;
   cudaStream_t st = as_stream(stream);
-  if (pl.pair) {  // M = 256 per product, over the CTA pair
-    const uint32_t base2 = (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 16) | ((256u >> 4) << 24);
-    ap.idesc_s = base2 | ((128u >> 3) << 17);
-    ap.idesc_o = base2 | ((128u >> 3) << 17);
-    return ab_dtype == AXON_BF16 ? dispatch_attn_pair<__nv_bfloat16>(c_dtype, mq, mk, mv, ap, st)
-                                 : dispatch_attn_pair<__half>(c_dtype, mq, mk, mv, ap, st);
-  }
   if (ab_dtype == AXON_BF16)
     return d == 64 ? dispatch_attn<64, __nv_bfloat16>(c_dtype, mq, mk, mv, ap, cap, st)
                    : dispatch_attn<128, __nv_bfloat16>(c_dtype, mq, mk, mv, ap, cap, st);

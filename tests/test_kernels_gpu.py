@@ -159,10 +159,6 @@ def test_softmax_mm(dims, cuda_device):
 @pytest.mark.parametrize("s,d,tune", [(1024, 128, None), (1000, 128, None), (2048, 64, None), (8192, 128, None),
                                       (2048, 128, {"split": 1}), (1000, 128, {"split": 3}),
                                       (4096, 128, {"max_ctas": 5}), (136, 64, None),
-                                      # the CTA-pair kernel: even and odd query-block counts, ragged s, splits
-                                      (8192, 128, {"block_m": 256}), (1000, 128, {"block_m": 256}),
-                                      (1100, 128, {"block_m": 256}), (2048, 128, {"block_m": 256, "split": 1}),
-                                      (4096, 128, {"block_m": 256, "split": 3}),
                                       (1024, 128, {"variant": 1}), (1000, 128, {"variant": 1}),
                                       (2048, 128, {"variant": 1, "block_n": 128}),
                                       (2048, 64, {"variant": 1, "block_n": 64}), (512, 512, None)])
