@@ -1747,12 +1747,6 @@ __device__ __forceinline__ int ld_acquire_gpu_s32(const int* p) {
   return v;
 }
 
-__device__ __forceinline__ int ld_acquire_sys_s32(const int* p) {
-  int v;
-  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
 __device__ __forceinline__ void red_release_sys_add(int* p, int v) {
   asm volatile("red.release.sys.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -1761,15 +1755,13 @@ __device__ __forceinline__ void st_shared_cluster_s32(uint32_t addr, int v) {
   asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
 }
 
-// Bounded wait until *ctr reaches target (wrap-safe); sys: the counter is
-// written by other GPUs.
-template <bool SYS>
+// Bounded wait until *ctr (raised by other CTAs of this GPU) reaches target
+// (wrap-safe).
 __device__ __forceinline__ bool wait_count(const int* ctr, int target, volatile int* abort_flag) {
-  auto ld = [&]() { return SYS ? ld_acquire_sys_s32(ctr) : ld_acquire_gpu_s32(ctr); };
-  if (ld() - target >= 0) return true;
+  if (ld_acquire_gpu_s32(ctr) - target >= 0) return true;
   const uint64_t t0 = globaltimer();
   for (uint32_t i = 1;; ++i) {
-    if (ld() - target >= 0) return true;
+    if (ld_acquire_gpu_s32(ctr) - target >= 0) return true;
     if ((i & 15) == 0) {
       if (*abort_flag) return false;
       if (globaltimer() - t0 > kTimeoutNs) {
@@ -2113,7 +2105,7 @@ __global__ void __launch_bounds__(mlp_threads(MODE), 1)
       if (t < 0) break;
       const MlpTile x = mlp_tile(t, grid);
       if (x.kind == 1) {
-        if (!wait_count<false>(p.ready + x.r, 8 * grid.ta_row, abort_flag)) break;
+        if (!wait_count(p.ready + x.r, 8 * grid.ta_row, abort_flag)) break;
         asm volatile("fence.proxy.async.global;" ::: "memory");  // generic-proxy activation stores -> TMA reads
       }
       const int kblocks = x.kind == 0 ? kb_a : kb_b;
