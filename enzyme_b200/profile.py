@@ -126,6 +126,27 @@ def case_attention_two_gemm(gen):
     return lambda: ops.attention(q, kt, v, out=y, tune={"variant": 1})
 
 
+def case_rmsnorm_matmul(gen):
+    """row_bulk_kernel (rsqrt of the row sums of squares) and the row-scaled
+    tcgen05 GEMM of rmsnorm_matmul at m 1024, n 8192, k 8192."""
+    from . import ops
+
+    x, w = _randn(1024, 8192, gen=gen), _randn(8192, 8192, gen=gen)
+    y = torch.empty(1024, 8192, dtype=torch.bfloat16, device="cuda")
+    ws = torch.empty(4 * 1024, dtype=torch.uint8, device="cuda")
+    return lambda: ops.rmsnorm_matmul(x, w, out=y, workspace=ws)
+
+
+def case_softmax_long(gen):
+    """row_streaming_kernel: softmax of 1024 fp32 rows of 65536 (256 KB:
+    past the bulk kernel's 32 KB rows and one CTA's registers)."""
+    from . import ops
+
+    x = torch.randn(1024, 65536, device="cuda", generator=gen)
+    y = torch.empty_like(x)
+    return lambda: ops.softmax(x, out=y)
+
+
 def _tp_shard(gen, inter):
     h = 4096
     x = _randn(4096, h, gen=gen)
@@ -168,6 +189,8 @@ CASES = {
     "qkv_split": (case_qkv_split, "resid3_reduce_kernel"),
     "attention": (case_attention, "attn_reduce_kernel"),
     "attention_two_gemm": (case_attention_two_gemm, "recip_sum_kernel"),
+    "rmsnorm_matmul": (case_rmsnorm_matmul, "gemm_tcgen05"),
+    "softmax_long": (case_softmax_long, "row_streaming_kernel"),
     "tp_slabs": (case_tp_slabs, "tp_reduce_push_kernel"),
     "tp_step": (case_tp_step, "swiglu_fused_pair"),
 }
