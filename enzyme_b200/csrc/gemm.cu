@@ -1722,7 +1722,8 @@ struct MlpParams {
   int rows_per_owner;
   int world;
   __half* act;              // [m, n1] f16
-  int* ready;               // [row blocks] phase-A epilogue warps done, then the tile counter
+  int* ready;               // [row blocks] phase-A epilogue warps done, the tile counter, the
+                            // reduction warps' unit counter, [row blocks] phase-B warps done
   int m, n1, k1, n2;
   int64_t ldc;
   int stages;
@@ -1921,9 +1922,9 @@ __device__ void mlp_step_reduce_warp(const MlpParams& p, int rb, int lane, volat
   const int units = rows_local * chunks;
   const int tb_row = (p.n2 + 255) / 256;
   // arrival count of a complete row block: kMlpStep counts granules into the
-  // owner (32 per tile, over the world ranks' tiles); kMlpStepMC counts every
-  // epilogue warp of every rank's tiles into every rank
-  const int per_block = MODE == kMlpStepMC ? W * tb_row * 8 : 32 * tb_row;
+  // owner (32 per tile, over the world ranks' tiles); kMlpStepMC counts one
+  // per rank (its last warp of the block publishes it)
+  const int per_block = MODE == kMlpStepMC ? W : 32 * tb_row;
   const int target = p.epoch * per_block;
   const int64_t slot = static_cast<int64_t>(rows_local) * p.n2;
   int* ctr = p.ready + rb + 1;
@@ -2238,10 +2239,23 @@ __global__ void __launch_bounds__(mlp_threads(MODE), 1)
           const int64_t col = static_cast<int64_t>(x.c) * BN + c * 32;
           if (row_ok && col < p.n2) store32<__half>(prow + col, v, col, p.n2);
         }
-        asm volatile("fence.proxy.alias;" ::: "memory");  // unicast stores -> the switch's multicast reads
-        __threadfence_system();
+        // Count the warp's rows into this rank's row-block count (GPU scope,
+        // release); the warp that completes the block's count acquires the
+        // other warps' stores and alone publishes the block to every rank
+        // with one system-scope fence -- a system fence per warp and tile
+        // stalls the epilogues and, through them, the tiles.
         __syncwarp();
-        if (lane < p.world) red_release_sys_add(p.arrive[lane] + x.r, 1);
+        if (lane == 0) {
+          int old;
+          asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(p.ready + grid.rb + 2 + x.r)
+                       : "memory");
+          if (old == 8 * grid.tb_row - 1) {
+            asm volatile("fence.proxy.alias;" ::: "memory");  // unicast stores -> the switch's multicast reads
+            __threadfence_system();
+            for (int d = 0; d < p.world; ++d)
+              asm volatile("red.relaxed.sys.global.add.s32 [%0], 1;" ::"l"(p.arrive[d] + x.r) : "memory");
+          }
+        }
       } else if constexpr (MODE != kMlpLocal) {
         __half* stg = reinterpret_cast<__half*>(smem + S * STAGE + 512) + q * 32 * kPeerStageHalves;
         GemmParams gp{};
@@ -2471,7 +2485,7 @@ int launch_swiglu_fused(const CUtensorMap& mx, const CUtensorMap& mg, const CUte
   if (mp.max_ctas > 0 && mp.max_ctas / 2 < pairs) pairs = mp.max_ctas / 2 > 0 ? mp.max_ctas / 2 : 1;
   if (tiles < pairs) pairs = tiles;
   // row-block counters and the tile counter start at zero every call
-  e = cudaMemsetAsync(mp.ready, 0, static_cast<size_t>(rb + 2) * sizeof(int), s);
+  e = cudaMemsetAsync(mp.ready, 0, static_cast<size_t>(2 * rb + 2) * sizeof(int), s);
   if (e != cudaSuccess) return fail(AXON_E_CUDA, "axon_silu_mlp: counter reset: %s", cudaGetErrorString(e));
   cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
   e = cudaLaunchKernelEx(&cfg, kern, mx, mg, mu, ma, md, mp);
@@ -2479,9 +2493,10 @@ int launch_swiglu_fused(const CUtensorMap& mx, const CUtensorMap& mg, const CUte
   return launch_status("axon_silu_mlp");
 }
 
-// Bytes of the fused kernel's counters: one per 256-row block, the tile
-// counter and the phase-C counter.
-int64_t swiglu_counter_bytes(int64_t m) { return ((m + 255) / 256 + 2) * 4; }
+// Bytes of the fused kernel's counters: one per 256-row block (activation
+// written), the tile counter, the reduction warps' unit counter and one per
+// 256-row block (down-projection partials written, kMlpStepMC).
+int64_t swiglu_counter_bytes(int64_t m) { return (2 * ((m + 255) / 256) + 2) * 4; }
 
 // The fused SwiGLU (precision 4): x [m, k1] bf16, w1/w2 [k1, n1] bf16, w3h [n1, n2]
 // f16 (the caller's f16 copy of W_down), act [m, n1] f16 and counters from the
