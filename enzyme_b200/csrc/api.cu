@@ -62,15 +62,18 @@ static const char* kVariants[][2] = {
     {"rmsnorm",
      "{\"op\":\"rmsnorm\",\"variants\":[{\"id\":0,\"name\":\"auto_bulk_or_resident\",\"knobs\":{\"threads\":[0,64,128,256,512,1024]}},"
      "{\"id\":1,\"name\":\"row_streaming\",\"knobs\":{\"threads\":[0,128,256,512,1024]}},"
-     "{\"id\":2,\"name\":\"row_bulk_warp\",\"knobs\":{\"threads\":[0,128,256,512,1024]}}]}"},
+     "{\"id\":2,\"name\":\"row_bulk_warp\",\"knobs\":{\"threads\":[0,128,256,512,1024]}},"
+     "{\"id\":3,\"name\":\"row_bulk_cta\",\"knobs\":{\"threads\":[0,256,512,1024],\"block_k\":[0,4,8,16,32]}}]}"},
     {"layernorm",
      "{\"op\":\"layernorm\",\"variants\":[{\"id\":0,\"name\":\"auto_bulk_or_resident\",\"knobs\":{\"threads\":[0,64,128,256,512,1024]}},"
      "{\"id\":1,\"name\":\"row_streaming\",\"knobs\":{\"threads\":[0,128,256,512,1024]}},"
-     "{\"id\":2,\"name\":\"row_bulk_warp\",\"knobs\":{\"threads\":[0,128,256,512,1024]}}]}"},
+     "{\"id\":2,\"name\":\"row_bulk_warp\",\"knobs\":{\"threads\":[0,128,256,512,1024]}},"
+     "{\"id\":3,\"name\":\"row_bulk_cta\",\"knobs\":{\"threads\":[0,256,512,1024],\"block_k\":[0,4,8,16,32]}}]}"},
     {"softmax",
      "{\"op\":\"softmax\",\"variants\":[{\"id\":0,\"name\":\"auto_bulk_or_resident\",\"knobs\":{\"threads\":[0,64,128,256,512,1024]}},"
      "{\"id\":1,\"name\":\"row_streaming\",\"knobs\":{\"threads\":[0,128,256,512,1024]}},"
-     "{\"id\":2,\"name\":\"row_bulk_warp\",\"knobs\":{\"threads\":[0,128,256,512,1024]}}]}"},
+     "{\"id\":2,\"name\":\"row_bulk_warp\",\"knobs\":{\"threads\":[0,128,256,512,1024]}},"
+     "{\"id\":3,\"name\":\"row_bulk_cta\",\"knobs\":{\"threads\":[0,256,512,1024],\"block_k\":[0,4,8,16,32]}}]}"},
     {"rope",
      "{\"op\":\"rope\",\"variants\":[{\"id\":0,\"name\":\"token_blocked\",\"knobs\":{}},"
      "{\"id\":1,\"name\":\"flat_vec16\",\"knobs\":{\"threads\":[0,128,256]}}]}"},

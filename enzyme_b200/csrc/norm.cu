@@ -10,7 +10,12 @@
 // whose starts are not 16-byte aligned: a CTA walks its row once per pass;
 // the second pass re-reads the row from L2 (rows in flight are far smaller
 // than the 126 MB L2). Variant 2 ("row_bulk_warp", below) stages rows in
-// shared memory with bulk copies and reduces one row per warp.
+// shared memory with bulk copies and reduces one row per warp. Variant 3
+// ("row_bulk_cta") stages rows of up to ~200 KB in shared memory chunk by
+// chunk, one persistent CTA per row at a time, refilling each chunk with the
+// CTA's next row as soon as the output pass has read it. Variant 0 picks
+// variant 3 for rows of 16 KB and more, variant 2 for shorter rows, when
+// there is at least a row per SM, else the register-resident kernel.
 #include <type_traits>
 
 #include "common.cuh"
@@ -463,6 +468,222 @@ __global__ void __launch_bounds__(1024) row_bulk_kernel(RowArgs a, int slots, ui
     for (int k = 0; k < 2000; ++k) __nanosleep(1000);
 }
 
+// Variant 3 ("row_bulk_cta"): one CTA per row, for rows past a warp's share
+// of shared memory (up to ~200 KB). The row is staged in shared memory by
+// 1-D bulk copies in chunks, each completing on its own mbarrier, so the
+// statistics pass starts on the first chunk while the others are landing.
+// CTAs are persistent over rows (row, row + grid, ...): as soon as the
+// output pass has read a chunk, that chunk's buffer is refilled with the same
+// chunk of the CTA's next row, so the next row's reads overlap this row's
+// writes -- the register-resident kernel (one CTA of a whole-row register
+// file per SM) loads, reduces and stores strictly in turn. One HBM read and
+// one HBM write per row; the rmsnorm weight is read from global memory (it
+// stays in L1/L2). Statistics are those of the other variants: fp32, two
+// passes over the staged row for layernorm and softmax.
+constexpr int kCtaThreads = 512;
+constexpr int kCtaBarBytes = 256;  // one mbarrier per chunk
+constexpr int kCtaMaxChunks = kCtaBarBytes / 8;
+constexpr int64_t kCtaMaxRowBytes = kBulkSmemBudget - kCtaBarBytes;
+constexpr int64_t kCtaChunkBytes = 16384;
+constexpr int64_t kCtaDefaultMinRowBytes = 16384;  // variant 0 runs variant 3 from this row size
+
+// Sum (or max) over all threads of the CTA. Ends with a CTA barrier, so every
+// shared-memory read issued before the call is complete on return.
+template <bool MAX>
+__device__ __forceinline__ float cta_allreduce(float v, float* red) {
+  v = MAX ? warp_max(v) : warp_sum(v);
+  const int nw = blockDim.x >> 5;
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float r = red[0];
+  for (int i = 1; i < nw; ++i) r = MAX ? fmaxf(r, red[i]) : r + red[i];
+  __syncthreads();
+  return r;
+}
+
+template <typename T, int OP>
+__global__ void __launch_bounds__(1024) row_cta_bulk_kernel(RowArgs a, uint32_t row_bytes, uint32_t chunk_bytes,
+                                                          int nch) {
+  constexpr int E = Vec<T>::E;
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ float red[32];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+  uint8_t* buf = smem + kCtaBarBytes;
+  const T* sx = reinterpret_cast<const T*>(buf);
+  const uint8_t* xb = static_cast<const uint8_t*>(a.x);
+  const int tid = threadIdx.x;
+  const uint32_t nt = blockDim.x;
+  const int64_t ld_bytes = a.ld_x * static_cast<int64_t>(sizeof(T));
+  const uint32_t pkc = chunk_bytes / 16;  // packets in a full chunk
+  const uint32_t npk = row_bytes / 16;    // packets in a row
+
+  // chunk c of `row` into its buffer; the last chunk may be shorter
+  auto issue = [&](int64_t row, int c) {
+    const uint32_t off = static_cast<uint32_t>(c) * chunk_bytes;
+    const uint32_t bytes = row_bytes - off < chunk_bytes ? row_bytes - off : chunk_bytes;
+    sm100::mbar_expect_tx(&bars[c], bytes);
+    sm100::bulk_g2s(buf + off, xb + row * ld_bytes + off, bytes, &bars[c]);
+  };
+  auto chunk_end = [&](int c) -> uint32_t {
+    const uint32_t e = static_cast<uint32_t>(c + 1) * pkc;
+    return e < npk ? e : npk;
+  };
+
+  if (tid == 0) {
+    for (int c = 0; c < nch; ++c) sm100::mbar_init(&bars[c], 1);
+    sm100::mbar_init_fence();
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_trigger();
+  if (tid == 0 && blockIdx.x < a.m)
+    for (int c = 0; c < nch; ++c) issue(blockIdx.x, c);
+
+  bool clean = true;
+  uint32_t parity = 0;
+  for (int64_t row = blockIdx.x; row < a.m; row += gridDim.x, parity ^= 1u) {
+    const int64_t next = row + gridDim.x;
+    // statistics pass, each chunk as soon as it has landed (every thread
+    // waits on every chunk, so the whole row is visible to it afterwards)
+    bool ok = true;
+    float s0 = OP == OP_SM ? -INFINITY : 0.f, s1 = 0.f;
+    for (int c = 0; c < nch; ++c) {
+      if (ok) ok = sm100::mbar_wait_bounded(&bars[c], parity, kRowWaitNs);
+      const uint32_t end = chunk_end(c);
+      for (uint32_t p = static_cast<uint32_t>(c) * pkc + tid; p < end; p += nt) {
+        const Vec<T> v = ld_smem_vec(sx + static_cast<size_t>(p) * E);
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const float f = to_f(v.e[e]);
+          if constexpr (OP == OP_RMS || OP == OP_RSQRT) s0 = fmaf(f, f, s0);
+          else if constexpr (OP == OP_LN) s0 += f;
+          else s0 = fmaxf(s0, f);
+        }
+      }
+    }
+    if (!__syncthreads_and(ok)) {  // the same decision in every thread
+      if (tid == 0) atomicExch(&g_row_error, AXON_E_TIMEOUT);
+      clean = false;
+      break;
+    }
+    if constexpr (OP == OP_RMS || OP == OP_RSQRT) {
+      s1 = rsqrtf(a.scale * cta_allreduce<false>(s0, red) + a.eps);
+    } else if constexpr (OP == OP_LN) {
+      s0 = cta_allreduce<false>(s0, red) / static_cast<float>(a.n);
+      float ss = 0.f;
+      for (uint32_t p = tid; p < npk; p += nt) {
+        const Vec<T> v = ld_smem_vec(sx + static_cast<size_t>(p) * E);
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const float d = to_f(v.e[e]) - s0;
+          ss = fmaf(d, d, ss);
+        }
+      }
+      s1 = rsqrtf(cta_allreduce<false>(ss, red) / static_cast<float>(a.n) + a.eps);
+    } else {  // OP_SM
+      s0 = cta_allreduce<true>(s0, red);
+      float sum = 0.f;
+      for (uint32_t p = tid; p < npk; p += nt) {
+        const Vec<T> v = ld_smem_vec(sx + static_cast<size_t>(p) * E);
+#pragma unroll
+        for (int e = 0; e < E; ++e) sum += __expf(to_f(v.e[e]) - s0);
+      }
+      s1 = 1.0f / cta_allreduce<false>(sum, red);
+    }
+    if constexpr (OP == OP_RSQRT) {
+      if (tid == 0) a.r_out[row] = s1;
+      // the reduction ended with a CTA barrier: the buffer is free
+      if (tid == 0 && next < a.m) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        for (int c = 0; c < nch; ++c) issue(next, c);
+      }
+    } else {
+      T* yr = static_cast<T*>(a.y) + row * a.ld_y;
+      const T* w = static_cast<const T*>(a.w);
+      for (int c = 0; c < nch; ++c) {
+        const uint32_t end = chunk_end(c);
+        for (uint32_t p = static_cast<uint32_t>(c) * pkc + tid; p < end; p += nt) {
+          const Vec<T> v = ld_smem_vec(sx + static_cast<size_t>(p) * E);
+          Vec<T> wv;
+          if constexpr (OP == OP_RMS) {
+            if (w != nullptr) wv = ld_vec(w + static_cast<size_t>(p) * E);
+          }
+          Vec<T> o;
+#pragma unroll
+          for (int e = 0; e < E; ++e) {
+            const float f = to_f(v.e[e]);
+            float r;
+            if constexpr (OP == OP_RMS) r = w != nullptr ? f * s1 * to_f(wv.e[e]) : f * s1;
+            else if constexpr (OP == OP_LN) r = (f - s0) * s1;
+            else r = __expf(f - s0) * s1;
+            o.e[e] = from_f<T>(r);
+          }
+          st_vec(yr + static_cast<size_t>(p) * E, o);
+        }
+        __syncthreads();  // every thread has read chunk c: refill it
+        if (tid == 0 && next < a.m) {
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          issue(next, c);
+        }
+      }
+    }
+  }
+  // A CTA that gave up may leave copies in flight: give them time to land
+  // before its shared memory is released (failure path only).
+  if (!clean && tid == 0)
+    for (int k = 0; k < 2000; ++k) __nanosleep(1000);
+}
+
+// tune: threads (a multiple of 32 in [64, 1024], default 512), block_k = chunk
+// size in KB (1..64, default 16 KB, doubled until the row has at most 32
+// chunks), max_ctas caps the persistent grid (default: every CTA that fits).
+template <typename T, int OP>
+int launch_rows_cta(const RowArgs& a, const axon_tune_t& t, cudaStream_t s, const char* name) {
+  const int64_t row_bytes = a.n * static_cast<int64_t>(sizeof(T));
+  if (row_bytes > kCtaMaxRowBytes)
+    return fail(AXON_E_UNSUPPORTED, "%s: rows of %lld bytes exceed the CTA bulk variant's %lld", name,
+                (long long)row_bytes, (long long)kCtaMaxRowBytes);
+  int threads = t.threads > 0 ? t.threads : kCtaThreads;
+  if (threads < 64) return fail(AXON_E_ARG, "%s: the CTA bulk variant runs at least 64 threads", name);
+  if (t.block_k < 0 || t.block_k > 64) return fail(AXON_E_ARG, "%s: block_k (chunk KB) must be in 1..64", name);
+  int64_t chunk = t.block_k > 0 ? static_cast<int64_t>(t.block_k) * 1024 : kCtaChunkBytes;
+  if (t.block_k == 0)
+    while ((row_bytes + chunk - 1) / chunk > kCtaMaxChunks) chunk *= 2;
+  const int64_t nch = (row_bytes + chunk - 1) / chunk;
+  if (nch > kCtaMaxChunks)
+    return fail(AXON_E_ARG, "%s: %lld chunks of %lld bytes, at most %d", name, (long long)nch, (long long)chunk,
+                kCtaMaxChunks);
+  if (t.max_ctas < 0) return fail(AXON_E_ARG, "%s: max_ctas must be >= 0", name);
+  const size_t smem = static_cast<size_t>(kCtaBarBytes + row_bytes);
+  auto kern = row_cta_bulk_kernel<T, OP>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return fail(AXON_E_LAUNCH, "%s: smem attribute: %s", name, cudaGetErrorString(e));
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem);
+  if (t.threads == 0 && e == cudaSuccess) {
+    // Rows in flight per SM set the pace: take 256 threads where 512 would
+    // let fewer rows (CTAs) be resident than shared memory allows. Measured
+    // on B200 (graph replay, inputs rotating past L2): layernorm 4096 x 16384
+    // bf16 48.7 us at 256 threads (6 CTAs per SM) vs 55.6 at 512 (4); 2048 x
+    // 8192 bf16 16.1 vs 20.7; softmax 2048 x 16384 fp32 (3 CTAs per SM
+    // either way) 49.3 at 512 vs 54.1; 4096 x 32768 fp32 (one) 211 vs 231.
+    int per_sm_256 = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm_256, kern, 256, smem) == cudaSuccess &&
+        per_sm_256 > per_sm) {
+      threads = 256;
+      per_sm = per_sm_256;
+    }
+  }
+  if (e != cudaSuccess || per_sm < 1)
+    return fail(AXON_E_LAUNCH, "%s: %d threads with %zu bytes of shared memory do not fit an SM", name, threads, smem);
+  int64_t grid = static_cast<int64_t>(sm_count()) * per_sm;
+  if (t.max_ctas > 0 && grid > t.max_ctas) grid = t.max_ctas;
+  if (grid > a.m) grid = a.m;
+  launch_k(kern, dim3(static_cast<unsigned>(grid)), dim3(threads), smem, s, a, static_cast<uint32_t>(row_bytes),
+           static_cast<uint32_t>(chunk), static_cast<int>(nch));
+  return launch_status(name);
+}
+
 template <typename T, int OP>
 int launch_rows_bulk(const RowArgs& a, const axon_tune_t& t, cudaStream_t s, const char* name) {
   const int64_t row_bytes = a.n * static_cast<int64_t>(sizeof(T));
@@ -516,9 +737,18 @@ int launch_rows(const RowArgs& a, const axon_tune_t& t, cudaStream_t s, const ch
   const int64_t nv = (a.n + E - 1) / E;
   const int64_t row_bytes = a.n * static_cast<int64_t>(sizeof(T));
   const bool bulk_ok = vec_ok && row_bytes % 16 == 0 && row_bytes <= kBulkMaxRowBytes;
-  // Default (variant 0, no thread count): the bulk warp-per-row kernel once
-  // there is at least a row per SM; it beat the register-resident kernel on
-  // every measured B200 shape (softmax 16384 x 4096 bf16: 62 vs 111 us).
+  // Default (variant 0, no thread count), once there is at least a row per
+  // SM: rows of 16 KB up to the shared-memory limit run the CTA-per-row bulk
+  // kernel (variant 3), shorter rows the bulk warp-per-row kernel (variant 2).
+  // Measured on B200 against the previous defaults: softmax 4096 x 32768 fp32
+  // 211 vs 261 us (register-resident), layernorm 4096 x 16384 bf16 48.7 vs
+  // 73.8 us and 2048 x 8192 bf16 16.1 vs 18.3 us (warp per row); at 8 KB rows
+  // the warp-per-row kernel stays ahead (rmsnorm 2048 x 4096 bf16 8.5 vs 9.5
+  // us). The warp-per-row kernel beat the register-resident one on every
+  // measured shape it takes (softmax 16384 x 4096 bf16: 62 vs 111 us).
+  if (OP != OP_RSQRT && t.variant == 0 && t.threads == 0 && vec_ok && row_bytes % 16 == 0 &&
+      row_bytes >= kCtaDefaultMinRowBytes && row_bytes <= kCtaMaxRowBytes && a.m >= sm_count())
+    return launch_rows_cta<T, OP>(a, t, s, name);
   if (t.variant == 0 && t.threads == 0 && bulk_ok && a.m >= sm_count()) return launch_rows_bulk<T, OP>(a, t, s, name);
   if (t.variant == 2) {
     if (!bulk_ok)
@@ -526,6 +756,13 @@ int launch_rows(const RowArgs& a, const axon_tune_t& t, cudaStream_t s, const ch
                   "%s: the bulk variant needs 16-byte aligned rows of a multiple of 16 bytes, at most %d bytes",
                   name, kBulkMaxRowBytes);
     return launch_rows_bulk<T, OP>(a, t, s, name);
+  }
+  if (t.variant == 3) {
+    if (!vec_ok || row_bytes % 16 || row_bytes > kCtaMaxRowBytes)
+      return fail(AXON_E_UNSUPPORTED,
+                  "%s: the CTA bulk variant needs 16-byte aligned rows of a multiple of 16 bytes, at most %lld bytes",
+                  name, (long long)kCtaMaxRowBytes);
+    return launch_rows_cta<T, OP>(a, t, s, name);
   }
   int tpr = 0, vpt = 0;
   if (t.variant == 0 && vec_ok) {
@@ -572,10 +809,10 @@ int launch_rows(const RowArgs& a, const axon_tune_t& t, cudaStream_t s, const ch
 template <int OP>
 int dispatch_rows(const RowArgs& a, int32_t dtype, const axon_tune_t* tune, void* stream, const char* name) {
   axon_tune_t t = tune_or_default(tune);
-  if (t.variant < 0 || t.variant > 2) return fail(AXON_E_ARG, "%s: unknown variant %d", name, t.variant);
-  if (t.variant == 2 && t.threads != 0 && (t.threads < 32 || t.threads > 1024 || t.threads % 32))
+  if (t.variant < 0 || t.variant > 3) return fail(AXON_E_ARG, "%s: unknown variant %d", name, t.variant);
+  if (t.variant >= 2 && t.threads != 0 && (t.threads < 32 || t.threads > 1024 || t.threads % 32))
     return fail(AXON_E_ARG, "%s: threads must be a multiple of 32 in [32, 1024], got %d", name, t.threads);
-  if (t.variant != 2 && t.threads != 0 && (t.threads < 32 || t.threads > 1024 || (t.threads & (t.threads - 1))))
+  if (t.variant < 2 && t.threads != 0 && (t.threads < 32 || t.threads > 1024 || (t.threads & (t.threads - 1))))
     return fail(AXON_E_ARG, "%s: threads must be a power of two in [32, 1024], got %d", name, t.threads);
   if (a.m < 0 || a.n < 0) return fail(AXON_E_SHAPE, "%s: negative size", name);
   if (a.ld_x < a.n || (OP != OP_RSQRT && a.ld_y < a.n))

@@ -193,7 +193,7 @@ def test_gemm_exp_row_sums(n, block_n, cuda_device):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 @pytest.mark.parametrize("shape", [(1, 8), (3, 1000), (7, 4096), (5, 8200), (2, 65536), (300, 96)])
-@pytest.mark.parametrize("variant", [0, 1, 2])
+@pytest.mark.parametrize("variant", [0, 1, 2, 3])
 def test_row_ops_shapes(dtype, shape, variant, cuda_device):
     g = torch.Generator().manual_seed(SEED)
     x = torch.randn(*shape, generator=g).to(dtype)
@@ -202,7 +202,7 @@ def test_row_ops_shapes(dtype, shape, variant, cuda_device):
     xn = x.float().numpy()
     tune = {"variant": variant}
     row_bytes = shape[1] * x.element_size()
-    if variant == 2 and (row_bytes % 16 or row_bytes > 32768):
+    if (variant == 2 and (row_bytes % 16 or row_bytes > 32768)) or (variant == 3 and row_bytes > CTA_MAX_ROW_BYTES):
         with pytest.raises(N.AxonError) as e:
             ops.layernorm(xd, tune=tune)
         assert e.value.code == N.AXON_E_UNSUPPORTED
@@ -238,6 +238,52 @@ def test_row_bulk_variant_many_rows(shape, threads, cuda_device):
     if shape == (2048, 4096):
         y0 = ops.rmsnorm(x, w, scale=1 / n, eps=1e-6, tune={"variant": 0})
         assert float((y0.float() - y.float()).abs().max()) <= float(y0.float().abs().max()) * 2 ** -7
+
+
+CTA_MAX_ROW_BYTES = 200 * 1024 - 256  # variant 3: the row plus its chunk barriers in 200 KB of shared memory
+
+
+@pytest.mark.parametrize("shape,dtype,tune", [
+    ((4096, 32768), torch.float32, {}),                      # 128 KB rows: 8 chunks of 16 KB, one CTA per SM
+    ((2048, 8192), torch.bfloat16, {}),                      # one 16 KB chunk, several CTAs per SM
+    ((1000, 20000), torch.float32, {"threads": 256, "block_k": 8}),  # 10 chunks, ragged last (6272 B)
+    ((1000, 20000), torch.float32, {"max_ctas": 7}),         # 143 rows per CTA: barrier phases flip many times
+    ((3000, 50000), torch.bfloat16, {"threads": 1024}),      # 100 KB rows, ragged last chunk (1696 B)
+    ((20000, 1024), torch.bfloat16, {"block_k": 1}),         # 2 KB rows in two 1 KB chunks, ~34 rows per CTA
+])
+def test_row_bulk_cta_variant(shape, dtype, tune, cuda_device):
+    """Variant 3: one persistent CTA per row, the row staged in shared memory
+    in chunks and each chunk refilled with the CTA's next row as soon as the
+    output pass has read it; against the float64 oracle on sampled rows."""
+    m, n = shape
+    g = torch.Generator(device=cuda_device).manual_seed(5)
+    x = torch.randn(m, n, generator=g, device=cuda_device).to(dtype)
+    w = (1 + 0.1 * torch.randn(n, generator=g, device=cuda_device)).to(dtype)
+    tune = {"variant": 3, **tune}
+    rows = np.unique(np.linspace(0, m - 1, 97).astype(int))
+    xs = _np(x)[rows]
+    rel = 1e-5 if dtype == torch.float32 else 8e-3
+    _close(_np(ops.rmsnorm(x, w, scale=1 / n, eps=1e-6, tune=tune))[rows], f64.rmsnorm_mean(xs, _np(w), 1e-6),
+           rel, 1e-5, "cta rmsnorm")
+    _close(_np(ops.rmsnorm(x, tune=tune))[rows], f64.rmsnorm_sum(xs), rel, 1e-6, "cta rmsnorm sum")
+    _close(_np(ops.layernorm(x, tune=tune))[rows], f64.layernorm(xs), rel, 1e-4, "cta layernorm")
+    y3 = ops.softmax(x, tune=tune)
+    _close(_np(y3)[rows], f64.softmax(xs), rel, 1e-7, "cta softmax")
+    ops.row_status()
+    # rows of 16 KB or more with a row per SM: the default runs this kernel
+    if len(tune) == 1 and n * x.element_size() >= 16384:
+        assert torch.equal(ops.softmax(x), y3)
+        assert torch.equal(ops.layernorm(x), ops.layernorm(x, tune=tune))
+
+
+@pytest.mark.parametrize("n,tune", [(1024, {"block_k": 65}),   # chunk larger than 64 KB
+                                    (8448, {"block_k": 1}),    # 33 chunks of 1 KB: more than the 32 barriers
+                                    (1024, {"threads": 32})])  # fewer than two warps
+def test_row_bulk_cta_rejects_bad_tunes(n, tune, cuda_device):
+    x = torch.zeros(4, n, device=cuda_device)
+    with pytest.raises(N.AxonError) as e:
+        ops.softmax(x, tune={"variant": 3, **tune})
+    assert e.value.code == N.AXON_E_ARG
 
 
 def test_row_ops_strided_and_unaligned(cuda_device):
