@@ -147,6 +147,16 @@ def case_softmax_long(gen):
     return lambda: ops.softmax(x, out=y)
 
 
+def case_softmax_cta(gen):
+    """row_cta_bulk_kernel: softmax of 2048 fp32 rows of 32768 (128 KB rows
+    staged in shared memory in 16 KB chunks; 512 MB streamed)."""
+    from . import ops
+
+    x = torch.randn(2048, 32768, device="cuda", generator=gen)
+    y = torch.empty_like(x)
+    return lambda: ops.softmax(x, out=y)
+
+
 def _tp_shard(gen, inter):
     h = 4096
     x = _randn(4096, h, gen=gen)
@@ -191,6 +201,7 @@ CASES = {
     "attention_two_gemm": (case_attention_two_gemm, "recip_sum_kernel"),
     "rmsnorm_matmul": (case_rmsnorm_matmul, "gemm_tcgen05"),
     "softmax_long": (case_softmax_long, "row_streaming_kernel"),
+    "softmax_cta": (case_softmax_cta, "row_cta_bulk_kernel"),
     "tp_slabs": (case_tp_slabs, "tp_reduce_push_kernel"),
     "tp_step": (case_tp_step, "swiglu_fused_pair"),
 }
