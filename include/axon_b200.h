@@ -113,12 +113,19 @@ AXON_API int axon_layernorm(const void* x, void* y, int64_t m, int64_t n, int64_
 AXON_API int axon_softmax(const void* x, void* y, int64_t m, int64_t n, int64_t ld_x,
                  int64_t ld_y, int32_t dtype, const axon_tune_t* tune, void* stream);
 
-/* Row-op variants (tune->variant) for the three calls above: 0 = rows held in
- * registers (the default), 1 = streaming passes (any length or alignment),
- * 2 = one warp per row staged in shared memory by bulk copies (16-byte
- * aligned rows of at most 32 KB; tune->threads = warps per CTA x 32).
- * Synchronise `stream` and report whether a variant-2 launch since the last
- * call gave up on a bounded copy wait (AXON_E_TIMEOUT; the flag is cleared).
+/* Row-op variants (tune->variant) for the three calls above: 0 = automatic
+ * (with 16-byte aligned rows and at least a row per SM: variant 3 for rows of
+ * 16 KB and more, variant 2 below; otherwise rows held in registers, or
+ * streaming passes for rows too long for them), 1 = streaming passes (any
+ * length or alignment), 2 = one warp per row staged in shared memory by bulk
+ * copies (16-byte aligned rows of at most 32 KB; tune->threads = warps per
+ * CTA x 32), 3 = one persistent CTA per row staged in shared memory in chunks
+ * by bulk copies, each chunk refilled with the CTA's next row once read
+ * (16-byte aligned rows of a multiple of 16 bytes up to 204544 bytes;
+ * tune->threads 64..1024, tune->block_k = chunk KB, tune->max_ctas caps the
+ * grid).
+ * Synchronise `stream` and report whether a variant-2 or -3 launch since the
+ * last call gave up on a bounded copy wait (AXON_E_TIMEOUT; the flag is cleared).
  * No counterpart in the reference (NKI kernels have no device status). */
 AXON_API int axon_row_status(void* stream);
 
