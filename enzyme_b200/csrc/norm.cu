@@ -501,9 +501,12 @@ __device__ __forceinline__ float cta_allreduce(float v, float* red) {
   return r;
 }
 
+// rmsnorm, layernorm and softmax (the rsqrt prologue of rmsnorm_matmul keeps
+// the warp-per-row kernel).
 template <typename T, int OP>
 __global__ void __launch_bounds__(1024) row_cta_bulk_kernel(RowArgs a, uint32_t row_bytes, uint32_t chunk_bytes,
                                                           int nch) {
+  static_assert(OP == OP_RMS || OP == OP_LN || OP == OP_SM, "row_cta_bulk_kernel: rmsnorm, layernorm, softmax");
   constexpr int E = Vec<T>::E;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ float red[32];
@@ -555,7 +558,7 @@ __global__ void __launch_bounds__(1024) row_cta_bulk_kernel(RowArgs a, uint32_t 
 #pragma unroll
         for (int e = 0; e < E; ++e) {
           const float f = to_f(v.e[e]);
-          if constexpr (OP == OP_RMS || OP == OP_RSQRT) s0 = fmaf(f, f, s0);
+          if constexpr (OP == OP_RMS) s0 = fmaf(f, f, s0);
           else if constexpr (OP == OP_LN) s0 += f;
           else s0 = fmaxf(s0, f);
         }
@@ -566,7 +569,7 @@ __global__ void __launch_bounds__(1024) row_cta_bulk_kernel(RowArgs a, uint32_t 
       clean = false;
       break;
     }
-    if constexpr (OP == OP_RMS || OP == OP_RSQRT) {
+    if constexpr (OP == OP_RMS) {
       s1 = rsqrtf(a.scale * cta_allreduce<false>(s0, red) + a.eps);
     } else if constexpr (OP == OP_LN) {
       s0 = cta_allreduce<false>(s0, red) / static_cast<float>(a.n);
@@ -590,41 +593,32 @@ __global__ void __launch_bounds__(1024) row_cta_bulk_kernel(RowArgs a, uint32_t 
       }
       s1 = 1.0f / cta_allreduce<false>(sum, red);
     }
-    if constexpr (OP == OP_RSQRT) {
-      if (tid == 0) a.r_out[row] = s1;
-      // the reduction ended with a CTA barrier: the buffer is free
+    T* yr = static_cast<T*>(a.y) + row * a.ld_y;
+    const T* w = static_cast<const T*>(a.w);
+    for (int c = 0; c < nch; ++c) {
+      const uint32_t end = chunk_end(c);
+      for (uint32_t p = static_cast<uint32_t>(c) * pkc + tid; p < end; p += nt) {
+        const Vec<T> v = ld_smem_vec(sx + static_cast<size_t>(p) * E);
+        Vec<T> wv;
+        if constexpr (OP == OP_RMS) {
+          if (w != nullptr) wv = ld_vec(w + static_cast<size_t>(p) * E);
+        }
+        Vec<T> o;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const float f = to_f(v.e[e]);
+          float r;
+          if constexpr (OP == OP_RMS) r = w != nullptr ? f * s1 * to_f(wv.e[e]) : f * s1;
+          else if constexpr (OP == OP_LN) r = (f - s0) * s1;
+          else r = __expf(f - s0) * s1;
+          o.e[e] = from_f<T>(r);
+        }
+        st_vec(yr + static_cast<size_t>(p) * E, o);
+      }
+      __syncthreads();  // every thread has read chunk c: refill it
       if (tid == 0 && next < a.m) {
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        for (int c = 0; c < nch; ++c) issue(next, c);
-      }
-    } else {
-      T* yr = static_cast<T*>(a.y) + row * a.ld_y;
-      const T* w = static_cast<const T*>(a.w);
-      for (int c = 0; c < nch; ++c) {
-        const uint32_t end = chunk_end(c);
-        for (uint32_t p = static_cast<uint32_t>(c) * pkc + tid; p < end; p += nt) {
-          const Vec<T> v = ld_smem_vec(sx + static_cast<size_t>(p) * E);
-          Vec<T> wv;
-          if constexpr (OP == OP_RMS) {
-            if (w != nullptr) wv = ld_vec(w + static_cast<size_t>(p) * E);
-          }
-          Vec<T> o;
-#pragma unroll
-          for (int e = 0; e < E; ++e) {
-            const float f = to_f(v.e[e]);
-            float r;
-            if constexpr (OP == OP_RMS) r = w != nullptr ? f * s1 * to_f(wv.e[e]) : f * s1;
-            else if constexpr (OP == OP_LN) r = (f - s0) * s1;
-            else r = __expf(f - s0) * s1;
-            o.e[e] = from_f<T>(r);
-          }
-          st_vec(yr + static_cast<size_t>(p) * E, o);
-        }
-        __syncthreads();  // every thread has read chunk c: refill it
-        if (tid == 0 && next < a.m) {
-          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          issue(next, c);
-        }
+        issue(next, c);
       }
     }
   }
@@ -746,9 +740,11 @@ int launch_rows(const RowArgs& a, const axon_tune_t& t, cudaStream_t s, const ch
   // the warp-per-row kernel stays ahead (rmsnorm 2048 x 4096 bf16 8.5 vs 9.5
   // us). The warp-per-row kernel beat the register-resident one on every
   // measured shape it takes (softmax 16384 x 4096 bf16: 62 vs 111 us).
-  if (OP != OP_RSQRT && t.variant == 0 && t.threads == 0 && vec_ok && row_bytes % 16 == 0 &&
-      row_bytes >= kCtaDefaultMinRowBytes && row_bytes <= kCtaMaxRowBytes && a.m >= sm_count())
-    return launch_rows_cta<T, OP>(a, t, s, name);
+  if constexpr (OP != OP_RSQRT) {
+    if (t.variant == 0 && t.threads == 0 && vec_ok && row_bytes % 16 == 0 && row_bytes >= kCtaDefaultMinRowBytes &&
+        row_bytes <= kCtaMaxRowBytes && a.m >= sm_count())
+      return launch_rows_cta<T, OP>(a, t, s, name);
+  }
   if (t.variant == 0 && t.threads == 0 && bulk_ok && a.m >= sm_count()) return launch_rows_bulk<T, OP>(a, t, s, name);
   if (t.variant == 2) {
     if (!bulk_ok)
@@ -758,11 +754,16 @@ int launch_rows(const RowArgs& a, const axon_tune_t& t, cudaStream_t s, const ch
     return launch_rows_bulk<T, OP>(a, t, s, name);
   }
   if (t.variant == 3) {
-    if (!vec_ok || row_bytes % 16 || row_bytes > kCtaMaxRowBytes)
-      return fail(AXON_E_UNSUPPORTED,
-                  "%s: the CTA bulk variant needs 16-byte aligned rows of a multiple of 16 bytes, at most %lld bytes",
-                  name, (long long)kCtaMaxRowBytes);
-    return launch_rows_cta<T, OP>(a, t, s, name);
+    if constexpr (OP == OP_RSQRT) {
+      return fail(AXON_E_UNSUPPORTED, "%s: no CTA bulk variant", name);
+    } else {
+      if (!vec_ok || row_bytes % 16 || row_bytes > kCtaMaxRowBytes)
+        return fail(AXON_E_UNSUPPORTED,
+                    "%s: the CTA bulk variant needs 16-byte aligned rows of a multiple of 16 bytes, at most %lld "
+                    "bytes",
+                    name, (long long)kCtaMaxRowBytes);
+      return launch_rows_cta<T, OP>(a, t, s, name);
+    }
   }
   int tpr = 0, vpt = 0;
   if (t.variant == 0 && vec_ok) {
