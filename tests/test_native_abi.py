@@ -30,6 +30,20 @@ def test_version_and_variants():
     assert e.value.code == N.AXON_E_UNSUPPORTED
 
 
+def test_row_variants_and_host_checks():
+    """Row ops list variants 0-3; an unknown variant and a CTA size that is not
+    whole warps are refused on the host, before any CUDA call."""
+    lib = N.lib()
+    for op in ("rmsnorm", "layernorm", "softmax"):
+        d = json.loads(N.variants(op))
+        assert [v["id"] for v in d["variants"]] == [0, 1, 2, 3]
+        assert d["variants"][3]["name"] == "row_bulk_cta"
+    fake = ctypes.c_void_p(0x10000)  # never dereferenced: validation fails first
+    for tune, text in ((N.Tune(variant=4), "unknown variant"), (N.Tune(variant=3, threads=100), "multiple of 32")):
+        rc = lib.axon_softmax(fake, fake, 4, 64, 64, 64, N.AXON_F32, ctypes.byref(tune), None)
+        assert rc == N.AXON_E_ARG and text in N.last_error()
+
+
 def test_variants_truncates_to_buffer():
     lib = N.lib()
     need = lib.axon_variants(b"gemm", None, 0)
